@@ -1,0 +1,206 @@
+/*
+ * kernrt_cuda.h — C ABI of the B200 (sm_100a) `cuda` backend for KernRT's
+ * per-row layer ops.
+ *
+ * The ABI mirrors KernRT's `Backend` trait (src/backends/mod.rs:264-404):
+ * activations live in backend-owned device memory and cross the boundary as
+ * opaque buffer handles (`kernrt_buf`, the trait's `Buf(usize)`,
+ * mod.rs:40-42).  Work is enqueued on the backend's own CUDA stream and may be
+ * deferred; `kernrt_cuda_read` is the barrier (mod.rs:8-15, 262-263, 280-282).
+ *
+ * Every function returns 0 on success and a nonzero KERNRT_E_* code on
+ * failure; `kernrt_cuda_last_error()` then holds a message for the calling
+ * thread.  The Rust side panics with that message, matching the reference's
+ * panic-on-misuse convention (e.g. reference.rs:60-61 "buffers must be
+ * distinct", reference.rs:135 "prepare() runs before compute").
+ *
+ * All sizes and offsets are in ELEMENTS of the buffer's element type (f32 for
+ * buffers made by alloc/upload), exactly as in the trait.  Handles are only
+ * valid for the context that made them.  A context is used by one host thread
+ * at a time (the trait is Send, not Sync); it may migrate between threads.
+ */
+#ifndef KERNRT_CUDA_H
+#define KERNRT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct kernrt_cuda_ctx kernrt_cuda_ctx;
+typedef uint64_t kernrt_buf;
+
+enum {
+    KERNRT_OK = 0,
+    KERNRT_E_NO_DEVICE = 1,   /* no CUDA device / driver: BackendError.detail (mod.rs:192-213) */
+    KERNRT_E_INVALID = 2,     /* bad handle, size, offset or aliasing: the reference panics */
+    KERNRT_E_CUDA = 3,        /* a CUDA runtime call failed */
+    KERNRT_E_DEVICE = 4,      /* a kernel reported a bad input (token / position out of range) */
+    KERNRT_E_STATE = 5        /* call out of order (e.g. embed before prepare) */
+};
+
+/* Storage kinds of the token embedding, as Matrix::kind names them
+ * (src/ops/quant.rs:565-572). */
+enum { KERNRT_F32 = 0, KERNRT_BF16 = 1, KERNRT_Q8_0 = 2, KERNRT_Q8_0X4 = 3 };
+
+/* Message for the last failing call on this thread ("" if none). */
+const char *kernrt_cuda_last_error(void);
+
+/* Number of visible CUDA devices (0 when there is no driver or device). */
+int kernrt_cuda_device_count(int *count);
+
+/* Backend construction: replaces `Metal::new` in `backends::open`
+ * (src/backends/mod.rs:228-244).  Fails with KERNRT_E_NO_DEVICE and the message
+ * "no CUDA device" when none is present (the detail tests/backends.rs:335-348
+ * checks for the Metal backend).  `device` < 0 selects KERNRT_CUDA_DEVICE or 0. */
+int kernrt_cuda_create(int device, kernrt_cuda_ctx **out);
+int kernrt_cuda_destroy(kernrt_cuda_ctx *ctx);
+
+/* Backend::name (mod.rs:266) -> "cuda"; Backend::storage (mod.rs:269). */
+const char *kernrt_cuda_name(const kernrt_cuda_ctx *ctx);
+const char *kernrt_cuda_storage(const kernrt_cuda_ctx *ctx);
+
+/* The device's CUDA stream (a cudaStream_t), for callers that time or order
+ * work against it. */
+int kernrt_cuda_stream(kernrt_cuda_ctx *ctx, void **stream);
+
+/* --- Backend::prepare (mod.rs:272): upload the token embedding once. --------
+ * The table is `[vocab, dim]` in the storage it was loaded at
+ * (ModelWeights.token_embedding, mod.rs:131-145):
+ *   f32   : float   [vocab*dim]
+ *   bf16  : uint16  [vocab*dim]  (bf16 bit patterns)
+ *   q8_0  : int8    [vocab*dim] + float scales [vocab*dim/32]  (quant.rs:509-515)
+ *   q8_0x4: the 136-byte four-row blocks of Q8_0x4 (quant.rs:102-117),
+ *           de-interleaved on the device to row-major Q8_0 (quant.rs:198-220). */
+int kernrt_cuda_prepare_embedding(kernrt_cuda_ctx *ctx, int kind, const void *data,
+                                  const float *scales, size_t vocab, size_t dim);
+
+/* --- buffers: Backend::alloc / upload / read (mod.rs:275-282) --------------- */
+/* `len` f32 elements.  Zero-filled (the trait says uninitialised; zeroing is
+ * what the LFM2 ring seeding relies on, lfm2.rs:311-318). */
+int kernrt_cuda_alloc(kernrt_cuda_ctx *ctx, size_t len, kernrt_buf *out);
+int kernrt_cuda_upload(kernrt_cuda_ctx *ctx, const float *data, size_t len, kernrt_buf *out);
+/* Completes all deferred work, then copies `len` elements of `src` to the host. */
+int kernrt_cuda_read(kernrt_cuda_ctx *ctx, kernrt_buf src, float *out, size_t len);
+/* Extensions beyond the trait, for typed outputs (int8 codes, u16 scales, i32
+ * ids): raw byte buffers, and a host->device write into an existing buffer. */
+int kernrt_cuda_alloc_bytes(kernrt_cuda_ctx *ctx, size_t bytes, kernrt_buf *out);
+int kernrt_cuda_write_bytes(kernrt_cuda_ctx *ctx, kernrt_buf dst, size_t dst_byte_off,
+                            const void *src, size_t bytes);
+int kernrt_cuda_read_bytes(kernrt_cuda_ctx *ctx, kernrt_buf src, size_t src_byte_off, void *dst,
+                           size_t bytes);
+/* Device address of a buffer (valid until destroy), for zero-copy interop. */
+int kernrt_cuda_device_ptr(kernrt_cuda_ctx *ctx, kernrt_buf buf, void **ptr);
+/* Wait for all deferred work. */
+int kernrt_cuda_synchronize(kernrt_cuda_ctx *ctx);
+
+/* --- the row ops ------------------------------------------------------------ */
+
+/* Backend::embed (mod.rs:285): decode_row(token) into out[offset..offset+dim]
+ * (reference.rs:133-140, quant.rs:659-693).  Deferred: consecutive calls are
+ * coalesced into one gather launch at the next other op or read. */
+int kernrt_cuda_embed(kernrt_cuda_ctx *ctx, size_t token, kernrt_buf out, size_t offset);
+
+/* Backend::copy (mod.rs:288; reference.rs:142-149): memmove semantics within
+ * one buffer. */
+int kernrt_cuda_copy(kernrt_cuda_ctx *ctx, kernrt_buf src, size_t src_offset, kernrt_buf dst,
+                     size_t dst_offset, size_t len);
+
+/* Backend::rms_norm (mod.rs:290-291; reference.rs:161-178).  out != x. */
+int kernrt_cuda_rms_norm(kernrt_cuda_ctx *ctx, kernrt_buf out, kernrt_buf x, kernrt_buf weight,
+                         size_t rows, size_t dim, float eps);
+
+/* Backend::qk_norm (mod.rs:294-302; reference.rs:180-207): per-head RMSNorm in
+ * place over width/head_size full heads of each row. */
+int kernrt_cuda_qk_norm(kernrt_cuda_ctx *ctx, kernrt_buf v, size_t rows, size_t width,
+                        size_t head_size, kernrt_buf weight, float eps);
+
+/* Backend::rope (mod.rs:306-315; reference.rs:209-257) with RopeSpec
+ * (mod.rs:149-155) flattened: positions[i] (host, usize) for row i; like the
+ * reference's `positions.iter().take(rows)`, min(rows, n_positions) rows are
+ * rotated.  q != k.  head_size must be even. */
+int kernrt_cuda_rope(kernrt_cuda_ctx *ctx, kernrt_buf q, kernrt_buf k, size_t q_width,
+                     size_t kv_width, size_t rows, const uint64_t *positions,
+                     size_t n_positions, size_t head_size, float theta, int interleaved);
+
+/* Backend::add_in_place (mod.rs:361-362; reference.rs:308-313).  dst != src. */
+int kernrt_cuda_add_in_place(kernrt_cuda_ctx *ctx, kernrt_buf dst, kernrt_buf src, size_t len);
+
+/* Backend::mul (mod.rs:370-379; reference.rs:315-363): any aliasing allowed,
+ * with the reference's in-order semantics. */
+int kernrt_cuda_mul(kernrt_cuda_ctx *ctx, kernrt_buf out, size_t out_off, kernrt_buf a,
+                    size_t a_off, kernrt_buf b, size_t b_off, size_t len);
+
+/* Backend::conv_prefill (mod.rs:388; reference.rs:365-370, 490-503). */
+int kernrt_cuda_conv_prefill(kernrt_cuda_ctx *ctx, kernrt_buf out, kernrt_buf x,
+                             kernrt_buf kernel, size_t rows, size_t dim, size_t k);
+
+/* Backend::conv_decode (mod.rs:397; reference.rs:372-393).  out may alias x. */
+int kernrt_cuda_conv_decode(kernrt_cuda_ctx *ctx, kernrt_buf out, kernrt_buf x, kernrt_buf kernel,
+                            kernrt_buf state, size_t dim, size_t k);
+
+/* Backend::silu_mul (mod.rs:399-400; reference.rs:395-400).  gate != up. */
+int kernrt_cuda_silu_mul(kernrt_cuda_ctx *ctx, kernrt_buf gate, kernrt_buf up, size_t len);
+
+/* --- Q8_0 activation quantisation (beyond the trait) -------------------------
+ * Q8Vec::quantize_into (src/ops/quant.rs:856-874) of each of `rows` rows of x:
+ * codes int8 [rows, ceil(dim/32)*32] (tail zero padded), scales f32
+ * [rows, ceil(dim/32)], scales_f16 u16 (same shape; 0 handle = skip).  The
+ * code/scale buffers are byte buffers (kernrt_cuda_alloc_bytes). */
+int kernrt_cuda_quantize_q8_0(kernrt_cuda_ctx *ctx, kernrt_buf x, size_t rows, size_t dim,
+                              kernrt_buf codes, kernrt_buf scales, kernrt_buf scales_f16);
+
+/* rms_norm fused with the quantisation that follows it on the CPU path
+ * (cpu.rs:143-158, 361-369, 501-514 after llama.rs:740/765/858): the normalised
+ * row never goes to HBM. */
+int kernrt_cuda_rms_norm_q8_0(kernrt_cuda_ctx *ctx, kernrt_buf x, kernrt_buf weight, size_t rows,
+                              size_t dim, float eps, kernrt_buf codes, kernrt_buf scales,
+                              kernrt_buf scales_f16);
+
+/* --- the fused layer-op chain ------------------------------------------------
+ * One launch runs a Llama-family block's row ops for `rows` token rows in the
+ * driver's order (llama.rs:734-770; row ops only, contractions elided):
+ *   x = embed(tokens) (if tokens) | x (input);  xb = rms_norm(x, w_att);
+ *   q,k = qk_norm (if w_q/w_k);  q,k = rope(positions);  gate = silu(gate)*up;
+ *   x = x + resid (if resid);  codes/scales = Q8_0(rms_norm(x, w_final)) (if w_final).
+ * Any stage whose buffer handle is 0 is skipped.  `tokens` and `positions`
+ * are int32 byte buffers already on the device; tokens index the prepared
+ * embedding.  The RoPE table must cover positions < rope_max_pos (see
+ * kernrt_cuda_rope_prepare). */
+typedef struct {
+    size_t rows, dim, q_dim, kv_dim, hidden, head_size;
+    float eps, theta, final_eps;
+    int interleaved;
+    kernrt_buf tokens;    /* int32 [rows] or 0 (then x is the input) */
+    kernrt_buf positions; /* int32 [rows] */
+    kernrt_buf x;         /* f32 [rows, dim]: output (embed) or input; x + resid written back */
+    kernrt_buf xb;        /* f32 [rows, dim] out, or 0 */
+    kernrt_buf w_att;     /* f32 [dim] */
+    kernrt_buf q, k;      /* f32 [rows, q_dim], [rows, kv_dim] in place, or 0 */
+    kernrt_buf w_q, w_k;  /* f32 [head_size] or 0 */
+    kernrt_buf gate, up;  /* f32 [rows, hidden], or 0 */
+    kernrt_buf resid;     /* f32 [rows, dim], or 0 */
+    kernrt_buf w_final;   /* f32 [dim], or 0 */
+    kernrt_buf codes, scales, scales_f16; /* Q8_0 outputs when w_final */
+} kernrt_chain_args;
+
+/* Build (or grow) the RoPE cos/sin table for (theta, head_size) to cover
+ * positions [0, max_pos).  Row ops build it on demand; the chain needs it
+ * prepared because its positions are already on the device. */
+int kernrt_cuda_rope_prepare(kernrt_cuda_ctx *ctx, float theta, size_t head_size, size_t max_pos);
+
+int kernrt_cuda_layer_chain(kernrt_cuda_ctx *ctx, const kernrt_chain_args *args);
+
+/* The LFM2 short-conv block's row ops in one launch (lfm2.rs:584-624):
+ * h = B*x; co = conv_prefill(h); ring <- last min(rows,k-1) rows of h;
+ * cy = C*co, with bcx = [B | C | x] thirds per row (lfm2.rs:9-15). */
+int kernrt_cuda_lfm2_conv_block(kernrt_cuda_ctx *ctx, kernrt_buf bcx, kernrt_buf kernel,
+                                kernrt_buf ring, kernrt_buf cy, size_t rows, size_t dim, size_t k);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KERNRT_CUDA_H */

@@ -1,0 +1,304 @@
+"""kernrt_b200 — the B200 (sm_100a) `cuda` backend for KernRT's per-row layer ops.
+
+The product is the C-ABI library ``_lib/libkernrt_cuda.so`` (declared in
+``include/kernrt_cuda.h``).  This package loads it through ctypes and exposes
+:class:`CudaBackend`, a Python mirror of KernRT's ``Backend`` trait
+(src/backends/mod.rs:264-404): same method names, same argument meaning,
+handles instead of slices, ``read`` as the only barrier.  Failures raise
+:class:`KernrtCudaError`, where the Rust reference panics.
+
+There is no CPU fallback: if the library is missing, :func:`load` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "_lib", "libkernrt_cuda.so")
+HEADER = os.path.join(ROOT, "include", "kernrt_cuda.h")
+
+F32, BF16, Q8_0, Q8_0X4 = 0, 1, 2, 3
+KIND_NAMES = {F32: "f32", BF16: "bf16", Q8_0: "q8_0", Q8_0X4: "q8_0x4"}
+E_NO_DEVICE, E_INVALID, E_CUDA, E_DEVICE, E_STATE = 1, 2, 3, 4, 5
+
+_lib = None
+
+
+class KernrtCudaError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+def build(force: bool = False) -> str:
+    """Compile the sm_100a library in-tree (nvcc; no GPU needed)."""
+    args = ["make", "-s", "-C", os.path.join(HERE, "csrc")]
+    if force:
+        subprocess.run(args + ["clean"], check=True)
+    subprocess.run(args, check=True)
+    return LIB_PATH
+
+
+Buf = C.c_uint64
+SZ = C.c_size_t
+P = C.c_void_p
+
+
+class ChainArgs(C.Structure):
+    """Mirror of ``kernrt_chain_args`` (include/kernrt_cuda.h)."""
+
+    _fields_ = [
+        ("rows", SZ), ("dim", SZ), ("q_dim", SZ), ("kv_dim", SZ), ("hidden", SZ), ("head_size", SZ),
+        ("eps", C.c_float), ("theta", C.c_float), ("final_eps", C.c_float), ("interleaved", C.c_int),
+        ("tokens", Buf), ("positions", Buf), ("x", Buf), ("xb", Buf), ("w_att", Buf),
+        ("q", Buf), ("k", Buf), ("w_q", Buf), ("w_k", Buf), ("gate", Buf), ("up", Buf),
+        ("resid", Buf), ("w_final", Buf), ("codes", Buf), ("scales", Buf), ("scales_f16", Buf),
+    ]
+
+
+# Every function include/kernrt_cuda.h declares, with its ctypes signature.
+SIGNATURES = {
+    "kernrt_cuda_last_error": (C.c_char_p, []),
+    "kernrt_cuda_device_count": (C.c_int, [C.POINTER(C.c_int)]),
+    "kernrt_cuda_create": (C.c_int, [C.c_int, C.POINTER(P)]),
+    "kernrt_cuda_destroy": (C.c_int, [P]),
+    "kernrt_cuda_name": (C.c_char_p, [P]),
+    "kernrt_cuda_storage": (C.c_char_p, [P]),
+    "kernrt_cuda_stream": (C.c_int, [P, C.POINTER(P)]),
+    "kernrt_cuda_prepare_embedding": (C.c_int, [P, C.c_int, P, P, SZ, SZ]),
+    "kernrt_cuda_alloc": (C.c_int, [P, SZ, C.POINTER(Buf)]),
+    "kernrt_cuda_upload": (C.c_int, [P, P, SZ, C.POINTER(Buf)]),
+    "kernrt_cuda_read": (C.c_int, [P, Buf, P, SZ]),
+    "kernrt_cuda_alloc_bytes": (C.c_int, [P, SZ, C.POINTER(Buf)]),
+    "kernrt_cuda_write_bytes": (C.c_int, [P, Buf, SZ, P, SZ]),
+    "kernrt_cuda_read_bytes": (C.c_int, [P, Buf, SZ, P, SZ]),
+    "kernrt_cuda_device_ptr": (C.c_int, [P, Buf, C.POINTER(P)]),
+    "kernrt_cuda_synchronize": (C.c_int, [P]),
+    "kernrt_cuda_embed": (C.c_int, [P, SZ, Buf, SZ]),
+    "kernrt_cuda_copy": (C.c_int, [P, Buf, SZ, Buf, SZ, SZ]),
+    "kernrt_cuda_rms_norm": (C.c_int, [P, Buf, Buf, Buf, SZ, SZ, C.c_float]),
+    "kernrt_cuda_qk_norm": (C.c_int, [P, Buf, SZ, SZ, SZ, Buf, C.c_float]),
+    "kernrt_cuda_rope": (C.c_int, [P, Buf, Buf, SZ, SZ, SZ, P, SZ, SZ, C.c_float, C.c_int]),
+    "kernrt_cuda_add_in_place": (C.c_int, [P, Buf, Buf, SZ]),
+    "kernrt_cuda_mul": (C.c_int, [P, Buf, SZ, Buf, SZ, Buf, SZ, SZ]),
+    "kernrt_cuda_conv_prefill": (C.c_int, [P, Buf, Buf, Buf, SZ, SZ, SZ]),
+    "kernrt_cuda_conv_decode": (C.c_int, [P, Buf, Buf, Buf, Buf, SZ, SZ]),
+    "kernrt_cuda_silu_mul": (C.c_int, [P, Buf, Buf, SZ]),
+    "kernrt_cuda_quantize_q8_0": (C.c_int, [P, Buf, SZ, SZ, Buf, Buf, Buf]),
+    "kernrt_cuda_rms_norm_q8_0": (C.c_int, [P, Buf, Buf, SZ, SZ, C.c_float, Buf, Buf, Buf]),
+    "kernrt_cuda_rope_prepare": (C.c_int, [P, C.c_float, SZ, SZ]),
+    "kernrt_cuda_layer_chain": (C.c_int, [P, C.POINTER(ChainArgs)]),
+    "kernrt_cuda_lfm2_conv_block": (C.c_int, [P, Buf, Buf, Buf, Buf, SZ, SZ, SZ]),
+}
+
+
+def load() -> C.CDLL:
+    """Load the backend library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise KernrtCudaError(E_STATE, f"{LIB_PATH} is not built (run kernrt_b200.build())")
+        lib = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    return load().kernrt_cuda_last_error().decode()
+
+
+def _ok(rc: int) -> None:
+    if rc != 0:
+        raise KernrtCudaError(rc, last_error())
+
+
+def device_count() -> int:
+    n = C.c_int(0)
+    _ok(load().kernrt_cuda_device_count(C.byref(n)))
+    return n.value
+
+
+def _ptr(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+class CudaBackend:
+    """KernRT's ``Backend`` trait over the sm_100a library (one CUDA device)."""
+
+    def __init__(self, device: int = -1):
+        self._lib = load()
+        ctx = P()
+        _ok(self._lib.kernrt_cuda_create(int(device), C.byref(ctx)))
+        self._ctx = ctx
+        self._lens: dict[int, int] = {}
+
+    # -- lifecycle ----------------------------------------------------------------
+    def close(self) -> None:
+        if getattr(self, "_ctx", None):
+            self._lib.kernrt_cuda_destroy(self._ctx)
+            self._ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -- identity (mod.rs:265-269) ----------------------------------------------------
+    def name(self) -> str:
+        return self._lib.kernrt_cuda_name(self._ctx).decode()
+
+    def storage(self) -> str:
+        return self._lib.kernrt_cuda_storage(self._ctx).decode()
+
+    def stream(self) -> int:
+        s = P()
+        _ok(self._lib.kernrt_cuda_stream(self._ctx, C.byref(s)))
+        return s.value or 0
+
+    # -- prepare ---------------------------------------------------------------------
+    def prepare_embedding(self, kind: int, data: np.ndarray, scales: np.ndarray | None,
+                          vocab: int, dim: int) -> None:
+        data = np.ascontiguousarray(data)
+        sc = None if scales is None else np.ascontiguousarray(scales, dtype=np.float32)
+        _ok(self._lib.kernrt_cuda_prepare_embedding(self._ctx, kind, _ptr(data),
+                                                    None if sc is None else _ptr(sc), vocab, dim))
+        self._keep = (data, sc)
+
+    # -- buffers ---------------------------------------------------------------------
+    def alloc(self, length: int) -> int:
+        h = Buf()
+        _ok(self._lib.kernrt_cuda_alloc(self._ctx, length, C.byref(h)))
+        return h.value
+
+    def alloc_bytes(self, nbytes: int) -> int:
+        h = Buf()
+        _ok(self._lib.kernrt_cuda_alloc_bytes(self._ctx, nbytes, C.byref(h)))
+        return h.value
+
+    def upload(self, data) -> int:
+        a = np.ascontiguousarray(data, dtype=np.float32).ravel()
+        h = Buf()
+        _ok(self._lib.kernrt_cuda_upload(self._ctx, _ptr(a), a.size, C.byref(h)))
+        return h.value
+
+    def upload_bytes(self, data: np.ndarray) -> int:
+        a = np.ascontiguousarray(data)
+        h = self.alloc_bytes(a.nbytes)
+        self.write_bytes(h, a)
+        return h
+
+    def write_bytes(self, buf: int, data: np.ndarray, byte_offset: int = 0) -> None:
+        a = np.ascontiguousarray(data)
+        _ok(self._lib.kernrt_cuda_write_bytes(self._ctx, buf, byte_offset, _ptr(a), a.nbytes))
+
+    def write_ptr(self, buf: int, host_ptr: int, nbytes: int, byte_offset: int = 0) -> None:
+        _ok(self._lib.kernrt_cuda_write_bytes(self._ctx, buf, byte_offset, host_ptr, nbytes))
+
+    def read(self, src: int, length: int) -> np.ndarray:
+        out = np.empty(length, np.float32)
+        _ok(self._lib.kernrt_cuda_read(self._ctx, src, _ptr(out), length))
+        return out
+
+    def read_into(self, src: int, out: np.ndarray) -> None:
+        _ok(self._lib.kernrt_cuda_read_bytes(self._ctx, src, 0, _ptr(out), out.nbytes))
+
+    def read_ptr(self, src: int, host_ptr: int, nbytes: int, byte_offset: int = 0) -> None:
+        _ok(self._lib.kernrt_cuda_read_bytes(self._ctx, src, byte_offset, host_ptr, nbytes))
+
+    def read_bytes(self, src: int, nbytes: int, dtype) -> np.ndarray:
+        out = np.empty(nbytes // np.dtype(dtype).itemsize, dtype)
+        _ok(self._lib.kernrt_cuda_read_bytes(self._ctx, src, 0, _ptr(out), out.nbytes))
+        return out
+
+    def device_ptr(self, buf: int) -> int:
+        p = P()
+        _ok(self._lib.kernrt_cuda_device_ptr(self._ctx, buf, C.byref(p)))
+        return p.value or 0
+
+    def synchronize(self) -> None:
+        _ok(self._lib.kernrt_cuda_synchronize(self._ctx))
+
+    # -- the row ops (mod.rs:284-400) ------------------------------------------------
+    def embed(self, token: int, out: int, offset: int) -> None:
+        _ok(self._lib.kernrt_cuda_embed(self._ctx, token, out, offset))
+
+    def copy(self, src: int, src_offset: int, dst: int, dst_offset: int, length: int) -> None:
+        _ok(self._lib.kernrt_cuda_copy(self._ctx, src, src_offset, dst, dst_offset, length))
+
+    def rms_norm(self, out: int, x: int, weight: int, rows: int, dim: int, eps: float) -> None:
+        _ok(self._lib.kernrt_cuda_rms_norm(self._ctx, out, x, weight, rows, dim, eps))
+
+    def qk_norm(self, v: int, rows: int, width: int, head_size: int, weight: int, eps: float) -> None:
+        _ok(self._lib.kernrt_cuda_qk_norm(self._ctx, v, rows, width, head_size, weight, eps))
+
+    def rope(self, q: int, k: int, q_width: int, kv_width: int, rows: int, positions,
+             head_size: int, theta: float, interleaved: bool) -> None:
+        pos = np.ascontiguousarray(positions, dtype=np.uint64)
+        _ok(self._lib.kernrt_cuda_rope(self._ctx, q, k, q_width, kv_width, rows, _ptr(pos), pos.size,
+                                       head_size, theta, int(bool(interleaved))))
+
+    def add_in_place(self, dst: int, src: int, length: int) -> None:
+        _ok(self._lib.kernrt_cuda_add_in_place(self._ctx, dst, src, length))
+
+    def mul(self, out: int, out_off: int, a: int, a_off: int, b: int, b_off: int, length: int) -> None:
+        _ok(self._lib.kernrt_cuda_mul(self._ctx, out, out_off, a, a_off, b, b_off, length))
+
+    def conv_prefill(self, out: int, x: int, kernel: int, rows: int, dim: int, k: int) -> None:
+        _ok(self._lib.kernrt_cuda_conv_prefill(self._ctx, out, x, kernel, rows, dim, k))
+
+    def conv_decode(self, out: int, x: int, kernel: int, state: int, dim: int, k: int) -> None:
+        _ok(self._lib.kernrt_cuda_conv_decode(self._ctx, out, x, kernel, state, dim, k))
+
+    def silu_mul(self, gate: int, up: int, length: int) -> None:
+        _ok(self._lib.kernrt_cuda_silu_mul(self._ctx, gate, up, length))
+
+    # -- beyond the trait --------------------------------------------------------------
+    def quantize_q8_0(self, x: int, rows: int, dim: int, codes: int, scales: int,
+                      scales_f16: int = 0) -> None:
+        _ok(self._lib.kernrt_cuda_quantize_q8_0(self._ctx, x, rows, dim, codes, scales, scales_f16))
+
+    def rms_norm_q8_0(self, x: int, weight: int, rows: int, dim: int, eps: float, codes: int,
+                      scales: int, scales_f16: int = 0) -> None:
+        _ok(self._lib.kernrt_cuda_rms_norm_q8_0(self._ctx, x, weight, rows, dim, eps, codes, scales,
+                                                scales_f16))
+
+    def rope_prepare(self, theta: float, head_size: int, max_pos: int) -> None:
+        _ok(self._lib.kernrt_cuda_rope_prepare(self._ctx, theta, head_size, max_pos))
+
+    def layer_chain(self, **kw) -> None:
+        a = ChainArgs()
+        for name, _ in ChainArgs._fields_:
+            if name in kw and kw[name] is not None:
+                setattr(a, name, kw[name])
+        unknown = set(kw) - {n for n, _ in ChainArgs._fields_}
+        if unknown:
+            raise TypeError(f"unknown chain arguments {sorted(unknown)}")
+        _ok(self._lib.kernrt_cuda_layer_chain(self._ctx, C.byref(a)))
+
+    def lfm2_conv_block(self, bcx: int, kernel: int, ring: int, cy: int, rows: int, dim: int,
+                        k: int) -> None:
+        _ok(self._lib.kernrt_cuda_lfm2_conv_block(self._ctx, bcx, kernel, ring, cy, rows, dim, k))
+
+
+def open_backend(name: str = "cuda", device: int = -1) -> CudaBackend:
+    """``backends::open`` for this package's one backend (mod.rs:228-244)."""
+    if name not in ("cuda", "nvidia"):
+        raise KernrtCudaError(E_INVALID, f'unknown backend "{name}"; available: cuda')
+    return CudaBackend(device)

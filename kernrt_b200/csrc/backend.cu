@@ -1,0 +1,882 @@
+// The `cuda` backend: a C++ mirror of KernRT's `Backend` trait
+// (src/backends/mod.rs:264-404) over the sm_100a kernels, exported through the
+// C ABI of include/kernrt_cuda.h.
+//
+// Ownership follows the trait: the backend owns every activation buffer and
+// hands out handles (`Buf(usize)`, mod.rs:40-42); buffers live until the
+// backend is destroyed.  Work is enqueued on one non-blocking CUDA stream per
+// backend; nothing waits except `read`/`synchronize`, the trait's single
+// barrier (mod.rs:262-263).  Host slices the trait borrows only for the call
+// (positions, token ids) are copied into a pinned staging ring at call time.
+// Consecutive `embed` calls are coalesced into one gather launch, flushed by
+// the next other op or barrier.
+//
+// Misuse that the reference turns into a panic (index out of range, aliasing
+// buffers that must be distinct) is detected on the host before any launch
+// and returned as KERNRT_E_INVALID with a message.
+#include "../../include/kernrt_cuda.h"
+#include "kernels.cuh"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace krt {
+
+void build_rope_table(float theta, int head, size_t max_pos, float *cos_out, float *sin_out);
+
+struct Error {
+    int code;
+    std::string msg;
+};
+
+[[noreturn]] static void fail(int code, const std::string &msg) { throw Error{code, msg}; }
+
+static void check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) fail(KERNRT_E_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+static const char *kind_name(int kind) {
+    switch (kind) {
+    case KERNRT_BF16: return "bf16";
+    case KERNRT_Q8_0: return "q8_0";
+    case KERNRT_Q8_0X4: return "q8_0x4";
+    default: return "f32";
+    }
+}
+
+class Backend {
+public:
+    explicit Backend(int device) : device_(device) {
+        check(cudaSetDevice(device_), "cudaSetDevice");
+        check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+        check(cudaMalloc(&d_err_, sizeof(int)), "cudaMalloc(error word)");
+        check(cudaMemsetAsync(d_err_, 0, sizeof(int), stream_), "cudaMemset");
+        check(cudaMallocHost(&h_err_, sizeof(int)), "cudaMallocHost");
+        grow_staging(1 << 20);
+    }
+
+    ~Backend() {
+        cudaSetDevice(device_);
+        cudaStreamSynchronize(stream_);
+        for (auto &b : bufs_) cudaFree(b.ptr);
+        for (auto &t : ropes_) {
+            cudaFree(t.cos);
+            cudaFree(t.sin);
+        }
+        cudaFree(emb_data_);
+        cudaFree(emb_scales_);
+        cudaFree(d_err_);
+        cudaFreeHost(h_err_);
+        cudaFreeHost(stage_host_);
+        cudaFree(stage_dev_);
+        cudaStreamDestroy(stream_);
+    }
+
+    const char *storage() const { return storage_; }
+    cudaStream_t stream() const { return stream_; }
+    void activate() const { check(cudaSetDevice(device_), "cudaSetDevice"); }
+
+    // ---- Backend::prepare: the token embedding in its stored format -------
+    void prepare_embedding(int kind, const void *data, const float *scales, size_t vocab, size_t dim) {
+        if (!data || vocab == 0 || dim == 0) fail(KERNRT_E_INVALID, "empty embedding table");
+        if (kind < KERNRT_F32 || kind > KERNRT_Q8_0X4) fail(KERNRT_E_INVALID, "unknown storage kind");
+        if ((kind == KERNRT_Q8_0 || kind == KERNRT_Q8_0X4) && dim % 32 != 0)
+            fail(KERNRT_E_INVALID, "Q8_0 rows must be a whole number of 32-element blocks");
+        if (kind == KERNRT_Q8_0X4 && vocab % 4 != 0)
+            fail(KERNRT_E_INVALID, "Q8_0x4 tables hold a multiple of four rows");
+        if (kind == KERNRT_Q8_0 && !scales) fail(KERNRT_E_INVALID, "Q8_0 table needs its scales");
+        if (vocab * dim > (size_t)INT32_MAX * 4 || vocab > (size_t)INT32_MAX || dim > (1u << 24))
+            fail(KERNRT_E_INVALID, "embedding table too large");
+        flush();
+        check(cudaStreamSynchronize(stream_), "synchronize");
+        cudaFree(emb_data_);
+        cudaFree(emb_scales_);
+        emb_data_ = nullptr;
+        emb_scales_ = nullptr;
+        const size_t n = vocab * dim;
+        if (kind == KERNRT_F32 || kind == KERNRT_BF16) {
+            const size_t bytes = n * (kind == KERNRT_F32 ? 4 : 2);
+            check(cudaMalloc(&emb_data_, bytes), "cudaMalloc(embedding)");
+            check(cudaMemcpy(emb_data_, data, bytes, cudaMemcpyHostToDevice), "upload embedding");
+            emb_src_ = kind == KERNRT_F32 ? SRC_F32 : SRC_BF16;
+        } else {
+            check(cudaMalloc(&emb_data_, n), "cudaMalloc(embedding)");
+            check(cudaMalloc(&emb_scales_, (n / 32) * sizeof(float)), "cudaMalloc(embedding scales)");
+            if (kind == KERNRT_Q8_0) {
+                check(cudaMemcpy(emb_data_, data, n, cudaMemcpyHostToDevice), "upload embedding");
+                check(cudaMemcpy(emb_scales_, scales, (n / 32) * sizeof(float), cudaMemcpyHostToDevice),
+                      "upload embedding scales");
+            } else {
+                // Q8_0x4 (quant.rs:102-117): 136 bytes per (4 rows x 32 columns),
+                // de-interleaved here to the row-major Q8_0 the kernels read.
+                const size_t blk_bytes = (vocab / 4) * (dim / 32) * 136;
+                void *tmp = nullptr;
+                check(cudaMalloc(&tmp, blk_bytes), "cudaMalloc(q8_0x4 staging)");
+                cudaError_t e = cudaMemcpy(tmp, data, blk_bytes, cudaMemcpyHostToDevice);
+                if (e == cudaSuccess)
+                    e = launch_q8x4_to_row_major(static_cast<const uint8_t *>(tmp), (int)vocab, (int)dim,
+                                                 static_cast<int8_t *>(emb_data_), emb_scales_, stream_);
+                if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+                cudaFree(tmp);
+                check(e, "Q8_0x4 de-interleave");
+            }
+            emb_src_ = SRC_Q8;
+        }
+        emb_kind_ = kind;
+        vocab_ = vocab;
+        dim_ = dim;
+        storage_ = kind_name(kind);
+    }
+
+    // ---- buffers ------------------------------------------------------------
+    kernrt_buf alloc_bytes(size_t bytes) {
+        Buffer b;
+        b.bytes = bytes;
+        check(cudaMalloc(&b.ptr, std::max<size_t>(bytes, 16)), "cudaMalloc");
+        check(cudaMemsetAsync(b.ptr, 0, std::max<size_t>(bytes, 16), stream_), "cudaMemset");
+        bufs_.push_back(b);
+        return (kernrt_buf)bufs_.size();  // handle = index + 1; 0 means "none"
+    }
+
+    kernrt_buf upload(const float *data, size_t len) {
+        if (len && !data) fail(KERNRT_E_INVALID, "null upload source");
+        const kernrt_buf h = alloc_bytes(len * sizeof(float));
+        write_bytes(h, 0, data, len * sizeof(float));
+        return h;
+    }
+
+    void write_bytes(kernrt_buf h, size_t off, const void *src, size_t bytes) {
+        Buffer &b = buf(h);
+        if (off > b.bytes || bytes > b.bytes - off) fail(KERNRT_E_INVALID, "write past the end of the buffer");
+        if (bytes == 0) return;
+        if (!src) fail(KERNRT_E_INVALID, "null write source");
+        flush();
+        check(cudaMemcpyAsync(b.ptr + off, src, bytes, cudaMemcpyHostToDevice, stream_), "cudaMemcpyAsync");
+        // A pageable source may be read after return; page-locked memory is the
+        // caller's to keep alive until the next barrier.
+        cudaPointerAttributes attr{};
+        if (cudaPointerGetAttributes(&attr, src) != cudaSuccess || attr.type != cudaMemoryTypeHost) {
+            cudaGetLastError();
+            check(cudaStreamSynchronize(stream_), "synchronize");
+        }
+    }
+
+    void read_bytes(kernrt_buf h, size_t off, void *dst, size_t bytes) {
+        Buffer &b = buf(h);
+        if (off > b.bytes || bytes > b.bytes - off) fail(KERNRT_E_INVALID, "read past the end of the buffer");
+        flush();
+        if (bytes) {
+            if (!dst) fail(KERNRT_E_INVALID, "null read destination");
+            check(cudaMemcpyAsync(dst, b.ptr + off, bytes, cudaMemcpyDeviceToHost, stream_), "cudaMemcpyAsync");
+        }
+        barrier();
+    }
+
+    void *device_ptr(kernrt_buf h) { return buf(h).ptr; }
+
+    // Completes deferred work and surfaces device-reported input errors.
+    void barrier() {
+        flush();
+        check(cudaMemcpyAsync(h_err_, d_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "error word");
+        check(cudaStreamSynchronize(stream_), "synchronize");
+        const int e = *h_err_;
+        if (e) {
+            check(cudaMemsetAsync(d_err_, 0, sizeof(int), stream_), "cudaMemset");
+            check(cudaStreamSynchronize(stream_), "synchronize");
+            std::string m = "device reported:";
+            if (e & ERR_TOKEN) m += " token id out of range of the embedding table;";
+            if (e & ERR_POSITION) m += " position outside the prepared RoPE table;";
+            fail(KERNRT_E_DEVICE, m);
+        }
+    }
+
+    // ---- Backend::embed (deferred, coalesced) --------------------------------
+    void embed(size_t token, kernrt_buf out, size_t offset) {
+        if (emb_kind_ < 0) fail(KERNRT_E_STATE, "prepare() runs before compute");
+        if (token >= vocab_) fail(KERNRT_E_INVALID, "token " + std::to_string(token) + " out of range for vocab " + std::to_string(vocab_));
+        const Buffer &b = buf(out);
+        if (offset > b.bytes / 4 || dim_ > b.bytes / 4 - offset) fail(KERNRT_E_INVALID, "embed writes past the end of the buffer");
+        if (!pending_.empty() && pending_.back().out != out) flush();
+        pending_.push_back({(int32_t)token, out, (int64_t)offset});
+    }
+
+    // ---- row ops ----------------------------------------------------------------
+    void copy(kernrt_buf src, size_t so, kernrt_buf dst, size_t d_o, size_t len) {
+        Buffer &s = buf(src), &d = buf(dst);
+        span(s, so, len, "copy source");
+        span(d, d_o, len, "copy destination");
+        flush();
+        if (len == 0) return;
+        char *sp = s.ptr + so * 4, *dp = d.ptr + d_o * 4;
+        const size_t bytes = len * 4;
+        if (src == dst && sp != dp && sp < dp + bytes && dp < sp + bytes) {
+            // copy_within: overlapping ranges go through a temporary.
+            void *tmp = nullptr;
+            check(cudaMallocAsync(&tmp, bytes, stream_), "cudaMallocAsync");
+            check(cudaMemcpyAsync(tmp, sp, bytes, cudaMemcpyDeviceToDevice, stream_), "copy");
+            check(cudaMemcpyAsync(dp, tmp, bytes, cudaMemcpyDeviceToDevice, stream_), "copy");
+            check(cudaFreeAsync(tmp, stream_), "cudaFreeAsync");
+        } else if (sp != dp) {
+            check(cudaMemcpyAsync(dp, sp, bytes, cudaMemcpyDeviceToDevice, stream_), "copy");
+        }
+    }
+
+    void rms_norm(kernrt_buf out, kernrt_buf x, kernrt_buf weight, size_t rows, size_t dim, float eps) {
+        distinct(out, x);
+        Buffer &o = buf(out), &xi = buf(x), &w = buf(weight);
+        span(o, 0, rows * dim, "rms_norm out");
+        span(xi, 0, rows * dim, "rms_norm x");
+        span(w, 0, dim, "rms_norm weight");
+        flush();
+        if (rows == 0 || dim == 0) return;
+        ChainArgs a = blank(rows, dim);
+        a.eps = eps;
+        a.x_in = f(xi);
+        a.xb = f(o);
+        a.w_att = f(w);
+        launch_or_fail(launch_chain(SRC_X, a, stream_), "rms_norm");
+    }
+
+    void qk_norm(kernrt_buf v, size_t rows, size_t width, size_t head, kernrt_buf weight, float eps) {
+        if (head == 0) fail(KERNRT_E_INVALID, "head_size must be positive");
+        Buffer &vb = buf(v), &w = buf(weight);
+        span(vb, 0, rows * width, "qk_norm v");
+        span(w, 0, head, "qk_norm weight");
+        fits_int(rows * width, "qk_norm");
+        flush();
+        launch_or_fail(launch_qk_norm(f(vb), (int)rows, (int)width, (int)head, f(w), eps, stream_), "qk_norm");
+    }
+
+    void rope(kernrt_buf q, kernrt_buf k, size_t qw, size_t kvw, size_t rows, const uint64_t *positions,
+              size_t n_positions, size_t head, float theta, int interleaved) {
+        distinct(q, k);
+        if (head == 0 || head % 2) fail(KERNRT_E_INVALID, "head_size must be a positive even number");
+        if (interleaved && kvw % 2) fail(KERNRT_E_INVALID, "interleaved RoPE needs an even kv width");
+        rows = std::min(rows, n_positions);
+        Buffer &qb = buf(q), &kb = buf(k);
+        span(qb, 0, rows * qw, "rope q");
+        span(kb, 0, rows * kvw, "rope k");
+        fits_int(rows * std::max(qw, kvw), "rope");
+        flush();
+        if (rows == 0) return;
+        if (!positions) fail(KERNRT_E_INVALID, "null positions");
+        std::vector<int32_t> pos(rows);
+        uint64_t maxp = 0;
+        for (size_t i = 0; i < rows; ++i) {
+            if (positions[i] > (uint64_t)INT32_MAX - 1) fail(KERNRT_E_INVALID, "position too large");
+            pos[i] = (int32_t)positions[i];
+            maxp = std::max(maxp, positions[i]);
+        }
+        const RopeTable &t = rope_table(theta, head, (size_t)maxp + 1);
+        const int32_t *dpos = static_cast<const int32_t *>(stage(pos.data(), rows * sizeof(int32_t)));
+        launch_or_fail(launch_rope(f(qb), f(kb), (int)qw, (int)kvw, (int)rows, (int)head, dpos, t.cos, t.sin,
+                                   (int)t.max_pos, interleaved, d_err_, stream_),
+                       "rope");
+    }
+
+    void add_in_place(kernrt_buf dst, kernrt_buf src, size_t len) {
+        distinct(dst, src);
+        Buffer &d = buf(dst), &s = buf(src);
+        span(d, 0, len, "add dst");
+        span(s, 0, len, "add src");
+        flush();
+        launch_or_fail(launch_add(f(d), f(s), len, stream_), "add_in_place");
+    }
+
+    void mul(kernrt_buf out, size_t oo, kernrt_buf a, size_t ao, kernrt_buf b, size_t bo, size_t len) {
+        Buffer &ob = buf(out), &ab = buf(a), &bb = buf(b);
+        span(ob, oo, len, "mul out");
+        span(ab, ao, len, "mul a");
+        span(bb, bo, len, "mul b");
+        flush();
+        // A write of one index can feed another index's read only when out
+        // shares a buffer with an operand at a different, overlapping offset.
+        auto hazard = [&](kernrt_buf x, size_t xo) {
+            return x == out && xo != oo && (xo < oo ? oo - xo : xo - oo) < len;
+        };
+        const bool seq = hazard(a, ao) || hazard(b, bo);
+        launch_or_fail(launch_mul(f(ob) + oo, f(ab) + ao, f(bb) + bo, len, seq, stream_), "mul");
+    }
+
+    void conv_prefill(kernrt_buf out, kernrt_buf x, kernrt_buf kernel, size_t rows, size_t dim, size_t k) {
+        if (k == 0) fail(KERNRT_E_INVALID, "conv kernel size must be positive");
+        Buffer &ob = buf(out), &xb = buf(x), &kb = buf(kernel);
+        span(ob, 0, rows * dim, "conv out");
+        span(xb, 0, rows * dim, "conv x");
+        span(kb, 0, dim * k, "conv kernel");
+        fits_int(rows * dim, "conv_prefill");
+        flush();
+        if (rows * dim == 0) return;
+        // The reference reads cloned inputs (reference.rs:366-369): an aliased
+        // input is snapshotted first.
+        const float *xp = f(xb), *kp = f(kb);
+        void *tx = nullptr, *tk = nullptr;
+        if (x == out) {
+            check(cudaMallocAsync(&tx, rows * dim * 4, stream_), "cudaMallocAsync");
+            check(cudaMemcpyAsync(tx, xp, rows * dim * 4, cudaMemcpyDeviceToDevice, stream_), "copy");
+            xp = static_cast<const float *>(tx);
+        }
+        if (kernel == out) {
+            check(cudaMallocAsync(&tk, dim * k * 4, stream_), "cudaMallocAsync");
+            check(cudaMemcpyAsync(tk, kp, dim * k * 4, cudaMemcpyDeviceToDevice, stream_), "copy");
+            kp = static_cast<const float *>(tk);
+        }
+        const cudaError_t e = launch_conv_prefill(f(ob), xp, kp, (int)rows, (int)dim, (int)k, stream_);
+        if (tx) cudaFreeAsync(tx, stream_);
+        if (tk) cudaFreeAsync(tk, stream_);
+        launch_or_fail(e, "conv_prefill");
+    }
+
+    void conv_decode(kernrt_buf out, kernrt_buf x, kernrt_buf kernel, kernrt_buf state, size_t dim, size_t k) {
+        if (k == 0) fail(KERNRT_E_INVALID, "conv kernel size must be positive");
+        if (state == out || state == x || state == kernel)
+            fail(KERNRT_E_INVALID, "conv_decode state must be distinct from out, x and kernel");
+        if (kernel == out) fail(KERNRT_E_INVALID, "conv_decode kernel must be distinct from out");
+        Buffer &ob = buf(out), &xb = buf(x), &kb = buf(kernel), &sb = buf(state);
+        span(ob, 0, dim, "conv_decode out");
+        span(xb, 0, dim, "conv_decode x");
+        span(kb, 0, dim * k, "conv_decode kernel");
+        span(sb, 0, (k - 1) * dim, "conv_decode state");
+        fits_int(dim * k, "conv_decode");
+        flush();
+        launch_or_fail(launch_conv_decode(f(ob), f(xb), f(kb), f(sb), (int)dim, (int)k, stream_), "conv_decode");
+    }
+
+    void silu_mul(kernrt_buf gate, kernrt_buf up, size_t len) {
+        distinct(gate, up);
+        Buffer &g = buf(gate), &u = buf(up);
+        span(g, 0, len, "silu gate");
+        span(u, 0, len, "silu up");
+        flush();
+        launch_or_fail(launch_silu_mul(f(g), f(u), len, stream_), "silu_mul");
+    }
+
+    // ---- Q8_0 -----------------------------------------------------------------
+    void quantize_q8_0(kernrt_buf x, size_t rows, size_t dim, kernrt_buf codes, kernrt_buf scales,
+                       kernrt_buf scales16) {
+        Buffer &xb = buf(x);
+        span(xb, 0, rows * dim, "quantize x");
+        int8_t *c;
+        float *s;
+        uint16_t *h;
+        q8_outputs(rows, dim, codes, scales, scales16, &c, &s, &h);
+        fits_int(rows * dim, "quantize");
+        flush();
+        launch_or_fail(launch_quantize_q8(f(xb), (int)rows, (int)dim, c, s, h, stream_), "quantize_q8_0");
+    }
+
+    void rms_norm_q8_0(kernrt_buf x, kernrt_buf weight, size_t rows, size_t dim, float eps, kernrt_buf codes,
+                       kernrt_buf scales, kernrt_buf scales16) {
+        Buffer &xb = buf(x), &w = buf(weight);
+        span(xb, 0, rows * dim, "rms_norm_q8_0 x");
+        span(w, 0, dim, "rms_norm_q8_0 weight");
+        ChainArgs a = blank(rows, dim);
+        q8_outputs(rows, dim, codes, scales, scales16, &a.codes, &a.scales, &a.scales16);
+        flush();
+        if (rows == 0 || dim == 0) return;
+        a.eps = eps;
+        a.final_eps = eps;
+        a.x_in = f(xb);
+        a.w_final = f(w);
+        launch_or_fail(launch_chain(SRC_X, a, stream_), "rms_norm_q8_0");
+    }
+
+    // ---- fused chains -------------------------------------------------------------
+    void rope_prepare(float theta, size_t head, size_t max_pos) {
+        if (head == 0 || head % 2) fail(KERNRT_E_INVALID, "head_size must be a positive even number");
+        flush();
+        rope_table(theta, head, max_pos);
+    }
+
+    void layer_chain(const kernrt_chain_args &c) {
+        const size_t rows = c.rows, dim = c.dim;
+        if (rows == 0) return;
+        if (dim == 0) fail(KERNRT_E_INVALID, "chain dim must be positive");
+        fits_int(rows * std::max({dim, c.q_dim, c.kv_dim, c.hidden}), "layer_chain");
+        ChainArgs a = blank(rows, dim);
+        a.eps = c.eps;
+        a.final_eps = c.final_eps;
+        int src = SRC_X;
+        if (!c.x) fail(KERNRT_E_INVALID, "chain needs x");
+        Buffer &xb = buf(c.x);
+        span(xb, 0, rows * dim, "chain x");
+        if (c.tokens) {
+            if (emb_kind_ < 0) fail(KERNRT_E_STATE, "prepare() runs before compute");
+            if (dim != dim_) fail(KERNRT_E_INVALID, "chain dim differs from the embedding width");
+            Buffer &tb = buf(c.tokens);
+            if (tb.bytes < rows * 4) fail(KERNRT_E_INVALID, "chain tokens buffer too small");
+            src = emb_src_;
+            a.table = emb_data_;
+            a.tscales = emb_scales_;
+            a.vocab = (int)vocab_;
+            a.tokens = reinterpret_cast<const int32_t *>(tb.ptr);
+            a.x_out = f(xb);
+        } else {
+            a.x_in = f(xb);
+            if (c.resid) a.x_out = f(xb);
+        }
+        if (!c.w_att) fail(KERNRT_E_INVALID, "chain needs w_att");
+        a.w_att = f(buf(c.w_att));
+        span(buf(c.w_att), 0, dim, "chain w_att");
+        if (c.xb) {
+            if (c.xb == c.x) fail(KERNRT_E_INVALID, "buffers must be distinct (xb, x)");
+            span(buf(c.xb), 0, rows * dim, "chain xb");
+            a.xb = f(buf(c.xb));
+        }
+        if (c.resid) {
+            if (c.resid == c.x) fail(KERNRT_E_INVALID, "buffers must be distinct (resid, x)");
+            span(buf(c.resid), 0, rows * dim, "chain resid");
+            a.resid = f(buf(c.resid));
+        }
+        const size_t head = c.head_size;
+        if (c.q || c.k || c.w_q || c.w_k) {
+            if (head == 0 || head % 2) fail(KERNRT_E_INVALID, "head_size must be a positive even number");
+            if (c.q && c.k && c.q == c.k) fail(KERNRT_E_INVALID, "buffers must be distinct (q, k)");
+            if (c.interleaved && c.kv_dim % 2) fail(KERNRT_E_INVALID, "interleaved RoPE needs an even kv width");
+            a.head = (int)head;
+            a.half = (int)(head / 2);
+            a.q_dim = (int)c.q_dim;
+            a.kv_dim = (int)c.kv_dim;
+            if (c.q) { span(buf(c.q), 0, rows * c.q_dim, "chain q"); a.q = f(buf(c.q)); }
+            if (c.k) { span(buf(c.k), 0, rows * c.kv_dim, "chain k"); a.k = f(buf(c.k)); }
+            if (c.w_q) { span(buf(c.w_q), 0, head, "chain w_q"); a.w_q = f(buf(c.w_q)); }
+            if (c.w_k) { span(buf(c.w_k), 0, head, "chain w_k"); a.w_k = f(buf(c.w_k)); }
+            if ((c.q || c.k) && c.positions) {
+                Buffer &pb = buf(c.positions);
+                if (pb.bytes < rows * 4) fail(KERNRT_E_INVALID, "chain positions buffer too small");
+                const RopeTable *t = find_rope(c.theta, head);
+                if (!t) fail(KERNRT_E_STATE, "kernrt_cuda_rope_prepare runs before a chain with RoPE");
+                a.pos = reinterpret_cast<const int32_t *>(pb.ptr);
+                a.cos_t = t->cos;
+                a.sin_t = t->sin;
+                a.max_pos = (int)t->max_pos;
+                a.rope_mode = c.interleaved ? 2 : 1;
+            }
+        }
+        if (c.gate) {
+            if (!c.up || c.up == c.gate) fail(KERNRT_E_INVALID, "buffers must be distinct (gate, up)");
+            span(buf(c.gate), 0, rows * c.hidden, "chain gate");
+            span(buf(c.up), 0, rows * c.hidden, "chain up");
+            a.gate = f(buf(c.gate));
+            a.up = f(buf(c.up));
+            a.hidden = (int)c.hidden;
+        }
+        if (c.w_final) {
+            span(buf(c.w_final), 0, dim, "chain w_final");
+            a.w_final = f(buf(c.w_final));
+            q8_outputs(rows, dim, c.codes, c.scales, c.scales_f16, &a.codes, &a.scales, &a.scales16);
+        }
+        flush();
+        launch_or_fail(launch_chain(src, a, stream_), "layer_chain");
+    }
+
+    void lfm2_conv_block(kernrt_buf bcx, kernrt_buf kernel, kernrt_buf ring, kernrt_buf cy, size_t rows,
+                         size_t dim, size_t k) {
+        if (k == 0) fail(KERNRT_E_INVALID, "conv kernel size must be positive");
+        if (cy == bcx || ring == bcx || ring == cy) fail(KERNRT_E_INVALID, "buffers must be distinct");
+        span(buf(bcx), 0, rows * 3 * dim, "conv block bcx");
+        span(buf(kernel), 0, dim * k, "conv block kernel");
+        span(buf(cy), 0, rows * dim, "conv block cy");
+        if (k > 1) span(buf(ring), 0, (k - 1) * dim, "conv block ring");
+        fits_int(rows * 3 * dim, "lfm2_conv_block");
+        flush();
+        launch_or_fail(launch_lfm2_conv_block(f(buf(bcx)), f(buf(kernel)), f(buf(ring)), f(buf(cy)), (int)rows,
+                                              (int)dim, (int)k, stream_),
+                       "lfm2_conv_block");
+    }
+
+    // Launch all pending embeds (one gather per run of calls into one buffer).
+    void flush() {
+        if (pending_.empty()) return;
+        const kernrt_buf out = pending_.front().out;
+        const size_t n = pending_.size();
+        std::vector<int32_t> tok(n);
+        std::vector<int64_t> off(n);
+        bool aligned = true;
+        for (size_t i = 0; i < n; ++i) {
+            tok[i] = pending_[i].token;
+            off[i] = pending_[i].offset;
+            aligned = aligned && (off[i] % 4 == 0);
+        }
+        pending_.clear();
+        GatherArgs g{};
+        g.table = emb_data_;
+        g.tscales = emb_scales_;
+        g.vocab = (int)vocab_;
+        g.dim = (int)dim_;
+        g.tokens = static_cast<const int32_t *>(stage(tok.data(), n * sizeof(int32_t)));
+        g.dst_off = static_cast<const int64_t *>(stage(off.data(), n * sizeof(int64_t)));
+        g.dst = f(buf(out));
+        g.n = (int)n;
+        g.err = d_err_;
+        const bool vec = aligned && (emb_src_ == SRC_BF16 ? dim_ % 8 == 0 : emb_src_ == SRC_Q8 ? dim_ % 16 == 0 : dim_ % 4 == 0);
+        launch_or_fail(launch_embed_gather(emb_src_, vec, g, stream_), "embed");
+    }
+
+private:
+    struct Buffer {
+        char *ptr = nullptr;
+        size_t bytes = 0;
+    };
+    struct RopeTable {
+        float theta;
+        size_t head;
+        size_t max_pos;
+        float *cos = nullptr;
+        float *sin = nullptr;
+    };
+    struct Pending {
+        int32_t token;
+        kernrt_buf out;
+        int64_t offset;
+    };
+
+    Buffer &buf(kernrt_buf h) {
+        if (h == 0 || h > bufs_.size()) fail(KERNRT_E_INVALID, "invalid buffer handle " + std::to_string(h));
+        return bufs_[h - 1];
+    }
+    static float *f(Buffer &b) { return reinterpret_cast<float *>(b.ptr); }
+    static void span(const Buffer &b, size_t off, size_t len, const char *what) {
+        const size_t n = b.bytes / 4;
+        if (off > n || len > n - off)
+            fail(KERNRT_E_INVALID, std::string(what) + ": range [" + std::to_string(off) + ", " +
+                                       std::to_string(off + len) + ") outside a buffer of " + std::to_string(n));
+    }
+    static void distinct(kernrt_buf a, kernrt_buf b) {
+        if (a == b) fail(KERNRT_E_INVALID, "buffers must be distinct");
+    }
+    static void fits_int(size_t n, const char *what) {
+        if (n > (size_t)INT32_MAX) fail(KERNRT_E_INVALID, std::string(what) + ": too many elements for one launch");
+    }
+    static void launch_or_fail(cudaError_t e, const char *what) { check(e, what); }
+
+    ChainArgs blank(size_t rows, size_t dim) const {
+        ChainArgs a{};
+        a.rows = (int)rows;
+        a.dim = (int)dim;
+        a.err = d_err_;
+        return a;
+    }
+
+    void q8_outputs(size_t rows, size_t dim, kernrt_buf codes, kernrt_buf scales, kernrt_buf scales16,
+                    int8_t **c, float **s, uint16_t **h) {
+        const size_t nb = (dim + 31) / 32;
+        Buffer &cb = buf(codes), &sb = buf(scales);
+        if (cb.bytes < rows * nb * 32) fail(KERNRT_E_INVALID, "codes buffer too small");
+        if (sb.bytes < rows * nb * 4) fail(KERNRT_E_INVALID, "scales buffer too small");
+        *c = reinterpret_cast<int8_t *>(cb.ptr);
+        *s = reinterpret_cast<float *>(sb.ptr);
+        *h = nullptr;
+        if (scales16) {
+            Buffer &hb = buf(scales16);
+            if (hb.bytes < rows * nb * 2) fail(KERNRT_E_INVALID, "f16 scales buffer too small");
+            *h = reinterpret_cast<uint16_t *>(hb.ptr);
+        }
+    }
+
+    const RopeTable *find_rope(float theta, size_t head) const {
+        for (const auto &t : ropes_)
+            if (t.theta == theta && t.head == head) return &t;
+        return nullptr;
+    }
+
+    // The table for (theta, head) covering positions < need, built or grown.
+    const RopeTable &rope_table(float theta, size_t head, size_t need) {
+        RopeTable *t = nullptr;
+        for (auto &r : ropes_)
+            if (r.theta == theta && r.head == head) t = &r;
+        if (t && t->max_pos >= need) return *t;
+        size_t cap = std::max<size_t>(need, 4096);
+        if (t) cap = std::max(cap, 2 * t->max_pos);
+        const size_t half = head / 2, n = cap * half;
+        std::vector<float> hc(n), hs(n);
+        build_rope_table(theta, (int)head, cap, hc.data(), hs.data());
+        check(cudaStreamSynchronize(stream_), "synchronize");  // old table may still be read
+        if (!t) {
+            ropes_.push_back(RopeTable{theta, head, 0, nullptr, nullptr});
+            t = &ropes_.back();
+        }
+        cudaFree(t->cos);
+        cudaFree(t->sin);
+        t->cos = t->sin = nullptr;
+        check(cudaMalloc(&t->cos, n * 4), "cudaMalloc(rope)");
+        check(cudaMalloc(&t->sin, n * 4), "cudaMalloc(rope)");
+        check(cudaMemcpy(t->cos, hc.data(), n * 4, cudaMemcpyHostToDevice), "upload rope table");
+        check(cudaMemcpy(t->sin, hs.data(), n * 4, cudaMemcpyHostToDevice), "upload rope table");
+        t->max_pos = cap;
+        return *t;
+    }
+
+    // Copy a host slice into the pinned ring and enqueue its upload; returns
+    // the device address.  The ring wraps after a stream synchronize, so a
+    // region is never rewritten while a copy from it may be pending.
+    void *stage(const void *src, size_t bytes) {
+        const size_t need = (bytes + 255) & ~(size_t)255;
+        if (need > stage_cap_) {
+            check(cudaStreamSynchronize(stream_), "synchronize");
+            grow_staging(2 * need);
+        } else if (stage_head_ + need > stage_cap_) {
+            check(cudaStreamSynchronize(stream_), "synchronize");
+            stage_head_ = 0;
+        }
+        char *h = stage_host_ + stage_head_;
+        char *d = stage_dev_ + stage_head_;
+        std::memcpy(h, src, bytes);
+        check(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, stream_), "stage");
+        stage_head_ += need;
+        return d;
+    }
+
+    void grow_staging(size_t cap) {
+        cudaFreeHost(stage_host_);
+        cudaFree(stage_dev_);
+        stage_host_ = nullptr;
+        stage_dev_ = nullptr;
+        check(cudaMallocHost(&stage_host_, cap), "cudaMallocHost(staging)");
+        check(cudaMalloc(&stage_dev_, cap), "cudaMalloc(staging)");
+        stage_cap_ = cap;
+        stage_head_ = 0;
+    }
+
+    int device_;
+    cudaStream_t stream_ = nullptr;
+    std::vector<Buffer> bufs_;
+    std::vector<RopeTable> ropes_;
+    std::vector<Pending> pending_;
+    int emb_kind_ = -1;
+    int emb_src_ = SRC_F32;
+    size_t vocab_ = 0, dim_ = 0;
+    void *emb_data_ = nullptr;
+    float *emb_scales_ = nullptr;
+    const char *storage_ = "f32";
+    int *d_err_ = nullptr;
+    int *h_err_ = nullptr;
+    char *stage_host_ = nullptr;
+    char *stage_dev_ = nullptr;
+    size_t stage_cap_ = 0, stage_head_ = 0;
+};
+
+}  // namespace krt
+
+// =============================================================================
+// C ABI
+// =============================================================================
+
+struct kernrt_cuda_ctx {
+    krt::Backend *b;
+};
+
+static thread_local std::string g_last_error;
+
+template <class F>
+static int guard(kernrt_cuda_ctx *ctx, F &&fn) {
+    if (!ctx || !ctx->b) {
+        g_last_error = "null kernrt_cuda context";
+        return KERNRT_E_INVALID;
+    }
+    try {
+        ctx->b->activate();
+        fn(*ctx->b);
+        return KERNRT_OK;
+    } catch (const krt::Error &e) {
+        g_last_error = e.msg;
+        return e.code;
+    } catch (const std::exception &e) {
+        g_last_error = e.what();
+        return KERNRT_E_CUDA;
+    }
+}
+
+extern "C" {
+
+const char *kernrt_cuda_last_error(void) { return g_last_error.c_str(); }
+
+int kernrt_cuda_device_count(int *count) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    if (count) *count = n;
+    return KERNRT_OK;
+}
+
+int kernrt_cuda_create(int device, kernrt_cuda_ctx **out) {
+    if (!out) {
+        g_last_error = "null output pointer";
+        return KERNRT_E_INVALID;
+    }
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        g_last_error = "no CUDA device";
+        return KERNRT_E_NO_DEVICE;
+    }
+    if (device < 0) {
+        const char *env = std::getenv("KERNRT_CUDA_DEVICE");
+        device = env && *env ? std::atoi(env) : 0;
+    }
+    if (device >= n) {
+        g_last_error = "CUDA device " + std::to_string(device) + " not present (" + std::to_string(n) + " visible)";
+        return KERNRT_E_NO_DEVICE;
+    }
+    try {
+        auto *c = new kernrt_cuda_ctx{new krt::Backend(device)};
+        *out = c;
+        return KERNRT_OK;
+    } catch (const krt::Error &e) {
+        g_last_error = e.msg;
+        return e.code;
+    }
+}
+
+int kernrt_cuda_destroy(kernrt_cuda_ctx *ctx) {
+    if (!ctx) return KERNRT_OK;
+    delete ctx->b;
+    delete ctx;
+    return KERNRT_OK;
+}
+
+const char *kernrt_cuda_name(const kernrt_cuda_ctx *) { return "cuda"; }
+
+const char *kernrt_cuda_storage(const kernrt_cuda_ctx *ctx) {
+    return ctx && ctx->b ? ctx->b->storage() : "f32";
+}
+
+int kernrt_cuda_stream(kernrt_cuda_ctx *ctx, void **stream) {
+    return guard(ctx, [&](krt::Backend &b) {
+        if (!stream) krt::fail(KERNRT_E_INVALID, "null output pointer");
+        *stream = (void *)b.stream();
+    });
+}
+
+int kernrt_cuda_prepare_embedding(kernrt_cuda_ctx *ctx, int kind, const void *data, const float *scales,
+                                  size_t vocab, size_t dim) {
+    return guard(ctx, [&](krt::Backend &b) { b.prepare_embedding(kind, data, scales, vocab, dim); });
+}
+
+int kernrt_cuda_alloc(kernrt_cuda_ctx *ctx, size_t len, kernrt_buf *out) {
+    return guard(ctx, [&](krt::Backend &b) {
+        if (!out) krt::fail(KERNRT_E_INVALID, "null output pointer");
+        *out = b.alloc_bytes(len * sizeof(float));
+    });
+}
+
+int kernrt_cuda_alloc_bytes(kernrt_cuda_ctx *ctx, size_t bytes, kernrt_buf *out) {
+    return guard(ctx, [&](krt::Backend &b) {
+        if (!out) krt::fail(KERNRT_E_INVALID, "null output pointer");
+        *out = b.alloc_bytes(bytes);
+    });
+}
+
+int kernrt_cuda_upload(kernrt_cuda_ctx *ctx, const float *data, size_t len, kernrt_buf *out) {
+    return guard(ctx, [&](krt::Backend &b) {
+        if (!out) krt::fail(KERNRT_E_INVALID, "null output pointer");
+        *out = b.upload(data, len);
+    });
+}
+
+int kernrt_cuda_read(kernrt_cuda_ctx *ctx, kernrt_buf src, float *out, size_t len) {
+    return guard(ctx, [&](krt::Backend &b) { b.read_bytes(src, 0, out, len * sizeof(float)); });
+}
+
+int kernrt_cuda_write_bytes(kernrt_cuda_ctx *ctx, kernrt_buf dst, size_t off, const void *src, size_t bytes) {
+    return guard(ctx, [&](krt::Backend &b) { b.write_bytes(dst, off, src, bytes); });
+}
+
+int kernrt_cuda_read_bytes(kernrt_cuda_ctx *ctx, kernrt_buf src, size_t off, void *dst, size_t bytes) {
+    return guard(ctx, [&](krt::Backend &b) { b.read_bytes(src, off, dst, bytes); });
+}
+
+int kernrt_cuda_device_ptr(kernrt_cuda_ctx *ctx, kernrt_buf h, void **ptr) {
+    return guard(ctx, [&](krt::Backend &b) {
+        if (!ptr) krt::fail(KERNRT_E_INVALID, "null output pointer");
+        *ptr = b.device_ptr(h);
+    });
+}
+
+int kernrt_cuda_synchronize(kernrt_cuda_ctx *ctx) {
+    return guard(ctx, [&](krt::Backend &b) { b.barrier(); });
+}
+
+int kernrt_cuda_embed(kernrt_cuda_ctx *ctx, size_t token, kernrt_buf out, size_t offset) {
+    return guard(ctx, [&](krt::Backend &b) { b.embed(token, out, offset); });
+}
+
+int kernrt_cuda_copy(kernrt_cuda_ctx *ctx, kernrt_buf src, size_t so, kernrt_buf dst, size_t d_o, size_t len) {
+    return guard(ctx, [&](krt::Backend &b) { b.copy(src, so, dst, d_o, len); });
+}
+
+int kernrt_cuda_rms_norm(kernrt_cuda_ctx *ctx, kernrt_buf out, kernrt_buf x, kernrt_buf weight, size_t rows,
+                         size_t dim, float eps) {
+    return guard(ctx, [&](krt::Backend &b) { b.rms_norm(out, x, weight, rows, dim, eps); });
+}
+
+int kernrt_cuda_qk_norm(kernrt_cuda_ctx *ctx, kernrt_buf v, size_t rows, size_t width, size_t head,
+                        kernrt_buf weight, float eps) {
+    return guard(ctx, [&](krt::Backend &b) { b.qk_norm(v, rows, width, head, weight, eps); });
+}
+
+int kernrt_cuda_rope(kernrt_cuda_ctx *ctx, kernrt_buf q, kernrt_buf k, size_t qw, size_t kvw, size_t rows,
+                     const uint64_t *positions, size_t n_positions, size_t head, float theta, int interleaved) {
+    return guard(ctx, [&](krt::Backend &b) {
+        b.rope(q, k, qw, kvw, rows, positions, n_positions, head, theta, interleaved);
+    });
+}
+
+int kernrt_cuda_add_in_place(kernrt_cuda_ctx *ctx, kernrt_buf dst, kernrt_buf src, size_t len) {
+    return guard(ctx, [&](krt::Backend &b) { b.add_in_place(dst, src, len); });
+}
+
+int kernrt_cuda_mul(kernrt_cuda_ctx *ctx, kernrt_buf out, size_t oo, kernrt_buf a, size_t ao, kernrt_buf bb,
+                    size_t bo, size_t len) {
+    return guard(ctx, [&](krt::Backend &b) { b.mul(out, oo, a, ao, bb, bo, len); });
+}
+
+int kernrt_cuda_conv_prefill(kernrt_cuda_ctx *ctx, kernrt_buf out, kernrt_buf x, kernrt_buf kernel, size_t rows,
+                             size_t dim, size_t k) {
+    return guard(ctx, [&](krt::Backend &b) { b.conv_prefill(out, x, kernel, rows, dim, k); });
+}
+
+int kernrt_cuda_conv_decode(kernrt_cuda_ctx *ctx, kernrt_buf out, kernrt_buf x, kernrt_buf kernel,
+                            kernrt_buf state, size_t dim, size_t k) {
+    return guard(ctx, [&](krt::Backend &b) { b.conv_decode(out, x, kernel, state, dim, k); });
+}
+
+int kernrt_cuda_silu_mul(kernrt_cuda_ctx *ctx, kernrt_buf gate, kernrt_buf up, size_t len) {
+    return guard(ctx, [&](krt::Backend &b) { b.silu_mul(gate, up, len); });
+}
+
+int kernrt_cuda_quantize_q8_0(kernrt_cuda_ctx *ctx, kernrt_buf x, size_t rows, size_t dim, kernrt_buf codes,
+                              kernrt_buf scales, kernrt_buf scales_f16) {
+    return guard(ctx, [&](krt::Backend &b) { b.quantize_q8_0(x, rows, dim, codes, scales, scales_f16); });
+}
+
+int kernrt_cuda_rms_norm_q8_0(kernrt_cuda_ctx *ctx, kernrt_buf x, kernrt_buf weight, size_t rows, size_t dim,
+                              float eps, kernrt_buf codes, kernrt_buf scales, kernrt_buf scales_f16) {
+    return guard(ctx, [&](krt::Backend &b) { b.rms_norm_q8_0(x, weight, rows, dim, eps, codes, scales, scales_f16); });
+}
+
+int kernrt_cuda_rope_prepare(kernrt_cuda_ctx *ctx, float theta, size_t head, size_t max_pos) {
+    return guard(ctx, [&](krt::Backend &b) { b.rope_prepare(theta, head, max_pos); });
+}
+
+int kernrt_cuda_layer_chain(kernrt_cuda_ctx *ctx, const kernrt_chain_args *args) {
+    return guard(ctx, [&](krt::Backend &b) {
+        if (!args) krt::fail(KERNRT_E_INVALID, "null chain arguments");
+        b.layer_chain(*args);
+    });
+}
+
+int kernrt_cuda_lfm2_conv_block(kernrt_cuda_ctx *ctx, kernrt_buf bcx, kernrt_buf kernel, kernrt_buf ring,
+                                kernrt_buf cy, size_t rows, size_t dim, size_t k) {
+    return guard(ctx, [&](krt::Backend &b) { b.lfm2_conv_block(bcx, kernel, ring, cy, rows, dim, k); });
+}
+
+}  // extern "C"

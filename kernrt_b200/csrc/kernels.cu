@@ -1,0 +1,951 @@
+// sm_100a kernels for KernRT's per-row layer ops.
+//
+// Parity rules (the reference is KernRT's scalar backend,
+// src/backends/reference.rs, whose arithmetic this file reproduces):
+//   * every f32 operation that the reference performs is issued as one
+//     separately rounded IEEE operation (__fmul_rn / __fadd_rn / __fsub_rn /
+//     __fdiv_rn / __fsqrt_rn), so nvcc cannot contract it into an FMA;
+//   * every reduction whose order is observable (the RMS sum of squares) runs
+//     left to right in one thread, exactly as the reference loop;
+//   * order-free reductions (the Q8 block amax: max is exact) use warp shuffles;
+//   * RoPE reads cos/sin from a table the host built with the same libm calls
+//     as the reference (powf, sinf, cosf), so only the rotation runs here;
+//   * SwiGLU calls CUDA's expf: the one op held to a tolerance, not bit parity.
+// No kernel asserts or traps: bad token ids / positions set a bit in a device
+// error word that the host checks at its next barrier.
+#include "kernels.cuh"
+
+#include <cuda_fp16.h>
+
+namespace krt {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float sub_rn(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, b); }
+
+// dot.rs:222-224: a bf16 pattern is the top half of an f32.
+__device__ __forceinline__ float bf16f(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+
+// reference.rs:171-173: ss /= n; ss += eps; scale = 1 / sqrt(ss).
+__device__ __forceinline__ float rms_scale(float ss, float n, float eps) {
+    ss = div_rn(ss, n);
+    ss = add_rn(ss, eps);
+    return div_rn(1.0f, __fsqrt_rn(ss));
+}
+
+// quant.rs:871: (v * inv).round().clamp(-127, 127) as i8 — round half away
+// from zero, NaN -> 0.
+__device__ __forceinline__ int8_t q8_code(float v) {
+    float r = roundf(v);
+    r = (r < -127.0f) ? -127.0f : r;
+    r = (r > 127.0f) ? 127.0f : r;
+    return (r != r) ? (int8_t)0 : (int8_t)__float2int_rz(r);
+}
+
+// quant.rs:722-758 is IEEE binary16 round-to-nearest-even; the block scale it
+// converts is never NaN (the amax fold drops NaNs), and for every other input
+// CUDA's RN conversion gives the same bits.
+__device__ __forceinline__ uint16_t f16_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
+
+// reference.rs:81-83 silu(g) * up.
+__device__ __forceinline__ float silu_mul1(float g, float u) {
+    return mul_rn(div_rn(g, add_rn(1.0f, expf(-g))), u);
+}
+
+__device__ __forceinline__ void set_err(int *err, int code) {
+    if (err) atomicOr(err, code);
+}
+
+// Streaming loads/stores for data touched once.
+__device__ __forceinline__ float4 ld4(const float *p) { return __ldcs(reinterpret_cast<const float4 *>(p)); }
+__device__ __forceinline__ void st4(float *p, float4 v) { __stcs(reinterpret_cast<float4 *>(p), v); }
+
+// --------------------------------------------------------------------------
+// Row-local building blocks (one warp per row)
+// --------------------------------------------------------------------------
+
+// reference.rs:180-207 qk_norm of one row, in place.  Lane h owns head h: its
+// sum of squares runs left to right over the head in one thread, then the
+// warp rescales the row with coalesced accesses.
+__device__ void qk_norm_row_warp(float *v, int width, int head, const float *__restrict__ w,
+                                 float eps, int lane) {
+    const int nh = width / head;
+    const bool vec = ((head | width) & 3) == 0;
+    for (int h0 = 0; h0 < nh; h0 += 32) {
+        const int h = h0 + lane;
+        float scale = 0.0f;
+        if (h < nh) {
+            const float *p = v + h * head;
+            float ss = 0.0f;
+            if (vec) {
+                for (int j = 0; j < head; j += 4) {
+                    const float4 t = *reinterpret_cast<const float4 *>(p + j);
+                    ss = add_rn(ss, mul_rn(t.x, t.x));
+                    ss = add_rn(ss, mul_rn(t.y, t.y));
+                    ss = add_rn(ss, mul_rn(t.z, t.z));
+                    ss = add_rn(ss, mul_rn(t.w, t.w));
+                }
+            } else {
+                for (int j = 0; j < head; ++j) ss = add_rn(ss, mul_rn(p[j], p[j]));
+            }
+            scale = rms_scale(ss, (float)head, eps);
+        }
+        __syncwarp();
+        const int lo = h0 * head, hi = min(nh, h0 + 32) * head;
+        if (vec) {
+            for (int base = lo; base < hi; base += 128) {
+                const int e = base + lane * 4;
+                const bool ok = e < hi;
+                const int hh = ok ? e / head - h0 : 0;
+                const float sc = __shfl_sync(kFull, scale, hh);
+                if (ok) {
+                    float4 x = *reinterpret_cast<float4 *>(v + e);
+                    const int j = e - (e / head) * head;
+                    const float4 ww = __ldg(reinterpret_cast<const float4 *>(w + j));
+                    x.x = mul_rn(ww.x, mul_rn(sc, x.x));
+                    x.y = mul_rn(ww.y, mul_rn(sc, x.y));
+                    x.z = mul_rn(ww.z, mul_rn(sc, x.z));
+                    x.w = mul_rn(ww.w, mul_rn(sc, x.w));
+                    *reinterpret_cast<float4 *>(v + e) = x;
+                }
+            }
+        } else {
+            for (int base = lo; base < hi; base += 32) {
+                const int e = base + lane;
+                const bool ok = e < hi;
+                const int hh = ok ? e / head - h0 : 0;
+                const float sc = __shfl_sync(kFull, scale, hh);
+                if (ok) v[e] = mul_rn(w[e % head], mul_rn(sc, v[e]));
+            }
+        }
+        __syncwarp();
+    }
+}
+
+// reference.rs:239-254 half-split RoPE of `nh` heads of one row.
+// ct/st: the table row of this row's position, `half` entries each.
+__device__ void rope_half_row(float *v, int nh, int head, int half, const float *__restrict__ ct,
+                              const float *__restrict__ st, bool vec, int lane) {
+    if (vec) {
+        const int per = half >> 2, n = nh * per;
+        for (int t = lane; t < n; t += 32) {
+            const int h = t / per;
+            const int j = (t - h * per) << 2;
+            float *b = v + h * head;
+            const float4 lo = *reinterpret_cast<const float4 *>(b + j);
+            const float4 hi = *reinterpret_cast<const float4 *>(b + half + j);
+            const float4 c = __ldg(reinterpret_cast<const float4 *>(ct + j));
+            const float4 s = __ldg(reinterpret_cast<const float4 *>(st + j));
+            float4 nl, nhv;
+            nl.x = sub_rn(mul_rn(lo.x, c.x), mul_rn(hi.x, s.x));
+            nl.y = sub_rn(mul_rn(lo.y, c.y), mul_rn(hi.y, s.y));
+            nl.z = sub_rn(mul_rn(lo.z, c.z), mul_rn(hi.z, s.z));
+            nl.w = sub_rn(mul_rn(lo.w, c.w), mul_rn(hi.w, s.w));
+            nhv.x = add_rn(mul_rn(lo.x, s.x), mul_rn(hi.x, c.x));
+            nhv.y = add_rn(mul_rn(lo.y, s.y), mul_rn(hi.y, c.y));
+            nhv.z = add_rn(mul_rn(lo.z, s.z), mul_rn(hi.z, c.z));
+            nhv.w = add_rn(mul_rn(lo.w, s.w), mul_rn(hi.w, c.w));
+            *reinterpret_cast<float4 *>(b + j) = nl;
+            *reinterpret_cast<float4 *>(b + half + j) = nhv;
+        }
+    } else {
+        const int n = nh * half;
+        for (int t = lane; t < n; t += 32) {
+            const int h = t / half, j = t - h * half;
+            float *b = v + h * head;
+            const float lo = b[j], hi = b[j + half], c = ct[j], s = st[j];
+            b[j] = sub_rn(mul_rn(lo, c), mul_rn(hi, s));
+            b[j + half] = add_rn(mul_rn(lo, s), mul_rn(hi, c));
+        }
+    }
+}
+
+// reference.rs:220-237 adjacent-pair RoPE over `npairs` pairs of one row;
+// pair i uses the frequency of head_dim = (2*i) % head.
+__device__ void rope_pair_row(float *v, int npairs, int head, const float *__restrict__ ct,
+                              const float *__restrict__ st, bool vec, int lane) {
+    if (vec) {  // two pairs per float4; head % 4 == 0 keeps them in one head
+        const int n = npairs >> 1;
+        for (int t = lane; t < n; t += 32) {
+            const int i = t << 2;
+            const int j = (i % head) >> 1;
+            float4 x = *reinterpret_cast<float4 *>(v + i);
+            const float2 c = __ldg(reinterpret_cast<const float2 *>(ct + j));
+            const float2 s = __ldg(reinterpret_cast<const float2 *>(st + j));
+            const float x0 = x.x, x1 = x.y, x2 = x.z, x3 = x.w;
+            x.x = sub_rn(mul_rn(x0, c.x), mul_rn(x1, s.x));
+            x.y = add_rn(mul_rn(x0, s.x), mul_rn(x1, c.x));
+            x.z = sub_rn(mul_rn(x2, c.y), mul_rn(x3, s.y));
+            x.w = add_rn(mul_rn(x2, s.y), mul_rn(x3, c.y));
+            *reinterpret_cast<float4 *>(v + i) = x;
+        }
+    } else {
+        for (int p = lane; p < npairs; p += 32) {
+            const int i = 2 * p;
+            const int j = (i % head) >> 1;
+            const float x0 = v[i], x1 = v[i + 1], c = ct[j], s = st[j];
+            v[i] = sub_rn(mul_rn(x0, c), mul_rn(x1, s));
+            v[i + 1] = add_rn(mul_rn(x0, s), mul_rn(x1, c));
+        }
+    }
+}
+
+// Pairs of K rotated by the reference's interleaved loop: i < kv_width while
+// i + 1 < q_width (reference.rs:221-236).
+__device__ __forceinline__ int k_pairs_interleaved(int q_width, int kv_width) {
+    return min(kv_width / 2, q_width / 2);
+}
+
+// reference.rs:395-400 silu_mul over [lo, hi) by threads t of nt.
+__device__ void silu_range(float *__restrict__ g, const float *__restrict__ u, size_t lo, size_t hi,
+                           int t, int nt) {
+    if (((lo | hi) & 3) == 0) {
+        for (size_t i = lo + 4 * (size_t)t; i < hi; i += 4 * (size_t)nt) {
+            float4 gv = ld4(g + i);
+            const float4 uv = ld4(u + i);
+            gv.x = silu_mul1(gv.x, uv.x);
+            gv.y = silu_mul1(gv.y, uv.y);
+            gv.z = silu_mul1(gv.z, uv.z);
+            gv.w = silu_mul1(gv.w, uv.w);
+            st4(g + i, gv);
+        }
+    } else {
+        for (size_t i = lo + t; i < hi; i += nt) g[i] = silu_mul1(g[i], u[i]);
+    }
+}
+
+// --------------------------------------------------------------------------
+// Embedding gather (reference.rs:133-140 -> quant.rs:659-693), one warp/row
+// --------------------------------------------------------------------------
+
+template <int KIND, bool VEC>
+__global__ void __launch_bounds__(kThreads) k_embed_gather(GatherArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (row >= a.n) return;
+    const int tok = a.tokens[row];
+    float *dst = a.dst + a.dst_off[row];
+    const int dim = a.dim;
+    if ((unsigned)tok >= (unsigned)a.vocab) {
+        if (lane == 0) set_err(a.err, ERR_TOKEN);
+        for (int i = lane; i < dim; i += 32) dst[i] = 0.0f;
+        return;
+    }
+    const size_t base = (size_t)tok * dim;
+    if constexpr (KIND == SRC_BF16) {
+        const uint16_t *src = static_cast<const uint16_t *>(a.table) + base;
+        if constexpr (VEC) {
+            for (int c = lane * 8; c < dim; c += 256) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src + c));
+                const float4 lo = make_float4(bf16f(v.x & 0xffffu), bf16f(v.x >> 16),
+                                              bf16f(v.y & 0xffffu), bf16f(v.y >> 16));
+                const float4 hi = make_float4(bf16f(v.z & 0xffffu), bf16f(v.z >> 16),
+                                              bf16f(v.w & 0xffffu), bf16f(v.w >> 16));
+                *reinterpret_cast<float4 *>(dst + c) = lo;
+                *reinterpret_cast<float4 *>(dst + c + 4) = hi;
+            }
+        } else {
+            for (int i = lane; i < dim; i += 32) dst[i] = bf16f(src[i]);
+        }
+    } else if constexpr (KIND == SRC_Q8) {
+        const int8_t *src = static_cast<const int8_t *>(a.table) + base;
+        const float *sc = a.tscales + (size_t)tok * (dim / 32);
+        if constexpr (VEC) {
+            for (int c = lane * 16; c < dim; c += 512) {
+                const uint4 v = __ldg(reinterpret_cast<const uint4 *>(src + c));
+                const float s = __ldg(sc + (c >> 5));
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t b = w4[q];
+                    float4 o;
+                    o.x = mul_rn((float)(int8_t)(b & 0xffu), s);
+                    o.y = mul_rn((float)(int8_t)((b >> 8) & 0xffu), s);
+                    o.z = mul_rn((float)(int8_t)((b >> 16) & 0xffu), s);
+                    o.w = mul_rn((float)(int8_t)(b >> 24), s);
+                    *reinterpret_cast<float4 *>(dst + c + 4 * q) = o;
+                }
+            }
+        } else {
+            for (int i = lane; i < dim; i += 32) dst[i] = mul_rn((float)src[i], sc[i >> 5]);
+        }
+    } else {
+        const float *src = static_cast<const float *>(a.table) + base;
+        if constexpr (VEC) {
+            for (int c = lane * 4; c < dim; c += 128)
+                *reinterpret_cast<float4 *>(dst + c) = __ldg(reinterpret_cast<const float4 *>(src + c));
+        } else {
+            for (int i = lane; i < dim; i += 32) dst[i] = src[i];
+        }
+    }
+}
+
+// --------------------------------------------------------------------------
+// The fused row-group kernel
+// --------------------------------------------------------------------------
+//
+// One CTA owns G consecutive token rows.  Stage 0 stages the rows being
+// normalised (raw table bytes of the gathered embedding rows, or the f32 x
+// rows) in shared memory with 16-byte loads.  Stage 1 splits the CTA: in warp
+// 0, lane r runs row r's sum of squares left to right out of shared memory
+// (the reference's exact order; row slots are padded by 16 bytes so the lanes'
+// 16-byte reads are bank-conflict free) while warps 1.. stream the same rows'
+// independent ops — qk_norm, RoPE, SwiGLU — from HBM.  Stage 2 writes the
+// normalised rows and the residual sum from the staged copy, so every
+// activation row crosses HBM once.
+
+template <int SRC>
+__device__ __forceinline__ int src_row_bytes(int dim) {
+    return SRC == SRC_BF16 ? dim * 2 : (SRC == SRC_Q8 ? dim : dim * 4);
+}
+
+__host__ __device__ __forceinline__ int align16(int v) { return (v + 15) & ~15; }
+
+// Decode n consecutive values of a staged row starting at column c.
+template <int SRC, int N>
+__device__ __forceinline__ void decode_staged(const unsigned char *row, int dim, int c, float *v) {
+    if constexpr (SRC == SRC_BF16) {
+        if constexpr (N == 8) {
+            const uint4 t = *reinterpret_cast<const uint4 *>(row + 2 * c);
+            v[0] = bf16f(t.x & 0xffffu); v[1] = bf16f(t.x >> 16);
+            v[2] = bf16f(t.y & 0xffffu); v[3] = bf16f(t.y >> 16);
+            v[4] = bf16f(t.z & 0xffffu); v[5] = bf16f(t.z >> 16);
+            v[6] = bf16f(t.w & 0xffffu); v[7] = bf16f(t.w >> 16);
+        } else if constexpr (N == 4) {
+            const uint2 t = *reinterpret_cast<const uint2 *>(row + 2 * c);
+            v[0] = bf16f(t.x & 0xffffu); v[1] = bf16f(t.x >> 16);
+            v[2] = bf16f(t.y & 0xffffu); v[3] = bf16f(t.y >> 16);
+        } else {
+#pragma unroll
+            for (int e = 0; e < N; ++e) v[e] = bf16f(reinterpret_cast<const uint16_t *>(row)[c + e]);
+        }
+    } else if constexpr (SRC == SRC_Q8) {
+        // codes at row[0..dim), block scales at row + align16(dim); one
+        // f32 multiply per value (quant.rs:686-688)
+        const float *sc = reinterpret_cast<const float *>(row + align16(dim));
+        if constexpr (N == 8 || N == 4) {
+            const float s = sc[c >> 5];  // c % N == 0, so all N share a block
+            if constexpr (N == 8) {
+                const uint2 t = *reinterpret_cast<const uint2 *>(row + c);
+                const uint32_t w2[2] = {t.x, t.y};
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+#pragma unroll
+                    for (int b = 0; b < 4; ++b)
+                        v[4 * q + b] = mul_rn((float)(int8_t)((w2[q] >> (8 * b)) & 0xffu), s);
+            } else {
+                const uint32_t t = *reinterpret_cast<const uint32_t *>(row + c);
+#pragma unroll
+                for (int b = 0; b < 4; ++b) v[b] = mul_rn((float)(int8_t)((t >> (8 * b)) & 0xffu), s);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < N; ++e)
+                v[e] = mul_rn((float)reinterpret_cast<const int8_t *>(row)[c + e], sc[(c + e) >> 5]);
+        }
+    } else {
+        const float *f = reinterpret_cast<const float *>(row);
+        if constexpr (N == 8) {
+            const float4 t0 = *reinterpret_cast<const float4 *>(f + c);
+            const float4 t1 = *reinterpret_cast<const float4 *>(f + c + 4);
+            v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w;
+            v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
+        } else if constexpr (N == 4) {
+            const float4 t0 = *reinterpret_cast<const float4 *>(f + c);
+            v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w;
+        } else {
+#pragma unroll
+            for (int e = 0; e < N; ++e) v[e] = f[c + e];
+        }
+    }
+}
+
+struct ChainLayout {
+    int G;        // rows per CTA
+    int xstride;  // bytes per staged source row slot
+    int rstride;  // bytes per staged residual row slot (FQ with resid), else 0
+    size_t smem;
+};
+
+template <int SRC, bool FQ, bool VEC>
+__global__ void __launch_bounds__(kThreads) k_chain(ChainArgs a, ChainLayout L) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const int dim = a.dim;
+    const int r0 = blockIdx.x * L.G;
+    const int g = min(L.G, a.rows - r0);
+    const bool fq_resid = FQ && a.resid != nullptr;
+    unsigned char *xs = smem;
+    unsigned char *rs = smem + (size_t)L.G * L.xstride;
+    float *sc1 = reinterpret_cast<float *>(rs + (size_t)L.G * L.rstride);
+    float *sc2 = sc1 + 32;
+
+    // ---- stage 0: stage the source rows (and, for the final norm, the residual rows)
+    auto src_row = [&](int r) -> const unsigned char * {
+        if constexpr (SRC == SRC_X) {
+            return reinterpret_cast<const unsigned char *>(a.x_in + (size_t)(r0 + r) * dim);
+        } else {
+            const int tok = a.tokens[r0 + r];
+            if ((unsigned)tok >= (unsigned)a.vocab) return nullptr;
+            return static_cast<const unsigned char *>(a.table) +
+                   (size_t)tok * (size_t)src_row_bytes<SRC>(dim);
+        }
+    };
+    {
+        const int rb = src_row_bytes<SRC>(dim);
+        if constexpr (VEC) {
+            const int n16 = rb >> 4;
+            for (int idx = tid; idx < g * n16; idx += blockDim.x) {
+                const int r = idx / n16, c = idx - r * n16;
+                const unsigned char *sp = src_row(r);
+                uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                if (sp) {
+                    v = __ldcs(reinterpret_cast<const uint4 *>(sp) + c);
+                } else if (c == 0) {
+                    set_err(a.err, ERR_TOKEN);
+                }
+                *reinterpret_cast<uint4 *>(xs + (size_t)r * L.xstride + 16 * c) = v;
+            }
+        } else {
+            for (int idx = tid; idx < g * rb; idx += blockDim.x) {
+                const int r = idx / rb, c = idx - r * rb;
+                const unsigned char *sp = src_row(r);
+                unsigned char v = 0;
+                if (sp) v = sp[c]; else if (c == 0) set_err(a.err, ERR_TOKEN);
+                xs[(size_t)r * L.xstride + c] = v;
+            }
+        }
+        if constexpr (SRC == SRC_Q8) {
+            const int nb = dim >> 5;
+            for (int idx = tid; idx < g * nb; idx += blockDim.x) {
+                const int r = idx / nb, b = idx - r * nb;
+                const int tok = a.tokens[r0 + r];
+                float s = 0.0f;
+                if ((unsigned)tok < (unsigned)a.vocab) s = __ldg(a.tscales + (size_t)tok * nb + b);
+                reinterpret_cast<float *>(xs + (size_t)r * L.xstride + align16(dim))[b] = s;
+            }
+        }
+        if (fq_resid) {
+            for (int idx = tid; idx < g * dim; idx += blockDim.x) {
+                const int r = idx / dim, c = idx - r * dim;
+                reinterpret_cast<float *>(rs + (size_t)r * L.rstride)[c] =
+                    a.resid[(size_t)(r0 + r) * dim + c];
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- stage 1
+    if (warp == 0) {
+        // Lane r: row r's sums of squares, left to right (reference.rs:167-170).
+        if (lane < g) {
+            const unsigned char *row = xs + (size_t)lane * L.xstride;
+            const float *rrow = reinterpret_cast<const float *>(rs + (size_t)lane * L.rstride);
+            float ss = 0.0f, ss2 = 0.0f;
+            if constexpr (VEC) {
+                for (int c = 0; c < dim; c += 8) {
+                    float v[8];
+                    decode_staged<SRC, 8>(row, dim, c, v);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        ss = add_rn(ss, mul_rn(v[e], v[e]));
+                        if constexpr (FQ) {
+                            const float xo = fq_resid ? add_rn(v[e], rrow[c + e]) : v[e];
+                            ss2 = add_rn(ss2, mul_rn(xo, xo));
+                        }
+                    }
+                }
+            } else {
+                for (int c = 0; c < dim; ++c) {
+                    float v[1];
+                    decode_staged<SRC, 1>(row, dim, c, v);
+                    ss = add_rn(ss, mul_rn(v[0], v[0]));
+                    if constexpr (FQ) {
+                        const float xo = fq_resid ? add_rn(v[0], rrow[c]) : v[0];
+                        ss2 = add_rn(ss2, mul_rn(xo, xo));
+                    }
+                }
+            }
+            sc1[lane] = rms_scale(ss, (float)dim, a.eps);
+            if constexpr (FQ) sc2[lane] = rms_scale(ss2, (float)dim, a.final_eps);
+        }
+    } else {
+        // Warps 1..: the rows' independent streams.
+        const int sw = warp - 1, nsw = nwarps - 1;
+        if (a.rope_mode != 0 || a.w_q != nullptr || a.w_k != nullptr) {
+            const bool half_vec = ((a.half | a.q_dim | a.kv_dim) & 3) == 0;
+            const bool pair_vec = ((a.head | a.q_dim | a.kv_dim) & 3) == 0;
+            for (int r = sw; r < g; r += nsw) {
+                const int row = r0 + r;
+                float *qr = a.q ? a.q + (size_t)row * a.q_dim : nullptr;
+                float *kr = a.k ? a.k + (size_t)row * a.kv_dim : nullptr;
+                if (a.w_q && qr) qk_norm_row_warp(qr, a.q_dim, a.head, a.w_q, a.eps, lane);
+                if (a.w_k && kr) qk_norm_row_warp(kr, a.kv_dim, a.head, a.w_k, a.eps, lane);
+                if (a.rope_mode == 0) continue;
+                const int p = a.pos[row];
+                if ((unsigned)p >= (unsigned)a.max_pos) {
+                    if (lane == 0) set_err(a.err, ERR_POSITION);
+                    continue;
+                }
+                const float *ct = a.cos_t + (size_t)p * a.half;
+                const float *st = a.sin_t + (size_t)p * a.half;
+                if (a.rope_mode == 1) {
+                    if (qr) rope_half_row(qr, a.q_dim / a.head, a.head, a.half, ct, st, half_vec, lane);
+                    if (kr) rope_half_row(kr, a.kv_dim / a.head, a.head, a.half, ct, st, half_vec, lane);
+                } else {
+                    if (qr) rope_pair_row(qr, a.q_dim / 2, a.head, ct, st, pair_vec, lane);
+                    if (kr)
+                        rope_pair_row(kr, k_pairs_interleaved(a.q_dim, a.kv_dim), a.head, ct, st,
+                                      pair_vec && (k_pairs_interleaved(a.q_dim, a.kv_dim) % 2 == 0),
+                                      lane);
+                }
+            }
+        }
+        if (a.gate) {
+            silu_range(a.gate, a.up, (size_t)r0 * a.hidden, (size_t)(r0 + g) * a.hidden, tid - 32,
+                       blockDim.x - 32);
+        }
+    }
+    __syncthreads();
+
+    // ---- stage 2: normalised rows and the residual sum from the staged copy
+    if constexpr (!FQ) {
+        if (a.xb == nullptr && a.x_out == nullptr) return;
+        if constexpr (VEC) {
+            const int n4 = dim >> 2;
+            for (int idx = tid; idx < g * n4; idx += blockDim.x) {
+                const int r = idx / n4, c = (idx - r * n4) << 2;
+                const size_t o = (size_t)(r0 + r) * dim + c;
+                float v[4];
+                decode_staged<SRC, 4>(xs + (size_t)r * L.xstride, dim, c, v);
+                if (a.xb) {
+                    const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
+                    const float s = sc1[r];
+                    st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[0])), mul_rn(w.y, mul_rn(s, v[1])),
+                                              mul_rn(w.z, mul_rn(s, v[2])), mul_rn(w.w, mul_rn(s, v[3]))));
+                }
+                if (a.x_out) {
+                    float4 xo = make_float4(v[0], v[1], v[2], v[3]);
+                    if (a.resid) {
+                        const float4 rr = ld4(a.resid + o);
+                        xo = make_float4(add_rn(v[0], rr.x), add_rn(v[1], rr.y), add_rn(v[2], rr.z),
+                                         add_rn(v[3], rr.w));
+                    }
+                    st4(a.x_out + o, xo);
+                }
+            }
+        } else {
+            for (int idx = tid; idx < g * dim; idx += blockDim.x) {
+                const int r = idx / dim, c = idx - r * dim;
+                const size_t o = (size_t)(r0 + r) * dim + c;
+                float v[1];
+                decode_staged<SRC, 1>(xs + (size_t)r * L.xstride, dim, c, v);
+                if (a.xb) a.xb[o] = mul_rn(a.w_att[c], mul_rn(sc1[r], v[0]));
+                if (a.x_out) a.x_out[o] = a.resid ? add_rn(v[0], a.resid[o]) : v[0];
+            }
+        }
+    } else {
+        // Final RMSNorm fused with Q8_0 quantisation (quant.rs:856-874): one
+        // warp per row, lane l holds element 32*b + l of block b.
+        const int nb = (dim + 31) >> 5;
+        for (int r = warp; r < g; r += nwarps) {
+            const int row = r0 + r;
+            const float s1 = sc1[r], s2 = sc2[r];
+            const unsigned char *xrow = xs + (size_t)r * L.xstride;
+            const float *rrow = reinterpret_cast<const float *>(rs + (size_t)r * L.rstride);
+            for (int b = 0; b < nb; ++b) {
+                const int i = b * 32 + lane;
+                const bool ok = i < dim;
+                float v[1] = {0.0f};
+                if (ok) decode_staged<SRC, 1>(xrow, dim, i, v);
+                const size_t o = (size_t)row * dim + i;
+                if (ok && a.xb) a.xb[o] = mul_rn(a.w_att[i], mul_rn(s1, v[0]));
+                const float xo = (ok && fq_resid) ? add_rn(v[0], rrow[i]) : v[0];
+                if (ok && a.x_out) a.x_out[o] = xo;
+                const float y = ok ? mul_rn(a.w_final[i], mul_rn(s2, xo)) : 0.0f;
+                float am = fmaxf(0.0f, fabsf(y));
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(kFull, am, off));
+                const float d = div_rn(am, 127.0f);
+                const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+                a.codes[(size_t)row * nb * 32 + i] = ok ? q8_code(mul_rn(y, inv)) : (int8_t)0;
+                if (lane == 0) {
+                    a.scales[(size_t)row * nb + b] = d;
+                    if (a.scales16) a.scales16[(size_t)row * nb + b] = f16_bits(d);
+                }
+            }
+        }
+    }
+}
+
+// --------------------------------------------------------------------------
+// Standalone row ops
+// --------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kThreads) k_qk_norm(float *v, int rows, int width, int head,
+                                                      const float *__restrict__ w, float eps) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (row >= rows) return;
+    qk_norm_row_warp(v + (size_t)row * width, width, head, w, eps, threadIdx.x & 31);
+}
+
+__global__ void __launch_bounds__(kThreads) k_rope(float *q, float *k, int q_width, int kv_width,
+                                                   int rows, int head, const int32_t *pos,
+                                                   const float *cos_t, const float *sin_t,
+                                                   int max_pos, int interleaved, int *err) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int p = pos[row];
+    if ((unsigned)p >= (unsigned)max_pos) {
+        if (lane == 0) set_err(err, ERR_POSITION);
+        return;
+    }
+    const int half = head >> 1;
+    const float *ct = cos_t + (size_t)p * half, *st = sin_t + (size_t)p * half;
+    float *qr = q + (size_t)row * q_width, *kr = k + (size_t)row * kv_width;
+    if (!interleaved) {
+        const bool vec = ((half | q_width | kv_width) & 3) == 0;
+        rope_half_row(qr, q_width / head, head, half, ct, st, vec, lane);
+        rope_half_row(kr, kv_width / head, head, half, ct, st, vec, lane);
+    } else {
+        const bool vec = ((head | q_width | kv_width) & 3) == 0;
+        const int kp = k_pairs_interleaved(q_width, kv_width);
+        rope_pair_row(qr, q_width / 2, head, ct, st, vec && (q_width / 2) % 2 == 0, lane);
+        rope_pair_row(kr, kp, head, ct, st, vec && kp % 2 == 0, lane);
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) k_silu_mul(float *g, const float *u, size_t n) {
+    silu_range(g, u, 0, n, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+}
+
+// reference.rs:308-313
+__global__ void __launch_bounds__(kThreads) k_add(float *__restrict__ d, const float *__restrict__ s,
+                                                  size_t n) {
+    const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nt = (size_t)gridDim.x * blockDim.x;
+    if ((n & 3) == 0) {
+        for (size_t i = 4 * t; i < n; i += 4 * nt) {
+            float4 a = ld4(d + i);
+            const float4 b = ld4(s + i);
+            a.x = add_rn(a.x, b.x); a.y = add_rn(a.y, b.y); a.z = add_rn(a.z, b.z); a.w = add_rn(a.w, b.w);
+            st4(d + i, a);
+        }
+    } else {
+        for (size_t i = t; i < n; i += nt) d[i] = add_rn(d[i], s[i]);
+    }
+}
+
+// reference.rs:315-363.  Parallel when no thread's write can feed another
+// thread's read; otherwise the sequential variant keeps the reference order.
+__global__ void __launch_bounds__(kThreads) k_mul(float *o, const float *a, const float *b, size_t n) {
+    const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nt = (size_t)gridDim.x * blockDim.x;
+    const bool vec = (((uintptr_t)o | (uintptr_t)a | (uintptr_t)b) & 15) == 0 && (n & 3) == 0;
+    if (vec) {
+        for (size_t i = 4 * t; i < n; i += 4 * nt) {
+            const float4 x = *reinterpret_cast<const float4 *>(a + i);
+            const float4 y = *reinterpret_cast<const float4 *>(b + i);
+            *reinterpret_cast<float4 *>(o + i) =
+                make_float4(mul_rn(x.x, y.x), mul_rn(x.y, y.y), mul_rn(x.z, y.z), mul_rn(x.w, y.w));
+        }
+    } else {
+        for (size_t i = t; i < n; i += nt) {
+            const float x = a[i], y = b[i];
+            o[i] = mul_rn(x, y);
+        }
+    }
+}
+
+__global__ void k_mul_sequential(float *o, const float *a, const float *b, size_t n) {
+    if (blockIdx.x != 0 || threadIdx.x != 0) return;
+    for (size_t i = 0; i < n; ++i) {
+        const float x = a[i], y = b[i];
+        o[i] = mul_rn(x, y);
+    }
+}
+
+// reference.rs:490-503 conv_rows, one thread per (row, channel).
+__global__ void __launch_bounds__(kThreads) k_conv_prefill(float *__restrict__ out,
+                                                           const float *__restrict__ x,
+                                                           const float *__restrict__ w, int rows,
+                                                           int dim, int k) {
+    const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    if (idx >= (size_t)rows * dim) return;
+    const int r = (int)(idx / dim), i = (int)(idx - (size_t)r * dim);
+    float acc = 0.0f;
+    for (int j = 0; j < k; ++j) {
+        const int h = r - (k - 1) + j;
+        if (h >= 0) acc = add_rn(acc, mul_rn(__ldg(w + (size_t)i * k + j), __ldg(x + (size_t)h * dim + i)));
+    }
+    out[idx] = acc;
+}
+
+// reference.rs:372-393: one thread per channel; every read precedes every
+// write of that channel, so out may alias x.
+__global__ void __launch_bounds__(kThreads) k_conv_decode(float *out, const float *x,
+                                                          const float *__restrict__ w,
+                                                          float *state, int dim, int k) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= dim) return;
+    const float xi = x[i];
+    float acc = 0.0f;
+    for (int j = 0; j < k - 1; ++j) acc = add_rn(acc, mul_rn(w[(size_t)i * k + j], state[(size_t)j * dim + i]));
+    acc = add_rn(acc, mul_rn(w[(size_t)i * k + (k - 1)], xi));
+    out[i] = acc;
+    if (k > 1) {
+        for (int j = 0; j + 1 < k - 1; ++j) state[(size_t)j * dim + i] = state[(size_t)(j + 1) * dim + i];
+        state[(size_t)(k - 2) * dim + i] = xi;
+    }
+}
+
+// lfm2.rs:584-624 conv block fused: h = B*x recomputed for the k-1 halo rows,
+// co = conv(h) in tap order, cy = C*co, ring <- the last k-1 rows of h.
+__global__ void __launch_bounds__(kThreads) k_lfm2_conv_block(const float *__restrict__ bcx,
+                                                              const float *__restrict__ w,
+                                                              float *__restrict__ ring,
+                                                              float *__restrict__ cy, int rows,
+                                                              int dim, int k) {
+    const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    if (idx >= (size_t)rows * dim) return;
+    const int r = (int)(idx / dim), i = (int)(idx - (size_t)r * dim);
+    const size_t w3 = (size_t)3 * dim;
+    float acc = 0.0f, hr = 0.0f;
+    for (int j = 0; j < k; ++j) {
+        const int h = r - (k - 1) + j;
+        if (h >= 0) {
+            const float hv = mul_rn(__ldg(bcx + h * w3 + i), __ldg(bcx + h * w3 + 2 * dim + i));
+            acc = add_rn(acc, mul_rn(__ldg(w + (size_t)i * k + j), hv));
+            if (h == r) hr = hv;
+        }
+    }
+    cy[idx] = mul_rn(__ldg(bcx + r * w3 + dim + i), acc);
+    if (k > 1) {
+        const int take = min(rows, k - 1);
+        if (r >= rows - take) ring[(size_t)(k - 1 - take + (r - (rows - take))) * dim + i] = hr;
+    }
+}
+
+// quant.rs:856-874 per row: one warp per row, lane l holds element 32b+l.
+__global__ void __launch_bounds__(kThreads) k_quantize_q8(const float *__restrict__ x, int rows, int dim,
+                                                          int8_t *codes, float *scales,
+                                                          uint16_t *scales16) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int nb = (dim + 31) >> 5;
+    for (int b = 0; b < nb; ++b) {
+        const int i = b * 32 + lane;
+        const bool ok = i < dim;
+        const float y = ok ? x[(size_t)row * dim + i] : 0.0f;
+        float am = fmaxf(0.0f, fabsf(y));
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(kFull, am, off));
+        const float d = div_rn(am, 127.0f);
+        const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+        codes[(size_t)row * nb * 32 + i] = ok ? q8_code(mul_rn(y, inv)) : (int8_t)0;
+        if (lane == 0) {
+            scales[(size_t)row * nb + b] = d;
+            if (scales16) scales16[(size_t)row * nb + b] = f16_bits(d);
+        }
+    }
+}
+
+// quant.rs:198-220 Q8_0x4::to_row_major with quant.rs:764-769's widening.
+__device__ __forceinline__ float f16_scale_to_f32(uint16_t bits) {
+    const uint32_t sign = (uint32_t)(bits >> 15) << 31;
+    const uint32_t exp = (bits >> 10) & 0x1fu;
+    const uint32_t mant = bits & 0x03ffu;
+    return __uint_as_float(sign | ((exp + 112u) << 23) | (mant << 13));
+}
+
+__global__ void __launch_bounds__(kThreads) k_q8x4_to_row_major(const uint8_t *__restrict__ blocks,
+                                                                int out_dim, int in_dim,
+                                                                int8_t *quants, float *scales) {
+    const int nb = in_dim >> 5;
+    const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;  // (group, block, rig)
+    if (idx >= (size_t)out_dim * nb) return;
+    const int rig = (int)(idx & 3);
+    const size_t gb = idx >> 2;
+    const int g = (int)(gb / nb), b = (int)(gb - (size_t)g * nb);
+    const uint8_t *blk = blocks + gb * 136;
+    const uint16_t sbits = (uint16_t)(blk[2 * rig] | (blk[2 * rig + 1] << 8));
+    const int row = g * 4 + rig;
+    scales[(size_t)row * nb + b] = f16_scale_to_f32(sbits);
+    int8_t *dst = quants + (size_t)row * in_dim + b * 32;
+    const int8_t *qs = reinterpret_cast<const int8_t *>(blk + 8);
+    for (int seg = 0; seg < 8; ++seg)
+        for (int lane = 0; lane < 4; ++lane) dst[seg * 4 + lane] = qs[seg * 16 + rig * 4 + lane];
+}
+
+inline unsigned grid_for(size_t work, unsigned per_block) {
+    size_t b = (work + per_block - 1) / per_block;
+    if (b < 1) b = 1;
+    if (b > 0x7fffffffull) b = 0x7fffffffull;
+    return (unsigned)b;
+}
+
+inline unsigned stream_grid(size_t n_elems) {
+    // enough CTAs to cover the SMs several times over, capped by the work
+    size_t want = (n_elems + 4 * kThreads - 1) / (4 * kThreads);
+    if (want > 148 * 16) want = 148 * 16;
+    if (want < 1) want = 1;
+    return (unsigned)want;
+}
+
+template <int SRC>
+ChainLayout chain_layout(const ChainArgs &a, bool fq, int G_override) {
+    ChainLayout L{};
+    const int rb = SRC == SRC_BF16 ? a.dim * 2 : (SRC == SRC_Q8 ? a.dim : a.dim * 4);
+    L.xstride = align16(rb) + (SRC == SRC_Q8 ? align16((a.dim / 32) * 4) : 0) + 16;
+    L.rstride = (fq && a.resid) ? align16(a.dim * 4) + 16 : 0;
+    const int per_row = L.xstride + L.rstride;
+    int G = G_override > 0 ? G_override : (int)((72 * 1024 - 256) / per_row);
+    if (G > 32) G = 32;
+    if (G < 1) G = 1;
+    L.G = G;
+    L.smem = (size_t)G * per_row + 64 * sizeof(float);
+    return L;
+}
+
+template <int SRC, bool FQ, bool VEC>
+cudaError_t launch_chain_t(const ChainArgs &a, cudaStream_t s) {
+    const ChainLayout L = chain_layout<SRC>(a, FQ, 0);
+    if (L.smem > 227 * 1024) return cudaErrorInvalidValue;
+    auto kern = k_chain<SRC, FQ, VEC>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
+    if (e != cudaSuccess) return e;
+    const unsigned grid = grid_for((size_t)a.rows, (unsigned)L.G);
+    kern<<<grid, kThreads, L.smem, s>>>(a, L);
+    return cudaGetLastError();
+}
+
+template <int SRC>
+cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s) {
+    const bool vec = (a.dim % 8) == 0 && (SRC != SRC_Q8 || a.dim % 32 == 0);
+    const bool fq = a.w_final != nullptr;
+    if (fq) return vec ? launch_chain_t<SRC, true, true>(a, s) : launch_chain_t<SRC, true, false>(a, s);
+    return vec ? launch_chain_t<SRC, false, true>(a, s) : launch_chain_t<SRC, false, false>(a, s);
+}
+
+}  // namespace
+
+cudaError_t launch_embed_gather(int kind, bool vec, const GatherArgs &a, cudaStream_t s) {
+    if (a.n <= 0) return cudaSuccess;
+    const unsigned grid = grid_for((size_t)a.n * 32, kThreads);
+    switch (kind) {
+    case SRC_BF16:
+        if (vec) k_embed_gather<SRC_BF16, true><<<grid, kThreads, 0, s>>>(a);
+        else k_embed_gather<SRC_BF16, false><<<grid, kThreads, 0, s>>>(a);
+        break;
+    case SRC_Q8:
+        if (vec) k_embed_gather<SRC_Q8, true><<<grid, kThreads, 0, s>>>(a);
+        else k_embed_gather<SRC_Q8, false><<<grid, kThreads, 0, s>>>(a);
+        break;
+    default:
+        if (vec) k_embed_gather<SRC_F32, true><<<grid, kThreads, 0, s>>>(a);
+        else k_embed_gather<SRC_F32, false><<<grid, kThreads, 0, s>>>(a);
+        break;
+    }
+    return cudaGetLastError();
+}
+
+size_t chain_smem_bytes(int src, const ChainArgs &a, int rows_per_cta) {
+    const bool fq = a.w_final != nullptr;
+    switch (src) {
+    case SRC_BF16: return chain_layout<SRC_BF16>(a, fq, rows_per_cta).smem;
+    case SRC_Q8: return chain_layout<SRC_Q8>(a, fq, rows_per_cta).smem;
+    case SRC_F32: return chain_layout<SRC_F32>(a, fq, rows_per_cta).smem;
+    default: return chain_layout<SRC_X>(a, fq, rows_per_cta).smem;
+    }
+}
+
+cudaError_t launch_chain(int src, const ChainArgs &a, cudaStream_t s) {
+    if (a.rows <= 0) return cudaSuccess;
+    switch (src) {
+    case SRC_BF16: return launch_chain_src<SRC_BF16>(a, s);
+    case SRC_Q8: return launch_chain_src<SRC_Q8>(a, s);
+    case SRC_F32: return launch_chain_src<SRC_F32>(a, s);
+    default: return launch_chain_src<SRC_X>(a, s);
+    }
+}
+
+cudaError_t launch_qk_norm(float *v, int rows, int width, int head, const float *w, float eps,
+                           cudaStream_t s) {
+    if (rows <= 0 || width / head == 0) return cudaSuccess;
+    k_qk_norm<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(v, rows, width, head, w, eps);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows, int head,
+                        const int32_t *pos, const float *cos_t, const float *sin_t, int max_pos,
+                        int interleaved, int *err, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    k_rope<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(
+        q, k, q_width, kv_width, rows, head, pos, cos_t, sin_t, max_pos, interleaved, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_silu_mul(float *g, const float *u, size_t n, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    k_silu_mul<<<stream_grid(n), kThreads, 0, s>>>(g, u, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_add(float *d, const float *src, size_t n, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    k_add<<<stream_grid(n), kThreads, 0, s>>>(d, src, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mul(float *o, const float *a, const float *b, size_t n, bool sequential,
+                       cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    if (sequential) k_mul_sequential<<<1, 1, 0, s>>>(o, a, b, n);
+    else k_mul<<<stream_grid(n), kThreads, 0, s>>>(o, a, b, n);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv_prefill(float *out, const float *x, const float *w, int rows, int dim, int k,
+                                cudaStream_t s) {
+    if (rows <= 0 || dim <= 0) return cudaSuccess;
+    k_conv_prefill<<<grid_for((size_t)rows * dim, kThreads), kThreads, 0, s>>>(out, x, w, rows, dim, k);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv_decode(float *out, const float *x, const float *w, float *state, int dim, int k,
+                               cudaStream_t s) {
+    if (dim <= 0) return cudaSuccess;
+    k_conv_decode<<<grid_for((size_t)dim, kThreads), kThreads, 0, s>>>(out, x, w, state, dim, k);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_lfm2_conv_block(const float *bcx, const float *w, float *ring, float *cy, int rows,
+                                   int dim, int k, cudaStream_t s) {
+    if (rows <= 0 || dim <= 0) return cudaSuccess;
+    k_lfm2_conv_block<<<grid_for((size_t)rows * dim, kThreads), kThreads, 0, s>>>(bcx, w, ring, cy,
+                                                                                  rows, dim, k);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes, float *scales,
+                               uint16_t *scales16, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    k_quantize_q8<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(x, rows, dim, codes, scales,
+                                                                              scales16);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_q8x4_to_row_major(const uint8_t *blocks, int out_dim, int in_dim, int8_t *quants,
+                                     float *scales, cudaStream_t s) {
+    const size_t n = (size_t)out_dim * (in_dim / 32);
+    if (n == 0) return cudaSuccess;
+    k_q8x4_to_row_major<<<grid_for(n, kThreads), kThreads, 0, s>>>(blocks, out_dim, in_dim, quants, scales);
+    return cudaGetLastError();
+}
+
+}  // namespace krt

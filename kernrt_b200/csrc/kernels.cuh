@@ -1,0 +1,71 @@
+// Launch interface between the host backend (backend.cu) and the sm_100a
+// kernels (kernels.cu).  All pointers are device pointers; all launches are
+// asynchronous on the given stream.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace krt {
+
+// Bits of the device error word (checked by the host at every barrier).
+enum : int { ERR_TOKEN = 1, ERR_POSITION = 2 };
+
+// Storage kinds of an embedding table / source of the normalised row.
+enum SrcKind : int { SRC_F32 = 0, SRC_BF16 = 1, SRC_Q8 = 2, SRC_X = 3 };
+
+struct GatherArgs {
+    const void *table;      // f32 / bf16 / int8 codes
+    const float *tscales;   // q8_0 block scales
+    int vocab, dim;
+    const int32_t *tokens;  // [n]
+    const int64_t *dst_off; // [n] element offsets into dst
+    float *dst;
+    int n;
+    int *err;
+};
+cudaError_t launch_embed_gather(int kind, bool vec, const GatherArgs &a, cudaStream_t s);
+
+// The fused per-row-group kernel: every stage optional (null pointer = skip).
+struct ChainArgs {
+    int rows, dim, q_dim, kv_dim, hidden, head, half;
+    float eps, final_eps;
+    // source of the row being normalised
+    const void *table; const float *tscales; int vocab; const int32_t *tokens; // SRC_F32/BF16/Q8
+    const float *x_in;                                                          // SRC_X
+    float *x_out;          // embed output, or x + resid
+    float *xb; const float *w_att;
+    float *q, *k; const float *w_q, *w_k;
+    const int32_t *pos; const float *cos_t, *sin_t; int max_pos; int rope_mode; // 0 none 1 half 2 pair
+    float *gate; const float *up;
+    const float *resid;
+    const float *w_final; int8_t *codes; float *scales; uint16_t *scales16;
+    int *err;
+};
+// Chooses rows-per-CTA and shared memory, then launches.
+cudaError_t launch_chain(int src, const ChainArgs &a, cudaStream_t s);
+// Shared memory a chain launch would need for one row group (to report limits).
+size_t chain_smem_bytes(int src, const ChainArgs &a, int rows_per_cta);
+
+cudaError_t launch_qk_norm(float *v, int rows, int width, int head, const float *w, float eps,
+                           cudaStream_t s);
+cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows, int head,
+                        const int32_t *pos, const float *cos_t, const float *sin_t, int max_pos,
+                        int interleaved, int *err, cudaStream_t s);
+cudaError_t launch_silu_mul(float *g, const float *u, size_t n, cudaStream_t s);
+cudaError_t launch_add(float *d, const float *src, size_t n, cudaStream_t s);
+cudaError_t launch_mul(float *o, const float *a, const float *b, size_t n, bool sequential,
+                       cudaStream_t s);
+cudaError_t launch_conv_prefill(float *out, const float *x, const float *w, int rows, int dim,
+                                int k, cudaStream_t s);
+cudaError_t launch_conv_decode(float *out, const float *x, const float *w, float *state, int dim,
+                               int k, cudaStream_t s);
+cudaError_t launch_lfm2_conv_block(const float *bcx, const float *w, float *ring, float *cy,
+                                   int rows, int dim, int k, cudaStream_t s);
+cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes, float *scales,
+                               uint16_t *scales16, cudaStream_t s);
+cudaError_t launch_q8x4_to_row_major(const uint8_t *blocks, int out_dim, int in_dim,
+                                     int8_t *quants, float *scales, cudaStream_t s);
+
+}  // namespace krt

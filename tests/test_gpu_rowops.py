@@ -1,0 +1,299 @@
+"""Per-op parity of the CUDA backend against the CPU oracle, through the C ABI.
+
+Every op is bit-exact against the oracle except silu_mul (CUDA expf vs glibc
+expf), which is held to |g - r| <= 1e-5 |r|.  Shapes cover the reference
+configurations plus ragged/odd sizes that take the kernels' scalar paths.
+"""
+import numpy as np
+import pytest
+
+from tests import _data
+from tests._parity import assert_bits_equal, assert_close_rel
+
+pytestmark = pytest.mark.gpu
+f32 = np.float32
+
+
+def up(gpu, a):
+    return gpu.upload(np.ascontiguousarray(a, f32))
+
+
+def rd(gpu, h, shape):
+    return gpu.read(h, int(np.prod(shape))).reshape(shape)
+
+
+# --- embed (reference.rs:133-140) -------------------------------------------------
+
+@pytest.mark.parametrize("vocab,dim", [(64, 96), (49, 576), (97, 2048), (16, 36), (13, 7)])
+def test_embed_bf16(gpu, oracle, vocab, dim):
+    table = _data.bf16_table(vocab, dim, 1)
+    toks = _data.tokens(23, vocab, 2)
+    gpu.prepare_embedding(oracle.BF16, table, None, vocab, dim)
+    assert gpu.storage() == "bf16"
+    out = gpu.alloc(len(toks) * dim)
+    for r, t in enumerate(toks):
+        gpu.embed(int(t), out, r * dim)
+    got = rd(gpu, out, (len(toks), dim))
+    assert_bits_equal(got, oracle.embed_rows(oracle.BF16, table, None, vocab, dim, toks), "embed bf16")
+
+
+@pytest.mark.parametrize("vocab,dim", [(64, 96), (40, 1024), (12, 32)])
+def test_embed_q8_0(gpu, oracle, vocab, dim):
+    codes, scales = _data.q8_table(vocab, dim, 3)
+    toks = _data.tokens(31, vocab, 4)
+    gpu.prepare_embedding(oracle.Q8_0, codes, scales, vocab, dim)
+    assert gpu.storage() == "q8_0"
+    out = gpu.alloc(len(toks) * dim)
+    for r, t in enumerate(toks):
+        gpu.embed(int(t), out, r * dim)
+    got = rd(gpu, out, (len(toks), dim))
+    assert_bits_equal(got, oracle.embed_rows(oracle.Q8_0, codes, scales, vocab, dim, toks), "embed q8_0")
+
+
+def test_embed_q8_0x4_deinterleaves_on_device(gpu, oracle):
+    vocab, dim = 32, 128
+    w = _data.lcg_normal(vocab * dim, 5, 0.0, 0.05).reshape(vocab, dim)
+    blocks = oracle.q8_0x4_pack(w)
+    gpu.prepare_embedding(oracle.Q8_0X4, blocks, None, vocab, dim)
+    assert gpu.storage() == "q8_0x4"
+    toks = _data.tokens(19, vocab, 6)
+    out = gpu.alloc(len(toks) * dim)
+    for r, t in enumerate(toks):
+        gpu.embed(int(t), out, r * dim)
+    got = rd(gpu, out, (len(toks), dim))
+    assert_bits_equal(got, oracle.embed_rows(oracle.Q8_0X4, blocks, None, vocab, dim, toks), "q8_0x4")
+
+
+def test_embed_f32_and_unaligned_offsets(gpu, oracle):
+    vocab, dim = 20, 12
+    table = _data.lcg_normal(vocab * dim, 7).reshape(vocab, dim)
+    gpu.prepare_embedding(oracle.F32, table, None, vocab, dim)
+    out = gpu.alloc(5 * dim + 3)
+    toks = [3, 19, 0, 7, 7]
+    for r, t in enumerate(toks):
+        gpu.embed(t, out, 3 + r * dim)  # offset 3: scalar path
+    got = gpu.read(out, 5 * dim + 3)
+    want = np.zeros(5 * dim + 3, f32)
+    want[3:] = oracle.embed_rows(oracle.F32, table, None, vocab, dim, toks).ravel()
+    assert_bits_equal(got, want, "embed f32")
+
+
+def test_embed_rejects_bad_token_and_offset(gpu, oracle):
+    import kernrt_b200
+
+    table = _data.bf16_table(8, 16, 8)
+    gpu.prepare_embedding(oracle.BF16, table, None, 8, 16)
+    out = gpu.alloc(32)
+    with pytest.raises(kernrt_b200.KernrtCudaError) as e:
+        gpu.embed(8, out, 0)
+    assert e.value.code == kernrt_b200.E_INVALID
+    with pytest.raises(kernrt_b200.KernrtCudaError):
+        gpu.embed(1, out, 17)  # 17 + 16 > 32
+    gpu.embed(1, out, 16)  # still usable
+    assert_bits_equal(gpu.read(out, 32)[16:], oracle.bf16_to_f32(table[1]), "embed after error")
+
+
+# --- rms_norm (reference.rs:161-178) ---------------------------------------------------
+
+@pytest.mark.parametrize("rows,dim,eps", [(1, 2048, 1e-5), (7, 576, 1e-5), (33, 1536, 1e-6),
+                                          (5, 37, 1e-5), (64, 1024, 1e-6), (3, 8192, 1e-5),
+                                          (2, 12, 0.0), (100, 2048, 1e-5)])
+def test_rms_norm(gpu, oracle, rows, dim, eps):
+    x = _data.lcg_normal(rows * dim, 10 + dim).reshape(rows, dim)
+    w = _data.lcg_normal(dim, 11, 1.0, 0.1)
+    hx, hw, ho = up(gpu, x), up(gpu, w), gpu.alloc(rows * dim)
+    gpu.rms_norm(ho, hx, hw, rows, dim, eps)
+    assert_bits_equal(rd(gpu, ho, (rows, dim)), oracle.rms_norm(x, w, eps), f"rms {rows}x{dim}")
+
+
+def test_rms_norm_partial_rows_leave_the_rest(gpu, oracle):
+    rows, dim = 9, 64
+    x = _data.lcg_normal(rows * dim, 12).reshape(rows, dim)
+    w = np.ones(dim, f32)
+    hx, hw, ho = up(gpu, x), up(gpu, w), gpu.alloc(rows * dim)
+    gpu.rms_norm(ho, hx, hw, 4, dim, 1e-5)
+    got = rd(gpu, ho, (rows, dim))
+    assert_bits_equal(got[:4], oracle.rms_norm(x[:4], w, 1e-5), "live rows")
+    assert np.all(got[4:] == 0)
+
+
+def test_rms_norm_rejects_aliasing(gpu):
+    import kernrt_b200
+
+    h = gpu.alloc(64)
+    w = gpu.alloc(64)
+    with pytest.raises(kernrt_b200.KernrtCudaError) as e:
+        gpu.rms_norm(h, h, w, 1, 64, 1e-5)
+    assert "distinct" in str(e.value)
+
+
+# --- qk_norm (reference.rs:180-207) ------------------------------------------------------
+
+@pytest.mark.parametrize("rows,width,head", [(5, 1024, 128), (3, 2048, 64), (2, 1536, 64),
+                                             (4, 512, 64), (3, 24, 6), (2, 4096, 64),
+                                             (2, 100, 32), (1, 2048, 128)])
+def test_qk_norm(gpu, oracle, rows, width, head):
+    v = _data.lcg_normal(rows * width, 20 + width).reshape(rows, width)
+    w = _data.lcg_normal(head, 21, 1.0, 0.1)
+    hv, hw = up(gpu, v), up(gpu, w)
+    gpu.qk_norm(hv, rows, width, head, hw, 1e-6)
+    assert_bits_equal(rd(gpu, hv, (rows, width)), oracle.qk_norm(v, head, w, 1e-6), "qk_norm")
+
+
+# --- rope (reference.rs:209-257) -----------------------------------------------------------
+
+ROPE_SHAPES = [(6, 576, 192, 64, 1e5), (4, 2048, 2048, 64, 1.3e5), (3, 2048, 1024, 128, 1e6),
+               (2, 1536, 512, 64, 1e6), (3, 12, 8, 6, 1e4), (5, 64, 96, 32, 1e4), (2, 8, 8, 4, 1e4)]
+
+
+@pytest.mark.parametrize("interleaved", [False, True])
+@pytest.mark.parametrize("rows,qw,kvw,head,theta", ROPE_SHAPES)
+def test_rope(gpu, oracle, rows, qw, kvw, head, theta, interleaved):
+    q = _data.lcg_normal(rows * qw, 30 + qw).reshape(rows, qw)
+    k = _data.lcg_normal(rows * kvw, 31 + kvw).reshape(rows, kvw)
+    pos = np.array([0, 1, 511, 4095, 8191, 3, 77][:rows], np.uint64)
+    hq, hk = up(gpu, q), up(gpu, k)
+    gpu.rope(hq, hk, qw, kvw, rows, pos, head, theta, interleaved)
+    wq, wk = oracle.rope(q, k, pos, head, theta, interleaved)
+    assert_bits_equal(rd(gpu, hq, (rows, qw)), wq, "rope q")
+    assert_bits_equal(rd(gpu, hk, (rows, kvw)), wk, "rope k")
+
+
+def test_rope_takes_min_of_rows_and_positions(gpu, oracle):
+    rows, w, head = 4, 64, 16
+    q = _data.lcg_normal(rows * w, 33).reshape(rows, w)
+    k = _data.lcg_normal(rows * w, 34).reshape(rows, w)
+    hq, hk = up(gpu, q), up(gpu, k)
+    gpu.rope(hq, hk, w, w, rows, [5, 9], head, 1e4, False)
+    wq, wk = oracle.rope(q[:2], k[:2], [5, 9], head, 1e4)
+    got = rd(gpu, hq, (rows, w))
+    assert_bits_equal(got[:2], wq, "rope rows")
+    assert_bits_equal(got[2:], q[2:], "untouched rows")
+
+
+# --- silu_mul / add / mul / copy -----------------------------------------------------------
+
+@pytest.mark.parametrize("n", [1, 3, 1000, 4608, 8192 * 5 + 3])
+def test_silu_mul(gpu, oracle, n):
+    g = _data.lcg_normal(n, 40, 0.0, 3.0)
+    u = _data.lcg_normal(n, 41)
+    if n > 8:
+        g[:8] = [0.0, -0.0, 20.0, -20.0, 80.0, -80.0, 1e-30, -1e-30]
+    hg, hu = up(gpu, g), up(gpu, u)
+    gpu.silu_mul(hg, hu, n)
+    assert_close_rel(gpu.read(hg, n), oracle.silu_mul(g, u), what="silu_mul")
+
+
+@pytest.mark.parametrize("n", [1, 2, 7, 4096, 65536 + 5])
+def test_add_in_place(gpu, oracle, n):
+    d = _data.lcg_normal(n, 42)
+    s = _data.lcg_normal(n, 43)
+    hd, hs = up(gpu, d), up(gpu, s)
+    gpu.add_in_place(hd, hs, n)
+    assert_bits_equal(gpu.read(hd, n), oracle.add_in_place(d, s), "add")
+
+
+def test_mul_offsets_and_aliasing(gpu, oracle):
+    n = 3 * 1536
+    base = _data.lcg_normal(n, 44)
+    # the LFM2 pattern: h = B * x over thirds of one buffer into another
+    hb = up(gpu, base)
+    hh = gpu.alloc(1536)
+    gpu.mul(hh, 0, hb, 0, hb, 2 * 1536, 1536)
+    want = np.zeros(1536, f32)
+    oracle.mul_into(want, 0, base, 0, base, 2 * 1536, 1536)
+    assert_bits_equal(gpu.read(hh, 1536), want, "mul thirds")
+    # in place, same offsets (benign) and overlapping different offsets (in-order)
+    for oo, ao, bo, length in [(0, 0, 100, 500), (10, 0, 2000, 700), (0, 5, 300, 900), (7, 7, 7, 50)]:
+        arr = base.copy()
+        h = up(gpu, arr)
+        gpu.mul(h, oo, h, ao, h, bo, length)
+        oracle.mul_into(arr, oo, arr, ao, arr, bo, length)
+        assert_bits_equal(gpu.read(h, n), arr, f"mul alias {oo},{ao},{bo}")
+
+
+def test_copy_overlapping_is_memmove(gpu, oracle):
+    n = 1000
+    base = _data.lcg_normal(n, 45)
+    for so, do, length in [(0, 10, 900), (10, 0, 900), (0, 500, 500), (3, 3, 10)]:
+        arr = base.copy()
+        h = up(gpu, arr)
+        gpu.copy(h, so, h, do, length)
+        oracle.copy_into(arr, so, arr, do, length)
+        assert_bits_equal(gpu.read(h, n), arr, f"copy {so}->{do}")
+    other = gpu.alloc(n)
+    h = up(gpu, base)
+    gpu.copy(h, 1, other, 0, 2)
+    assert list(gpu.read(other, 2)) == list(base[1:3])
+
+
+# --- conv (reference.rs:365-393, 490-503) -------------------------------------------------
+
+@pytest.mark.parametrize("rows,dim,k", [(9, 40, 3), (1, 1536, 3), (64, 1536, 3), (5, 8, 1),
+                                        (7, 33, 4), (2, 16, 3)])
+def test_conv_prefill(gpu, oracle, rows, dim, k):
+    x = _data.lcg_normal(rows * dim, 50 + dim).reshape(rows, dim)
+    w = _data.lcg_normal(dim * k, 51, 0.0, 0.3)
+    hx, hw, ho = up(gpu, x), up(gpu, w), gpu.alloc(rows * dim)
+    gpu.conv_prefill(ho, hx, hw, rows, dim, k)
+    assert_bits_equal(rd(gpu, ho, (rows, dim)), oracle.conv_prefill(x, w, k), "conv_prefill")
+
+
+def test_conv_prefill_in_place_reads_the_original(gpu, oracle):
+    rows, dim, k = 6, 16, 3
+    x = _data.lcg_normal(rows * dim, 52).reshape(rows, dim)
+    w = _data.lcg_normal(dim * k, 53)
+    hx, hw = up(gpu, x), up(gpu, w)
+    gpu.conv_prefill(hx, hx, hw, rows, dim, k)
+    assert_bits_equal(rd(gpu, hx, (rows, dim)), oracle.conv_prefill(x, w, k), "conv in place")
+
+
+@pytest.mark.parametrize("dim,k", [(4, 3), (1536, 3), (33, 4), (8, 1), (8, 2)])
+def test_conv_decode_steps_match_prefill(gpu, oracle, dim, k):
+    rows = 6
+    h = _data.lcg_normal(rows * dim, 54).reshape(rows, dim)
+    w = _data.lcg_normal(dim * k, 55, 0.0, 0.3)
+    hw = up(gpu, w)
+    state = gpu.alloc(max(1, (k - 1) * dim))
+    ost = np.zeros(max(1, (k - 1) * dim), f32)
+    for r in range(rows):
+        hx = up(gpu, h[r])
+        gpu.conv_decode(hx, hx, hw, state, dim, k)  # out aliases x
+        want, ost_new = oracle.conv_decode(h[r], w, ost[:(k - 1) * dim] if k > 1 else np.zeros(0, f32), k)
+        if k > 1:
+            ost[:(k - 1) * dim] = ost_new
+        assert_bits_equal(gpu.read(hx, dim), want, f"decode row {r}")
+        if k > 1:
+            assert_bits_equal(gpu.read(state, (k - 1) * dim), ost[:(k - 1) * dim], f"ring row {r}")
+
+
+# --- Q8_0 (quant.rs:856-874) -------------------------------------------------------------------
+
+@pytest.mark.parametrize("rows,dim", [(3, 1000), (256, 1024), (2, 37), (1, 2048)])
+def test_quantize_q8_0(gpu, oracle, rows, dim):
+    x = _data.lcg_normal(rows * dim, 60 + dim).reshape(rows, dim)
+    x[0, :5] = [0.0, -0.0, 1e-38, 3.0, -3.0]
+    if dim >= 64:
+        x[0, 32:64] = 0.0  # an all-zero block: scale 0, inv 0
+    nb = (dim + 31) // 32
+    hx = up(gpu, x)
+    hc, hs, hh = gpu.alloc_bytes(rows * nb * 32), gpu.alloc_bytes(rows * nb * 4), gpu.alloc_bytes(rows * nb * 2)
+    gpu.quantize_q8_0(hx, rows, dim, hc, hs, hh)
+    wc, ws, wh = oracle.q8_quantize_rows(x)
+    assert_bits_equal(gpu.read_bytes(hc, rows * nb * 32, np.int8).reshape(rows, -1), wc, "codes")
+    assert_bits_equal(gpu.read_bytes(hs, rows * nb * 4, np.float32).reshape(rows, -1), ws, "scales")
+    assert_bits_equal(gpu.read_bytes(hh, rows * nb * 2, np.uint16).reshape(rows, -1), wh, "f16 scales")
+
+
+@pytest.mark.parametrize("rows,dim,eps", [(256, 1024, 1e-6), (5, 2048, 1e-5), (3, 40, 1e-5)])
+def test_rms_norm_q8_0_fused(gpu, oracle, rows, dim, eps):
+    x = _data.lcg_normal(rows * dim, 70 + dim).reshape(rows, dim)
+    w = _data.lcg_normal(dim, 71, 1.0, 0.1)
+    nb = (dim + 31) // 32
+    hx, hw = up(gpu, x), up(gpu, w)
+    hc, hs, hh = gpu.alloc_bytes(rows * nb * 32), gpu.alloc_bytes(rows * nb * 4), gpu.alloc_bytes(rows * nb * 2)
+    gpu.rms_norm_q8_0(hx, hw, rows, dim, eps, hc, hs, hh)
+    wc, ws, wh = oracle.q8_quantize_rows(oracle.rms_norm(x, w, eps))
+    assert_bits_equal(gpu.read_bytes(hc, rows * nb * 32, np.int8).reshape(rows, -1), wc, "codes")
+    assert_bits_equal(gpu.read_bytes(hs, rows * nb * 4, np.float32).reshape(rows, -1), ws, "scales")
+    assert_bits_equal(gpu.read_bytes(hh, rows * nb * 2, np.uint16).reshape(rows, -1), wh, "f16")
