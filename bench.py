@@ -48,6 +48,8 @@ def parse():
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--rows", type=int, default=0,
+                   help="profiling only: run a smaller row count than the workload's")
     return p.parse_args()
 
 
@@ -67,7 +69,7 @@ def peaks():
 
 def profile_traffic():
     """Per-launch DRAM bytes of the chain kernel from the committed ncu summary
-    (profiles/chain_bf16_65536rows.json), scaled to this rank's rows."""
+    (profiles/k_chain_smollm2-1.7b_traffic.json), scaled to this rank's rows."""
     path = os.path.join(ROOT, "profiles", "chain_bf16_65536rows.json")
     try:
         with open(path) as fh:
@@ -78,29 +80,69 @@ def profile_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled through NVML every 20 ms during
+    the timed region (nvidia-smi as the fallback)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = [("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4)]
 
-    def __init__(self, index: int):
-        self.index = index
-        self.rows = []
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.sm, self.max_sm, self.reasons = [], [], set()
         self._stop = threading.Event()
         self._t = None
+        self._nvml = None
+        self._h = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            props = torch.cuda.get_device_properties(cuda_index)
+            bus = getattr(props, "pci_bus_id", None)
+            if bus is not None:
+                dom = getattr(props, "pci_domain_id", 0)
+                dev = getattr(props, "pci_device_id", 0)
+                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(f"{dom:08x}:{bus:02x}:{dev:02x}.0")
+            else:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(cuda_index)
+        except Exception:
+            self._nvml = None
+
+    def _sample_nvml(self):
+        n = self._nvml
+        self.sm.append(n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM))
+        self.max_sm.append(n.nvmlDeviceGetMaxClockInfo(self._h, n.NVML_CLOCK_SM))
+        get = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            n.nvmlDeviceGetCurrentClocksThrottleReasons
+        mask = get(self._h)
+        for name, const, bit in self.REASONS:
+            if mask & getattr(n, const, bit):
+                self.reasons.add(name)
+
+    def _sample_smi(self):
+        out = subprocess.run(["nvidia-smi", f"--id={self.cuda_index}",
+                              "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                              "clocks_event_reasons.hw_thermal_slowdown,"
+                              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                              "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                             timeout=5).stdout.strip().split(",")
+        self.sm.append(float(out[0]))
+        self.max_sm.append(float(out[1]))
+        for (name, _, _), v in zip(self.REASONS, out[2:]):
+            if v.strip().lower().startswith("active"):
+                self.reasons.add(name)
 
     def _run(self):
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                     timeout=5).stdout.strip()
-                if out:
-                    self.rows.append([c.strip() for c in out.split(",")])
+                self._sample_nvml() if self._nvml else self._sample_smi()
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(0.02)
 
     def __enter__(self):
         self._t = threading.Thread(target=self._run, daemon=True)
@@ -112,15 +154,11 @@ class ClockSampler:
         self._t.join(timeout=10)
 
     def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4)
-                          if len(r) > 5 + i and r[5 + i].lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+        if not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock samples"]}
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": max(self.max_sm),
+                "reasons": sorted(self.reasons), "samples": len(self.sm),
+                "source": "nvml" if self._nvml else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------------
@@ -229,7 +267,8 @@ def run_kernrt(args, rank, world, local):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    lo, hi = W.shard_rows(WL.rows, world, rank)
+    total_rows = args.rows if args.rows > 0 else WL.rows
+    lo, hi = W.shard_rows(total_rows, world, rank)
     R = hi - lo
     H, Q, KV, I = WL.dim, WL.q_dim, WL.kv_dim, WL.hidden
     b = kernrt_b200.CudaBackend(local)
@@ -278,7 +317,7 @@ def run_kernrt(args, rank, world, local):
     per_launch = [s.elapsed_time(e) for s, e in ev]  # ms
     total_ms = ev[0][0].elapsed_time(ev[-1][1])
     total_ms = max_over_ranks(total_ms)
-    value = WL.rows * args.steps / (total_ms / 1000.0)
+    value = total_rows * args.steps / (total_ms / 1000.0)
     avg_launch_s = statistics.mean(per_launch) / 1000.0
     bpr = WL.bytes_per_row()
     achieved = bpr * R / avg_launch_s / 1e9
@@ -286,35 +325,41 @@ def run_kernrt(args, rank, world, local):
     tpr = profile_traffic()
 
     # ---- end to end through the C ABI with pinned host buffers
-    host_in = {n: torch.empty(R * w, dtype=dt, pin_memory=True)
-               for n, w, dt in [("tokens", 1, torch.int32), ("positions", 1, torch.int32),
-                                ("q", Q, torch.float32), ("k", KV, torch.float32),
-                                ("gate", I, torch.float32), ("up", I, torch.float32),
-                                ("resid", H, torch.float32)]}
-    host_in["tokens"].copy_(torch.from_numpy(tokens))
-    host_in["positions"].copy_(torch.from_numpy(positions))
-    gh = torch.Generator(device=f"cuda:{local}").manual_seed(200 + rank)
-    for n, w in [("q", Q), ("k", KV), ("gate", I), ("up", I), ("resid", H)]:
-        host_in[n].copy_(torch.randn(R * w, device=f"cuda:{local}", generator=gh).cpu())
-    host_out = {n: torch.empty(R * w, dtype=torch.float32, pin_memory=True)
-                for n, w in [("x", H), ("xb", H), ("q", Q), ("k", KV), ("gate", I)]}
-    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
-    d2h = sum(t.numel() * t.element_size() for t in host_out.values())
+    e2e = None
+    if args.e2e_steps > 0:
+        host_in = {n: torch.empty(R * w, dtype=dt, pin_memory=True)
+                   for n, w, dt in [("tokens", 1, torch.int32), ("positions", 1, torch.int32),
+                                    ("q", Q, torch.float32), ("k", KV, torch.float32),
+                                    ("gate", I, torch.float32), ("up", I, torch.float32),
+                                    ("resid", H, torch.float32)]}
+        host_in["tokens"].copy_(torch.from_numpy(tokens))
+        host_in["positions"].copy_(torch.from_numpy(positions))
+        gh = torch.Generator(device=f"cuda:{local}").manual_seed(200 + rank)
+        for n, w in [("q", Q), ("k", KV), ("gate", I), ("up", I), ("resid", H)]:
+            host_in[n].copy_(torch.randn(R * w, device=f"cuda:{local}", generator=gh).cpu())
+        host_out = {n: torch.empty(R * w, dtype=torch.float32, pin_memory=True)
+                    for n, w in [("x", H), ("xb", H), ("q", Q), ("k", KV), ("gate", I)]}
+        h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+        d2h = sum(t.numel() * t.element_size() for t in host_out.values())
 
-    def e2e_step():
-        for n, t in host_in.items():
-            b.write_ptr(h[n], t.data_ptr(), t.numel() * t.element_size())
-        b.layer_chain(**chain)
-        for n, t in host_out.items():
-            b.read_ptr(h[n], t.data_ptr(), t.numel() * t.element_size())
+        def e2e_step():
+            for n, t in host_in.items():
+                b.write_ptr(h[n], t.data_ptr(), t.numel() * t.element_size())
+            b.layer_chain(**chain)
+            for n, t in host_out.items():
+                b.read_ptr(h[n], t.data_ptr(), t.numel() * t.element_size())
 
-    e2e_step()
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
         e2e_step()
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
-    e2e_value = WL.rows * args.e2e_steps / e2e_s
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+        e2e = {"value": total_rows * args.e2e_steps / e2e_s, "unit": UNIT,
+               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+               "steps": args.e2e_steps,
+               "path": "kernrt_cuda_write_bytes (pinned) -> kernrt_cuda_layer_chain -> "
+                       "kernrt_cuda_read_bytes"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -332,7 +377,7 @@ def run_kernrt(args, rank, world, local):
             "warmup": max(3, args.warmup), "ms_per_step": total_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded; bf16 embedding ~N(0,0.02), activations ~N(0,1), random init)",
-            "config": {"workload": WL.name, "rows": WL.rows, "rows_per_gpu": R, "hidden": H,
+            "config": {"workload": WL.name, "rows": total_rows, "rows_per_gpu": R, "hidden": H,
                        "q_heads": WL.n_heads, "kv_heads": WL.n_kv_heads, "head_dim": WL.head,
                        "intermediate": I, "vocab": WL.vocab, "rope_theta": WL.theta,
                        "positions": "row % 4096", "parallelism": f"row-shard x{world}, no collective",
@@ -343,10 +388,7 @@ def run_kernrt(args, rank, world, local):
                          "algorithmic_bytes_per_launch": bpr * R,
                          "bytes_per_row": bpr, "launch_ms_mean": statistics.mean(per_launch),
                          "launch_ms_min": min(per_launch)},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d * world,
-                    "d2h_bytes_per_step": d2h * world, "steps": args.e2e_steps,
-                    "path": "kernrt_cuda_write_bytes (pinned) -> kernrt_cuda_layer_chain -> "
-                            "kernrt_cuda_read_bytes"},
+            "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": args.steps,
