@@ -70,7 +70,7 @@ def peaks():
 def profile_traffic():
     """Per-launch DRAM bytes of the chain kernel from the committed ncu summary
     (profiles/k_chain_smollm2-1.7b_traffic.json), scaled to this rank's rows."""
-    path = os.path.join(ROOT, "profiles", "chain_bf16_65536rows.json")
+    path = os.path.join(ROOT, "profiles", "k_chain_smollm2-1.7b_traffic.json")
     try:
         with open(path) as fh:
             d = json.load(fh)
