@@ -199,6 +199,33 @@ int kernrt_cuda_layer_chain(kernrt_cuda_ctx *ctx, const kernrt_chain_args *args)
 int kernrt_cuda_lfm2_conv_block(kernrt_cuda_ctx *ctx, kernrt_buf bcx, kernrt_buf kernel,
                                 kernrt_buf ring, kernrt_buf cy, size_t rows, size_t dim, size_t k);
 
+/* --- Embedding gather without allocation --------------------------------------
+ * No counterpart in the reference: KernRT's backends allocate their own memory.
+ * Some callers of this library cannot let it allocate device memory: a host
+ * runtime that owns all of HBM through its own pre-reserved pool, or a serving
+ * loop that must not hit the device-wide synchronisation cudaMalloc and
+ * cudaFree can cause.  This entry point needs no context and calls no
+ * allocator: it gathers rows `tokens[0..n)` (host int32 ids < vocab) of a
+ * device-resident table into the caller's device rows `out[r*dim ..]`, on
+ * `stream` (a cudaStream_t; NULL = the legacy default stream) of `device`.
+ * The table is f32, bf16 or row-major Q8_0 (codes + f32 block scales), laid
+ * out as for kernrt_cuda_prepare_embedding; results equal kernrt_cuda_embed's.
+ *
+ * The per-row ids and offsets go to a fixed scratch array compiled into the
+ * library: KERNRT_NOALLOC_MAX_ROWS rows (768 KiB), held on every GPU that
+ * loads the library until the process exits.  Larger n is rejected with
+ * KERNRT_E_INVALID; split the call.  All calls on a device share the array,
+ * so calls that may overlap on the GPU (other streams, other threads) race
+ * and must be ordered by the caller.  The first call on each device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture begins.  The ids
+ * are read from host memory during the call when pageable; page-locked ids
+ * must stay unchanged until the stream has passed this call. */
+#define KERNRT_NOALLOC_MAX_ROWS 65536
+int kernrt_cuda_embed_rows_noalloc(int device, int kind, const void *table, const float *scales,
+                                   size_t vocab, size_t dim, const int32_t *tokens, size_t n,
+                                   float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

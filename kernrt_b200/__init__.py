@@ -94,7 +94,10 @@ SIGNATURES = {
     "kernrt_cuda_rope_prepare": (C.c_int, [P, C.c_float, SZ, SZ]),
     "kernrt_cuda_layer_chain": (C.c_int, [P, C.POINTER(ChainArgs)]),
     "kernrt_cuda_lfm2_conv_block": (C.c_int, [P, Buf, Buf, Buf, Buf, SZ, SZ, SZ]),
+    "kernrt_cuda_embed_rows_noalloc": (C.c_int, [C.c_int, C.c_int, P, P, SZ, SZ, P, SZ, P, P]),
 }
+
+NOALLOC_MAX_ROWS = 65536
 
 
 def load() -> C.CDLL:
@@ -295,6 +298,16 @@ class CudaBackend:
     def lfm2_conv_block(self, bcx: int, kernel: int, ring: int, cy: int, rows: int, dim: int,
                         k: int) -> None:
         _ok(self._lib.kernrt_cuda_lfm2_conv_block(self._ctx, bcx, kernel, ring, cy, rows, dim, k))
+
+
+def embed_rows_noalloc(device: int, kind: int, table_ptr: int, scales_ptr: int, vocab: int, dim: int,
+                       tokens, out_ptr: int, stream: int = 0) -> None:
+    """kernrt_cuda_embed_rows_noalloc: gather `tokens` rows of a device table
+    into the caller's device rows at `out_ptr` without allocating anything
+    (fixed scratch of NOALLOC_MAX_ROWS rows; see include/kernrt_cuda.h)."""
+    toks = np.ascontiguousarray(tokens, dtype=np.int32)
+    _ok(load().kernrt_cuda_embed_rows_noalloc(device, kind, table_ptr, scales_ptr or None, vocab, dim,
+                                              _ptr(toks), toks.size, out_ptr, stream or None))
 
 
 def open_backend(name: str = "cuda", device: int = -1) -> CudaBackend:

@@ -673,6 +673,10 @@ struct kernrt_cuda_ctx {
 
 static thread_local std::string g_last_error;
 
+namespace krt {
+void set_last_error(const std::string &msg) { g_last_error = msg; }
+}  // namespace krt
+
 template <class F>
 static int guard(kernrt_cuda_ctx *ctx, F &&fn) {
     if (!ctx || !ctx->b) {
