@@ -48,6 +48,10 @@ enum { KERNRT_F32 = 0, KERNRT_BF16 = 1, KERNRT_Q8_0 = 2, KERNRT_Q8_0X4 = 3 };
 /* Message for the last failing call on this thread ("" if none). */
 const char *kernrt_cuda_last_error(void);
 
+/* Kernels this library has launched in this process, over all contexts and
+ * devices (for profiling and for checking what a timed region ran). */
+int kernrt_cuda_kernel_launches(uint64_t *count);
+
 /* Number of visible CUDA devices (0 when there is no driver or device). */
 int kernrt_cuda_device_count(int *count);
 

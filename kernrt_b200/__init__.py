@@ -65,6 +65,7 @@ class ChainArgs(C.Structure):
 SIGNATURES = {
     "kernrt_cuda_last_error": (C.c_char_p, []),
     "kernrt_cuda_device_count": (C.c_int, [C.POINTER(C.c_int)]),
+    "kernrt_cuda_kernel_launches": (C.c_int, [C.POINTER(C.c_uint64)]),
     "kernrt_cuda_create": (C.c_int, [C.c_int, C.POINTER(P)]),
     "kernrt_cuda_destroy": (C.c_int, [P]),
     "kernrt_cuda_name": (C.c_char_p, [P]),
@@ -127,6 +128,13 @@ def _ok(rc: int) -> None:
 def device_count() -> int:
     n = C.c_int(0)
     _ok(load().kernrt_cuda_device_count(C.byref(n)))
+    return n.value
+
+
+def kernel_launches() -> int:
+    """Kernels the library has launched in this process (all devices)."""
+    n = C.c_uint64(0)
+    _ok(load().kernrt_cuda_kernel_launches(C.byref(n)))
     return n.value
 
 

@@ -700,6 +700,15 @@ extern "C" {
 
 const char *kernrt_cuda_last_error(void) { return g_last_error.c_str(); }
 
+int kernrt_cuda_kernel_launches(uint64_t *count) {
+    if (!count) {
+        g_last_error = "null output pointer";
+        return KERNRT_E_INVALID;
+    }
+    *count = krt::kernel_launches();
+    return KERNRT_OK;
+}
+
 int kernrt_cuda_device_count(int *count) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess) {

@@ -17,7 +17,21 @@
 
 #include <cuda_fp16.h>
 
+#include <atomic>
+#include <cstdlib>
+
 namespace krt {
+
+// Kernels this library has launched in this process (all devices).
+static std::atomic<unsigned long long> g_kernel_launches{0};
+void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+unsigned long long kernel_launches() { return g_kernel_launches.load(std::memory_order_relaxed); }
+// The launch status of the kernel just launched, counting it.
+static cudaError_t launched() {
+    count_launch();
+    return cudaGetLastError();
+}
+
 namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
@@ -52,9 +66,21 @@ __device__ __forceinline__ int8_t q8_code(float v) {
 // CUDA's RN conversion gives the same bits.
 __device__ __forceinline__ uint16_t f16_bits(float v) { return __half_as_ushort(__float2half_rn(v)); }
 
+// The correctly rounded f32 quotient a / b, computed as a double division
+// rounded to f32.  Rounding twice is harmless here: the double quotient carries
+// 53 >= 2*24 + 2 bits, so rounding it to f32 gives the correctly rounded f32
+// quotient (S. Figueroa, "When is double rounding innocuous?", SIGNUM
+// Newsletter 30(3), 1995).  Unlike an f32 division, whose subnormal operands
+// take a slow path, f32 values are never subnormal as doubles, so the cost does
+// not depend on the data (in-place SwiGLU outputs drift toward subnormals when
+// a step is repeated on its own output).
+__device__ __forceinline__ float div_rn_exact(float a, float b) {
+    return __double2float_rn(__ddiv_rn((double)a, (double)b));
+}
+
 // reference.rs:81-83 silu(g) * up.
 __device__ __forceinline__ float silu_mul1(float g, float u) {
-    return mul_rn(div_rn(g, add_rn(1.0f, expf(-g))), u);
+    return mul_rn(div_rn_exact(g, add_rn(1.0f, expf(-g))), u);
 }
 
 __device__ __forceinline__ void set_err(int *err, int code) {
@@ -201,11 +227,32 @@ __device__ __forceinline__ int k_pairs_interleaved(int q_width, int kv_width) {
     return min(kv_width / 2, q_width / 2);
 }
 
-// reference.rs:395-400 silu_mul over [lo, hi) by threads t of nt.
+// reference.rs:395-400 silu_mul over [lo, hi) by threads t of nt.  Each
+// thread keeps U independent float4 pairs in flight before using any of them:
+// the loop is bound by HBM latency x bytes in flight, not by arithmetic.
+template <int U>
 __device__ void silu_range(float *__restrict__ g, const float *__restrict__ u, size_t lo, size_t hi,
                            int t, int nt) {
     if (((lo | hi) & 3) == 0) {
-        for (size_t i = lo + 4 * (size_t)t; i < hi; i += 4 * (size_t)nt) {
+        const size_t step = 4 * (size_t)nt;
+        size_t i = lo + 4 * (size_t)t;
+        for (; i + (U - 1) * step < hi; i += U * step) {
+            float4 gv[U], uv[U];
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                gv[k] = ld4(g + i + k * step);
+                uv[k] = ld4(u + i + k * step);
+            }
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                gv[k].x = silu_mul1(gv[k].x, uv[k].x);
+                gv[k].y = silu_mul1(gv[k].y, uv[k].y);
+                gv[k].z = silu_mul1(gv[k].z, uv[k].z);
+                gv[k].w = silu_mul1(gv[k].w, uv[k].w);
+                st4(g + i + k * step, gv[k]);
+            }
+        }
+        for (; i < hi; i += step) {
             float4 gv = ld4(g + i);
             const float4 uv = ld4(u + i);
             gv.x = silu_mul1(gv.x, uv.x);
@@ -216,6 +263,61 @@ __device__ void silu_range(float *__restrict__ g, const float *__restrict__ u, s
         }
     } else {
         for (size_t i = lo + t; i < hi; i += nt) g[i] = silu_mul1(g[i], u[i]);
+    }
+}
+
+// Half-split RoPE (reference.rs:239-254) over rows [r0, r0 + g) of a
+// [rows, width] buffer as one flat range of float4 (lo, hi) pairs, U pairs in
+// flight per thread.  Requires half % 4 == 0 and width % 4 == 0.
+template <int U>
+__device__ void rope_half_rows(float *v, int width, int head, int half, int r0, int g,
+                               const int32_t *__restrict__ pos, const float *__restrict__ cos_t,
+                               const float *__restrict__ sin_t, int max_pos, int *err, int t, int nt) {
+    const int per = half >> 2;
+    const int nh = width / head;
+    const int per_row = nh * per;
+    const int n = g * per_row;
+    int i = t;
+    for (; i < n; i += U * nt) {
+        float4 lo[U], hi[U];
+        float *b[U];
+        int j[U], p[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int it = i + k * nt;
+            b[k] = nullptr;
+            if (it < n) {
+                const int r = it / per_row;
+                const int rem = it - r * per_row;
+                const int h = rem / per;
+                j[k] = (rem - h * per) << 2;
+                p[k] = pos[r0 + r];
+                b[k] = v + (size_t)(r0 + r) * width + h * head;
+                lo[k] = *reinterpret_cast<const float4 *>(b[k] + j[k]);
+                hi[k] = *reinterpret_cast<const float4 *>(b[k] + half + j[k]);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            if (!b[k]) continue;
+            if ((unsigned)p[k] >= (unsigned)max_pos) {
+                set_err(err, ERR_POSITION);
+                continue;
+            }
+            const float4 c = __ldg(reinterpret_cast<const float4 *>(cos_t + (size_t)p[k] * half + j[k]));
+            const float4 s = __ldg(reinterpret_cast<const float4 *>(sin_t + (size_t)p[k] * half + j[k]));
+            float4 nl, nhv;
+            nl.x = sub_rn(mul_rn(lo[k].x, c.x), mul_rn(hi[k].x, s.x));
+            nl.y = sub_rn(mul_rn(lo[k].y, c.y), mul_rn(hi[k].y, s.y));
+            nl.z = sub_rn(mul_rn(lo[k].z, c.z), mul_rn(hi[k].z, s.z));
+            nl.w = sub_rn(mul_rn(lo[k].w, c.w), mul_rn(hi[k].w, s.w));
+            nhv.x = add_rn(mul_rn(lo[k].x, s.x), mul_rn(hi[k].x, c.x));
+            nhv.y = add_rn(mul_rn(lo[k].y, s.y), mul_rn(hi[k].y, c.y));
+            nhv.z = add_rn(mul_rn(lo[k].z, s.z), mul_rn(hi[k].z, c.z));
+            nhv.w = add_rn(mul_rn(lo[k].w, s.w), mul_rn(hi[k].w, c.w));
+            *reinterpret_cast<float4 *>(b[k] + j[k]) = nl;
+            *reinterpret_cast<float4 *>(b[k] + half + j[k]) = nhv;
+        }
     }
 }
 
@@ -372,8 +474,15 @@ struct ChainLayout {
     size_t smem;
 };
 
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 template <int SRC, bool FQ, bool VEC>
-__global__ void __launch_bounds__(kThreads) k_chain(ChainArgs a, ChainLayout L) {
+__global__ void __launch_bounds__(kThreads, 3) k_chain(ChainArgs a, ChainLayout L) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     const int dim = a.dim;
@@ -385,7 +494,6 @@ __global__ void __launch_bounds__(kThreads) k_chain(ChainArgs a, ChainLayout L) 
     float *sc1 = reinterpret_cast<float *>(rs + (size_t)L.G * L.rstride);
     float *sc2 = sc1 + 32;
 
-    // ---- stage 0: stage the source rows (and, for the final norm, the residual rows)
     auto src_row = [&](int r) -> const unsigned char * {
         if constexpr (SRC == SRC_X) {
             return reinterpret_cast<const unsigned char *>(a.x_in + (size_t)(r0 + r) * dim);
@@ -396,53 +504,45 @@ __global__ void __launch_bounds__(kThreads) k_chain(ChainArgs a, ChainLayout L) 
                    (size_t)tok * (size_t)src_row_bytes<SRC>(dim);
         }
     };
-    {
-        const int rb = src_row_bytes<SRC>(dim);
-        if constexpr (VEC) {
-            const int n16 = rb >> 4;
-            for (int idx = tid; idx < g * n16; idx += blockDim.x) {
-                const int r = idx / n16, c = idx - r * n16;
-                const unsigned char *sp = src_row(r);
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if (sp) {
-                    v = __ldcs(reinterpret_cast<const uint4 *>(sp) + c);
-                } else if (c == 0) {
-                    set_err(a.err, ERR_TOKEN);
-                }
-                *reinterpret_cast<uint4 *>(xs + (size_t)r * L.xstride + 16 * c) = v;
-            }
-        } else {
-            for (int idx = tid; idx < g * rb; idx += blockDim.x) {
-                const int r = idx / rb, c = idx - r * rb;
-                const unsigned char *sp = src_row(r);
-                unsigned char v = 0;
-                if (sp) v = sp[c]; else if (c == 0) set_err(a.err, ERR_TOKEN);
-                xs[(size_t)r * L.xstride + c] = v;
-            }
-        }
-        if constexpr (SRC == SRC_Q8) {
-            const int nb = dim >> 5;
-            for (int idx = tid; idx < g * nb; idx += blockDim.x) {
-                const int r = idx / nb, b = idx - r * nb;
-                const int tok = a.tokens[r0 + r];
-                float s = 0.0f;
-                if ((unsigned)tok < (unsigned)a.vocab) s = __ldg(a.tscales + (size_t)tok * nb + b);
-                reinterpret_cast<float *>(xs + (size_t)r * L.xstride + align16(dim))[b] = s;
-            }
-        }
-        if (fq_resid) {
-            for (int idx = tid; idx < g * dim; idx += blockDim.x) {
-                const int r = idx / dim, c = idx - r * dim;
-                reinterpret_cast<float *>(rs + (size_t)r * L.rstride)[c] =
-                    a.resid[(size_t)(r0 + r) * dim + c];
-            }
-        }
-    }
-    __syncthreads();
 
-    // ---- stage 1
     if (warp == 0) {
-        // Lane r: row r's sums of squares, left to right (reference.rs:167-170).
+        // ---- stage 0 (warp 0 alone): stage the rows being normalised, and for
+        // the final norm the residual rows, into shared memory.  cp.async keeps
+        // every copy in flight at once without a register round trip.
+        const int rb = src_row_bytes<SRC>(dim);
+        for (int r = 0; r < g; ++r) {
+            const unsigned char *sp = src_row(r);
+            unsigned char *dst = xs + (size_t)r * L.xstride;
+            if (!sp && lane == 0) set_err(a.err, ERR_TOKEN);
+            if constexpr (VEC) {
+                for (int c = lane; c < (rb >> 4); c += 32) {
+                    if (sp) cp_async16(dst + 16 * c, sp + 16 * c);
+                    else *reinterpret_cast<uint4 *>(dst + 16 * c) = make_uint4(0u, 0u, 0u, 0u);
+                }
+            } else {
+                for (int c = lane; c < rb; c += 32) dst[c] = sp ? sp[c] : (unsigned char)0;
+            }
+            if constexpr (SRC == SRC_Q8) {
+                const int nb = dim >> 5;
+                const int tok = a.tokens[r0 + r];
+                float *sdst = reinterpret_cast<float *>(dst + align16(dim));
+                for (int b = lane; b < nb; b += 32) sdst[b] = sp ? __ldg(a.tscales + (size_t)tok * nb + b) : 0.0f;
+            }
+            if (fq_resid) {
+                const float *rsrc = a.resid + (size_t)(r0 + r) * dim;
+                float *rdst = reinterpret_cast<float *>(rs + (size_t)r * L.rstride);
+                if constexpr (VEC) {
+                    for (int c = lane; c < (dim >> 2); c += 32) cp_async16(rdst + 4 * c, rsrc + 4 * c);
+                } else {
+                    for (int c = lane; c < dim; c += 32) rdst[c] = rsrc[c];
+                }
+            }
+        }
+        if constexpr (VEC) cp_async_wait_all();
+        __syncwarp();
+
+        // ---- stage 1, warp 0: lane r sums row r's squares left to right
+        // (reference.rs:167-170), out of shared memory.
         if (lane < g) {
             const unsigned char *row = xs + (size_t)lane * L.xstride;
             const float *rrow = reinterpret_cast<const float *>(rs + (size_t)lane * L.rstride);
@@ -475,10 +575,16 @@ __global__ void __launch_bounds__(kThreads) k_chain(ChainArgs a, ChainLayout L) 
             if constexpr (FQ) sc2[lane] = rms_scale(ss2, (float)dim, a.final_eps);
         }
     } else {
-        // Warps 1..: the rows' independent streams.
+        // ---- stage 1, warps 1..: the rows' independent streams, from HBM.
+        const int st = tid - 32, nst = blockDim.x - 32;
         const int sw = warp - 1, nsw = nwarps - 1;
-        if (a.rope_mode != 0 || a.w_q != nullptr || a.w_k != nullptr) {
-            const bool half_vec = ((a.half | a.q_dim | a.kv_dim) & 3) == 0;
+        const bool half_vec = ((a.half | a.q_dim | a.kv_dim) & 3) == 0;
+        if (a.rope_mode == 1 && half_vec && a.w_q == nullptr && a.w_k == nullptr) {
+            if (a.q) rope_half_rows<2>(a.q, a.q_dim, a.head, a.half, r0, g, a.pos, a.cos_t, a.sin_t, a.max_pos,
+                                       a.err, st, nst);
+            if (a.k) rope_half_rows<2>(a.k, a.kv_dim, a.head, a.half, r0, g, a.pos, a.cos_t, a.sin_t, a.max_pos,
+                                       a.err, st, nst);
+        } else if (a.rope_mode != 0 || a.w_q != nullptr || a.w_k != nullptr) {
             const bool pair_vec = ((a.head | a.q_dim | a.kv_dim) & 3) == 0;
             for (int r = sw; r < g; r += nsw) {
                 const int row = r0 + r;
@@ -493,23 +599,18 @@ __global__ void __launch_bounds__(kThreads) k_chain(ChainArgs a, ChainLayout L) 
                     continue;
                 }
                 const float *ct = a.cos_t + (size_t)p * a.half;
-                const float *st = a.sin_t + (size_t)p * a.half;
+                const float *stt = a.sin_t + (size_t)p * a.half;
                 if (a.rope_mode == 1) {
-                    if (qr) rope_half_row(qr, a.q_dim / a.head, a.head, a.half, ct, st, half_vec, lane);
-                    if (kr) rope_half_row(kr, a.kv_dim / a.head, a.head, a.half, ct, st, half_vec, lane);
+                    if (qr) rope_half_row(qr, a.q_dim / a.head, a.head, a.half, ct, stt, half_vec, lane);
+                    if (kr) rope_half_row(kr, a.kv_dim / a.head, a.head, a.half, ct, stt, half_vec, lane);
                 } else {
-                    if (qr) rope_pair_row(qr, a.q_dim / 2, a.head, ct, st, pair_vec, lane);
-                    if (kr)
-                        rope_pair_row(kr, k_pairs_interleaved(a.q_dim, a.kv_dim), a.head, ct, st,
-                                      pair_vec && (k_pairs_interleaved(a.q_dim, a.kv_dim) % 2 == 0),
-                                      lane);
+                    const int kp = k_pairs_interleaved(a.q_dim, a.kv_dim);
+                    if (qr) rope_pair_row(qr, a.q_dim / 2, a.head, ct, stt, pair_vec, lane);
+                    if (kr) rope_pair_row(kr, kp, a.head, ct, stt, pair_vec && kp % 2 == 0, lane);
                 }
             }
         }
-        if (a.gate) {
-            silu_range(a.gate, a.up, (size_t)r0 * a.hidden, (size_t)(r0 + g) * a.hidden, tid - 32,
-                       blockDim.x - 32);
-        }
+        if (a.gate) silu_range<4>(a.gate, a.up, (size_t)r0 * a.hidden, (size_t)(r0 + g) * a.hidden, st, nst);
     }
     __syncthreads();
 
@@ -517,26 +618,40 @@ __global__ void __launch_bounds__(kThreads) k_chain(ChainArgs a, ChainLayout L) 
     if constexpr (!FQ) {
         if (a.xb == nullptr && a.x_out == nullptr) return;
         if constexpr (VEC) {
+            constexpr int U = 4;
             const int n4 = dim >> 2;
-            for (int idx = tid; idx < g * n4; idx += blockDim.x) {
-                const int r = idx / n4, c = (idx - r * n4) << 2;
-                const size_t o = (size_t)(r0 + r) * dim + c;
-                float v[4];
-                decode_staged<SRC, 4>(xs + (size_t)r * L.xstride, dim, c, v);
-                if (a.xb) {
-                    const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
-                    const float s = sc1[r];
-                    st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[0])), mul_rn(w.y, mul_rn(s, v[1])),
-                                              mul_rn(w.z, mul_rn(s, v[2])), mul_rn(w.w, mul_rn(s, v[3]))));
-                }
-                if (a.x_out) {
-                    float4 xo = make_float4(v[0], v[1], v[2], v[3]);
-                    if (a.resid) {
-                        const float4 rr = ld4(a.resid + o);
-                        xo = make_float4(add_rn(v[0], rr.x), add_rn(v[1], rr.y), add_rn(v[2], rr.z),
-                                         add_rn(v[3], rr.w));
+            const int total = g * n4;
+            for (int i0 = tid; i0 < total; i0 += U * blockDim.x) {
+                float4 rr[U];
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    const int idx = i0 + k * blockDim.x;
+                    if (idx < total && a.resid && a.x_out) {
+                        const int r = idx / n4, c = (idx - r * n4) << 2;
+                        rr[k] = ld4(a.resid + (size_t)(r0 + r) * dim + c);
                     }
-                    st4(a.x_out + o, xo);
+                }
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    const int idx = i0 + k * blockDim.x;
+                    if (idx >= total) continue;
+                    const int r = idx / n4, c = (idx - r * n4) << 2;
+                    const size_t o = (size_t)(r0 + r) * dim + c;
+                    float v[4];
+                    decode_staged<SRC, 4>(xs + (size_t)r * L.xstride, dim, c, v);
+                    if (a.xb) {
+                        const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
+                        const float s = sc1[r];
+                        st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[0])), mul_rn(w.y, mul_rn(s, v[1])),
+                                                  mul_rn(w.z, mul_rn(s, v[2])), mul_rn(w.w, mul_rn(s, v[3]))));
+                    }
+                    if (a.x_out) {
+                        float4 xo = make_float4(v[0], v[1], v[2], v[3]);
+                        if (a.resid)
+                            xo = make_float4(add_rn(v[0], rr[k].x), add_rn(v[1], rr[k].y), add_rn(v[2], rr[k].z),
+                                             add_rn(v[3], rr[k].w));
+                        st4(a.x_out + o, xo);
+                    }
                 }
             }
         } else {
@@ -583,6 +698,168 @@ __global__ void __launch_bounds__(kThreads) k_chain(ChainArgs a, ChainLayout L) 
     }
 }
 
+// The norm stage alone (embed/x -> RMSNorm -> xb, residual add), as a
+// persistent, warp-specialised pipeline over groups of G rows held in three
+// shared-memory slots.  In iteration i of a CTA:
+//   warp 1      stages group i+1 into slot (i+1)%3 with cp.async,
+//   warp 0      sums group i (slot i%3): lane r runs row r's squares left to
+//               right, the reference's order,
+//   warps 2..7  write group i-1 (slot (i-1)%3): xb = w*(scale*x), x + resid.
+// The three slots are always distinct, and one __syncthreads per iteration
+// hands each slot to its next role, so the serial sums hide behind the HBM
+// traffic of the neighbouring groups.
+template <int SRC, bool VEC>
+__global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLayout L) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int dim = a.dim;
+    const int G = L.G;
+    const int ngroups = (a.rows + G - 1) / G;
+    const int nmine = (int)blockIdx.x < ngroups ? (ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    const size_t slot_bytes = (size_t)G * L.xstride;
+    float *scales = reinterpret_cast<float *>(smem + 3 * slot_bytes);  // [3][32]
+    const int rb = src_row_bytes<SRC>(dim);
+
+    auto first_row = [&](int i) { return (int)(blockIdx.x + (unsigned)i * gridDim.x) * G; };
+    auto slot = [&](int i) { return smem + (size_t)(i % 3) * slot_bytes; };
+
+    auto load = [&](int i) {  // warp 1
+        const int r0 = first_row(i), g = min(G, a.rows - r0);
+        unsigned char *base = slot(i);
+        for (int r = 0; r < g; ++r) {
+            const unsigned char *sp;
+            int tok = 0;
+            if constexpr (SRC == SRC_X) {
+                sp = reinterpret_cast<const unsigned char *>(a.x_in + (size_t)(r0 + r) * dim);
+            } else {
+                tok = a.tokens[r0 + r];
+                sp = (unsigned)tok < (unsigned)a.vocab
+                         ? static_cast<const unsigned char *>(a.table) + (size_t)tok * (size_t)rb
+                         : nullptr;
+                if (!sp && lane == 0) set_err(a.err, ERR_TOKEN);
+            }
+            unsigned char *dst = base + (size_t)r * L.xstride;
+            if constexpr (VEC) {
+                for (int c = lane; c < (rb >> 4); c += 32) {
+                    if (sp) cp_async16(dst + 16 * c, sp + 16 * c);
+                    else *reinterpret_cast<uint4 *>(dst + 16 * c) = make_uint4(0u, 0u, 0u, 0u);
+                }
+            } else {
+                for (int c = lane; c < rb; c += 32) dst[c] = sp ? sp[c] : (unsigned char)0;
+            }
+            if constexpr (SRC == SRC_Q8) {
+                const int nb = dim >> 5;
+                float *sdst = reinterpret_cast<float *>(dst + align16(dim));
+                for (int b = lane; b < nb; b += 32) sdst[b] = sp ? __ldg(a.tscales + (size_t)tok * nb + b) : 0.0f;
+            }
+        }
+        if constexpr (VEC) cp_async_wait_all();
+    };
+
+    auto sum = [&](int i) {  // warp 0
+        const int r0 = first_row(i), g = min(G, a.rows - r0);
+        if (lane >= g) return;
+        const unsigned char *row = slot(i) + (size_t)lane * L.xstride;
+        float ss = 0.0f;
+        if constexpr (VEC) {
+            for (int c = 0; c < dim; c += 8) {
+                float v[8];
+                decode_staged<SRC, 8>(row, dim, c, v);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
+            }
+        } else {
+            for (int c = 0; c < dim; ++c) {
+                float v[1];
+                decode_staged<SRC, 1>(row, dim, c, v);
+                ss = add_rn(ss, mul_rn(v[0], v[0]));
+            }
+        }
+        scales[(i % 3) * 32 + lane] = rms_scale(ss, (float)dim, a.eps);
+    };
+
+    auto write = [&](int i) {  // warps 2..7
+        const int r0 = first_row(i), g = min(G, a.rows - r0);
+        const unsigned char *base = slot(i);
+        const float *sc = scales + (i % 3) * 32;
+        const int wt = tid - 64, nwt = blockDim.x - 64;
+        if constexpr (VEC) {
+            constexpr int U = 8;
+            const int n4 = dim >> 2, total = g * n4;
+            for (int i0 = wt; i0 < total; i0 += U * nwt) {
+                float4 rr[U];
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    const int idx = i0 + k * nwt;
+                    if (idx < total && a.resid && a.x_out) {
+                        const int r = idx / n4, c = (idx - r * n4) << 2;
+                        rr[k] = ld4(a.resid + (size_t)(r0 + r) * dim + c);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    const int idx = i0 + k * nwt;
+                    if (idx >= total) continue;
+                    const int r = idx / n4, c = (idx - r * n4) << 2;
+                    const size_t o = (size_t)(r0 + r) * dim + c;
+                    float v[4];
+                    decode_staged<SRC, 4>(base + (size_t)r * L.xstride, dim, c, v);
+                    if (a.xb) {
+                        const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
+                        const float s = sc[r];
+                        st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[0])), mul_rn(w.y, mul_rn(s, v[1])),
+                                                  mul_rn(w.z, mul_rn(s, v[2])), mul_rn(w.w, mul_rn(s, v[3]))));
+                    }
+                    if (a.x_out) {
+                        float4 xo = make_float4(v[0], v[1], v[2], v[3]);
+                        if (a.resid)
+                            xo = make_float4(add_rn(v[0], rr[k].x), add_rn(v[1], rr[k].y), add_rn(v[2], rr[k].z),
+                                             add_rn(v[3], rr[k].w));
+                        st4(a.x_out + o, xo);
+                    }
+                }
+            }
+        } else {
+            for (int idx = wt; idx < g * dim; idx += nwt) {
+                const int r = idx / dim, c = idx - r * dim;
+                const size_t o = (size_t)(r0 + r) * dim + c;
+                float v[1];
+                decode_staged<SRC, 1>(base + (size_t)r * L.xstride, dim, c, v);
+                if (a.xb) a.xb[o] = mul_rn(a.w_att[c], mul_rn(sc[r], v[0]));
+                if (a.x_out) a.x_out[o] = a.resid ? add_rn(v[0], a.resid[o]) : v[0];
+            }
+        }
+    };
+
+    if (warp == 1 && nmine > 0) load(0);
+    __syncthreads();
+    for (int i = 0; i <= nmine; ++i) {
+        if (warp == 1) {
+            if (i + 1 < nmine) load(i + 1);
+        } else if (warp == 0) {
+            if (i < nmine) sum(i);
+        } else {
+            if (i >= 1) write(i - 1);
+        }
+        __syncthreads();
+    }
+}
+
+// The chain's pure streams (RoPE on Q and K, SwiGLU) over all rows: no
+// shared memory and few registers, so an SM holds many more warps than the
+// norm stage's CTAs allow.  Grid-stride over one flat index space.
+template <int U>
+__global__ void __launch_bounds__(kThreads) k_stream(ChainArgs a) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x, nt = gridDim.x * blockDim.x;
+    if (a.rope_mode == 1) {
+        if (a.q) rope_half_rows<U>(a.q, a.q_dim, a.head, a.half, 0, a.rows, a.pos, a.cos_t, a.sin_t, a.max_pos,
+                                   a.err, t, nt);
+        if (a.k) rope_half_rows<U>(a.k, a.kv_dim, a.head, a.half, 0, a.rows, a.pos, a.cos_t, a.sin_t, a.max_pos,
+                                   a.err, t, nt);
+    }
+    if (a.gate) silu_range<U>(a.gate, a.up, 0, (size_t)a.rows * a.hidden, t, nt);
+}
+
 // --------------------------------------------------------------------------
 // Standalone row ops
 // --------------------------------------------------------------------------
@@ -622,7 +899,7 @@ __global__ void __launch_bounds__(kThreads) k_rope(float *q, float *k, int q_wid
 }
 
 __global__ void __launch_bounds__(kThreads) k_silu_mul(float *g, const float *u, size_t n) {
-    silu_range(g, u, 0, n, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+    silu_range<4>(g, u, 0, n, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
 }
 
 // reference.rs:308-313
@@ -804,8 +1081,26 @@ ChainLayout chain_layout(const ChainArgs &a, bool fq, int G_override) {
     L.xstride = align16(rb) + (SRC == SRC_Q8 ? align16((a.dim / 32) * 4) : 0) + 16;
     L.rstride = (fq && a.resid) ? align16(a.dim * 4) + 16 : 0;
     const int per_row = L.xstride + L.rstride;
-    int G = G_override > 0 ? G_override : (int)((72 * 1024 - 256) / per_row);
+    // At most what lets three CTAs share an SM's shared memory (and 32, the
+    // lanes of the summing warp); fewer when the rows would otherwise fill
+    // under four waves of CTAs.
+    int G = (int)((72 * 1024 - 256) / per_row);
     if (G > 32) G = 32;
+    static const int env_g = [] {
+        const char *e = std::getenv("KERNRT_CHAIN_ROWS_PER_CTA");
+        return e ? std::atoi(e) : 0;
+    }();
+    if (G_override <= 0 && env_g > 0) G_override = env_g < G ? env_g : G;
+    if (G_override > 0) {
+        G = G_override;
+    } else {
+        int sms = 148;
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess)
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const long want = ((long)a.rows + (long)sms * 3 * 4 - 1) / ((long)sms * 3 * 4);
+        if (want < G) G = (int)want;
+    }
     if (G < 1) G = 1;
     L.G = G;
     L.smem = (size_t)G * per_row + 64 * sizeof(float);
@@ -821,11 +1116,89 @@ cudaError_t launch_chain_t(const ChainArgs &a, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     const unsigned grid = grid_for((size_t)a.rows, (unsigned)L.G);
     kern<<<grid, kThreads, L.smem, s>>>(a, L);
-    return cudaGetLastError();
+    return launched();
+}
+
+int device_sms() {
+    static int sms[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!sms[dev]) {
+        int n = 148;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        sms[dev] = n > 0 ? n : 148;
+    }
+    return sms[dev];
+}
+
+// The norm stage as the persistent pipeline: rows per group from the shared
+// memory that lets two CTAs share an SM (three slots each), fewer when the
+// rows would give a CTA under eight groups.
+template <int SRC, bool VEC>
+cudaError_t launch_norm_pipe(const ChainArgs &a, cudaStream_t s) {
+    ChainLayout L{};
+    const int rb = SRC == SRC_BF16 ? a.dim * 2 : (SRC == SRC_Q8 ? a.dim : a.dim * 4);
+    L.xstride = align16(rb) + (SRC == SRC_Q8 ? align16((a.dim / 32) * 4) : 0) + 16;
+    L.rstride = 0;
+    const size_t budget = 110 * 1024 - 3 * 32 * sizeof(float);
+    int G = (int)(budget / (3 * (size_t)L.xstride));
+    if (G > 32) G = 32;
+    if (G < 1) G = 1;
+    const int sms = device_sms();
+    const long want = ((long)a.rows + (long)sms * 2 * 8 - 1) / ((long)sms * 2 * 8);
+    if (want < G) G = (int)(want > 0 ? want : 1);
+    L.G = G;
+    L.smem = 3 * (size_t)G * L.xstride + 3 * 32 * sizeof(float);
+    if (L.smem > 227 * 1024) return cudaErrorInvalidValue;
+    auto kern = k_norm_pipe<SRC, VEC>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, L.smem);
+    if (e != cudaSuccess) return e;
+    const long groups = ((long)a.rows + G - 1) / G;
+    long grid = (long)sms * (per_sm > 0 ? per_sm : 1);
+    if (grid > groups) grid = groups;
+    kern<<<(unsigned)grid, kThreads, L.smem, s>>>(a, L);
+    return launched();
 }
 
 template <int SRC>
+cudaError_t launch_chain_src_fused(const ChainArgs &a, cudaStream_t s);
+
+// Llama-family chains (no q/k norm, no final Q8, half-split RoPE or none) run
+// as two launches on the caller's stream: the norm stage's pipeline, then the
+// independent RoPE/SwiGLU streams at full occupancy.  The stages share no
+// data, so splitting them moves no extra bytes; it lets each run at the
+// occupancy its resources allow.  Other chains run as the one fused kernel.
+template <int SRC>
 cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s) {
+    const bool vec = (a.dim % 8) == 0 && (SRC != SRC_Q8 || a.dim % 32 == 0);
+    const bool streams_vec = ((a.half | a.q_dim | a.kv_dim | a.hidden) & 3) == 0;
+    const bool split = a.w_final == nullptr && a.w_q == nullptr && a.w_k == nullptr && a.rope_mode != 2 &&
+                       (streams_vec || (a.q == nullptr && a.k == nullptr && a.gate == nullptr));
+    if (!split) return launch_chain_src_fused<SRC>(a, s);
+    cudaError_t e = cudaSuccess;
+    if (a.xb || a.x_out) e = vec ? launch_norm_pipe<SRC, true>(a, s) : launch_norm_pipe<SRC, false>(a, s);
+    if (e != cudaSuccess) return e;
+    if ((a.rope_mode == 1 && (a.q || a.k)) || a.gate) {
+        static unsigned grid[64] = {0};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64) dev = 0;
+        if (!grid[dev]) {
+            int per_sm = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_stream<2>, kThreads, 0);
+            grid[dev] = (unsigned)(device_sms() * (per_sm > 0 ? per_sm : 1));
+        }
+        k_stream<2><<<grid[dev], kThreads, 0, s>>>(a);
+        e = launched();
+    }
+    return e;
+}
+
+template <int SRC>
+cudaError_t launch_chain_src_fused(const ChainArgs &a, cudaStream_t s) {
     const bool vec = (a.dim % 8) == 0 && (SRC != SRC_Q8 || a.dim % 32 == 0);
     const bool fq = a.w_final != nullptr;
     if (fq) return vec ? launch_chain_t<SRC, true, true>(a, s) : launch_chain_t<SRC, true, false>(a, s);
@@ -851,7 +1224,7 @@ cudaError_t launch_embed_gather(int kind, bool vec, const GatherArgs &a, cudaStr
         else k_embed_gather<SRC_F32, false><<<grid, kThreads, 0, s>>>(a);
         break;
     }
-    return cudaGetLastError();
+    return launched();
 }
 
 size_t chain_smem_bytes(int src, const ChainArgs &a, int rows_per_cta) {
@@ -878,7 +1251,7 @@ cudaError_t launch_qk_norm(float *v, int rows, int width, int head, const float 
                            cudaStream_t s) {
     if (rows <= 0 || width / head == 0) return cudaSuccess;
     k_qk_norm<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(v, rows, width, head, w, eps);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows, int head,
@@ -887,19 +1260,19 @@ cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows,
     if (rows <= 0) return cudaSuccess;
     k_rope<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(
         q, k, q_width, kv_width, rows, head, pos, cos_t, sin_t, max_pos, interleaved, err);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_silu_mul(float *g, const float *u, size_t n, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
     k_silu_mul<<<stream_grid(n), kThreads, 0, s>>>(g, u, n);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_add(float *d, const float *src, size_t n, cudaStream_t s) {
     if (n == 0) return cudaSuccess;
     k_add<<<stream_grid(n), kThreads, 0, s>>>(d, src, n);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_mul(float *o, const float *a, const float *b, size_t n, bool sequential,
@@ -907,21 +1280,21 @@ cudaError_t launch_mul(float *o, const float *a, const float *b, size_t n, bool 
     if (n == 0) return cudaSuccess;
     if (sequential) k_mul_sequential<<<1, 1, 0, s>>>(o, a, b, n);
     else k_mul<<<stream_grid(n), kThreads, 0, s>>>(o, a, b, n);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_conv_prefill(float *out, const float *x, const float *w, int rows, int dim, int k,
                                 cudaStream_t s) {
     if (rows <= 0 || dim <= 0) return cudaSuccess;
     k_conv_prefill<<<grid_for((size_t)rows * dim, kThreads), kThreads, 0, s>>>(out, x, w, rows, dim, k);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_conv_decode(float *out, const float *x, const float *w, float *state, int dim, int k,
                                cudaStream_t s) {
     if (dim <= 0) return cudaSuccess;
     k_conv_decode<<<grid_for((size_t)dim, kThreads), kThreads, 0, s>>>(out, x, w, state, dim, k);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_lfm2_conv_block(const float *bcx, const float *w, float *ring, float *cy, int rows,
@@ -929,7 +1302,7 @@ cudaError_t launch_lfm2_conv_block(const float *bcx, const float *w, float *ring
     if (rows <= 0 || dim <= 0) return cudaSuccess;
     k_lfm2_conv_block<<<grid_for((size_t)rows * dim, kThreads), kThreads, 0, s>>>(bcx, w, ring, cy,
                                                                                   rows, dim, k);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes, float *scales,
@@ -937,7 +1310,7 @@ cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes,
     if (rows <= 0) return cudaSuccess;
     k_quantize_q8<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(x, rows, dim, codes, scales,
                                                                               scales16);
-    return cudaGetLastError();
+    return launched();
 }
 
 cudaError_t launch_q8x4_to_row_major(const uint8_t *blocks, int out_dim, int in_dim, int8_t *quants,
@@ -945,7 +1318,7 @@ cudaError_t launch_q8x4_to_row_major(const uint8_t *blocks, int out_dim, int in_
     const size_t n = (size_t)out_dim * (in_dim / 32);
     if (n == 0) return cudaSuccess;
     k_q8x4_to_row_major<<<grid_for(n, kThreads), kThreads, 0, s>>>(blocks, out_dim, in_dim, quants, scales);
-    return cudaGetLastError();
+    return launched();
 }
 
 }  // namespace krt

@@ -12,6 +12,11 @@ namespace krt {
 // Bits of the device error word (checked by the host at every barrier).
 enum : int { ERR_TOKEN = 1, ERR_POSITION = 2 };
 
+// Kernels this library has launched in this process, and the counter hook
+// every launcher calls.
+unsigned long long kernel_launches();
+void count_launch();
+
 // Storage kinds of an embedding table / source of the normalised row.
 enum SrcKind : int { SRC_F32 = 0, SRC_BF16 = 1, SRC_Q8 = 2, SRC_X = 3 };
 

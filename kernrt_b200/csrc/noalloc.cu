@@ -96,6 +96,7 @@ extern "C" int kernrt_cuda_embed_rows_noalloc(int device, int kind, const void *
         e = cudaMemcpyAsync(tok, tokens, n * sizeof(int32_t), cudaMemcpyHostToDevice, s);
         if (e == cudaSuccess) {
             k_row_offsets<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(off, (int)n, (int64_t)dim);
+            krt::count_launch();
             e = cudaGetLastError();
         }
         if (e == cudaSuccess) {
