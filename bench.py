@@ -67,14 +67,15 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic():
-    """Per-launch DRAM bytes of the chain kernel from the committed ncu summary
-    (profiles/k_chain_smollm2-1.7b_traffic.json), scaled to this rank's rows."""
-    path = os.path.join(ROOT, "profiles", "k_chain_smollm2-1.7b_traffic.json")
+def profile_traffic(kernel: str):
+    """DRAM bytes per row that ncu measured for `kernel` on a smaller capture of
+    this workload (profiles/chain_smollm2-1.7b_traffic.json); traffic grows in
+    proportion to rows, so it scales to this rank's launch by rows."""
+    path = os.path.join(ROOT, "profiles", "chain_smollm2-1.7b_traffic.json")
     try:
         with open(path) as fh:
             d = json.load(fh)
-        return float(d["dram_bytes_per_row"])
+        return float(d["kernels"][kernel]["dram_bytes_per_row"])
     except Exception:
         return None
 
@@ -319,6 +320,7 @@ def run_kernrt(args, rank, world, local):
           for _ in range(args.steps)]
     t_region = time.perf_counter()
     launches0 = kernrt_b200.kernel_launches()
+    b.stage_timing(True)
     with ClockSampler(local) as clk:
         for s, e in ev:
             restore_gate()
@@ -329,14 +331,22 @@ def run_kernrt(args, rank, world, local):
     torch.cuda.synchronize()
     region_s = time.perf_counter() - t_region
     launches = kernrt_b200.kernel_launches() - launches0
+    stages = b.stage_times()
+    b.stage_timing(False)
     per_launch = [s.elapsed_time(e) for s, e in ev]  # ms
     total_ms = max_over_ranks(sum(per_launch))
     value = total_rows * args.steps / (total_ms / 1000.0)
-    avg_launch_s = statistics.mean(per_launch) / 1000.0
     bpr = WL.bytes_per_row()
-    achieved = bpr * R / avg_launch_s / 1e9
     peak, peak_kind = peaks()
-    tpr = profile_traffic()
+    # The roofline is the dominant kernel's: its algorithmic bytes per launch
+    # over its own mean launch time, from the backend's stage events.
+    stage_bytes = WL.stage_bytes_per_row()
+    dominant = max((k for k in stages if stages[k][1] > 0), key=lambda k: stages[k][0])
+    dom_ms, dom_n = stages[dominant]
+    dom_bytes = stage_bytes.get(dominant, bpr) * R
+    achieved = dom_bytes / (dom_ms / dom_n / 1000.0) / 1e9
+    tpr = profile_traffic(dominant)
+    step_achieved = bpr * R / (statistics.mean(per_launch) / 1000.0) / 1e9
 
     # ---- end to end through the C ABI with pinned host buffers
     e2e = None
@@ -399,12 +409,18 @@ def run_kernrt(args, rank, world, local):
                        "timing": "CUDA events around each step's launch(es); gate restored from a "
                                  "pristine device copy before each step, outside the events",
                        "region_wall_s_incl_restores": region_s},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind,
+            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
+                         "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": None if tpr is None else tpr * R,
-                         "algorithmic_bytes_per_launch": bpr * R,
-                         "bytes_per_row": bpr, "launch_ms_mean": statistics.mean(per_launch),
-                         "launch_ms_min": min(per_launch)},
+                         "algorithmic_bytes_per_launch": dom_bytes,
+                         "launch_ms_mean": dom_ms / dom_n,
+                         "stages": {k: {"ms_per_launch": v[0] / v[1], "launches": v[1],
+                                        "algorithmic_bytes_per_launch": stage_bytes.get(k, 0) * R,
+                                        "achieved_gbs": stage_bytes.get(k, 0) * R / (v[0] / v[1] / 1000.0) / 1e9}
+                                    for k, v in stages.items() if v[1] > 0},
+                         "step": {"bytes_per_row": bpr, "ms_mean": statistics.mean(per_launch),
+                                  "ms_min": min(per_launch), "achieved_gbs": step_achieved,
+                                  "frac": step_achieved / peak}},
             "e2e": e2e,
             "cpu_baseline": cpu,
             "clocks": clocks,

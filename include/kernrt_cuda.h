@@ -197,6 +197,16 @@ int kernrt_cuda_rope_prepare(kernrt_cuda_ctx *ctx, float theta, size_t head_size
 
 int kernrt_cuda_layer_chain(kernrt_cuda_ctx *ctx, const kernrt_chain_args *args);
 
+/* Stage timing (off by default): while enabled, every chain launch
+ * (kernrt_cuda_rms_norm, _rms_norm_q8_0, _layer_chain) records a CUDA event
+ * around each kernel it issues.  kernrt_cuda_stage_times completes pending
+ * work and returns, per stage, the device milliseconds and launch count since
+ * timing was enabled: [0] the norm pipeline (k_norm_pipe), [1] the RoPE/SwiGLU
+ * stream (k_stream), [2] the single fused kernel (k_chain).  Enabling clears
+ * the record. */
+int kernrt_cuda_stage_timing(kernrt_cuda_ctx *ctx, int enable);
+int kernrt_cuda_stage_times(kernrt_cuda_ctx *ctx, double ms[3], uint64_t launches[3]);
+
 /* The LFM2 short-conv block's row ops in one launch (lfm2.rs:584-624):
  * h = B*x; co = conv_prefill(h); ring <- last min(rows,k-1) rows of h;
  * cy = C*co, with bcx = [B | C | x] thirds per row (lfm2.rs:9-15). */

@@ -95,6 +95,8 @@ SIGNATURES = {
     "kernrt_cuda_rope_prepare": (C.c_int, [P, C.c_float, SZ, SZ]),
     "kernrt_cuda_layer_chain": (C.c_int, [P, C.POINTER(ChainArgs)]),
     "kernrt_cuda_lfm2_conv_block": (C.c_int, [P, Buf, Buf, Buf, Buf, SZ, SZ, SZ]),
+    "kernrt_cuda_stage_timing": (C.c_int, [P, C.c_int]),
+    "kernrt_cuda_stage_times": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "kernrt_cuda_embed_rows_noalloc": (C.c_int, [C.c_int, C.c_int, P, P, SZ, SZ, P, SZ, P, P]),
 }
 
@@ -302,6 +304,18 @@ class CudaBackend:
         if unknown:
             raise TypeError(f"unknown chain arguments {sorted(unknown)}")
         _ok(self._lib.kernrt_cuda_layer_chain(self._ctx, C.byref(a)))
+
+    STAGES = ("k_norm_pipe", "k_stream", "k_chain")
+
+    def stage_timing(self, enable: bool) -> None:
+        _ok(self._lib.kernrt_cuda_stage_timing(self._ctx, int(bool(enable))))
+
+    def stage_times(self) -> dict:
+        """{kernel: (total device ms, launches)} since stage timing was enabled."""
+        ms = (C.c_double * 3)()
+        n = (C.c_uint64 * 3)()
+        _ok(self._lib.kernrt_cuda_stage_times(self._ctx, ms, n))
+        return {k: (ms[i], n[i]) for i, k in enumerate(self.STAGES)}
 
     def lfm2_conv_block(self, bcx: int, kernel: int, ring: int, cy: int, rows: int, dim: int,
                         k: int) -> None:

@@ -74,6 +74,7 @@ public:
         cudaFreeHost(h_err_);
         cudaFreeHost(stage_host_);
         cudaFree(stage_dev_);
+        for (auto e : events_) cudaEventDestroy(e);
         cudaStreamDestroy(stream_);
     }
 
@@ -239,7 +240,7 @@ public:
         a.x_in = f(xi);
         a.xb = f(o);
         a.w_att = f(w);
-        launch_or_fail(launch_chain(SRC_X, a, stream_), "rms_norm");
+        launch_or_fail(chain_launch(SRC_X, a), "rms_norm");
     }
 
     void qk_norm(kernrt_buf v, size_t rows, size_t width, size_t head, kernrt_buf weight, float eps) {
@@ -383,7 +384,7 @@ public:
         a.final_eps = eps;
         a.x_in = f(xb);
         a.w_final = f(w);
-        launch_or_fail(launch_chain(SRC_X, a, stream_), "rms_norm_q8_0");
+        launch_or_fail(chain_launch(SRC_X, a), "rms_norm_q8_0");
     }
 
     // ---- fused chains -------------------------------------------------------------
@@ -472,7 +473,7 @@ public:
             q8_outputs(rows, dim, c.codes, c.scales, c.scales_f16, &a.codes, &a.scales, &a.scales16);
         }
         flush();
-        launch_or_fail(launch_chain(src, a, stream_), "layer_chain");
+        launch_or_fail(chain_launch(src, a), "layer_chain");
     }
 
     void lfm2_conv_block(kernrt_buf bcx, kernrt_buf kernel, kernrt_buf ring, kernrt_buf cy, size_t rows,
@@ -488,6 +489,32 @@ public:
         launch_or_fail(launch_lfm2_conv_block(f(buf(bcx)), f(buf(kernel)), f(buf(ring)), f(buf(cy)), (int)rows,
                                               (int)dim, (int)k, stream_),
                        "lfm2_conv_block");
+    }
+
+    // ---- stage timing: CUDA events around each kernel of a chain launch --------
+    void stage_timing(bool on) {
+        flush();
+        check(cudaStreamSynchronize(stream_), "synchronize");
+        timing_ = on;
+        marks_.clear();
+        used_events_ = 0;
+    }
+
+    // Per stage: total device milliseconds and launch count since timing began.
+    void stage_times(double *ms, uint64_t *launches) {
+        barrier();
+        for (int i = 0; i < STAGE_COUNT; ++i) {
+            ms[i] = 0.0;
+            launches[i] = 0;
+        }
+        for (size_t i = 0; i + 1 < marks_.size(); ++i) {
+            const int st = marks_[i].stage;
+            if (st < 0 || st >= STAGE_COUNT) continue;
+            float t = 0.0f;
+            check(cudaEventElapsedTime(&t, marks_[i].ev, marks_[i + 1].ev), "cudaEventElapsedTime");
+            ms[st] += t;
+            launches[st] += 1;
+        }
     }
 
     // Launch all pending embeds (one gather per run of calls into one buffer).
@@ -643,6 +670,31 @@ private:
         stage_head_ = 0;
     }
 
+    struct Mark {
+        int stage;
+        cudaEvent_t ev;
+    };
+    static void on_stage(void *self, int stage) {
+        auto *b = static_cast<Backend *>(self);
+        if (b->used_events_ == b->events_.size()) {
+            cudaEvent_t e = nullptr;
+            check(cudaEventCreate(&e), "cudaEventCreate");
+            b->events_.push_back(e);
+        }
+        cudaEvent_t e = b->events_[b->used_events_++];
+        check(cudaEventRecord(e, b->stream_), "cudaEventRecord");
+        b->marks_.push_back({stage, e});
+    }
+    cudaError_t chain_launch(int src, const ChainArgs &a) {
+        if (!timing_) return launch_chain(src, a, stream_);
+        const LaunchHook hook{&Backend::on_stage, this};
+        return launch_chain(src, a, stream_, &hook);
+    }
+
+    bool timing_ = false;
+    std::vector<cudaEvent_t> events_;
+    size_t used_events_ = 0;
+    std::vector<Mark> marks_;
     int device_;
     cudaStream_t stream_ = nullptr;
     std::vector<Buffer> bufs_;
@@ -884,6 +936,17 @@ int kernrt_cuda_layer_chain(kernrt_cuda_ctx *ctx, const kernrt_chain_args *args)
     return guard(ctx, [&](krt::Backend &b) {
         if (!args) krt::fail(KERNRT_E_INVALID, "null chain arguments");
         b.layer_chain(*args);
+    });
+}
+
+int kernrt_cuda_stage_timing(kernrt_cuda_ctx *ctx, int enable) {
+    return guard(ctx, [&](krt::Backend &b) { b.stage_timing(enable != 0); });
+}
+
+int kernrt_cuda_stage_times(kernrt_cuda_ctx *ctx, double *ms, uint64_t *launches) {
+    return guard(ctx, [&](krt::Backend &b) {
+        if (!ms || !launches) krt::fail(KERNRT_E_INVALID, "null output pointer");
+        b.stage_times(ms, launches);
     });
 }
 

@@ -1171,17 +1171,30 @@ cudaError_t launch_chain_src_fused(const ChainArgs &a, cudaStream_t s);
 // independent RoPE/SwiGLU streams at full occupancy.  The stages share no
 // data, so splitting them moves no extra bytes; it lets each run at the
 // occupancy its resources allow.  Other chains run as the one fused kernel.
+inline void mark(const LaunchHook *hook, int stage) {
+    if (hook && hook->fn) hook->fn(hook->user, stage);
+}
+
 template <int SRC>
-cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s) {
+cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHook *hook) {
     const bool vec = (a.dim % 8) == 0 && (SRC != SRC_Q8 || a.dim % 32 == 0);
     const bool streams_vec = ((a.half | a.q_dim | a.kv_dim | a.hidden) & 3) == 0;
     const bool split = a.w_final == nullptr && a.w_q == nullptr && a.w_k == nullptr && a.rope_mode != 2 &&
                        (streams_vec || (a.q == nullptr && a.k == nullptr && a.gate == nullptr));
-    if (!split) return launch_chain_src_fused<SRC>(a, s);
+    if (!split) {
+        mark(hook, STAGE_FUSED);
+        const cudaError_t e = launch_chain_src_fused<SRC>(a, s);
+        mark(hook, STAGE_END);
+        return e;
+    }
     cudaError_t e = cudaSuccess;
-    if (a.xb || a.x_out) e = vec ? launch_norm_pipe<SRC, true>(a, s) : launch_norm_pipe<SRC, false>(a, s);
+    if (a.xb || a.x_out) {
+        mark(hook, STAGE_NORM);
+        e = vec ? launch_norm_pipe<SRC, true>(a, s) : launch_norm_pipe<SRC, false>(a, s);
+    }
     if (e != cudaSuccess) return e;
     if ((a.rope_mode == 1 && (a.q || a.k)) || a.gate) {
+        mark(hook, STAGE_STREAM);
         static unsigned grid[64] = {0};
         int dev = 0;
         cudaGetDevice(&dev);
@@ -1194,6 +1207,7 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s) {
         k_stream<2><<<grid[dev], kThreads, 0, s>>>(a);
         e = launched();
     }
+    mark(hook, STAGE_END);
     return e;
 }
 
@@ -1237,13 +1251,13 @@ size_t chain_smem_bytes(int src, const ChainArgs &a, int rows_per_cta) {
     }
 }
 
-cudaError_t launch_chain(int src, const ChainArgs &a, cudaStream_t s) {
+cudaError_t launch_chain(int src, const ChainArgs &a, cudaStream_t s, const LaunchHook *hook) {
     if (a.rows <= 0) return cudaSuccess;
     switch (src) {
-    case SRC_BF16: return launch_chain_src<SRC_BF16>(a, s);
-    case SRC_Q8: return launch_chain_src<SRC_Q8>(a, s);
-    case SRC_F32: return launch_chain_src<SRC_F32>(a, s);
-    default: return launch_chain_src<SRC_X>(a, s);
+    case SRC_BF16: return launch_chain_src<SRC_BF16>(a, s, hook);
+    case SRC_Q8: return launch_chain_src<SRC_Q8>(a, s, hook);
+    case SRC_F32: return launch_chain_src<SRC_F32>(a, s, hook);
+    default: return launch_chain_src<SRC_X>(a, s, hook);
     }
 }
 

@@ -48,8 +48,16 @@ struct ChainArgs {
     const float *w_final; int8_t *codes; float *scales; uint16_t *scales16;
     int *err;
 };
+// Optional callback around the kernels a chain launch issues: called with the
+// stage about to launch, and with STAGE_END after the last one (the backend
+// records CUDA events there when stage timing is on).
+enum : int { STAGE_NORM = 0, STAGE_STREAM = 1, STAGE_FUSED = 2, STAGE_COUNT = 3, STAGE_END = -1 };
+struct LaunchHook {
+    void (*fn)(void *user, int stage);
+    void *user;
+};
 // Chooses rows-per-CTA and shared memory, then launches.
-cudaError_t launch_chain(int src, const ChainArgs &a, cudaStream_t s);
+cudaError_t launch_chain(int src, const ChainArgs &a, cudaStream_t s, const LaunchHook *hook = nullptr);
 // Shared memory a chain launch would need for one row group (to report limits).
 size_t chain_smem_bytes(int src, const ChainArgs &a, int rows_per_cta);
 

@@ -67,6 +67,13 @@ class Workload:
             b += 32 * nb + 4 * nb                 # codes + f32 scales
         return b
 
+    def stage_bytes_per_row(self) -> dict:
+        """The same compulsory bytes split by the kernel that moves them when
+        the chain runs as the norm pipeline plus the RoPE/SwiGLU stream."""
+        f = 4
+        stream = 2 * f * self.q_dim + 2 * f * self.kv_dim + 3 * f * self.hidden
+        return {"k_norm_pipe": self.bytes_per_row() - stream, "k_stream": stream}
+
 
 SMOLLM2_135M = Workload("smollm2-135m-prefill128", 49152, 576, 9, 3, 64, 1536, 1e5, 1e-5, "bf16",
                         rows=128, seq_len=128)

@@ -258,3 +258,17 @@ def test_headline_workload_full_size_sampled(gpu, oracle):
                         k=before["k"], gate=before["gate"], up=before["up"], resid=before["resid"],
                         tokens=tokens[sample], table=(oracle.BF16, table, None, wl.vocab), threads=8)
     check(after, want, False)
+
+
+def test_stage_timing_records_each_kernel(gpu):
+    """kernrt_cuda_stage_timing/_stage_times: the Llama chain issues the norm
+    pipeline and the RoPE/SwiGLU stream; each is timed once per launch."""
+    wl = W.Workload("tiny", 64, 256, 4, 4, 64, 512, 1e4, 1e-5, "bf16", rows=300, seq_len=300)
+    d = make_inputs(wl, 1006)
+    gpu.stage_timing(True)
+    gpu_chain(gpu, wl, d)
+    gpu_chain(gpu, wl, d)
+    t = gpu.stage_times()
+    gpu.stage_timing(False)
+    assert t["k_norm_pipe"][1] == 2 and t["k_stream"][1] == 2 and t["k_chain"][1] == 0
+    assert t["k_norm_pipe"][0] > 0 and t["k_stream"][0] > 0
