@@ -367,11 +367,15 @@ def run_kernrt(args, rank, world, local):
         d2h = sum(t.numel() * t.element_size() for t in host_out.values())
 
         def e2e_step():
-            for n, t in host_in.items():
-                b.write_ptr(h[n], t.data_ptr(), t.numel() * t.element_size())
-            b.layer_chain(**chain)
-            for n, t in host_out.items():
-                b.read_ptr(h[n], t.data_ptr(), t.numel() * t.element_size())
+            b.layer_chain_host(rows=R, dim=H, q_dim=Q, kv_dim=KV, hidden=I, head_size=WL.head,
+                               eps=WL.eps, theta=WL.theta,
+                               tokens=host_in["tokens"].data_ptr(), positions=host_in["positions"].data_ptr(),
+                               q_in=host_in["q"].data_ptr(), k_in=host_in["k"].data_ptr(),
+                               gate_in=host_in["gate"].data_ptr(), up=host_in["up"].data_ptr(),
+                               resid=host_in["resid"].data_ptr(), x_out=host_out["x"].data_ptr(),
+                               xb_out=host_out["xb"].data_ptr(), q_out=host_out["q"].data_ptr(),
+                               k_out=host_out["k"].data_ptr(), gate_out=host_out["gate"].data_ptr(),
+                               w_att=h["w_att"])
 
         e2e_step()
         barrier()
@@ -382,8 +386,8 @@ def run_kernrt(args, rank, world, local):
         e2e = {"value": total_rows * args.e2e_steps / e2e_s, "unit": UNIT,
                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
                "steps": args.e2e_steps,
-               "path": "kernrt_cuda_write_bytes (pinned) -> kernrt_cuda_layer_chain -> "
-                       "kernrt_cuda_read_bytes"}
+               "path": "kernrt_cuda_layer_chain_host on page-locked host buffers (row chunks; "
+                       "H2D, kernels and D2H overlapped on three streams)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

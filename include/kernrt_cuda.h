@@ -197,6 +197,39 @@ int kernrt_cuda_rope_prepare(kernrt_cuda_ctx *ctx, float theta, size_t head_size
 
 int kernrt_cuda_layer_chain(kernrt_cuda_ctx *ctx, const kernrt_chain_args *args);
 
+/* The same chain on HOST buffers, for callers whose rows live in host memory:
+ * the rows are processed in chunks of `chunk_rows` (0 = chosen by the
+ * backend), each chunk's inputs copied to the device, run through the chain,
+ * and its outputs copied back, with the copies in both directions and the
+ * kernels of neighbouring chunks overlapping on three streams.  Returns when
+ * every output is in host memory.  Page-locked host buffers give the overlap;
+ * pageable ones still work, with the copies serialised.  Any input/output
+ * pointer may be NULL to skip that stage (as a 0 handle does in
+ * kernrt_chain_args); an output may alias its input (q_out == q_in, ...).
+ * Token ids and positions are checked on the host; the RoPE table is built
+ * or grown as needed.  Weights are device buffers (handles). */
+typedef struct {
+    size_t rows, dim, q_dim, kv_dim, hidden, head_size;
+    float eps, theta, final_eps;
+    int interleaved;
+    size_t chunk_rows;
+    const int32_t *tokens;     /* [rows], or NULL: then x_in is the input */
+    const int32_t *positions;  /* [rows] */
+    const float *x_in;         /* [rows, dim] when tokens == NULL */
+    const float *q_in, *k_in;  /* [rows, q_dim], [rows, kv_dim] */
+    const float *gate_in, *up; /* [rows, hidden] */
+    const float *resid;        /* [rows, dim] */
+    float *x_out, *xb_out;     /* [rows, dim] */
+    float *q_out, *k_out;      /* [rows, q_dim], [rows, kv_dim] */
+    float *gate_out;           /* [rows, hidden] */
+    int8_t *codes;             /* [rows, ceil(dim/32)*32] when w_final */
+    float *scales;             /* [rows, ceil(dim/32)] when w_final */
+    uint16_t *scales_f16;      /* [rows, ceil(dim/32)] or NULL */
+    kernrt_buf w_att, w_q, w_k, w_final;
+} kernrt_chain_host_args;
+
+int kernrt_cuda_layer_chain_host(kernrt_cuda_ctx *ctx, const kernrt_chain_host_args *args);
+
 /* Stage timing (off by default): while enabled, every chain launch
  * (kernrt_cuda_rms_norm, _rms_norm_q8_0, _layer_chain) records a CUDA event
  * around each kernel it issues.  kernrt_cuda_stage_times completes pending

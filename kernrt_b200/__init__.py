@@ -61,6 +61,20 @@ class ChainArgs(C.Structure):
     ]
 
 
+class ChainHostArgs(C.Structure):
+    """Mirror of ``kernrt_chain_host_args`` (include/kernrt_cuda.h)."""
+
+    _fields_ = [
+        ("rows", SZ), ("dim", SZ), ("q_dim", SZ), ("kv_dim", SZ), ("hidden", SZ), ("head_size", SZ),
+        ("eps", C.c_float), ("theta", C.c_float), ("final_eps", C.c_float), ("interleaved", C.c_int),
+        ("chunk_rows", SZ),
+        ("tokens", P), ("positions", P), ("x_in", P), ("q_in", P), ("k_in", P), ("gate_in", P),
+        ("up", P), ("resid", P), ("x_out", P), ("xb_out", P), ("q_out", P), ("k_out", P),
+        ("gate_out", P), ("codes", P), ("scales", P), ("scales_f16", P),
+        ("w_att", Buf), ("w_q", Buf), ("w_k", Buf), ("w_final", Buf),
+    ]
+
+
 # Every function include/kernrt_cuda.h declares, with its ctypes signature.
 SIGNATURES = {
     "kernrt_cuda_last_error": (C.c_char_p, []),
@@ -95,6 +109,7 @@ SIGNATURES = {
     "kernrt_cuda_rope_prepare": (C.c_int, [P, C.c_float, SZ, SZ]),
     "kernrt_cuda_layer_chain": (C.c_int, [P, C.POINTER(ChainArgs)]),
     "kernrt_cuda_lfm2_conv_block": (C.c_int, [P, Buf, Buf, Buf, Buf, SZ, SZ, SZ]),
+    "kernrt_cuda_layer_chain_host": (C.c_int, [P, C.POINTER(ChainHostArgs)]),
     "kernrt_cuda_stage_timing": (C.c_int, [P, C.c_int]),
     "kernrt_cuda_stage_times": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "kernrt_cuda_embed_rows_noalloc": (C.c_int, [C.c_int, C.c_int, P, P, SZ, SZ, P, SZ, P, P]),
@@ -304,6 +319,26 @@ class CudaBackend:
         if unknown:
             raise TypeError(f"unknown chain arguments {sorted(unknown)}")
         _ok(self._lib.kernrt_cuda_layer_chain(self._ctx, C.byref(a)))
+
+    def layer_chain_host(self, **kw) -> None:
+        """kernrt_cuda_layer_chain_host: host arrays (numpy, or integer host
+        addresses) for the row inputs/outputs, handles for the weights."""
+        a = ChainHostArgs()
+        names = {n for n, _ in ChainHostArgs._fields_}
+        unknown = set(kw) - names
+        if unknown:
+            raise TypeError(f"unknown chain arguments {sorted(unknown)}")
+        keep = []
+        for name, ctype in ChainHostArgs._fields_:
+            v = kw.get(name)
+            if v is None:
+                continue
+            if ctype is P and isinstance(v, np.ndarray):
+                assert v.flags["C_CONTIGUOUS"]
+                keep.append(v)
+                v = v.ctypes.data
+            setattr(a, name, v)
+        _ok(self._lib.kernrt_cuda_layer_chain_host(self._ctx, C.byref(a)))
 
     STAGES = ("k_norm_pipe", "k_stream", "k_chain")
 

@@ -58,6 +58,11 @@ public:
         check(cudaMemsetAsync(d_err_, 0, sizeof(int), stream_), "cudaMemset");
         check(cudaMallocHost(&h_err_, sizeof(int)), "cudaMallocHost");
         grow_staging(1 << 20);
+        check(cudaStreamCreateWithFlags(&h2d_, cudaStreamNonBlocking), "cudaStreamCreate");
+        check(cudaStreamCreateWithFlags(&d2h_, cudaStreamNonBlocking), "cudaStreamCreate");
+        for (auto &set : sets_)
+            for (cudaEvent_t *e : {&set.h2d_done, &set.comp_done, &set.d2h_done})
+                check(cudaEventCreateWithFlags(e, cudaEventDisableTiming), "cudaEventCreate");
     }
 
     ~Backend() {
@@ -75,6 +80,16 @@ public:
         cudaFreeHost(stage_host_);
         cudaFree(stage_dev_);
         for (auto e : events_) cudaEventDestroy(e);
+        cudaStreamSynchronize(h2d_);
+        cudaStreamSynchronize(d2h_);
+        for (auto &set : sets_) {
+            cudaFree(set.arena);
+            cudaEventDestroy(set.h2d_done);
+            cudaEventDestroy(set.comp_done);
+            cudaEventDestroy(set.d2h_done);
+        }
+        cudaStreamDestroy(h2d_);
+        cudaStreamDestroy(d2h_);
         cudaStreamDestroy(stream_);
     }
 
@@ -491,6 +506,190 @@ public:
                        "lfm2_conv_block");
     }
 
+    // ---- the chain on host buffers, pipelined over row chunks --------------------
+    // Chunk i uses device buffer set i % 3: its inputs go up on h2d_, the chain
+    // runs on stream_, its outputs come back on d2h_, each step waiting on the
+    // previous one's event for that set; a set is refilled only after its last
+    // outputs left (h2d_ waits on d2h_done).  So the copies of chunk i+1 and
+    // i-1 overlap the kernels of chunk i.
+    void layer_chain_host(const kernrt_chain_host_args &h) {
+        const size_t rows = h.rows, dim = h.dim;
+        if (rows == 0) return;
+        if (dim == 0) fail(KERNRT_E_INVALID, "chain dim must be positive");
+        fits_int(rows * std::max({dim, h.q_dim, h.kv_dim, h.hidden}), "layer_chain_host");
+        const bool has_q = h.q_in != nullptr, has_k = h.k_in != nullptr, has_g = h.gate_in != nullptr;
+        if ((has_q && !h.q_out) || (has_k && !h.k_out) || (has_g && (!h.gate_out || !h.up)))
+            fail(KERNRT_E_INVALID, "every streamed input needs its output (and gate needs up)");
+        if (!h.tokens && !h.x_in) fail(KERNRT_E_INVALID, "chain needs token ids or x");
+        if (!h.w_att) fail(KERNRT_E_INVALID, "chain needs w_att");
+        span(buf(h.w_att), 0, dim, "chain w_att");
+        const size_t head = h.head_size;
+        if (has_q || has_k || h.w_q || h.w_k) {
+            if (head == 0 || head % 2) fail(KERNRT_E_INVALID, "head_size must be a positive even number");
+            if (h.interleaved && h.kv_dim % 2) fail(KERNRT_E_INVALID, "interleaved RoPE needs an even kv width");
+        }
+        if (h.w_q) span(buf(h.w_q), 0, head, "chain w_q");
+        if (h.w_k) span(buf(h.w_k), 0, head, "chain w_k");
+        if (h.w_final) {
+            span(buf(h.w_final), 0, dim, "chain w_final");
+            if (!h.codes || !h.scales) fail(KERNRT_E_INVALID, "the final Q8_0 stage needs codes and scales");
+        }
+        if (h.tokens) {
+            if (emb_kind_ < 0) fail(KERNRT_E_STATE, "prepare() runs before compute");
+            if (dim != dim_) fail(KERNRT_E_INVALID, "chain dim differs from the embedding width");
+            for (size_t r = 0; r < rows; ++r)
+                if (h.tokens[r] < 0 || (size_t)h.tokens[r] >= vocab_)
+                    fail(KERNRT_E_INVALID, "token " + std::to_string(h.tokens[r]) + " at row " + std::to_string(r) +
+                                               " out of range for vocab " + std::to_string(vocab_));
+        }
+        const RopeTable *table = nullptr;
+        if (has_q || has_k) {
+            if (!h.positions) fail(KERNRT_E_INVALID, "null positions");
+            int32_t maxp = 0;
+            for (size_t r = 0; r < rows; ++r) {
+                if (h.positions[r] < 0) fail(KERNRT_E_INVALID, "negative position");
+                maxp = std::max(maxp, h.positions[r]);
+            }
+            flush();
+            table = &rope_table(h.theta, head, (size_t)maxp + 1);
+        }
+        flush();
+
+        // Per-row bytes of every buffer a set holds, and the chunk size.
+        const size_t nb = (dim + 31) / 32;
+        struct Part { size_t per_row; size_t off; };
+        Part p_tok{h.tokens ? 4u : 0u, 0}, p_pos{(has_q || has_k) ? 4u : 0u, 0}, p_x{4 * dim, 0}, p_xb{h.xb_out ? 4 * dim : 0, 0},
+            p_q{has_q ? 4 * h.q_dim : 0, 0}, p_k{has_k ? 4 * h.kv_dim : 0, 0}, p_g{has_g ? 4 * h.hidden : 0, 0},
+            p_u{has_g ? 4 * h.hidden : 0, 0}, p_r{h.resid ? 4 * dim : 0, 0}, p_c{h.w_final ? 32 * nb : 0, 0},
+            p_s{h.w_final ? 4 * nb : 0, 0}, p_h{(h.w_final && h.scales_f16) ? 2 * nb : 0, 0};
+        Part *parts[] = {&p_tok, &p_pos, &p_x, &p_xb, &p_q, &p_k, &p_g, &p_u, &p_r, &p_c, &p_s, &p_h};
+        size_t row_bytes = 0;
+        for (Part *pt : parts) row_bytes += pt->per_row;
+        size_t C = h.chunk_rows;
+        if (C == 0) C = std::max<size_t>(1, (64u << 20) / std::max<size_t>(row_bytes, 1));
+        C = std::min(C, rows);
+        size_t arena = 0;
+        for (Part *pt : parts) {
+            pt->off = arena;
+            arena += (pt->per_row * C + 255) & ~(size_t)255;
+        }
+        for (auto &set : sets_) {
+            if (set.bytes < arena) {
+                check(cudaStreamSynchronize(stream_), "synchronize");
+                cudaFree(set.arena);
+                set.arena = nullptr;
+                set.bytes = 0;
+                check(cudaMalloc(&set.arena, arena), "cudaMalloc(host pipeline)");
+                set.bytes = arena;
+            }
+            set.used = false;
+        }
+
+        // The copy streams start after everything already queued on stream_.
+        check(cudaEventRecord(sets_[0].comp_done, stream_), "cudaEventRecord");
+        check(cudaStreamWaitEvent(h2d_, sets_[0].comp_done, 0), "cudaStreamWaitEvent");
+        try {
+            for (size_t i = 0, c0 = 0; c0 < rows; ++i, c0 += C) {
+                const size_t n = std::min(C, rows - c0);
+                PipeSet &S = sets_[i % 3];
+                char *A = static_cast<char *>(S.arena);
+                auto dev = [&](const Part &pt) { return pt.per_row ? A + pt.off : nullptr; };
+                auto up_rows = [&](const Part &pt, const void *host) {
+                    if (pt.per_row && host)
+                        check(cudaMemcpyAsync(A + pt.off, static_cast<const char *>(host) + c0 * pt.per_row,
+                                              n * pt.per_row, cudaMemcpyHostToDevice, h2d_),
+                              "cudaMemcpyAsync(h2d)");
+                };
+                auto down_rows = [&](const Part &pt, void *host) {
+                    if (pt.per_row && host)
+                        check(cudaMemcpyAsync(static_cast<char *>(host) + c0 * pt.per_row, A + pt.off,
+                                              n * pt.per_row, cudaMemcpyDeviceToHost, d2h_),
+                              "cudaMemcpyAsync(d2h)");
+                };
+                if (S.used) check(cudaStreamWaitEvent(h2d_, S.d2h_done, 0), "cudaStreamWaitEvent");
+                up_rows(p_tok, h.tokens);
+                up_rows(p_pos, h.positions);
+                if (!h.tokens) up_rows(p_x, h.x_in);
+                up_rows(p_q, h.q_in);
+                up_rows(p_k, h.k_in);
+                up_rows(p_g, h.gate_in);
+                up_rows(p_u, h.up);
+                up_rows(p_r, h.resid);
+                check(cudaEventRecord(S.h2d_done, h2d_), "cudaEventRecord");
+
+                check(cudaStreamWaitEvent(stream_, S.h2d_done, 0), "cudaStreamWaitEvent");
+                ChainArgs a = blank(n, dim);
+                a.eps = h.eps;
+                a.final_eps = h.final_eps;
+                int src = SRC_X;
+                if (h.tokens) {
+                    src = emb_src_;
+                    a.table = emb_data_;
+                    a.tscales = emb_scales_;
+                    a.vocab = (int)vocab_;
+                    a.tokens = reinterpret_cast<const int32_t *>(dev(p_tok));
+                    a.x_out = reinterpret_cast<float *>(dev(p_x));
+                } else {
+                    a.x_in = reinterpret_cast<const float *>(dev(p_x));
+                    if (h.resid) a.x_out = reinterpret_cast<float *>(dev(p_x));
+                }
+                a.w_att = f(buf(h.w_att));
+                a.xb = reinterpret_cast<float *>(dev(p_xb));
+                a.resid = reinterpret_cast<const float *>(dev(p_r));
+                if (has_q || has_k || h.w_q || h.w_k) {
+                    a.head = (int)head;
+                    a.half = (int)(head / 2);
+                    a.q_dim = (int)h.q_dim;
+                    a.kv_dim = (int)h.kv_dim;
+                    a.q = reinterpret_cast<float *>(dev(p_q));
+                    a.k = reinterpret_cast<float *>(dev(p_k));
+                    a.w_q = h.w_q ? f(buf(h.w_q)) : nullptr;
+                    a.w_k = h.w_k ? f(buf(h.w_k)) : nullptr;
+                    if (table) {
+                        a.pos = reinterpret_cast<const int32_t *>(dev(p_pos));
+                        a.cos_t = table->cos;
+                        a.sin_t = table->sin;
+                        a.max_pos = (int)table->max_pos;
+                        a.rope_mode = h.interleaved ? 2 : 1;
+                    }
+                }
+                if (has_g) {
+                    a.gate = reinterpret_cast<float *>(dev(p_g));
+                    a.up = reinterpret_cast<const float *>(dev(p_u));
+                    a.hidden = (int)h.hidden;
+                }
+                if (h.w_final) {
+                    a.w_final = f(buf(h.w_final));
+                    a.codes = reinterpret_cast<int8_t *>(dev(p_c));
+                    a.scales = reinterpret_cast<float *>(dev(p_s));
+                    a.scales16 = reinterpret_cast<uint16_t *>(dev(p_h));
+                }
+                launch_or_fail(chain_launch(src, a), "layer_chain_host");
+                check(cudaEventRecord(S.comp_done, stream_), "cudaEventRecord");
+
+                check(cudaStreamWaitEvent(d2h_, S.comp_done, 0), "cudaStreamWaitEvent");
+                down_rows(p_x, h.x_out);
+                down_rows(p_xb, h.xb_out);
+                down_rows(p_q, h.q_out);
+                down_rows(p_k, h.k_out);
+                down_rows(p_g, h.gate_out);
+                down_rows(p_c, h.codes);
+                down_rows(p_s, h.scales);
+                down_rows(p_h, h.scales_f16);
+                check(cudaEventRecord(S.d2h_done, d2h_), "cudaEventRecord");
+                S.used = true;
+            }
+        } catch (...) {
+            cudaStreamSynchronize(h2d_);
+            cudaStreamSynchronize(stream_);
+            cudaStreamSynchronize(d2h_);
+            throw;
+        }
+        check(cudaStreamSynchronize(h2d_), "synchronize");
+        check(cudaStreamSynchronize(d2h_), "synchronize");
+        barrier();
+    }
+
     // ---- stage timing: CUDA events around each kernel of a chain launch --------
     void stage_timing(bool on) {
         flush();
@@ -690,6 +889,15 @@ private:
         const LaunchHook hook{&Backend::on_stage, this};
         return launch_chain(src, a, stream_, &hook);
     }
+
+    struct PipeSet {
+        void *arena = nullptr;
+        size_t bytes = 0;
+        bool used = false;
+        cudaEvent_t h2d_done = nullptr, comp_done = nullptr, d2h_done = nullptr;
+    };
+    PipeSet sets_[3];
+    cudaStream_t h2d_ = nullptr, d2h_ = nullptr;
 
     bool timing_ = false;
     std::vector<cudaEvent_t> events_;
@@ -936,6 +1144,13 @@ int kernrt_cuda_layer_chain(kernrt_cuda_ctx *ctx, const kernrt_chain_args *args)
     return guard(ctx, [&](krt::Backend &b) {
         if (!args) krt::fail(KERNRT_E_INVALID, "null chain arguments");
         b.layer_chain(*args);
+    });
+}
+
+int kernrt_cuda_layer_chain_host(kernrt_cuda_ctx *ctx, const kernrt_chain_host_args *args) {
+    return guard(ctx, [&](krt::Backend &b) {
+        if (!args) krt::fail(KERNRT_E_INVALID, "null chain arguments");
+        b.layer_chain_host(*args);
     });
 }
 

@@ -272,3 +272,44 @@ def test_stage_timing_records_each_kernel(gpu):
     gpu.stage_timing(False)
     assert t["k_norm_pipe"][1] == 2 and t["k_stream"][1] == 2 and t["k_chain"][1] == 0
     assert t["k_norm_pipe"][0] > 0 and t["k_stream"][0] > 0
+
+
+@pytest.mark.parametrize("wl,chunk", [(W.SMOLLM2_135M, 37), (W.QWEN3_06B_Q8, 0), (W.LFM2_700M, 100),
+                                      (W.SMOLLM2_17B_PREFILL, 64)], ids=lambda v: str(getattr(v, "name", v)))
+def test_chain_on_host_buffers_matches_oracle(gpu, oracle, wl, chunk):
+    """kernrt_cuda_layer_chain_host: the same chain on host arrays, pipelined in
+    row chunks (outputs written over their inputs here, which is allowed)."""
+    d = make_inputs(wl, 1010)
+    rows, nb = wl.rows, (wl.dim + 31) // 32
+    if wl.storage == "bf16":
+        gpu.prepare_embedding(kernrt_b200.BF16, d["table"], None, d["vocab"], wl.dim)
+    elif wl.storage == "q8_0":
+        gpu.prepare_embedding(kernrt_b200.Q8_0, d["codes"], d["tscales"], d["vocab"], wl.dim)
+    w = {n: gpu.upload(d[n]) for n in ["w_att", "w_q", "w_k", "w_final"] if n in d}
+    q, k, gate = d["q"].copy(), d["k"].copy(), d["gate"].copy()
+    x_out = np.zeros((rows, wl.dim), f32)
+    xb_out = np.zeros((rows, wl.dim), f32)
+    codes = np.zeros((rows, nb * 32), np.int8) if wl.final_q8 else None
+    scales = np.zeros((rows, nb), f32) if wl.final_q8 else None
+    s16 = np.zeros((rows, nb), np.uint16) if wl.final_q8 else None
+    gpu.layer_chain_host(rows=rows, dim=wl.dim, q_dim=wl.q_dim, kv_dim=wl.kv_dim, hidden=wl.hidden,
+                         head_size=wl.head, eps=wl.eps, theta=wl.theta, final_eps=wl.eps, chunk_rows=chunk,
+                         tokens=d["tokens"] if wl.storage != "none" else None,
+                         positions=d["positions"], x_in=d.get("x"), q_in=q, k_in=k, gate_in=gate,
+                         up=d["up"], resid=d["resid"], x_out=x_out, xb_out=xb_out, q_out=q, k_out=k,
+                         gate_out=gate, codes=codes, scales=scales, scales_f16=s16, **w)
+    got = {"x": x_out, "xb": xb_out, "q": q, "k": k, "gate": gate, "codes": codes, "scales": scales,
+           "scales_f16": s16}
+    check(got, oracle_chain(oracle, wl, d), wl.final_q8)
+
+
+def test_chain_on_host_buffers_rejects_bad_token(gpu):
+    wl = W.Workload("tiny", 16, 64, 2, 2, 32, 64, 1e4, 1e-5, "bf16", rows=8, seq_len=8)
+    d = make_inputs(wl, 1011)
+    gpu.prepare_embedding(kernrt_b200.BF16, d["table"], None, 16, 64)
+    d["tokens"][5] = -1
+    out = np.zeros((8, 64), f32)
+    with pytest.raises(kernrt_b200.KernrtCudaError) as e:
+        gpu.layer_chain_host(rows=8, dim=64, eps=1e-5, tokens=d["tokens"], x_out=out,
+                             w_att=gpu.upload(d["w_att"]))
+    assert e.value.code == kernrt_b200.E_INVALID and "out of range" in str(e.value)
