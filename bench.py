@@ -261,6 +261,13 @@ def run_kernrt(args, rank, world, local):
         if dist is not None:
             dist.barrier()
 
+    def sum_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
     def max_over_ranks(v: float) -> float:
         if dist is None:
             return v
@@ -330,7 +337,7 @@ def run_kernrt(args, rank, world, local):
         b.synchronize()
     torch.cuda.synchronize()
     region_s = time.perf_counter() - t_region
-    launches = kernrt_b200.kernel_launches() - launches0
+    launches = int(sum_over_ranks(float(kernrt_b200.kernel_launches() - launches0)))
     stages = b.stage_times()
     b.stage_timing(False)
     per_launch = [s.elapsed_time(e) for s, e in ev]  # ms
