@@ -217,6 +217,7 @@ public:
         if (token >= vocab_) fail(KERNRT_E_INVALID, "token " + std::to_string(token) + " out of range for vocab " + std::to_string(vocab_));
         const Buffer &b = buf(out);
         if (offset > b.bytes / 4 || dim_ > b.bytes / 4 - offset) fail(KERNRT_E_INVALID, "embed writes past the end of the buffer");
+        flush_deferred();
         if (!pending_.empty() && pending_.back().out != out) flush();
         pending_.push_back({(int32_t)token, out, (int64_t)offset});
     }
@@ -248,6 +249,8 @@ public:
         span(o, 0, rows * dim, "rms_norm out");
         span(xi, 0, rows * dim, "rms_norm x");
         span(w, 0, dim, "rms_norm weight");
+        if (rows > 0 && dim > 0 && fuse_embed_rms(out, x, weight, rows, dim, eps)) return;
+        if (rows > 0 && dim > 0 && fuse_add_rms(out, x, weight, rows, dim, eps)) return;
         flush();
         if (rows == 0 || dim == 0) return;
         ChainArgs a = blank(rows, dim);
@@ -264,8 +267,23 @@ public:
         span(vb, 0, rows * width, "qk_norm v");
         span(w, 0, head, "qk_norm weight");
         fits_int(rows * width, "qk_norm");
+        // Deferred: a following rope over the same rows runs both in one pass.
+        if (pqk_.n == 1 && pqk_.rows == rows && pqk_.head == head && pqk_.eps == eps && pqk_.v[0] != v) {
+            pqk_.v[1] = v;
+            pqk_.width[1] = width;
+            pqk_.w[1] = weight;
+            pqk_.n = 2;
+            return;
+        }
         flush();
-        launch_or_fail(launch_qk_norm(f(vb), (int)rows, (int)width, (int)head, f(w), eps, stream_), "qk_norm");
+        pqk_ = PendQK{};
+        pqk_.n = 1;
+        pqk_.v[0] = v;
+        pqk_.width[0] = width;
+        pqk_.w[0] = weight;
+        pqk_.rows = rows;
+        pqk_.head = head;
+        pqk_.eps = eps;
     }
 
     void rope(kernrt_buf q, kernrt_buf k, size_t qw, size_t kvw, size_t rows, const uint64_t *positions,
@@ -278,8 +296,10 @@ public:
         span(qb, 0, rows * qw, "rope q");
         span(kb, 0, rows * kvw, "rope k");
         fits_int(rows * std::max(qw, kvw), "rope");
-        flush();
-        if (rows == 0) return;
+        if (rows == 0) {
+            flush();
+            return;
+        }
         if (!positions) fail(KERNRT_E_INVALID, "null positions");
         std::vector<int32_t> pos(rows);
         uint64_t maxp = 0;
@@ -289,7 +309,25 @@ public:
             maxp = std::max(maxp, positions[i]);
         }
         const RopeTable &t = rope_table(theta, head, (size_t)maxp + 1);
+        // A pending qk_norm of q and/or k over exactly these rows fuses in.
+        const float *wq = nullptr, *wk = nullptr;
+        bool fuse = pqk_.n > 0 && pqk_.rows == rows && pqk_.head == head;
+        for (int i = 0; fuse && i < pqk_.n; ++i) {
+            if (pqk_.v[i] == q && pqk_.width[i] == qw) wq = f(buf(pqk_.w[i]));
+            else if (pqk_.v[i] == k && pqk_.width[i] == kvw) wk = f(buf(pqk_.w[i]));
+            else fuse = false;
+        }
+        if (!fuse) wq = wk = nullptr;
+        float eps = pqk_.eps;
+        if (fuse) pqk_.n = 0;
+        flush();
         const int32_t *dpos = static_cast<const int32_t *>(stage(pos.data(), rows * sizeof(int32_t)));
+        if (fuse) {
+            launch_or_fail(launch_qk_rope(f(qb), f(kb), (int)qw, (int)kvw, (int)rows, (int)head, wq, wk, eps, dpos,
+                                          t.cos, t.sin, (int)t.max_pos, interleaved, d_err_, stream_),
+                           "qk_norm+rope");
+            return;
+        }
         launch_or_fail(launch_rope(f(qb), f(kb), (int)qw, (int)kvw, (int)rows, (int)head, dpos, t.cos, t.sin,
                                    (int)t.max_pos, interleaved, d_err_, stream_),
                        "rope");
@@ -301,7 +339,8 @@ public:
         span(d, 0, len, "add dst");
         span(s, 0, len, "add src");
         flush();
-        launch_or_fail(launch_add(f(d), f(s), len, stream_), "add_in_place");
+        // Deferred: a following rms_norm of dst runs both in one pass.
+        padd_ = PendAdd{dst, src, len};
     }
 
     void mul(kernrt_buf out, size_t oo, kernrt_buf a, size_t ao, kernrt_buf b, size_t bo, size_t len) {
@@ -309,6 +348,34 @@ public:
         span(ob, oo, len, "mul out");
         span(ab, ao, len, "mul a");
         span(bb, bo, len, "mul b");
+        if (len == 0) {
+            flush();
+            return;
+        }
+        // Consecutive calls on the same three distinct buffers with constant
+        // offset strides (the LFM2 driver's per-row calls) run as one launch.
+        if (out != a && out != b) {
+            if (pmul_.count > 0 && pmul_.out == out && pmul_.a == a && pmul_.b == b && pmul_.len == len) {
+                const long long so = (long long)oo - (long long)pmul_.oo, sa = (long long)ao - (long long)pmul_.ao,
+                                sb = (long long)bo - (long long)pmul_.bo;
+                const long long c = pmul_.count;
+                bool ok;
+                if (c == 1) ok = (so >= (long long)len || so <= -(long long)len);
+                else ok = so == c * pmul_.so && sa == c * pmul_.sa && sb == c * pmul_.sb;
+                if (ok) {
+                    if (c == 1) {
+                        pmul_.so = so;
+                        pmul_.sa = sa;
+                        pmul_.sb = sb;
+                    }
+                    pmul_.count += 1;
+                    return;
+                }
+            }
+            flush();
+            pmul_ = PendMul{out, a, b, oo, ao, bo, len, 0, 0, 0, 1};
+            return;
+        }
         flush();
         // A write of one index can feed another index's read only when out
         // shares a buffer with an operand at a different, overlapping offset.
@@ -716,8 +783,78 @@ public:
         }
     }
 
-    // Launch all pending embeds (one gather per run of calls into one buffer).
+    // Launch whatever is deferred: pending embeds, or the one pending op.
     void flush() {
+        flush_embeds();
+        flush_deferred();
+    }
+
+    void flush_deferred() {
+        if (padd_.len) {
+            const PendAdd p = padd_;
+            padd_ = PendAdd{};
+            launch_or_fail(launch_add(f(buf(p.dst)), f(buf(p.src)), p.len, stream_), "add_in_place");
+        }
+        if (pqk_.n) {
+            const PendQK p = pqk_;
+            pqk_.n = 0;
+            for (int i = 0; i < p.n; ++i)
+                launch_or_fail(launch_qk_norm(f(buf(p.v[i])), (int)p.rows, (int)p.width[i], (int)p.head,
+                                              f(buf(p.w[i])), p.eps, stream_),
+                               "qk_norm");
+        }
+        if (pmul_.count) {
+            const PendMul p = pmul_;
+            pmul_.count = 0;
+            launch_or_fail(launch_mul_strided(f(buf(p.out)) + p.oo, f(buf(p.a)) + p.ao, f(buf(p.b)) + p.bo,
+                                              p.count > 1 ? p.so : 0, p.count > 1 ? p.sa : 0,
+                                              p.count > 1 ? p.sb : 0, (int)p.len, (int)p.count, stream_),
+                           "mul");
+        }
+    }
+
+    // rms_norm right after a run of embeds that wrote exactly rows 0..rows-1
+    // of x: gather, normalise and keep x in one pass.
+    bool fuse_embed_rms(kernrt_buf out, kernrt_buf x, kernrt_buf weight, size_t rows, size_t dim, float eps) {
+        if (pending_.size() != rows || dim != dim_ || rows > (size_t)INT32_MAX) return false;
+        for (size_t r = 0; r < rows; ++r)
+            if (pending_[r].out != x || pending_[r].offset != (int64_t)(r * dim)) return false;
+        std::vector<int32_t> tok(rows);
+        for (size_t r = 0; r < rows; ++r) tok[r] = pending_[r].token;
+        pending_.clear();
+        ChainArgs a = blank(rows, dim);
+        a.eps = eps;
+        a.table = emb_data_;
+        a.tscales = emb_scales_;
+        a.vocab = (int)vocab_;
+        a.tokens = static_cast<const int32_t *>(stage(tok.data(), rows * sizeof(int32_t)));
+        a.x_out = f(buf(x));
+        a.xb = f(buf(out));
+        a.w_att = f(buf(weight));
+        launch_or_fail(chain_launch(emb_src_, a), "embed+rms_norm");
+        return true;
+    }
+
+    // rms_norm of x right after add_in_place(x, src): add, normalise, one pass.
+    bool fuse_add_rms(kernrt_buf out, kernrt_buf x, kernrt_buf weight, size_t rows, size_t dim, float eps) {
+        if (!padd_.len || padd_.dst != x || padd_.len != rows * dim || padd_.src == out || dim % 8 != 0)
+            return false;
+        const PendAdd p = padd_;
+        padd_ = PendAdd{};
+        flush_embeds();
+        ChainArgs a = blank(rows, dim);
+        a.eps = eps;
+        a.x_in = f(buf(x));
+        a.x_out = f(buf(x));
+        a.resid = f(buf(p.src));
+        a.xb = f(buf(out));
+        a.w_att = f(buf(weight));
+        launch_or_fail(launch_add_rms_norm(a, stream_), "add_in_place+rms_norm");
+        return true;
+    }
+
+    // Launch all pending embeds (one gather per run of calls into one buffer).
+    void flush_embeds() {
         if (pending_.empty()) return;
         const kernrt_buf out = pending_.front().out;
         const size_t n = pending_.size();
@@ -889,6 +1026,28 @@ private:
         const LaunchHook hook{&Backend::on_stage, this};
         return launch_chain(src, a, stream_, &hook);
     }
+
+    struct PendAdd {
+        kernrt_buf dst = 0, src = 0;
+        size_t len = 0;
+    };
+    struct PendQK {
+        int n = 0;
+        kernrt_buf v[2] = {0, 0};
+        size_t width[2] = {0, 0};
+        kernrt_buf w[2] = {0, 0};
+        size_t rows = 0, head = 0;
+        float eps = 0.0f;
+    };
+    struct PendMul {
+        kernrt_buf out = 0, a = 0, b = 0;
+        size_t oo = 0, ao = 0, bo = 0, len = 0;
+        long long so = 0, sa = 0, sb = 0;
+        long long count = 0;
+    };
+    PendAdd padd_;
+    PendQK pqk_;
+    PendMul pmul_;
 
     struct PipeSet {
         void *arena = nullptr;

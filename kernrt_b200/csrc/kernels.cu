@@ -708,8 +708,15 @@ __global__ void __launch_bounds__(kThreads, 3) k_chain(ChainArgs a, ChainLayout 
 // The three slots are always distinct, and one __syncthreads per iteration
 // hands each slot to its next role, so the serial sums hide behind the HBM
 // traffic of the neighbouring groups.
-template <int SRC, bool VEC>
+//
+// PRE_ADD (f32 x only) is the driver's add_in_place -> rms_norm pair
+// (llama.rs:762-765, 769-740): the residual is added first, x = x + resid is
+// written back by the loaders (warps 1..3) as they stage it, and the norm is
+// taken of the sum; the writers then store only xb.
+template <int SRC, bool VEC, bool PRE_ADD>
 __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLayout L) {
+    static_assert(!PRE_ADD || (SRC == SRC_X && VEC), "the pre-add form stages f32 rows with vector loads");
+    constexpr int NL = PRE_ADD ? 3 : 1;  // loader warps 1..NL; writers NL+1..7
     extern __shared__ __align__(16) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int dim = a.dim;
@@ -723,9 +730,38 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
     auto first_row = [&](int i) { return (int)(blockIdx.x + (unsigned)i * gridDim.x) * G; };
     auto slot = [&](int i) { return smem + (size_t)(i % 3) * slot_bytes; };
 
-    auto load = [&](int i) {  // warp 1
+    auto load = [&](int i) {  // warps 1..NL
         const int r0 = first_row(i), g = min(G, a.rows - r0);
         unsigned char *base = slot(i);
+        if constexpr (PRE_ADD) {
+            // x + resid, staged and written back, U float4 pairs in flight.
+            constexpr int U = 4;
+            const int lt = tid - 32, nlt = NL * 32;
+            const int n4 = dim >> 2, total = g * n4;
+            for (int i0 = lt; i0 < total; i0 += U * nlt) {
+                float4 xv[U], rv[U];
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    const int idx = i0 + k * nlt;
+                    if (idx < total) {
+                        const int r = idx / n4, c = (idx - r * n4) << 2;
+                        xv[k] = ld4(a.x_in + (size_t)(r0 + r) * dim + c);
+                        rv[k] = ld4(a.resid + (size_t)(r0 + r) * dim + c);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    const int idx = i0 + k * nlt;
+                    if (idx >= total) continue;
+                    const int r = idx / n4, c = (idx - r * n4) << 2;
+                    const float4 xo = make_float4(add_rn(xv[k].x, rv[k].x), add_rn(xv[k].y, rv[k].y),
+                                                  add_rn(xv[k].z, rv[k].z), add_rn(xv[k].w, rv[k].w));
+                    *reinterpret_cast<float4 *>(base + (size_t)r * L.xstride + 4 * c) = xo;
+                    st4(a.x_out + (size_t)(r0 + r) * dim + c, xo);
+                }
+            }
+            return;
+        }
         for (int r = 0; r < g; ++r) {
             const unsigned char *sp;
             int tok = 0;
@@ -778,11 +814,11 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
         scales[(i % 3) * 32 + lane] = rms_scale(ss, (float)dim, a.eps);
     };
 
-    auto write = [&](int i) {  // warps 2..7
+    auto write = [&](int i) {  // warps NL+1..7
         const int r0 = first_row(i), g = min(G, a.rows - r0);
         const unsigned char *base = slot(i);
         const float *sc = scales + (i % 3) * 32;
-        const int wt = tid - 64, nwt = blockDim.x - 64;
+        const int wt = tid - 32 * (NL + 1), nwt = blockDim.x - 32 * (NL + 1);
         if constexpr (VEC) {
             constexpr int U = 8;
             const int n4 = dim >> 2, total = g * n4;
@@ -791,7 +827,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
 #pragma unroll
                 for (int k = 0; k < U; ++k) {
                     const int idx = i0 + k * nwt;
-                    if (idx < total && a.resid && a.x_out) {
+                    if (!PRE_ADD && idx < total && a.resid && a.x_out) {
                         const int r = idx / n4, c = (idx - r * n4) << 2;
                         rr[k] = ld4(a.resid + (size_t)(r0 + r) * dim + c);
                     }
@@ -810,7 +846,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
                         st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[0])), mul_rn(w.y, mul_rn(s, v[1])),
                                                   mul_rn(w.z, mul_rn(s, v[2])), mul_rn(w.w, mul_rn(s, v[3]))));
                     }
-                    if (a.x_out) {
+                    if (!PRE_ADD && a.x_out) {
                         float4 xo = make_float4(v[0], v[1], v[2], v[3]);
                         if (a.resid)
                             xo = make_float4(add_rn(v[0], rr[k].x), add_rn(v[1], rr[k].y), add_rn(v[2], rr[k].z),
@@ -831,10 +867,10 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
         }
     };
 
-    if (warp == 1 && nmine > 0) load(0);
+    if (warp >= 1 && warp <= NL && nmine > 0) load(0);
     __syncthreads();
     for (int i = 0; i <= nmine; ++i) {
-        if (warp == 1) {
+        if (warp >= 1 && warp <= NL) {
             if (i + 1 < nmine) load(i + 1);
         } else if (warp == 0) {
             if (i < nmine) sum(i);
@@ -895,6 +931,69 @@ __global__ void __launch_bounds__(kThreads) k_rope(float *q, float *k, int q_wid
         const int kp = k_pairs_interleaved(q_width, kv_width);
         rope_pair_row(qr, q_width / 2, head, ct, st, vec && (q_width / 2) % 2 == 0, lane);
         rope_pair_row(kr, kp, head, ct, st, vec && kp % 2 == 0, lane);
+    }
+}
+
+// The driver's qk_norm(q), qk_norm(k), rope(q, k) sequence (llama.rs:744-754)
+// in one pass per row: one warp per row normalises each head (reference.rs
+// :180-207) and rotates it (reference.rs:209-257).  Either norm weight may
+// be null (that vector is only rotated).
+__global__ void __launch_bounds__(kThreads) k_qk_rope(float *q, float *k, int q_width, int kv_width, int rows,
+                                                      int head, const float *wq, const float *wk, float eps,
+                                                      const int32_t *pos, const float *cos_t, const float *sin_t,
+                                                      int max_pos, int interleaved, int *err) {
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float *qr = q + (size_t)row * q_width, *kr = k + (size_t)row * kv_width;
+    if (wq) qk_norm_row_warp(qr, q_width, head, wq, eps, lane);
+    if (wk) qk_norm_row_warp(kr, kv_width, head, wk, eps, lane);
+    const int p = pos[row];
+    if ((unsigned)p >= (unsigned)max_pos) {
+        if (lane == 0) set_err(err, ERR_POSITION);
+        return;
+    }
+    const int half = head >> 1;
+    const float *ct = cos_t + (size_t)p * half, *st = sin_t + (size_t)p * half;
+    if (!interleaved) {
+        const bool vec = ((half | q_width | kv_width) & 3) == 0;
+        rope_half_row(qr, q_width / head, head, half, ct, st, vec, lane);
+        rope_half_row(kr, kv_width / head, head, half, ct, st, vec, lane);
+    } else {
+        const bool vec = ((head | q_width | kv_width) & 3) == 0;
+        const int kp = k_pairs_interleaved(q_width, kv_width);
+        rope_pair_row(qr, q_width / 2, head, ct, st, vec && (q_width / 2) % 2 == 0, lane);
+        rope_pair_row(kr, kp, head, ct, st, vec && kp % 2 == 0, lane);
+    }
+}
+
+// A run of `count` mul calls (reference.rs:315-363) with fixed strides between
+// consecutive calls' offsets, as the LFM2 driver issues once per row
+// (lfm2.rs:586-596, 612-622).  The host only batches runs whose output buffer
+// is not an operand, so the calls are independent.
+__global__ void __launch_bounds__(kThreads) k_mul_strided(float *out, const float *a, const float *b, long long so,
+                                                          long long sa, long long sb, int len, int count) {
+    const long long n = (long long)len * count;
+    const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const long long nt = (long long)gridDim.x * blockDim.x;
+    const bool vec = (((uintptr_t)out | (uintptr_t)a | (uintptr_t)b) & 15) == 0 && ((so | sa | sb | len) & 3) == 0;
+    if (vec) {
+        const int l4 = len >> 2;
+        const long long n4 = (long long)l4 * count;
+        for (long long e = t; e < n4; e += nt) {
+            const long long i = e / l4;
+            const int j = (int)(e - i * l4) << 2;
+            const float4 x = *reinterpret_cast<const float4 *>(a + i * sa + j);
+            const float4 y = *reinterpret_cast<const float4 *>(b + i * sb + j);
+            *reinterpret_cast<float4 *>(out + i * so + j) =
+                make_float4(mul_rn(x.x, y.x), mul_rn(x.y, y.y), mul_rn(x.z, y.z), mul_rn(x.w, y.w));
+        }
+    } else {
+        for (long long e = t; e < n; e += nt) {
+            const long long i = e / len;
+            const int j = (int)(e - i * len);
+            out[i * so + j] = mul_rn(a[i * sa + j], b[i * sb + j]);
+        }
     }
 }
 
@@ -1134,7 +1233,7 @@ int device_sms() {
 // The norm stage as the persistent pipeline: rows per group from the shared
 // memory that lets two CTAs share an SM (three slots each), fewer when the
 // rows would give a CTA under eight groups.
-template <int SRC, bool VEC>
+template <int SRC, bool VEC, bool PRE_ADD = false>
 cudaError_t launch_norm_pipe(const ChainArgs &a, cudaStream_t s) {
     ChainLayout L{};
     const int rb = SRC == SRC_BF16 ? a.dim * 2 : (SRC == SRC_Q8 ? a.dim : a.dim * 4);
@@ -1150,7 +1249,7 @@ cudaError_t launch_norm_pipe(const ChainArgs &a, cudaStream_t s) {
     L.G = G;
     L.smem = 3 * (size_t)G * L.xstride + 3 * 32 * sizeof(float);
     if (L.smem > 227 * 1024) return cudaErrorInvalidValue;
-    auto kern = k_norm_pipe<SRC, VEC>;
+    auto kern = k_norm_pipe<SRC, VEC, PRE_ADD>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
@@ -1274,6 +1373,29 @@ cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows,
     if (rows <= 0) return cudaSuccess;
     k_rope<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(
         q, k, q_width, kv_width, rows, head, pos, cos_t, sin_t, max_pos, interleaved, err);
+    return launched();
+}
+
+cudaError_t launch_add_rms_norm(const ChainArgs &a, cudaStream_t s) {
+    if (a.rows <= 0) return cudaSuccess;
+    if (a.dim % 8 != 0) return cudaErrorInvalidValue;
+    return launch_norm_pipe<SRC_X, true, true>(a, s);
+}
+
+cudaError_t launch_qk_rope(float *q, float *k, int q_width, int kv_width, int rows, int head, const float *wq,
+                           const float *wk, float eps, const int32_t *pos, const float *cos_t, const float *sin_t,
+                           int max_pos, int interleaved, int *err, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    k_qk_rope<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(q, k, q_width, kv_width, rows, head, wq, wk,
+                                                                          eps, pos, cos_t, sin_t, max_pos,
+                                                                          interleaved, err);
+    return launched();
+}
+
+cudaError_t launch_mul_strided(float *out, const float *a, const float *b, long long so, long long sa, long long sb,
+                               int len, int count, cudaStream_t s) {
+    if (len <= 0 || count <= 0) return cudaSuccess;
+    k_mul_strided<<<stream_grid((size_t)len * count), kThreads, 0, s>>>(out, a, b, so, sa, sb, len, count);
     return launched();
 }
 

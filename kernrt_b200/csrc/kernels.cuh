@@ -63,6 +63,16 @@ size_t chain_smem_bytes(int src, const ChainArgs &a, int rows_per_cta);
 
 cudaError_t launch_qk_norm(float *v, int rows, int width, int head, const float *w, float eps,
                            cudaStream_t s);
+// x = x + resid, then xb = rms_norm(x) with weight w_att (a.x_in == a.x_out):
+// the driver's add_in_place -> rms_norm pair in one pass.  dim % 8 == 0.
+cudaError_t launch_add_rms_norm(const ChainArgs &a, cudaStream_t s);
+// qk_norm(q), qk_norm(k) (either weight may be null), then rope(q, k).
+cudaError_t launch_qk_rope(float *q, float *k, int q_width, int kv_width, int rows, int head, const float *wq,
+                           const float *wk, float eps, const int32_t *pos, const float *cos_t, const float *sin_t,
+                           int max_pos, int interleaved, int *err, cudaStream_t s);
+// out[i*so + j] = a[i*sa + j] * b[i*sb + j] for i < count, j < len.
+cudaError_t launch_mul_strided(float *out, const float *a, const float *b, long long so, long long sa, long long sb,
+                               int len, int count, cudaStream_t s);
 cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows, int head,
                         const int32_t *pos, const float *cos_t, const float *sin_t, int max_pos,
                         int interleaved, int *err, cudaStream_t s);
