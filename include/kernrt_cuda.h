@@ -99,6 +99,9 @@ int kernrt_cuda_read_bytes(kernrt_cuda_ctx *ctx, kernrt_buf src, size_t src_byte
 int kernrt_cuda_device_ptr(kernrt_cuda_ctx *ctx, kernrt_buf buf, void **ptr);
 /* Wait for all deferred work. */
 int kernrt_cuda_synchronize(kernrt_cuda_ctx *ctx);
+/* Launch every deferred op (pending embeds, an op held for fusion) onto the
+ * backend's stream without waiting for it. */
+int kernrt_cuda_flush(kernrt_cuda_ctx *ctx);
 
 /* --- the row ops ------------------------------------------------------------ */
 

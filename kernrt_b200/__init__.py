@@ -94,6 +94,7 @@ SIGNATURES = {
     "kernrt_cuda_read_bytes": (C.c_int, [P, Buf, SZ, P, SZ]),
     "kernrt_cuda_device_ptr": (C.c_int, [P, Buf, C.POINTER(P)]),
     "kernrt_cuda_synchronize": (C.c_int, [P]),
+    "kernrt_cuda_flush": (C.c_int, [P]),
     "kernrt_cuda_embed": (C.c_int, [P, SZ, Buf, SZ]),
     "kernrt_cuda_copy": (C.c_int, [P, Buf, SZ, Buf, SZ, SZ]),
     "kernrt_cuda_rms_norm": (C.c_int, [P, Buf, Buf, Buf, SZ, SZ, C.c_float]),
@@ -262,6 +263,10 @@ class CudaBackend:
 
     def synchronize(self) -> None:
         _ok(self._lib.kernrt_cuda_synchronize(self._ctx))
+
+    def flush(self) -> None:
+        """Launch deferred work without waiting for it."""
+        _ok(self._lib.kernrt_cuda_flush(self._ctx))
 
     # -- the row ops (mod.rs:284-400) ------------------------------------------------
     def embed(self, token: int, out: int, offset: int) -> None:

@@ -23,6 +23,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace krt {
@@ -79,6 +80,10 @@ public:
         cudaFreeHost(h_err_);
         cudaFreeHost(stage_host_);
         cudaFree(stage_dev_);
+        for (auto &r : retired_) {
+            cudaFreeHost(r.first);
+            cudaFree(r.second);
+        }
         for (auto e : events_) cudaEventDestroy(e);
         cudaStreamSynchronize(h2d_);
         cudaStreamSynchronize(d2h_);
@@ -200,6 +205,11 @@ public:
         flush();
         check(cudaMemcpyAsync(h_err_, d_err_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "error word");
         check(cudaStreamSynchronize(stream_), "synchronize");
+        for (auto &r : retired_) {
+            cudaFreeHost(r.first);
+            cudaFree(r.second);
+        }
+        retired_.clear();
         const int e = *h_err_;
         if (e) {
             check(cudaMemsetAsync(d_err_, 0, sizeof(int), stream_), "cudaMemset");
@@ -867,13 +877,18 @@ public:
             aligned = aligned && (off[i] % 4 == 0);
         }
         pending_.clear();
+        // One staging call per launch: offsets then token ids in one block.
+        std::vector<unsigned char> packed(n * (sizeof(int64_t) + sizeof(int32_t)));
+        std::memcpy(packed.data(), off.data(), n * sizeof(int64_t));
+        std::memcpy(packed.data() + n * sizeof(int64_t), tok.data(), n * sizeof(int32_t));
+        unsigned char *dev = static_cast<unsigned char *>(stage(packed.data(), packed.size()));
         GatherArgs g{};
         g.table = emb_data_;
         g.tscales = emb_scales_;
         g.vocab = (int)vocab_;
         g.dim = (int)dim_;
-        g.tokens = static_cast<const int32_t *>(stage(tok.data(), n * sizeof(int32_t)));
-        g.dst_off = static_cast<const int64_t *>(stage(off.data(), n * sizeof(int64_t)));
+        g.dst_off = reinterpret_cast<const int64_t *>(dev);
+        g.tokens = reinterpret_cast<const int32_t *>(dev + n * sizeof(int64_t));
         g.dst = f(buf(out));
         g.n = (int)n;
         g.err = d_err_;
@@ -977,7 +992,10 @@ private:
 
     // Copy a host slice into the pinned ring and enqueue its upload; returns
     // the device address.  The ring wraps after a stream synchronize, so a
-    // region is never rewritten while a copy from it may be pending.
+    // region is never rewritten while a copy from it, or a kernel reading it,
+    // may be pending.  Each launch takes its staged data from one call, made
+    // right before the launch; a ring that grows is retired, not freed, until
+    // the next barrier.
     void *stage(const void *src, size_t bytes) {
         const size_t need = (bytes + 255) & ~(size_t)255;
         if (need > stage_cap_) {
@@ -996,8 +1014,7 @@ private:
     }
 
     void grow_staging(size_t cap) {
-        cudaFreeHost(stage_host_);
-        cudaFree(stage_dev_);
+        if (stage_host_ || stage_dev_) retired_.push_back({stage_host_, stage_dev_});
         stage_host_ = nullptr;
         stage_dev_ = nullptr;
         check(cudaMallocHost(&stage_host_, cap), "cudaMallocHost(staging)");
@@ -1077,6 +1094,7 @@ private:
     int *h_err_ = nullptr;
     char *stage_host_ = nullptr;
     char *stage_dev_ = nullptr;
+    std::vector<std::pair<char *, char *>> retired_;  // grown-out staging rings, freed at the next barrier
     size_t stage_cap_ = 0, stage_head_ = 0;
 };
 
@@ -1235,6 +1253,10 @@ int kernrt_cuda_device_ptr(kernrt_cuda_ctx *ctx, kernrt_buf h, void **ptr) {
 
 int kernrt_cuda_synchronize(kernrt_cuda_ctx *ctx) {
     return guard(ctx, [&](krt::Backend &b) { b.barrier(); });
+}
+
+int kernrt_cuda_flush(kernrt_cuda_ctx *ctx) {
+    return guard(ctx, [&](krt::Backend &b) { b.flush(); });
 }
 
 int kernrt_cuda_embed(kernrt_cuda_ctx *ctx, size_t token, kernrt_buf out, size_t offset) {

@@ -221,6 +221,99 @@ __device__ void rope_pair_row(float *v, int npairs, int head, const float *__res
     }
 }
 
+// One row's q or k vector through qk_norm (w != null, reference.rs:180-207)
+// and RoPE (mode 1 half-split, 2 adjacent pairs; reference.rs:209-257), staged
+// in this warp's shared memory `sm`: the row is loaded once with 16-byte
+// coalesced loads into head slots padded by 4 floats, lane h sums head h's
+// squares left to right out of shared memory (bank-conflict free), then the
+// warp normalises, rotates and stores the row with coalesced 16-byte stores.
+// Covers the row's nh = width/head full heads; in pair mode the first
+// `npairs` pairs are rotated (all of them when the row is whole heads).
+// Requires head % 4 == 0 and width % 4 == 0.  sm holds nh*(head+4) + nh floats.
+__device__ void qk_rope_row_smem(float *v, int width, int head, const float *__restrict__ w, float eps,
+                                 const float *__restrict__ ct, const float *__restrict__ st, int mode, int npairs,
+                                 float *sm, int lane) {
+    const int nh = width / head;
+    if (nh == 0) return;
+    const int hs = head + 4, half = head >> 1;
+    float *sc = sm + nh * hs;
+    const int n4 = (nh * head) >> 2, per = head >> 2;
+    for (int t = lane; t < n4; t += 32) {
+        const int h = t / per, j = (t - h * per) << 2;
+        *reinterpret_cast<float4 *>(sm + h * hs + j) = *reinterpret_cast<const float4 *>(v + 4 * t);
+    }
+    __syncwarp();
+    if (w) {
+        for (int h = lane; h < nh; h += 32) {
+            const float *p = sm + h * hs;
+            float ss = 0.0f;
+            for (int j = 0; j < head; j += 4) {
+                const float4 t4 = *reinterpret_cast<const float4 *>(p + j);
+                ss = add_rn(ss, mul_rn(t4.x, t4.x));
+                ss = add_rn(ss, mul_rn(t4.y, t4.y));
+                ss = add_rn(ss, mul_rn(t4.z, t4.z));
+                ss = add_rn(ss, mul_rn(t4.w, t4.w));
+            }
+            sc[h] = rms_scale(ss, (float)head, eps);
+        }
+        __syncwarp();
+    }
+    auto norm4 = [&](float4 x, int h, int j) {
+        if (!w) return x;
+        const float s = sc[h];
+        const float4 ww = __ldg(reinterpret_cast<const float4 *>(w + j));
+        return make_float4(mul_rn(ww.x, mul_rn(s, x.x)), mul_rn(ww.y, mul_rn(s, x.y)), mul_rn(ww.z, mul_rn(s, x.z)),
+                           mul_rn(ww.w, mul_rn(s, x.w)));
+    };
+    if (mode == 1) {
+        const int ph = half >> 2;  // float4 items per head (lo half)
+        for (int t = lane; t < nh * ph; t += 32) {
+            const int h = t / ph, j = (t - h * ph) << 2;
+            const float4 lo = norm4(*reinterpret_cast<const float4 *>(sm + h * hs + j), h, j);
+            const float4 hi = norm4(*reinterpret_cast<const float4 *>(sm + h * hs + half + j), h, half + j);
+            const float4 c = __ldg(reinterpret_cast<const float4 *>(ct + j));
+            const float4 s = __ldg(reinterpret_cast<const float4 *>(st + j));
+            float4 nl, nhv;
+            nl.x = sub_rn(mul_rn(lo.x, c.x), mul_rn(hi.x, s.x));
+            nl.y = sub_rn(mul_rn(lo.y, c.y), mul_rn(hi.y, s.y));
+            nl.z = sub_rn(mul_rn(lo.z, c.z), mul_rn(hi.z, s.z));
+            nl.w = sub_rn(mul_rn(lo.w, c.w), mul_rn(hi.w, s.w));
+            nhv.x = add_rn(mul_rn(lo.x, s.x), mul_rn(hi.x, c.x));
+            nhv.y = add_rn(mul_rn(lo.y, s.y), mul_rn(hi.y, c.y));
+            nhv.z = add_rn(mul_rn(lo.z, s.z), mul_rn(hi.z, c.z));
+            nhv.w = add_rn(mul_rn(lo.w, s.w), mul_rn(hi.w, c.w));
+            *reinterpret_cast<float4 *>(v + h * head + j) = nl;
+            *reinterpret_cast<float4 *>(v + h * head + half + j) = nhv;
+        }
+    } else {
+        for (int t = lane; t < n4; t += 32) {
+            const int h = t / per, j = (t - h * per) << 2;
+            float4 x = norm4(*reinterpret_cast<const float4 *>(sm + h * hs + j), h, j);
+            const int i = 4 * t;  // element index in the row = pair 2t, 2t+1
+            if (mode == 2 && 2 * t < npairs) {
+                const int jj = j >> 1;  // (i % head) / 2, with i % head == j
+                const float2 c = __ldg(reinterpret_cast<const float2 *>(ct + jj));
+                const float2 s = __ldg(reinterpret_cast<const float2 *>(st + jj));
+                const float x0 = x.x, x1 = x.y, x2 = x.z, x3 = x.w;
+                x.x = sub_rn(mul_rn(x0, c.x), mul_rn(x1, s.x));
+                x.y = add_rn(mul_rn(x0, s.x), mul_rn(x1, c.x));
+                if (2 * t + 1 < npairs) {
+                    x.z = sub_rn(mul_rn(x2, c.y), mul_rn(x3, s.y));
+                    x.w = add_rn(mul_rn(x2, s.y), mul_rn(x3, c.y));
+                }
+            }
+            *reinterpret_cast<float4 *>(v + i) = x;
+        }
+    }
+    __syncwarp();
+}
+
+// Floats of shared memory qk_rope_row_smem needs for a row of `width`.
+__host__ __device__ __forceinline__ int qk_smem_floats(int width, int head) {
+    const int nh = width / head;
+    return ((nh * (head + 4) + nh) + 3) & ~3;
+}
+
 // Pairs of K rotated by the reference's interleaved loop: i < kv_width while
 // i + 1 < q_width (reference.rs:221-236).
 __device__ __forceinline__ int k_pairs_interleaved(int q_width, int kv_width) {
@@ -713,9 +806,15 @@ __global__ void __launch_bounds__(kThreads, 3) k_chain(ChainArgs a, ChainLayout 
 // (llama.rs:762-765, 769-740): the residual is added first, x = x + resid is
 // written back by the loaders (warps 1..3) as they stage it, and the norm is
 // taken of the sum; the writers then store only xb.
-template <int SRC, bool VEC, bool PRE_ADD>
+//
+// FQ is the final RMSNorm fused with Q8_0 quantisation (quant.rs:856-874): the
+// summing lanes also run the sum of the row that gets quantised (x, or
+// x + resid with the residual rows staged beside x), and the writers emit the
+// int8 codes and block scales, eight lanes per 32-element block.
+template <int SRC, bool VEC, bool PRE_ADD, bool FQ>
 __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLayout L) {
     static_assert(!PRE_ADD || (SRC == SRC_X && VEC), "the pre-add form stages f32 rows with vector loads");
+    static_assert(!FQ || (VEC && !PRE_ADD), "the quantising form needs whole 32-element blocks");
     constexpr int NL = PRE_ADD ? 3 : 1;  // loader warps 1..NL; writers NL+1..7
     extern __shared__ __align__(16) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -723,8 +822,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
     const int G = L.G;
     const int ngroups = (a.rows + G - 1) / G;
     const int nmine = (int)blockIdx.x < ngroups ? (ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
-    const size_t slot_bytes = (size_t)G * L.xstride;
-    float *scales = reinterpret_cast<float *>(smem + 3 * slot_bytes);  // [3][32]
+    const size_t slot_bytes = (size_t)G * (L.xstride + L.rstride);
+    float *scales = reinterpret_cast<float *>(smem + 3 * slot_bytes);  // [3][64]: s1[32] s2[32]
+    const bool fq_resid = FQ && a.resid != nullptr;
     const int rb = src_row_bytes<SRC>(dim);
 
     auto first_row = [&](int i) { return (int)(blockIdx.x + (unsigned)i * gridDim.x) * G; };
@@ -788,6 +888,11 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
                 float *sdst = reinterpret_cast<float *>(dst + align16(dim));
                 for (int b = lane; b < nb; b += 32) sdst[b] = sp ? __ldg(a.tscales + (size_t)tok * nb + b) : 0.0f;
             }
+            if (fq_resid) {
+                const float *rsrc = a.resid + (size_t)(r0 + r) * dim;
+                unsigned char *rdst = base + (size_t)G * L.xstride + (size_t)r * L.rstride;
+                for (int c = lane; c < (dim >> 2); c += 32) cp_async16(rdst + 16 * c, rsrc + 4 * c);
+            }
         }
         if constexpr (VEC) cp_async_wait_all();
     };
@@ -797,7 +902,24 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
         if (lane >= g) return;
         const unsigned char *row = slot(i) + (size_t)lane * L.xstride;
         float ss = 0.0f;
-        if constexpr (VEC) {
+        if constexpr (FQ) {
+            const float *rrow =
+                reinterpret_cast<const float *>(slot(i) + (size_t)G * L.xstride + (size_t)lane * L.rstride);
+            float ss2 = 0.0f;
+            for (int c = 0; c < dim; c += 8) {
+                float v[8];
+                decode_staged<SRC, 8>(row, dim, c, v);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    ss = add_rn(ss, mul_rn(v[e], v[e]));
+                    const float xo = fq_resid ? add_rn(v[e], rrow[c + e]) : v[e];
+                    ss2 = add_rn(ss2, mul_rn(xo, xo));
+                }
+            }
+            scales[(i % 3) * 64 + lane] = rms_scale(ss, (float)dim, a.eps);
+            scales[(i % 3) * 64 + 32 + lane] = rms_scale(ss2, (float)dim, a.final_eps);
+            return;
+        } else if constexpr (VEC) {
             for (int c = 0; c < dim; c += 8) {
                 float v[8];
                 decode_staged<SRC, 8>(row, dim, c, v);
@@ -811,14 +933,68 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
                 ss = add_rn(ss, mul_rn(v[0], v[0]));
             }
         }
-        scales[(i % 3) * 32 + lane] = rms_scale(ss, (float)dim, a.eps);
+        scales[(i % 3) * 64 + lane] = rms_scale(ss, (float)dim, a.eps);
     };
 
     auto write = [&](int i) {  // warps NL+1..7
         const int r0 = first_row(i), g = min(G, a.rows - r0);
         const unsigned char *base = slot(i);
-        const float *sc = scales + (i % 3) * 32;
+        const float *sc = scales + (i % 3) * 64;
         const int wt = tid - 32 * (NL + 1), nwt = blockDim.x - 32 * (NL + 1);
+        if constexpr (FQ) {
+            // 8 lanes x float4 per 32-element block; the loop is warp-uniform
+            // so every lane reaches the group shuffles.
+            const int nb = dim >> 5, total = g * nb * 8;
+            const float *sc2 = sc + 32;
+            for (int base_i = wt - lane; base_i < total; base_i += nwt) {
+                const int idx = base_i + lane;
+                const bool ok = idx < total;
+                const int blk = ok ? idx >> 3 : 0, sub = idx & 7;
+                const int r = blk / nb, b = blk - r * nb, c = b * 32 + sub * 4;
+                const int row = r0 + r;
+                float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (ok) {
+                    decode_staged<SRC, 4>(base + (size_t)r * L.xstride, dim, c, v);
+                    const size_t o = (size_t)row * dim + c;
+                    if (a.xb) {
+                        const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
+                        const float s1 = sc[r];
+                        st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s1, v[0])), mul_rn(w.y, mul_rn(s1, v[1])),
+                                                  mul_rn(w.z, mul_rn(s1, v[2])), mul_rn(w.w, mul_rn(s1, v[3]))));
+                    }
+                    float4 xo = make_float4(v[0], v[1], v[2], v[3]);
+                    if (fq_resid) {
+                        const float4 rr = *reinterpret_cast<const float4 *>(base + (size_t)G * L.xstride +
+                                                                            (size_t)r * L.rstride + 4 * c);
+                        xo = make_float4(add_rn(v[0], rr.x), add_rn(v[1], rr.y), add_rn(v[2], rr.z), add_rn(v[3], rr.w));
+                    }
+                    if (a.x_out) st4(a.x_out + o, xo);
+                    const float4 wf = __ldg(reinterpret_cast<const float4 *>(a.w_final + c));
+                    const float s2 = sc2[r];
+                    y = make_float4(mul_rn(wf.x, mul_rn(s2, xo.x)), mul_rn(wf.y, mul_rn(s2, xo.y)),
+                                    mul_rn(wf.z, mul_rn(s2, xo.z)), mul_rn(wf.w, mul_rn(s2, xo.w)));
+                }
+                float am = fmaxf(fmaxf(fmaxf(0.0f, fabsf(y.x)), fmaxf(0.0f, fabsf(y.y))),
+                                 fmaxf(fmaxf(0.0f, fabsf(y.z)), fmaxf(0.0f, fabsf(y.w))));
+                am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
+                am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
+                am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
+                if (!ok) continue;
+                const float d = div_rn(am, 127.0f);
+                const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+                const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y.x, inv)) |
+                                        ((uint32_t)(uint8_t)q8_code(mul_rn(y.y, inv)) << 8) |
+                                        ((uint32_t)(uint8_t)q8_code(mul_rn(y.z, inv)) << 16) |
+                                        ((uint32_t)(uint8_t)q8_code(mul_rn(y.w, inv)) << 24);
+                *reinterpret_cast<uint32_t *>(a.codes + (size_t)row * nb * 32 + c) = packed;
+                if (sub == 0) {
+                    a.scales[(size_t)row * nb + b] = d;
+                    if (a.scales16) a.scales16[(size_t)row * nb + b] = f16_bits(d);
+                }
+            }
+            return;
+        }
         if constexpr (VEC) {
             constexpr int U = 8;
             const int n4 = dim >> 2, total = g * n4;
@@ -965,6 +1141,78 @@ __global__ void __launch_bounds__(kThreads) k_qk_rope(float *q, float *k, int q_
         rope_pair_row(qr, q_width / 2, head, ct, st, vec && (q_width / 2) % 2 == 0, lane);
         rope_pair_row(kr, kp, head, ct, st, vec && kp % 2 == 0, lane);
     }
+}
+
+// Row-staged forms of qk_norm, qk_norm+RoPE and the chain's q/k stream: one
+// warp per row (grid-stride over rows), each warp with `smf` floats of
+// dynamic shared memory (qk_rope_row_smem).
+__global__ void __launch_bounds__(kThreads) k_qk_norm_smem(float *v, int rows, int width, int head,
+                                                           const float *__restrict__ w, float eps, int smf) {
+    extern __shared__ __align__(16) float qsm[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float *sm = qsm + warp * smf;
+    const int wpb = blockDim.x >> 5;
+    for (int row = blockIdx.x * wpb + warp; row < rows; row += gridDim.x * wpb)
+        qk_rope_row_smem(v + (size_t)row * width, width, head, w, eps, nullptr, nullptr, 0, 0, sm, lane);
+}
+
+__global__ void __launch_bounds__(kThreads) k_qk_rope_smem(float *q, float *k, int q_width, int kv_width, int rows,
+                                                           int head, const float *wq, const float *wk, float eps,
+                                                           const int32_t *pos, const float *cos_t,
+                                                           const float *sin_t, int max_pos, int interleaved,
+                                                           int *err, int smf) {
+    extern __shared__ __align__(16) float qsm[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float *sm = qsm + warp * smf;
+    const int wpb = blockDim.x >> 5, half = head >> 1;
+    const int mode = interleaved ? 2 : 1;
+    const int kp = k_pairs_interleaved(q_width, kv_width);
+    for (int row = blockIdx.x * wpb + warp; row < rows; row += gridDim.x * wpb) {
+        const int p = pos[row];
+        const bool ok = (unsigned)p < (unsigned)max_pos;
+        if (!ok && lane == 0) set_err(err, ERR_POSITION);
+        const float *ct = ok ? cos_t + (size_t)p * half : nullptr;
+        const float *st = ok ? sin_t + (size_t)p * half : nullptr;
+        // an out-of-table position still gets its norm; the rotation is skipped
+        qk_rope_row_smem(q + (size_t)row * q_width, q_width, head, wq, eps, ct, st, ok ? mode : 0, q_width / 2, sm,
+                         lane);
+        qk_rope_row_smem(k + (size_t)row * kv_width, kv_width, head, wk, eps, ct, st, ok ? mode : 0, kp, sm, lane);
+    }
+}
+
+// The chain's streams when q/k carry per-head norms (Qwen3, LFM2): the q/k
+// rows through qk_rope_row_smem, then SwiGLU over all rows.
+__global__ void __launch_bounds__(kThreads) k_stream_qk(ChainArgs a, int smf) {
+    extern __shared__ __align__(16) float qsm[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float *sm = qsm + warp * smf;
+    const int wpb = blockDim.x >> 5;
+    const int kp = k_pairs_interleaved(a.q_dim, a.kv_dim);
+    if (a.q || a.k) {
+        for (int row = blockIdx.x * wpb + warp; row < a.rows; row += gridDim.x * wpb) {
+            const float *ct = nullptr, *st = nullptr;
+            int mode = 0;
+            if (a.rope_mode) {
+                const int p = a.pos[row];
+                if ((unsigned)p < (unsigned)a.max_pos) {
+                    ct = a.cos_t + (size_t)p * a.half;
+                    st = a.sin_t + (size_t)p * a.half;
+                    mode = a.rope_mode;
+                } else if (lane == 0) {
+                    set_err(a.err, ERR_POSITION);
+                }
+            }
+            if (a.q)
+                qk_rope_row_smem(a.q + (size_t)row * a.q_dim, a.q_dim, a.head, a.w_q, a.eps, ct, st, mode,
+                                 a.q_dim / 2, sm, lane);
+            if (a.k)
+                qk_rope_row_smem(a.k + (size_t)row * a.kv_dim, a.kv_dim, a.head, a.w_k, a.eps, ct, st, mode, kp, sm,
+                                 lane);
+        }
+    }
+    if (a.gate)
+        silu_range<2>(a.gate, a.up, 0, (size_t)a.rows * a.hidden, blockIdx.x * blockDim.x + threadIdx.x,
+                      gridDim.x * blockDim.x);
 }
 
 // A run of `count` mul calls (reference.rs:315-363) with fixed strides between
@@ -1131,6 +1379,45 @@ __global__ void __launch_bounds__(kThreads) k_quantize_q8(const float *__restric
     }
 }
 
+// The same quantisation for rows of whole 32-element blocks: eight lanes per
+// block, four values per lane, the block amax over the 8-lane group (the loop
+// is warp-uniform so every lane reaches the shuffles), codes stored four at a
+// time.
+__global__ void __launch_bounds__(kThreads) k_quantize_q8v(const float *__restrict__ x, int rows, int dim,
+                                                           int8_t *codes, float *scales, uint16_t *scales16) {
+    const int nb = dim >> 5;
+    const long long total = (long long)rows * nb * 8;
+    const int lane = threadIdx.x & 31;
+    const long long gt = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const long long nt = (long long)gridDim.x * blockDim.x;
+    for (long long base = gt - lane; base < total; base += nt) {
+        const long long idx = base + lane;
+        const bool ok = idx < total;
+        const long long blk = ok ? idx >> 3 : 0;
+        const int sub = (int)(idx & 7);
+        const long long row = blk / nb;
+        const int b = (int)(blk - row * nb), c = b * 32 + sub * 4;
+        const float4 y = ok ? ld4(x + row * dim + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float am = fmaxf(fmaxf(fmaxf(0.0f, fabsf(y.x)), fmaxf(0.0f, fabsf(y.y))),
+                         fmaxf(fmaxf(0.0f, fabsf(y.z)), fmaxf(0.0f, fabsf(y.w))));
+        am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
+        am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
+        if (!ok) continue;
+        const float d = div_rn(am, 127.0f);
+        const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+        const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y.x, inv)) |
+                                ((uint32_t)(uint8_t)q8_code(mul_rn(y.y, inv)) << 8) |
+                                ((uint32_t)(uint8_t)q8_code(mul_rn(y.z, inv)) << 16) |
+                                ((uint32_t)(uint8_t)q8_code(mul_rn(y.w, inv)) << 24);
+        *reinterpret_cast<uint32_t *>(codes + row * nb * 32 + c) = packed;
+        if (sub == 0) {
+            scales[row * nb + b] = d;
+            if (scales16) scales16[row * nb + b] = f16_bits(d);
+        }
+    }
+}
+
 // quant.rs:198-220 Q8_0x4::to_row_major with quant.rs:764-769's widening.
 __device__ __forceinline__ float f16_scale_to_f32(uint16_t bits) {
     const uint32_t sign = (uint32_t)(bits >> 15) << 31;
@@ -1230,26 +1517,60 @@ int device_sms() {
     return sms[dev];
 }
 
+// Warps per CTA and grid for the row-staged q/k kernels; 0 warps when a row
+// does not fit, so the caller keeps the unstaged form.
+struct QkLaunch {
+    int warps = 0, smf = 0;
+    size_t smem = 0;
+    unsigned grid = 0;
+};
+
+template <class K>
+QkLaunch qk_launch_config(K kern, int width, int head, int rows) {
+    QkLaunch c;
+    if (head <= 0 || (head & 3) || (width & 3)) return c;
+    c.smf = qk_smem_floats(width, head);
+    const size_t per_warp = (size_t)c.smf * sizeof(float);
+    if (per_warp == 0) return c;
+    int warps = (int)((200 * 1024) / per_warp);
+    if (warps > kThreads / 32) warps = kThreads / 32;
+    if (warps < 1) return c;
+    c.warps = warps;
+    c.smem = per_warp * warps;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem) != cudaSuccess) {
+        cudaGetLastError();
+        c.warps = 0;
+        return c;
+    }
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, warps * 32, c.smem);
+    long grid = (long)device_sms() * (per_sm > 0 ? per_sm : 1);
+    const long need = (rows + warps - 1) / warps;
+    c.grid = (unsigned)(grid < need ? grid : need);
+    if (c.grid == 0) c.grid = 1;
+    return c;
+}
+
 // The norm stage as the persistent pipeline: rows per group from the shared
 // memory that lets two CTAs share an SM (three slots each), fewer when the
 // rows would give a CTA under eight groups.
-template <int SRC, bool VEC, bool PRE_ADD = false>
+template <int SRC, bool VEC, bool PRE_ADD = false, bool FQ = false>
 cudaError_t launch_norm_pipe(const ChainArgs &a, cudaStream_t s) {
     ChainLayout L{};
     const int rb = SRC == SRC_BF16 ? a.dim * 2 : (SRC == SRC_Q8 ? a.dim : a.dim * 4);
     L.xstride = align16(rb) + (SRC == SRC_Q8 ? align16((a.dim / 32) * 4) : 0) + 16;
-    L.rstride = 0;
-    const size_t budget = 110 * 1024 - 3 * 32 * sizeof(float);
-    int G = (int)(budget / (3 * (size_t)L.xstride));
+    L.rstride = (FQ && a.resid) ? align16(a.dim * 4) + 16 : 0;
+    const size_t budget = 110 * 1024 - 3 * 64 * sizeof(float);
+    int G = (int)(budget / (3 * (size_t)(L.xstride + L.rstride)));
     if (G > 32) G = 32;
     if (G < 1) G = 1;
     const int sms = device_sms();
     const long want = ((long)a.rows + (long)sms * 2 * 8 - 1) / ((long)sms * 2 * 8);
     if (want < G) G = (int)(want > 0 ? want : 1);
     L.G = G;
-    L.smem = 3 * (size_t)G * L.xstride + 3 * 32 * sizeof(float);
+    L.smem = 3 * (size_t)G * (L.xstride + L.rstride) + 3 * 64 * sizeof(float);
     if (L.smem > 227 * 1024) return cudaErrorInvalidValue;
-    auto kern = k_norm_pipe<SRC, VEC, PRE_ADD>;
+    auto kern = k_norm_pipe<SRC, VEC, PRE_ADD, FQ>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
@@ -1277,9 +1598,17 @@ inline void mark(const LaunchHook *hook, int stage) {
 template <int SRC>
 cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHook *hook) {
     const bool vec = (a.dim % 8) == 0 && (SRC != SRC_Q8 || a.dim % 32 == 0);
+    const bool has_qk = (a.w_q && a.q) || (a.w_k && a.k);
+    const bool has_rope = a.rope_mode != 0 && (a.q || a.k);
+    // q/k norms or pair-mode RoPE go through the row-staged stream kernel.
+    const bool qk_stream = has_qk || (has_rope && a.rope_mode == 2);
+    const bool qk_ok = ((a.head | a.q_dim | a.kv_dim) & 3) == 0 && a.head > 0 &&
+                       (a.rope_mode != 2 || (a.q_dim % a.head == 0 && a.kv_dim % a.head == 0));
     const bool streams_vec = ((a.half | a.q_dim | a.kv_dim | a.hidden) & 3) == 0;
-    const bool split = a.w_final == nullptr && a.w_q == nullptr && a.w_k == nullptr && a.rope_mode != 2 &&
-                       (streams_vec || (a.q == nullptr && a.k == nullptr && a.gate == nullptr));
+    const bool any_stream = has_qk || has_rope || a.gate;
+    const bool fq_pipe = a.w_final != nullptr && vec && a.dim % 32 == 0;
+    const bool split = (a.w_final == nullptr || fq_pipe) &&
+                       (!any_stream || (qk_stream ? qk_ok && (a.hidden & 3) == 0 : streams_vec));
     if (!split) {
         mark(hook, STAGE_FUSED);
         const cudaError_t e = launch_chain_src_fused<SRC>(a, s);
@@ -1287,13 +1616,25 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
         return e;
     }
     cudaError_t e = cudaSuccess;
-    if (a.xb || a.x_out) {
+    if (fq_pipe) {
+        mark(hook, STAGE_NORM);
+        e = launch_norm_pipe<SRC, true, false, true>(a, s);
+    } else if (a.xb || a.x_out) {
         mark(hook, STAGE_NORM);
         e = vec ? launch_norm_pipe<SRC, true>(a, s) : launch_norm_pipe<SRC, false>(a, s);
     }
     if (e != cudaSuccess) return e;
-    if ((a.rope_mode == 1 && (a.q || a.k)) || a.gate) {
+    if (any_stream && qk_stream) {
+        const QkLaunch c = qk_launch_config(k_stream_qk, a.q_dim > a.kv_dim ? a.q_dim : a.kv_dim, a.head, a.rows);
+        if (!c.warps) return cudaErrorInvalidValue;
+        // the grid also covers SwiGLU: use every resident CTA slot
+        int per_sm = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_stream_qk, c.warps * 32, c.smem);
+        const unsigned grid = (unsigned)(device_sms() * (per_sm > 0 ? per_sm : 1));
         mark(hook, STAGE_STREAM);
+        k_stream_qk<<<grid, c.warps * 32, c.smem, s>>>(a, c.smf);
+        e = launched();
+    } else if (any_stream) {
         static unsigned grid[64] = {0};
         int dev = 0;
         cudaGetDevice(&dev);
@@ -1303,6 +1644,7 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_stream<2>, kThreads, 0);
             grid[dev] = (unsigned)(device_sms() * (per_sm > 0 ? per_sm : 1));
         }
+        mark(hook, STAGE_STREAM);
         k_stream<2><<<grid[dev], kThreads, 0, s>>>(a);
         e = launched();
     }
@@ -1363,6 +1705,11 @@ cudaError_t launch_chain(int src, const ChainArgs &a, cudaStream_t s, const Laun
 cudaError_t launch_qk_norm(float *v, int rows, int width, int head, const float *w, float eps,
                            cudaStream_t s) {
     if (rows <= 0 || width / head == 0) return cudaSuccess;
+    const QkLaunch c = qk_launch_config(k_qk_norm_smem, width, head, rows);
+    if (c.warps) {
+        k_qk_norm_smem<<<c.grid, c.warps * 32, c.smem, s>>>(v, rows, width, head, w, eps, c.smf);
+        return launched();
+    }
     k_qk_norm<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(v, rows, width, head, w, eps);
     return launched();
 }
@@ -1379,13 +1726,21 @@ cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows,
 cudaError_t launch_add_rms_norm(const ChainArgs &a, cudaStream_t s) {
     if (a.rows <= 0) return cudaSuccess;
     if (a.dim % 8 != 0) return cudaErrorInvalidValue;
-    return launch_norm_pipe<SRC_X, true, true>(a, s);
+    return launch_norm_pipe<SRC_X, true, true, false>(a, s);
 }
 
 cudaError_t launch_qk_rope(float *q, float *k, int q_width, int kv_width, int rows, int head, const float *wq,
                            const float *wk, float eps, const int32_t *pos, const float *cos_t, const float *sin_t,
                            int max_pos, int interleaved, int *err, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
+    const bool whole = !interleaved || (q_width % head == 0 && kv_width % head == 0);
+    const QkLaunch c = whole ? qk_launch_config(k_qk_rope_smem, q_width > kv_width ? q_width : kv_width, head, rows)
+                             : QkLaunch{};
+    if (c.warps && ((q_width | kv_width) & 3) == 0) {
+        k_qk_rope_smem<<<c.grid, c.warps * 32, c.smem, s>>>(q, k, q_width, kv_width, rows, head, wq, wk, eps, pos,
+                                                           cos_t, sin_t, max_pos, interleaved, err, c.smf);
+        return launched();
+    }
     k_qk_rope<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(q, k, q_width, kv_width, rows, head, wq, wk,
                                                                           eps, pos, cos_t, sin_t, max_pos,
                                                                           interleaved, err);
@@ -1444,6 +1799,10 @@ cudaError_t launch_lfm2_conv_block(const float *bcx, const float *w, float *ring
 cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes, float *scales,
                                uint16_t *scales16, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
+    if (dim % 32 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)codes & 3) == 0) {
+        k_quantize_q8v<<<stream_grid((size_t)rows * dim), kThreads, 0, s>>>(x, rows, dim, codes, scales, scales16);
+        return launched();
+    }
     k_quantize_q8<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(x, rows, dim, codes, scales,
                                                                               scales16);
     return launched();

@@ -1,0 +1,317 @@
+"""Per-op and per-workload throughput of the backend (1 GPU).
+
+    python -m kernrt_b200.opbench [--reps N] [--json]
+
+Times every row op of the trait, the fused driver pairs, the fused chain on
+each benchmark workload and the single-row decode latency, with CUDA events on
+the backend's stream (inputs resident in HBM; working sets far above the
+126 MB L2 except where a row says otherwise).  GB/s is compulsory bytes over
+time; the fraction is against the measured copy bandwidth in
+MEASURED_PEAKS.json when present.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import time
+
+import numpy as np
+
+from . import BF16, Q8_0, CudaBackend, kernel_launches
+from . import workloads as W
+from .interop import as_torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def peak_gbs():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["hbm_gbs"])
+    except Exception:
+        return 6650.0
+
+
+class Bench:
+    def __init__(self, reps: int):
+        import torch
+
+        self.torch = torch
+        self.b = CudaBackend(0)
+        self.stream = torch.cuda.ExternalStream(self.b.stream(), device="cuda:0")
+        self.g = torch.Generator(device="cuda:0").manual_seed(0)
+        self.reps = reps
+        self.peak = peak_gbs()
+        self.rows = []
+
+    def fill(self, h, n, scale=1.0):
+        self.b.synchronize()
+        as_torch(self.b, h, (n,)).copy_(torch_randn(self, n) * scale)
+        self.torch.cuda.synchronize()
+
+    def buf(self, n, scale=1.0):
+        h = self.b.alloc(n)
+        self.fill(h, n, scale)
+        return h
+
+    def time(self, name, fn, nbytes, setup=None, note=""):
+        """Median device time per call.  Without a setup step the calls run back
+        to back between one pair of events, so host-side work per call (e.g.
+        staging host positions) overlaps the previous call's kernels; with one
+        (a device copy restoring an in-place input), each call is timed alone
+        and its host work overlaps that copy."""
+        torch = self.torch
+        for _ in range(3):
+            if setup:
+                setup()
+            fn()
+        self.b.synchronize()
+        n0 = kernel_launches()
+        times = []
+        if setup is None:
+            for _ in range(3):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(self.stream)
+                for _ in range(self.reps):
+                    fn()
+                self.b.flush()
+                e.record(self.stream)
+                e.synchronize()
+                times.append(s.elapsed_time(e) / self.reps)
+            calls = 3 * self.reps
+        else:
+            for _ in range(self.reps):
+                setup()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(self.stream)
+                fn()
+                self.b.flush()  # launch any op the backend holds for fusion
+                e.record(self.stream)
+                e.synchronize()
+                times.append(s.elapsed_time(e))
+            calls = self.reps
+        launches = (kernel_launches() - n0) / calls
+        ms = statistics.median(times)
+        gbs = nbytes / (ms / 1e3) / 1e9 if nbytes else None
+        row = {"name": name, "ms": ms, "ms_min": min(times), "gbs": gbs,
+               "frac": None if gbs is None else gbs / self.peak, "launches": launches, "note": note}
+        self.rows.append(row)
+        return row
+
+
+def torch_randn(bench, n):
+    return bench.torch.randn(n, device="cuda:0", generator=bench.g)
+
+
+def run(reps: int):
+    import torch
+
+    B = Bench(reps)
+    b = B.b
+    wl = W.SMOLLM2_17B_65K
+    R, H, Q, KV, I = wl.rows, wl.dim, wl.q_dim, wl.kv_dim, wl.hidden
+
+    # --- tables and weights
+    table = (torch.randn(wl.vocab, H, device="cuda:0", generator=B.g) * 0.02).to(torch.bfloat16)
+    b.prepare_embedding(BF16, table.view(torch.int16).cpu().numpy().view(np.uint16), None, wl.vocab, H)
+    del table
+    w = b.upload(np.ones(H, np.float32))
+    tokens = np.random.default_rng(1).integers(0, wl.vocab, R).astype(np.int32)
+    positions = wl.positions()
+
+    # --- a1 embed (coalesced per-row calls: one gather launch)
+    x, xb = b.alloc(R * H), b.alloc(R * H)
+
+    def embed_all():
+        for r in range(R):
+            b.embed(int(tokens[r]), x, r * H)
+
+    B.time("embed (65536 per-row calls, bf16 table)", embed_all, R * (2 * H + 4 * H),
+           note="host loop of 65536 calls included")
+
+    # --- a2 rms_norm (f32 x)
+    B.fill(x, R * H)
+    B.time("rms_norm 65536x2048", lambda: b.rms_norm(xb, x, w, R, H, 1e-5), R * 8 * H)
+
+    # --- fused driver pairs
+    o = B.buf(R * H)
+    x0 = B.buf(R * H)
+
+    def add_rms():
+        b.add_in_place(x, o, R * H)
+        b.rms_norm(xb, x, w, R, H, 1e-5)
+
+    B.time("add_in_place + rms_norm (fused)", add_rms, R * 16 * H, setup=lambda: b.copy(x0, 0, x, 0, R * H))
+    B.time("add_in_place 65536x2048", lambda: b.add_in_place(x, o, R * H), R * 12 * H,
+           setup=lambda: b.copy(x0, 0, x, 0, R * H))
+
+    def embed_rms():
+        embed_all()
+        b.rms_norm(xb, x, w, R, H, 1e-5)
+
+    B.time("embed x65536 + rms_norm (fused)", embed_rms, R * (2 * H + 8 * H),
+           note="host loop of 65536 calls included")
+
+    # --- a3/a4 qk_norm, rope and the fused triple (Qwen3 shape: 16x128 / 8x128)
+    qd, kd, hd = 2048, 1024, 128
+    q, k = B.buf(R * qd), B.buf(R * kd)
+    wq = b.upload(np.ones(hd, np.float32))
+    B.time("qk_norm q 65536x(16x128)", lambda: b.qk_norm(q, R, qd, hd, wq, 1e-6), R * 8 * qd)
+    B.time("rope q,k 65536x(16+8)x128", lambda: b.rope(q, k, qd, kd, R, positions, hd, 1e6, False),
+           R * 8 * (qd + kd))
+
+    def qk_rope():
+        b.qk_norm(q, R, qd, hd, wq, 1e-6)
+        b.qk_norm(k, R, kd, hd, wq, 1e-6)
+        b.rope(q, k, qd, kd, R, positions, hd, 1e6, False)
+
+    B.time("qk_norm q + qk_norm k + rope (fused)", qk_rope, R * 8 * (qd + kd))
+
+    # --- a5 silu_mul
+    g, u = B.buf(R * I), B.buf(R * I)
+    g0 = b.alloc(R * I)
+    b.copy(g, 0, g0, 0, R * I)
+    B.time("silu_mul 65536x8192", lambda: b.silu_mul(g, u, R * I), R * 12 * I,
+           setup=lambda: b.copy(g0, 0, g, 0, R * I))
+
+    # --- a7/a8 LFM2 conv (1024 rows x 1536, and 65536 rows for bandwidth)
+    for rows in (1024, 16384):
+        d = 1536
+        bcx, kern = B.buf(rows * 3 * d), B.buf(d * 3, 0.3)
+        h, co, cy, ring = b.alloc(rows * d), b.alloc(rows * d), b.alloc(rows * d), b.alloc(2 * d)
+        B.time(f"mul (B*x) {rows}x1536", lambda: [b.mul(h, r * d, bcx, r * 3 * d, bcx, r * 3 * d + 2 * d, d)
+                                                   for r in range(rows)], rows * 12 * d,
+               note="per-row calls (host loop included), batched into one launch")
+        B.time(f"conv_prefill {rows}x1536 k3", lambda: b.conv_prefill(co, h, kern, rows, d, 3), rows * 8 * d)
+        B.time(f"lfm2_conv_block {rows}x1536 (fused)", lambda: b.lfm2_conv_block(bcx, kern, ring, cy, rows, d, 3),
+               rows * 16 * d)
+
+    # --- a9 conv_decode latency, a11 Q8
+    d = 1536
+    xr, kern, st = B.buf(d), B.buf(d * 3), B.buf(2 * d)
+    B.time("conv_decode 1x1536 (latency)", lambda: b.conv_decode(xr, xr, kern, st, d, 3), None)
+    qd8 = 1024
+    xq = B.buf(R * qd8)
+    nb = qd8 // 32
+    c8, s8, h8 = b.alloc_bytes(R * qd8), b.alloc_bytes(R * nb * 4), b.alloc_bytes(R * nb * 2)
+    wq8 = b.upload(np.ones(qd8, np.float32))
+    B.time("quantize_q8_0 65536x1024", lambda: b.quantize_q8_0(xq, R, qd8, c8, s8, h8), R * (4 * qd8 + qd8 + 6 * nb))
+    B.time("rms_norm_q8_0 65536x1024 (fused)", lambda: b.rms_norm_q8_0(xq, wq8, R, qd8, 1e-6, c8, s8, h8),
+           R * (4 * qd8 + qd8 + 6 * nb))
+
+    # --- the chain on every workload
+    for wk in (W.SMOLLM2_135M, W.SMOLLM2_17B_PREFILL, W.QWEN3_06B_Q8, W.LFM2_700M, W.SMOLLM2_17B_65K):
+        chain_time(B, wk)
+
+    # --- decode latency: one row through the trait ops, read() each step
+    decode_latency(B)
+    return B
+
+
+def chain_time(B, wk):
+    import torch
+
+    b = B.b
+    R = wk.rows
+    if wk.storage == "bf16":
+        t = (torch.randn(wk.vocab, wk.dim, device="cuda:0", generator=B.g) * 0.02).to(torch.bfloat16)
+        b.prepare_embedding(BF16, t.view(torch.int16).cpu().numpy().view(np.uint16), None, wk.vocab, wk.dim)
+    elif wk.storage == "q8_0":
+        rng = np.random.default_rng(2)
+        codes = rng.integers(-127, 128, size=(wk.vocab, wk.dim), dtype=np.int8)
+        sc = rng.uniform(1e-4, 1e-2, size=(wk.vocab, wk.dim // 32)).astype(np.float32)
+        b.prepare_embedding(Q8_0, codes, sc, wk.vocab, wk.dim)
+    h = {n: B.buf(R * n_) for n, n_ in [("q", wk.q_dim), ("k", wk.kv_dim), ("gate", wk.hidden), ("up", wk.hidden),
+                                         ("resid", wk.dim)]}
+    h["gate0"] = b.alloc(R * wk.hidden)
+    b.copy(h["gate"], 0, h["gate0"], 0, R * wk.hidden)
+    h["x"] = B.buf(R * wk.dim) if wk.storage == "none" else b.alloc(R * wk.dim)
+    h["xb"] = b.alloc(R * wk.dim)
+    h["w_att"] = b.upload(np.ones(wk.dim, np.float32))
+    kw = {}
+    if wk.storage != "none":
+        kw["tokens"] = b.upload_bytes(np.random.default_rng(3).integers(0, wk.vocab, R).astype(np.int32))
+    kw["positions"] = b.upload_bytes(wk.positions())
+    if wk.qk_norm:
+        kw["w_q"] = b.upload(np.ones(wk.head, np.float32))
+        kw["w_k"] = b.upload(np.ones(wk.head, np.float32))
+    nb = (wk.dim + 31) // 32
+    if wk.final_q8:
+        kw.update(w_final=b.upload(np.ones(wk.dim, np.float32)), codes=b.alloc_bytes(R * nb * 32),
+                  scales=b.alloc_bytes(R * nb * 4), scales_f16=b.alloc_bytes(R * nb * 2))
+    b.rope_prepare(wk.theta, wk.head, wk.seq_len + wk.pos0)
+    args = dict(rows=R, dim=wk.dim, q_dim=wk.q_dim, kv_dim=wk.kv_dim, hidden=wk.hidden, head_size=wk.head,
+                eps=wk.eps, theta=wk.theta, final_eps=wk.eps, x=h["x"], xb=h["xb"], w_att=h["w_att"],
+                q=h["q"], k=h["k"], gate=h["gate"], up=h["up"], resid=h["resid"], **kw)
+    x0 = None
+    if wk.storage == "none":
+        x0 = b.alloc(R * wk.dim)
+        b.copy(h["x"], 0, x0, 0, R * wk.dim)
+
+    def setup():
+        b.copy(h["gate0"], 0, h["gate"], 0, R * wk.hidden)
+        if x0 is not None:
+            b.copy(x0, 0, h["x"], 0, R * wk.dim)
+
+    B.time(f"chain: {wk.name} ({R} rows)", lambda: b.layer_chain(**args), R * wk.bytes_per_row(), setup=setup,
+           note="working set below L2" if R * wk.bytes_per_row() < 126e6 else "")
+
+
+def decode_latency(B):
+    """configs[1] decode: one token at position 511 through the row ops of a
+    SmolLM2-1.7B block as the driver calls them, with a read() per step."""
+    import torch
+
+    b = B.b
+    wk = W.SMOLLM2_17B_DECODE
+    t = (torch.randn(wk.vocab, wk.dim, device="cuda:0", generator=B.g) * 0.02).to(torch.bfloat16)
+    b.prepare_embedding(BF16, t.view(torch.int16).cpu().numpy().view(np.uint16), None, wk.vocab, wk.dim)
+    x, xb = b.alloc(wk.dim), b.alloc(wk.dim)
+    q, k, o = B.buf(wk.q_dim), B.buf(wk.kv_dim), B.buf(wk.dim)
+    g, u = B.buf(wk.hidden), B.buf(wk.hidden)
+    w = b.upload(np.ones(wk.dim, np.float32))
+    out = np.empty(wk.dim, np.float32)
+    samples = []
+    for i in range(300 + 20):
+        t0 = time.perf_counter()
+        b.embed(7, x, 0)
+        b.rms_norm(xb, x, w, 1, wk.dim, wk.eps)
+        b.rope(q, k, wk.q_dim, wk.kv_dim, 1, [511], wk.head, wk.theta, False)
+        b.add_in_place(x, o, wk.dim)
+        b.rms_norm(xb, x, w, 1, wk.dim, wk.eps)
+        b.silu_mul(g, u, wk.hidden)
+        b.add_in_place(x, o, wk.dim)
+        b.read_into(x, out)
+        if i >= 20:
+            samples.append((time.perf_counter() - t0) * 1e6)
+    samples.sort()
+    B.rows.append({"name": "decode step, 1 row (configs[1], pos 511): row ops + read()", "ms": None,
+                   "us_p10": samples[len(samples) // 10], "us_median": samples[len(samples) // 2], "gbs": None,
+                   "frac": None, "launches": None, "note": "host wall clock, 300 samples"})
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--reps", type=int, default=10)
+    p.add_argument("--json", action="store_true")
+    args = p.parse_args()
+    B = run(args.reps)
+    if args.json:
+        for r in B.rows:
+            print(json.dumps(r))
+        return
+    print(f"| op | ms (median) | GB/s | of {B.peak:.0f} GB/s | launches | note |")
+    print("|---|---:|---:|---:|---:|---|")
+    for r in B.rows:
+        if r.get("ms") is None:
+            print(f"| {r['name']} | p10 {r['us_p10']:.1f} us, median {r['us_median']:.1f} us | | | | {r['note']} |")
+            continue
+        gbs = "" if r["gbs"] is None else f"{r['gbs']:.0f}"
+        frac = "" if r["frac"] is None else f"{r['frac']:.3f}"
+        print(f"| {r['name']} | {r['ms']:.4f} | {gbs} | {frac} | {r['launches']:.0f} | {r['note']} |")
+
+
+if __name__ == "__main__":
+    main()

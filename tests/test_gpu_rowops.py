@@ -297,3 +297,18 @@ def test_rms_norm_q8_0_fused(gpu, oracle, rows, dim, eps):
     assert_bits_equal(gpu.read_bytes(hc, rows * nb * 32, np.int8).reshape(rows, -1), wc, "codes")
     assert_bits_equal(gpu.read_bytes(hs, rows * nb * 4, np.float32).reshape(rows, -1), ws, "scales")
     assert_bits_equal(gpu.read_bytes(hh, rows * nb * 2, np.uint16).reshape(rows, -1), wh, "f16")
+
+
+def test_embed_many_calls_grow_the_staging_ring(gpu, oracle):
+    """300 000 deferred embeds flush as one gather whose ids and offsets
+    (3.6 MB) outgrow the initial staging ring: the grown ring must hold them
+    and the old one stay valid until the next barrier."""
+    vocab, dim, n = 97, 8, 300_000
+    table = _data.bf16_table(vocab, dim, 77)
+    gpu.prepare_embedding(oracle.BF16, table, None, vocab, dim)
+    toks = _data.tokens(n, vocab, 78)
+    out = gpu.alloc(n * dim)
+    for r, t in enumerate(toks.tolist()):
+        gpu.embed(t, out, r * dim)
+    got = gpu.read(out, n * dim).reshape(n, dim)
+    assert_bits_equal(got, oracle.embed_rows(oracle.BF16, table, None, vocab, dim, toks), "embed x300000")
