@@ -791,31 +791,69 @@ __global__ void __launch_bounds__(kThreads, 3) k_chain(ChainArgs a, ChainLayout 
     }
 }
 
+// Four consecutive values of row `row`'s source straight from global memory
+// (the f32 x row, or the gathered embedding row in its stored format), as
+// decode_staged reads them from a staged slot; nullptr-row for a bad token.
+template <int SRC>
+__device__ __forceinline__ void decode_global4(const ChainArgs &a, const float *xsrc, int row, int c, float *v) {
+    if constexpr (SRC == SRC_X) {
+        const float4 t = ld4(xsrc + (size_t)row * a.dim + c);
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+        const int tok = a.tokens[row];
+        if ((unsigned)tok >= (unsigned)a.vocab) {
+            v[0] = v[1] = v[2] = v[3] = 0.0f;
+            return;
+        }
+        if constexpr (SRC == SRC_BF16) {
+            const uint2 t = __ldg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(a.table) +
+                                                                  (size_t)tok * a.dim + c));
+            v[0] = bf16f(t.x & 0xffffu); v[1] = bf16f(t.x >> 16);
+            v[2] = bf16f(t.y & 0xffffu); v[3] = bf16f(t.y >> 16);
+        } else if constexpr (SRC == SRC_Q8) {
+            const uint32_t t = __ldg(reinterpret_cast<const uint32_t *>(static_cast<const int8_t *>(a.table) +
+                                                                        (size_t)tok * a.dim + c));
+            const float s = __ldg(a.tscales + (size_t)tok * (a.dim >> 5) + (c >> 5));
+#pragma unroll
+            for (int b = 0; b < 4; ++b) v[b] = mul_rn((float)(int8_t)((t >> (8 * b)) & 0xffu), s);
+        } else {
+            const float4 t = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(a.table) +
+                                                                    (size_t)tok * a.dim + c));
+            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        }
+    }
+}
+
 // The norm stage alone (embed/x -> RMSNorm -> xb, residual add), as a
-// persistent, warp-specialised pipeline over groups of G rows held in three
+// persistent, warp-specialised pipeline over groups of G rows held in NS
 // shared-memory slots.  In iteration i of a CTA:
-//   warp 1      stages group i+1 into slot (i+1)%3 with cp.async,
-//   warp 0      sums group i (slot i%3): lane r runs row r's squares left to
-//               right, the reference's order,
-//   warps 2..7  write group i-1 (slot (i-1)%3): xb = w*(scale*x), x + resid.
-// The three slots are always distinct, and one __syncthreads per iteration
-// hands each slot to its next role, so the serial sums hide behind the HBM
-// traffic of the neighbouring groups.
+//   warps 1..NL stage group i+1 into slot (i+1)%NS (cp.async, or through
+//               registers for PRE_ADD),
+//   warp 0      sums group i out of slot i%NS: lane r runs row r's squares
+//               left to right, the reference's order (reference.rs:167-170),
+//   warps NL+1.. write group i-1: xb = w*(scale*x), x + resid.
+// One __syncthreads per iteration hands each slot to its next role.
 //
-// PRE_ADD (f32 x only) is the driver's add_in_place -> rms_norm pair
-// (llama.rs:762-765, 769-740): the residual is added first, x = x + resid is
-// written back by the loaders (warps 1..3) as they stage it, and the norm is
-// taken of the sum; the writers then store only xb.
+// The writers take group i-1's values either from its slot (RR false: three
+// slots, so staging, summing and writing use distinct ones) or again from
+// global memory (RR true: two slots), where the rows are still L2-resident
+// from the staging one iteration earlier.  RR frees a slot, so a slot holds
+// 1.5x the rows and more exact chains run per SM; it pays where the re-read
+// is one contiguous f32 row (rms_norm of x), not where it is a token gather.
 //
+// PRE_ADD (f32 x) is the driver's add_in_place -> rms_norm pair (llama.rs:
+// 762-765, 769-740): the loaders add the residual while staging, write
+// x = x + resid back, and the norm is taken of the sum; writers store xb.
 // FQ is the final RMSNorm fused with Q8_0 quantisation (quant.rs:856-874): the
 // summing lanes also run the sum of the row that gets quantised (x, or
 // x + resid with the residual rows staged beside x), and the writers emit the
 // int8 codes and block scales, eight lanes per 32-element block.
-template <int SRC, bool VEC, bool PRE_ADD, bool FQ>
+template <int SRC, bool VEC, bool PRE_ADD, bool FQ, bool RR>
 __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLayout L) {
     static_assert(!PRE_ADD || (SRC == SRC_X && VEC), "the pre-add form stages f32 rows with vector loads");
     static_assert(!FQ || (VEC && !PRE_ADD), "the quantising form needs whole 32-element blocks");
     constexpr int NL = PRE_ADD ? 3 : 1;  // loader warps 1..NL; writers NL+1..7
+    constexpr int NS = RR ? 2 : 3;       // slots
     extern __shared__ __align__(16) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int dim = a.dim;
@@ -823,18 +861,19 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
     const int ngroups = (a.rows + G - 1) / G;
     const int nmine = (int)blockIdx.x < ngroups ? (ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
     const size_t slot_bytes = (size_t)G * (L.xstride + L.rstride);
-    float *scales = reinterpret_cast<float *>(smem + 3 * slot_bytes);  // [3][64]: s1[32] s2[32]
+    float *scales = reinterpret_cast<float *>(smem + NS * slot_bytes);  // [NS][64]: s1[32] s2[32]
     const bool fq_resid = FQ && a.resid != nullptr;
     const int rb = src_row_bytes<SRC>(dim);
+    // The rows the writers re-read: the loaders' x + resid for PRE_ADD.
+    const float *xsrc = PRE_ADD ? a.x_out : a.x_in;
 
     auto first_row = [&](int i) { return (int)(blockIdx.x + (unsigned)i * gridDim.x) * G; };
-    auto slot = [&](int i) { return smem + (size_t)(i % 3) * slot_bytes; };
+    auto slot = [&](int i) { return smem + (size_t)(i % NS) * slot_bytes; };
 
     auto load = [&](int i) {  // warps 1..NL
         const int r0 = first_row(i), g = min(G, a.rows - r0);
         unsigned char *base = slot(i);
         if constexpr (PRE_ADD) {
-            // x + resid, staged and written back, U float4 pairs in flight.
             constexpr int U = 4;
             const int lt = tid - 32, nlt = NL * 32;
             const int n4 = dim >> 2, total = g * n4;
@@ -857,7 +896,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
                     const float4 xo = make_float4(add_rn(xv[k].x, rv[k].x), add_rn(xv[k].y, rv[k].y),
                                                   add_rn(xv[k].z, rv[k].z), add_rn(xv[k].w, rv[k].w));
                     *reinterpret_cast<float4 *>(base + (size_t)r * L.xstride + 4 * c) = xo;
-                    st4(a.x_out + (size_t)(r0 + r) * dim + c, xo);
+                    // a normal store: the writers re-read it from L2 next iteration
+                    *reinterpret_cast<float4 *>(a.x_out + (size_t)(r0 + r) * dim + c) = xo;
                 }
             }
             return;
@@ -901,11 +941,13 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
         const int r0 = first_row(i), g = min(G, a.rows - r0);
         if (lane >= g) return;
         const unsigned char *row = slot(i) + (size_t)lane * L.xstride;
+        float *sc = scales + (i % NS) * 64;
         float ss = 0.0f;
         if constexpr (FQ) {
             const float *rrow =
                 reinterpret_cast<const float *>(slot(i) + (size_t)G * L.xstride + (size_t)lane * L.rstride);
             float ss2 = 0.0f;
+#pragma unroll 4
             for (int c = 0; c < dim; c += 8) {
                 float v[8];
                 decode_staged<SRC, 8>(row, dim, c, v);
@@ -916,10 +958,11 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
                     ss2 = add_rn(ss2, mul_rn(xo, xo));
                 }
             }
-            scales[(i % 3) * 64 + lane] = rms_scale(ss, (float)dim, a.eps);
-            scales[(i % 3) * 64 + 32 + lane] = rms_scale(ss2, (float)dim, a.final_eps);
+            sc[lane] = rms_scale(ss, (float)dim, a.eps);
+            sc[32 + lane] = rms_scale(ss2, (float)dim, a.final_eps);
             return;
         } else if constexpr (VEC) {
+#pragma unroll 4
             for (int c = 0; c < dim; c += 8) {
                 float v[8];
                 decode_staged<SRC, 8>(row, dim, c, v);
@@ -933,13 +976,19 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
                 ss = add_rn(ss, mul_rn(v[0], v[0]));
             }
         }
-        scales[(i % 3) * 64 + lane] = rms_scale(ss, (float)dim, a.eps);
+        sc[lane] = rms_scale(ss, (float)dim, a.eps);
+    };
+
+    // Four values of x (staged or re-read) at (group row r, column c).
+    auto fetch4 = [&](const unsigned char *base, int r0, int r, int c, float *v) {
+        if constexpr (RR) decode_global4<SRC>(a, xsrc, r0 + r, c, v);
+        else decode_staged<SRC, 4>(base + (size_t)r * L.xstride, dim, c, v);
     };
 
     auto write = [&](int i) {  // warps NL+1..7
         const int r0 = first_row(i), g = min(G, a.rows - r0);
         const unsigned char *base = slot(i);
-        const float *sc = scales + (i % 3) * 64;
+        const float *sc = scales + (i % NS) * 64;
         const int wt = tid - 32 * (NL + 1), nwt = blockDim.x - 32 * (NL + 1);
         if constexpr (FQ) {
             // 8 lanes x float4 per 32-element block; the loop is warp-uniform
@@ -952,10 +1001,10 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
                 const int blk = ok ? idx >> 3 : 0, sub = idx & 7;
                 const int r = blk / nb, b = blk - r * nb, c = b * 32 + sub * 4;
                 const int row = r0 + r;
-                float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 if (ok) {
-                    decode_staged<SRC, 4>(base + (size_t)r * L.xstride, dim, c, v);
+                    float v[4];
+                    fetch4(base, r0, r, c, v);
                     const size_t o = (size_t)row * dim + c;
                     if (a.xb) {
                         const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
@@ -965,8 +1014,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
                     }
                     float4 xo = make_float4(v[0], v[1], v[2], v[3]);
                     if (fq_resid) {
-                        const float4 rr = *reinterpret_cast<const float4 *>(base + (size_t)G * L.xstride +
-                                                                            (size_t)r * L.rstride + 4 * c);
+                        const float4 rr = RR ? ld4(a.resid + o)
+                                             : *reinterpret_cast<const float4 *>(base + (size_t)G * L.xstride +
+                                                                                (size_t)r * L.rstride + 4 * c);
                         xo = make_float4(add_rn(v[0], rr.x), add_rn(v[1], rr.y), add_rn(v[2], rr.z), add_rn(v[3], rr.w));
                     }
                     if (a.x_out) st4(a.x_out + o, xo);
@@ -996,16 +1046,18 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
             return;
         }
         if constexpr (VEC) {
-            constexpr int U = 8;
+            constexpr int U = 4;
             const int n4 = dim >> 2, total = g * n4;
             for (int i0 = wt; i0 < total; i0 += U * nwt) {
+                float v[U][4];
                 float4 rr[U];
 #pragma unroll
                 for (int k = 0; k < U; ++k) {
                     const int idx = i0 + k * nwt;
-                    if (!PRE_ADD && idx < total && a.resid && a.x_out) {
+                    if (idx < total) {
                         const int r = idx / n4, c = (idx - r * n4) << 2;
-                        rr[k] = ld4(a.resid + (size_t)(r0 + r) * dim + c);
+                        fetch4(base, r0, r, c, v[k]);
+                        if (!PRE_ADD && a.resid && a.x_out) rr[k] = ld4(a.resid + (size_t)(r0 + r) * dim + c);
                     }
                 }
 #pragma unroll
@@ -1014,19 +1066,17 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
                     if (idx >= total) continue;
                     const int r = idx / n4, c = (idx - r * n4) << 2;
                     const size_t o = (size_t)(r0 + r) * dim + c;
-                    float v[4];
-                    decode_staged<SRC, 4>(base + (size_t)r * L.xstride, dim, c, v);
                     if (a.xb) {
                         const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
                         const float s = sc[r];
-                        st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[0])), mul_rn(w.y, mul_rn(s, v[1])),
-                                                  mul_rn(w.z, mul_rn(s, v[2])), mul_rn(w.w, mul_rn(s, v[3]))));
+                        st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[k][0])), mul_rn(w.y, mul_rn(s, v[k][1])),
+                                                  mul_rn(w.z, mul_rn(s, v[k][2])), mul_rn(w.w, mul_rn(s, v[k][3]))));
                     }
                     if (!PRE_ADD && a.x_out) {
-                        float4 xo = make_float4(v[0], v[1], v[2], v[3]);
+                        float4 xo = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
                         if (a.resid)
-                            xo = make_float4(add_rn(v[0], rr[k].x), add_rn(v[1], rr[k].y), add_rn(v[2], rr[k].z),
-                                             add_rn(v[3], rr[k].w));
+                            xo = make_float4(add_rn(v[k][0], rr[k].x), add_rn(v[k][1], rr[k].y),
+                                             add_rn(v[k][2], rr[k].z), add_rn(v[k][3], rr[k].w));
                         st4(a.x_out + o, xo);
                     }
                 }
@@ -1035,10 +1085,24 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
             for (int idx = wt; idx < g * dim; idx += nwt) {
                 const int r = idx / dim, c = idx - r * dim;
                 const size_t o = (size_t)(r0 + r) * dim + c;
-                float v[1];
-                decode_staged<SRC, 1>(base + (size_t)r * L.xstride, dim, c, v);
-                if (a.xb) a.xb[o] = mul_rn(a.w_att[c], mul_rn(sc[r], v[0]));
-                if (a.x_out) a.x_out[o] = a.resid ? add_rn(v[0], a.resid[o]) : v[0];
+                float v;
+                if constexpr (!RR) {
+                    float t[1];
+                    decode_staged<SRC, 1>(base + (size_t)r * L.xstride, dim, c, t);
+                    v = t[0];
+                } else if constexpr (SRC == SRC_X) {
+                    v = xsrc[o];
+                } else {
+                    const int tok = a.tokens[r0 + r];
+                    if ((unsigned)tok >= (unsigned)a.vocab) v = 0.0f;
+                    else if constexpr (SRC == SRC_BF16) v = bf16f(static_cast<const uint16_t *>(a.table)[(size_t)tok * dim + c]);
+                    else if constexpr (SRC == SRC_Q8)
+                        v = mul_rn((float)static_cast<const int8_t *>(a.table)[(size_t)tok * dim + c],
+                                   a.tscales[(size_t)tok * (dim >> 5) + (c >> 5)]);
+                    else v = static_cast<const float *>(a.table)[(size_t)tok * dim + c];
+                }
+                if (a.xb) a.xb[o] = mul_rn(a.w_att[c], mul_rn(sc[r], v));
+                if (a.x_out) a.x_out[o] = a.resid ? add_rn(v, a.resid[o]) : v;
             }
         }
     };
@@ -1354,6 +1418,120 @@ __global__ void __launch_bounds__(kThreads) k_lfm2_conv_block(const float *__res
     }
 }
 
+// The row-tiled forms of the two convolutions for the kernel sizes the
+// models use (K = 2..4).  A thread owns V adjacent channels over RT
+// consecutive rows: it loads the K-1 halo rows and its RT rows once, all
+// loads issued before any arithmetic, then runs each output's taps in the
+// reference's order from registers.  Channels are the fastest-varying thread
+// index, so a warp's loads of one row are contiguous, and the halo rows a
+// tile re-reads were fetched by its neighbour tile moments earlier (L2).
+template <int V>
+__device__ __forceinline__ void ldv(const float *p, float *v) {
+    if constexpr (V == 4) {
+        const float4 t = __ldg(reinterpret_cast<const float4 *>(p));
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+        v[0] = __ldg(p);
+    }
+}
+template <int V>
+__device__ __forceinline__ void stv(float *p, const float *v) {
+    if constexpr (V == 4) *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    else p[0] = v[0];
+}
+
+// reference.rs:490-503 conv_rows.
+template <int K, int V, int RT>
+__global__ void __launch_bounds__(kThreads) k_conv_prefill_tiled(float *__restrict__ out,
+                                                                 const float *__restrict__ x,
+                                                                 const float *__restrict__ w, int rows,
+                                                                 int dim) {
+    const int ncg = dim / V;
+    const unsigned t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int tile = (int)(t / (unsigned)ncg), c = (int)(t - (unsigned)tile * ncg) * V;
+    const int r0 = tile * RT;
+    if (r0 >= rows) return;
+    float wk[V][K];
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+#pragma unroll
+        for (int j = 0; j < K; ++j) wk[v][j] = __ldg(w + (size_t)(c + v) * K + j);
+    // xs[q] holds row r0 - (K-1) + q.
+    float xs[RT + K - 1][V];
+#pragma unroll
+    for (int q = 0; q < RT + K - 1; ++q) {
+        const int h = r0 - (K - 1) + q;
+        if (h >= 0 && h < rows) ldv<V>(x + (size_t)h * dim + c, xs[q]);
+    }
+#pragma unroll
+    for (int q = 0; q < RT; ++q) {
+        const int r = r0 + q;
+        if (r >= rows) break;
+        float o[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < K; ++j)
+                if (r - (K - 1) + j >= 0) acc = add_rn(acc, mul_rn(wk[v][j], xs[q + j][v]));
+            o[v] = acc;
+        }
+        stv<V>(out + (size_t)r * dim + c, o);
+    }
+}
+
+// lfm2.rs:584-624, row-tiled: h = B*x for the tile's rows and its halo, the
+// taps in order, cy = C*co, and the last k-1 rows of h into the ring.
+template <int K, int V, int RT>
+__global__ void __launch_bounds__(kThreads) k_lfm2_conv_block_tiled(const float *__restrict__ bcx,
+                                                                    const float *__restrict__ w,
+                                                                    float *__restrict__ ring,
+                                                                    float *__restrict__ cy, int rows, int dim) {
+    const int ncg = dim / V;
+    const unsigned t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int tile = (int)(t / (unsigned)ncg), c = (int)(t - (unsigned)tile * ncg) * V;
+    const int r0 = tile * RT;
+    if (r0 >= rows) return;
+    const size_t w3 = (size_t)3 * dim;
+    float wk[V][K];
+#pragma unroll
+    for (int v = 0; v < V; ++v)
+#pragma unroll
+        for (int j = 0; j < K; ++j) wk[v][j] = __ldg(w + (size_t)(c + v) * K + j);
+    float bs[RT + K - 1][V], xs[RT + K - 1][V], cs[RT][V];
+#pragma unroll
+    for (int q = 0; q < RT + K - 1; ++q) {
+        const int h = r0 - (K - 1) + q;
+        if (h >= 0 && h < rows) {
+            ldv<V>(bcx + (size_t)h * w3 + c, bs[q]);
+            ldv<V>(bcx + (size_t)h * w3 + 2 * dim + c, xs[q]);
+        }
+        if (q >= K - 1 && h < rows) ldv<V>(bcx + (size_t)h * w3 + dim + c, cs[q - (K - 1)]);
+    }
+    float hs[RT + K - 1][V];
+#pragma unroll
+    for (int q = 0; q < RT + K - 1; ++q)
+#pragma unroll
+        for (int v = 0; v < V; ++v) hs[q][v] = mul_rn(bs[q][v], xs[q][v]);
+    const int take = min(rows, K - 1);
+#pragma unroll
+    for (int q = 0; q < RT; ++q) {
+        const int r = r0 + q;
+        if (r >= rows) break;
+        float o[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            float acc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < K; ++j)
+                if (r - (K - 1) + j >= 0) acc = add_rn(acc, mul_rn(wk[v][j], hs[q + j][v]));
+            o[v] = mul_rn(cs[q][v], acc);
+        }
+        stv<V>(cy + (size_t)r * dim + c, o);
+        if (r >= rows - take) stv<V>(ring + (size_t)(K - 1 - take + (r - (rows - take))) * dim + c, hs[q + K - 1]);
+    }
+}
+
 // quant.rs:856-874 per row: one warp per row, lane l holds element 32b+l.
 __global__ void __launch_bounds__(kThreads) k_quantize_q8(const float *__restrict__ x, int rows, int dim,
                                                           int8_t *codes, float *scales,
@@ -1379,41 +1557,46 @@ __global__ void __launch_bounds__(kThreads) k_quantize_q8(const float *__restric
     }
 }
 
-// The same quantisation for rows of whole 32-element blocks: eight lanes per
-// block, four values per lane, the block amax over the 8-lane group (the loop
-// is warp-uniform so every lane reaches the shuffles), codes stored four at a
-// time.
-__global__ void __launch_bounds__(kThreads) k_quantize_q8v(const float *__restrict__ x, int rows, int dim,
+// The same quantisation for rows of whole 32-element blocks.  With dim a
+// multiple of 32 the blocks of all rows are contiguous, so float4 item i
+// holds elements 4i..4i+3 of block i/8 and its codes go to bytes 4i..4i+3:
+// the kernel is one flat stream with no row arithmetic.  Eight lanes per
+// block, the block amax over the 8-lane group (the loop is warp-uniform so
+// every lane reaches the shuffles); each lane loads U items before any
+// arithmetic, so U loads per lane are in flight.
+template <int U>
+__global__ void __launch_bounds__(kThreads) k_quantize_q8v(const float *__restrict__ x, size_t items,
                                                            int8_t *codes, float *scales, uint16_t *scales16) {
-    const int nb = dim >> 5;
-    const long long total = (long long)rows * nb * 8;
-    const int lane = threadIdx.x & 31;
-    const long long gt = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-    const long long nt = (long long)gridDim.x * blockDim.x;
-    for (long long base = gt - lane; base < total; base += nt) {
-        const long long idx = base + lane;
-        const bool ok = idx < total;
-        const long long blk = ok ? idx >> 3 : 0;
-        const int sub = (int)(idx & 7);
-        const long long row = blk / nb;
-        const int b = (int)(blk - row * nb), c = b * 32 + sub * 4;
-        const float4 y = ok ? ld4(x + row * dim + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        float am = fmaxf(fmaxf(fmaxf(0.0f, fabsf(y.x)), fmaxf(0.0f, fabsf(y.y))),
-                         fmaxf(fmaxf(0.0f, fabsf(y.z)), fmaxf(0.0f, fabsf(y.w))));
-        am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
-        am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
-        am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
-        if (!ok) continue;
-        const float d = div_rn(am, 127.0f);
-        const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
-        const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y.x, inv)) |
-                                ((uint32_t)(uint8_t)q8_code(mul_rn(y.y, inv)) << 8) |
-                                ((uint32_t)(uint8_t)q8_code(mul_rn(y.z, inv)) << 16) |
-                                ((uint32_t)(uint8_t)q8_code(mul_rn(y.w, inv)) << 24);
-        *reinterpret_cast<uint32_t *>(codes + row * nb * 32 + c) = packed;
-        if (sub == 0) {
-            scales[row * nb + b] = d;
-            if (scales16) scales16[row * nb + b] = f16_bits(d);
+    const unsigned lane = threadIdx.x & 31;
+    const size_t warp0 = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+    const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
+    for (size_t base = warp0 * 32 * U; base < items; base += nwarps * 32 * U) {
+        float4 y[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const size_t idx = base + 32 * k + lane;
+            y[k] = idx < items ? ld4(x + 4 * idx) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const size_t idx = base + 32 * k + lane;
+            float am = fmaxf(fmaxf(fmaxf(0.0f, fabsf(y[k].x)), fmaxf(0.0f, fabsf(y[k].y))),
+                             fmaxf(fmaxf(0.0f, fabsf(y[k].z)), fmaxf(0.0f, fabsf(y[k].w))));
+            am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
+            am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
+            am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
+            if (idx >= items) continue;
+            const float d = div_rn(am, 127.0f);
+            const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+            const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y[k].x, inv)) |
+                                    ((uint32_t)(uint8_t)q8_code(mul_rn(y[k].y, inv)) << 8) |
+                                    ((uint32_t)(uint8_t)q8_code(mul_rn(y[k].z, inv)) << 16) |
+                                    ((uint32_t)(uint8_t)q8_code(mul_rn(y[k].w, inv)) << 24);
+            reinterpret_cast<uint32_t *>(codes)[idx] = packed;
+            if ((idx & 7) == 0) {
+                scales[idx >> 3] = d;
+                if (scales16) scales16[idx >> 3] = f16_bits(d);
+            }
         }
     }
 }
@@ -1552,25 +1735,28 @@ QkLaunch qk_launch_config(K kern, int width, int head, int rows) {
 }
 
 // The norm stage as the persistent pipeline: rows per group from the shared
-// memory that lets two CTAs share an SM (three slots each), fewer when the
-// rows would give a CTA under eight groups.
+// memory that lets two CTAs share an SM, fewer when the rows would give a CTA
+// under eight groups.  Contiguous f32 rows are re-read by the writers (two
+// slots); gathered or quantising rows are written from their slot (three).
 template <int SRC, bool VEC, bool PRE_ADD = false, bool FQ = false>
 cudaError_t launch_norm_pipe(const ChainArgs &a, cudaStream_t s) {
+    constexpr bool RR = SRC == SRC_X && !FQ;
+    constexpr int NS = RR ? 2 : 3;
     ChainLayout L{};
     const int rb = SRC == SRC_BF16 ? a.dim * 2 : (SRC == SRC_Q8 ? a.dim : a.dim * 4);
     L.xstride = align16(rb) + (SRC == SRC_Q8 ? align16((a.dim / 32) * 4) : 0) + 16;
     L.rstride = (FQ && a.resid) ? align16(a.dim * 4) + 16 : 0;
-    const size_t budget = 110 * 1024 - 3 * 64 * sizeof(float);
-    int G = (int)(budget / (3 * (size_t)(L.xstride + L.rstride)));
+    const size_t budget = 110 * 1024 - NS * 64 * sizeof(float);
+    int G = (int)(budget / (NS * (size_t)(L.xstride + L.rstride)));
     if (G > 32) G = 32;
     if (G < 1) G = 1;
     const int sms = device_sms();
     const long want = ((long)a.rows + (long)sms * 2 * 8 - 1) / ((long)sms * 2 * 8);
     if (want < G) G = (int)(want > 0 ? want : 1);
     L.G = G;
-    L.smem = 3 * (size_t)G * (L.xstride + L.rstride) + 3 * 64 * sizeof(float);
+    L.smem = NS * (size_t)G * (L.xstride + L.rstride) + NS * 64 * sizeof(float);
     if (L.smem > 227 * 1024) return cudaErrorInvalidValue;
-    auto kern = k_norm_pipe<SRC, VEC, PRE_ADD, FQ>;
+    auto kern = k_norm_pipe<SRC, VEC, PRE_ADD, FQ, RR>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
@@ -1774,9 +1960,30 @@ cudaError_t launch_mul(float *o, const float *a, const float *b, size_t n, bool 
     return launched();
 }
 
+// The row-tiled kernels for K = 2..4 (float4 channels when dim and the
+// pointers allow), the per-element kernel for other sizes.
+template <int K, int V, int RT, typename Kern, typename... Args>
+cudaError_t launch_conv_tiled(Kern kern, int rows, int dim, cudaStream_t s, Args... args) {
+    const size_t threads = (size_t)(dim / V) * (size_t)((rows + RT - 1) / RT);
+    kern<<<grid_for(threads, kThreads), kThreads, 0, s>>>(args..., rows, dim);
+    return launched();
+}
+
+inline bool aligned16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
 cudaError_t launch_conv_prefill(float *out, const float *x, const float *w, int rows, int dim, int k,
                                 cudaStream_t s) {
     if (rows <= 0 || dim <= 0) return cudaSuccess;
+    const bool v4 = dim % 4 == 0 && aligned16(out) && aligned16(x);
+    constexpr int RT = 8;
+#define KRT_CONV(KK)                                                                                        \
+    if (k == KK)                                                                                            \
+        return v4 ? launch_conv_tiled<KK, 4, RT>(k_conv_prefill_tiled<KK, 4, RT>, rows, dim, s, out, x, w)  \
+                  : launch_conv_tiled<KK, 1, RT>(k_conv_prefill_tiled<KK, 1, RT>, rows, dim, s, out, x, w);
+    KRT_CONV(2)
+    KRT_CONV(3)
+    KRT_CONV(4)
+#undef KRT_CONV
     k_conv_prefill<<<grid_for((size_t)rows * dim, kThreads), kThreads, 0, s>>>(out, x, w, rows, dim, k);
     return launched();
 }
@@ -1791,6 +1998,18 @@ cudaError_t launch_conv_decode(float *out, const float *x, const float *w, float
 cudaError_t launch_lfm2_conv_block(const float *bcx, const float *w, float *ring, float *cy, int rows,
                                    int dim, int k, cudaStream_t s) {
     if (rows <= 0 || dim <= 0) return cudaSuccess;
+    const bool v4 = dim % 4 == 0 && aligned16(bcx) && aligned16(cy) && aligned16(ring);
+    constexpr int RT = 4;
+#define KRT_CONV(KK)                                                                                     \
+    if (k == KK)                                                                                         \
+        return v4 ? launch_conv_tiled<KK, 4, RT>(k_lfm2_conv_block_tiled<KK, 4, RT>, rows, dim, s, bcx, w, \
+                                                 ring, cy)                                               \
+                  : launch_conv_tiled<KK, 1, RT>(k_lfm2_conv_block_tiled<KK, 1, RT>, rows, dim, s, bcx, w, \
+                                                 ring, cy);
+    KRT_CONV(2)
+    KRT_CONV(3)
+    KRT_CONV(4)
+#undef KRT_CONV
     k_lfm2_conv_block<<<grid_for((size_t)rows * dim, kThreads), kThreads, 0, s>>>(bcx, w, ring, cy,
                                                                                   rows, dim, k);
     return launched();
@@ -1800,7 +2019,9 @@ cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes,
                                uint16_t *scales16, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
     if (dim % 32 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)codes & 3) == 0) {
-        k_quantize_q8v<<<stream_grid((size_t)rows * dim), kThreads, 0, s>>>(x, rows, dim, codes, scales, scales16);
+        const size_t items = (size_t)rows * dim / 4;
+        k_quantize_q8v<4><<<stream_grid((size_t)rows * dim / 4), kThreads, 0, s>>>(x, items, codes, scales,
+                                                                                  scales16);
         return launched();
     }
     k_quantize_q8<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(x, rows, dim, codes, scales,

@@ -1,6 +1,6 @@
 """Per-op and per-workload throughput of the backend (1 GPU).
 
-    python -m kernrt_b200.opbench [--reps N] [--json]
+    python -m kernrt_b200.opbench [--reps N] [--json] [--only REGEX]
 
 Times every row op of the trait, the fused driver pairs, the fused chain on
 each benchmark workload and the single-row decode latency, with CUDA events on
@@ -14,6 +14,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import time
 
@@ -35,7 +36,7 @@ def peak_gbs():
 
 
 class Bench:
-    def __init__(self, reps: int):
+    def __init__(self, reps: int, only: str | None = None):
         import torch
 
         self.torch = torch
@@ -43,8 +44,15 @@ class Bench:
         self.stream = torch.cuda.ExternalStream(self.b.stream(), device="cuda:0")
         self.g = torch.Generator(device="cuda:0").manual_seed(0)
         self.reps = reps
+        self.only = re.compile(only) if only else None
         self.peak = peak_gbs()
         self.rows = []
+
+    def want(self, *names):
+        """Whether any op named by these (sub)strings passes --only."""
+        if self.only is None:
+            return True
+        return any(self.only.search(n) or n in self.only.pattern for n in names)
 
     def fill(self, h, n, scale=1.0):
         self.b.synchronize()
@@ -63,6 +71,8 @@ class Bench:
         (a device copy restoring an in-place input), each call is timed alone
         and its host work overlaps that copy."""
         torch = self.torch
+        if self.only is not None and not self.only.search(name):
+            return None
         for _ in range(3):
             if setup:
                 setup()
@@ -105,79 +115,78 @@ def torch_randn(bench, n):
     return bench.torch.randn(n, device="cuda:0", generator=bench.g)
 
 
-def run(reps: int):
+def run(reps: int, only: str | None = None):
     import torch
 
-    B = Bench(reps)
+    B = Bench(reps, only)
     b = B.b
     wl = W.SMOLLM2_17B_65K
     R, H, Q, KV, I = wl.rows, wl.dim, wl.q_dim, wl.kv_dim, wl.hidden
-
-    # --- tables and weights
-    table = (torch.randn(wl.vocab, H, device="cuda:0", generator=B.g) * 0.02).to(torch.bfloat16)
-    b.prepare_embedding(BF16, table.view(torch.int16).cpu().numpy().view(np.uint16), None, wl.vocab, H)
-    del table
-    w = b.upload(np.ones(H, np.float32))
-    tokens = np.random.default_rng(1).integers(0, wl.vocab, R).astype(np.int32)
     positions = wl.positions()
 
-    # --- a1 embed (coalesced per-row calls: one gather launch)
-    x, xb = b.alloc(R * H), b.alloc(R * H)
+    # --- a1 embed, a2 rms_norm and the fused driver pairs (SmolLM2-1.7B rows)
+    if B.want("embed", "rms_norm 65536x2048", "add_in_place"):
+        table = (torch.randn(wl.vocab, H, device="cuda:0", generator=B.g) * 0.02).to(torch.bfloat16)
+        b.prepare_embedding(BF16, table.view(torch.int16).cpu().numpy().view(np.uint16), None, wl.vocab, H)
+        del table
+        w = b.upload(np.ones(H, np.float32))
+        tokens = np.random.default_rng(1).integers(0, wl.vocab, R).astype(np.int32)
+        x, xb = b.alloc(R * H), b.alloc(R * H)
 
-    def embed_all():
-        for r in range(R):
-            b.embed(int(tokens[r]), x, r * H)
+        def embed_all():
+            for r in range(R):
+                b.embed(int(tokens[r]), x, r * H)
 
-    B.time("embed (65536 per-row calls, bf16 table)", embed_all, R * (2 * H + 4 * H),
-           note="host loop of 65536 calls included")
+        B.time("embed (65536 per-row calls, bf16 table)", embed_all, R * (2 * H + 4 * H),
+               note="host loop of 65536 calls included")
+        B.fill(x, R * H)
+        B.time("rms_norm 65536x2048", lambda: b.rms_norm(xb, x, w, R, H, 1e-5), R * 8 * H)
+        o = B.buf(R * H)
+        x0 = B.buf(R * H)
 
-    # --- a2 rms_norm (f32 x)
-    B.fill(x, R * H)
-    B.time("rms_norm 65536x2048", lambda: b.rms_norm(xb, x, w, R, H, 1e-5), R * 8 * H)
+        def add_rms():
+            b.add_in_place(x, o, R * H)
+            b.rms_norm(xb, x, w, R, H, 1e-5)
 
-    # --- fused driver pairs
-    o = B.buf(R * H)
-    x0 = B.buf(R * H)
+        B.time("add_in_place + rms_norm (fused)", add_rms, R * 16 * H, setup=lambda: b.copy(x0, 0, x, 0, R * H))
+        B.time("add_in_place 65536x2048", lambda: b.add_in_place(x, o, R * H), R * 12 * H,
+               setup=lambda: b.copy(x0, 0, x, 0, R * H))
 
-    def add_rms():
-        b.add_in_place(x, o, R * H)
-        b.rms_norm(xb, x, w, R, H, 1e-5)
+        def embed_rms():
+            embed_all()
+            b.rms_norm(xb, x, w, R, H, 1e-5)
 
-    B.time("add_in_place + rms_norm (fused)", add_rms, R * 16 * H, setup=lambda: b.copy(x0, 0, x, 0, R * H))
-    B.time("add_in_place 65536x2048", lambda: b.add_in_place(x, o, R * H), R * 12 * H,
-           setup=lambda: b.copy(x0, 0, x, 0, R * H))
-
-    def embed_rms():
-        embed_all()
-        b.rms_norm(xb, x, w, R, H, 1e-5)
-
-    B.time("embed x65536 + rms_norm (fused)", embed_rms, R * (2 * H + 8 * H),
-           note="host loop of 65536 calls included")
+        B.time("embed x65536 + rms_norm (fused)", embed_rms, R * (2 * H + 8 * H),
+               note="host loop of 65536 calls included")
 
     # --- a3/a4 qk_norm, rope and the fused triple (Qwen3 shape: 16x128 / 8x128)
-    qd, kd, hd = 2048, 1024, 128
-    q, k = B.buf(R * qd), B.buf(R * kd)
-    wq = b.upload(np.ones(hd, np.float32))
-    B.time("qk_norm q 65536x(16x128)", lambda: b.qk_norm(q, R, qd, hd, wq, 1e-6), R * 8 * qd)
-    B.time("rope q,k 65536x(16+8)x128", lambda: b.rope(q, k, qd, kd, R, positions, hd, 1e6, False),
-           R * 8 * (qd + kd))
+    if B.want("qk_norm", "rope"):
+        qd, kd, hd = 2048, 1024, 128
+        q, k = B.buf(R * qd), B.buf(R * kd)
+        wq = b.upload(np.ones(hd, np.float32))
+        B.time("qk_norm q 65536x(16x128)", lambda: b.qk_norm(q, R, qd, hd, wq, 1e-6), R * 8 * qd)
+        B.time("rope q,k 65536x(16+8)x128", lambda: b.rope(q, k, qd, kd, R, positions, hd, 1e6, False),
+               R * 8 * (qd + kd))
 
-    def qk_rope():
-        b.qk_norm(q, R, qd, hd, wq, 1e-6)
-        b.qk_norm(k, R, kd, hd, wq, 1e-6)
-        b.rope(q, k, qd, kd, R, positions, hd, 1e6, False)
+        def qk_rope():
+            b.qk_norm(q, R, qd, hd, wq, 1e-6)
+            b.qk_norm(k, R, kd, hd, wq, 1e-6)
+            b.rope(q, k, qd, kd, R, positions, hd, 1e6, False)
 
-    B.time("qk_norm q + qk_norm k + rope (fused)", qk_rope, R * 8 * (qd + kd))
+        B.time("qk_norm q + qk_norm k + rope (fused)", qk_rope, R * 8 * (qd + kd))
 
     # --- a5 silu_mul
-    g, u = B.buf(R * I), B.buf(R * I)
-    g0 = b.alloc(R * I)
-    b.copy(g, 0, g0, 0, R * I)
-    B.time("silu_mul 65536x8192", lambda: b.silu_mul(g, u, R * I), R * 12 * I,
-           setup=lambda: b.copy(g0, 0, g, 0, R * I))
+    if B.want("silu_mul"):
+        g, u = B.buf(R * I), B.buf(R * I)
+        g0 = b.alloc(R * I)
+        b.copy(g, 0, g0, 0, R * I)
+        B.time("silu_mul 65536x8192", lambda: b.silu_mul(g, u, R * I), R * 12 * I,
+               setup=lambda: b.copy(g0, 0, g, 0, R * I))
 
-    # --- a7/a8 LFM2 conv (1024 rows x 1536, and 65536 rows for bandwidth)
+    # --- a7/a8 LFM2 conv (1024 rows x 1536, and 16384 rows for bandwidth)
     for rows in (1024, 16384):
+        if not B.want(f"{rows}x1536"):
+            continue
         d = 1536
         bcx, kern = B.buf(rows * 3 * d), B.buf(d * 3, 0.3)
         h, co, cy, ring = b.alloc(rows * d), b.alloc(rows * d), b.alloc(rows * d), b.alloc(2 * d)
@@ -190,23 +199,28 @@ def run(reps: int):
 
     # --- a9 conv_decode latency, a11 Q8
     d = 1536
-    xr, kern, st = B.buf(d), B.buf(d * 3), B.buf(2 * d)
-    B.time("conv_decode 1x1536 (latency)", lambda: b.conv_decode(xr, xr, kern, st, d, 3), None)
-    qd8 = 1024
-    xq = B.buf(R * qd8)
-    nb = qd8 // 32
-    c8, s8, h8 = b.alloc_bytes(R * qd8), b.alloc_bytes(R * nb * 4), b.alloc_bytes(R * nb * 2)
-    wq8 = b.upload(np.ones(qd8, np.float32))
-    B.time("quantize_q8_0 65536x1024", lambda: b.quantize_q8_0(xq, R, qd8, c8, s8, h8), R * (4 * qd8 + qd8 + 6 * nb))
-    B.time("rms_norm_q8_0 65536x1024 (fused)", lambda: b.rms_norm_q8_0(xq, wq8, R, qd8, 1e-6, c8, s8, h8),
-           R * (4 * qd8 + qd8 + 6 * nb))
+    if B.want("conv_decode"):
+        xr, kern, st = B.buf(d), B.buf(d * 3), B.buf(2 * d)
+        B.time("conv_decode 1x1536 (latency)", lambda: b.conv_decode(xr, xr, kern, st, d, 3), None)
+    if B.want("q8_0"):
+        qd8 = 1024
+        xq = B.buf(R * qd8)
+        nb = qd8 // 32
+        c8, s8, h8 = b.alloc_bytes(R * qd8), b.alloc_bytes(R * nb * 4), b.alloc_bytes(R * nb * 2)
+        wq8 = b.upload(np.ones(qd8, np.float32))
+        B.time("quantize_q8_0 65536x1024", lambda: b.quantize_q8_0(xq, R, qd8, c8, s8, h8),
+               R * (4 * qd8 + qd8 + 6 * nb))
+        B.time("rms_norm_q8_0 65536x1024 (fused)", lambda: b.rms_norm_q8_0(xq, wq8, R, qd8, 1e-6, c8, s8, h8),
+               R * (4 * qd8 + qd8 + 6 * nb))
 
     # --- the chain on every workload
     for wk in (W.SMOLLM2_135M, W.SMOLLM2_17B_PREFILL, W.QWEN3_06B_Q8, W.LFM2_700M, W.SMOLLM2_17B_65K):
-        chain_time(B, wk)
+        if B.want(f"chain: {wk.name}"):
+            chain_time(B, wk)
 
     # --- decode latency: one row through the trait ops, read() each step
-    decode_latency(B)
+    if B.want("decode step"):
+        decode_latency(B)
     return B
 
 
@@ -296,8 +310,9 @@ def main():
     p = argparse.ArgumentParser()
     p.add_argument("--reps", type=int, default=10)
     p.add_argument("--json", action="store_true")
+    p.add_argument("--only", default=None, help="regex: time only the ops whose name matches")
     args = p.parse_args()
-    B = run(args.reps)
+    B = run(args.reps, args.only)
     if args.json:
         for r in B.rows:
             print(json.dumps(r))

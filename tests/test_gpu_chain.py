@@ -168,9 +168,10 @@ def test_chain_position_outside_table_reports(gpu):
     gpu.synchronize()  # the context stays usable
 
 
-def test_lfm2_conv_block(gpu, oracle):
-    rows, dim, k = 1024, 1536, 3
-    rng = np.random.default_rng(7)
+@pytest.mark.parametrize("rows,dim,k", [(1024, 1536, 3), (37, 100, 2), (13, 33, 4), (9, 64, 5),
+                                        (3, 8, 4), (4, 12, 3), (6, 7, 2)])
+def test_lfm2_conv_block(gpu, oracle, rows, dim, k):
+    rng = np.random.default_rng(7 + rows + k)
     bcx = rng.standard_normal((rows, 3 * dim), dtype=f32)
     kernel = (0.3 * rng.standard_normal(dim * k)).astype(f32)
     ring0 = rng.standard_normal((k - 1) * dim, dtype=f32)

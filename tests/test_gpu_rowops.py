@@ -229,8 +229,13 @@ def test_copy_overlapping_is_memmove(gpu, oracle):
 
 # --- conv (reference.rs:365-393, 490-503) -------------------------------------------------
 
+# Row-tiled kernels for k = 2..4 (float4 channels when dim % 4 == 0, tiles of 8
+# rows, ragged last tiles, prompts shorter than the halo) and the per-element
+# kernel for other sizes.
 @pytest.mark.parametrize("rows,dim,k", [(9, 40, 3), (1, 1536, 3), (64, 1536, 3), (5, 8, 1),
-                                        (7, 33, 4), (2, 16, 3)])
+                                        (7, 33, 4), (2, 16, 3), (33, 1536, 2), (19, 12, 4),
+                                        (1000, 64, 3), (3, 8, 4), (1, 4, 2), (100, 96, 5),
+                                        (77, 35, 2)])
 def test_conv_prefill(gpu, oracle, rows, dim, k):
     x = _data.lcg_normal(rows * dim, 50 + dim).reshape(rows, dim)
     w = _data.lcg_normal(dim * k, 51, 0.0, 0.3)
