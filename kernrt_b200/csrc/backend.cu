@@ -217,6 +217,7 @@ public:
             std::string m = "device reported:";
             if (e & ERR_TOKEN) m += " token id out of range of the embedding table;";
             if (e & ERR_POSITION) m += " position outside the prepared RoPE table;";
+            if (e & ERR_TIMEOUT) m += " a kernel's wait for its staged rows timed out;";
             fail(KERNRT_E_DEVICE, m);
         }
     }

@@ -36,6 +36,10 @@ namespace {
 
 constexpr unsigned kFull = 0xffffffffu;
 constexpr int kThreads = 256;
+// The norm pipeline runs one 16-warp CTA per SM: one summing warp, so the
+// serial sums own an SM sub-partition's issue slots, and all of the SM's
+// shared memory for its row slots.
+constexpr int kPipeThreads = 512;
 
 __device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
@@ -849,7 +853,7 @@ __device__ __forceinline__ void decode_global4(const ChainArgs &a, const float *
 // x + resid with the residual rows staged beside x), and the writers emit the
 // int8 codes and block scales, eight lanes per 32-element block.
 template <int SRC, bool VEC, bool PRE_ADD, bool FQ, bool RR>
-__global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLayout L) {
+__global__ void __launch_bounds__(kPipeThreads, 1) k_norm_pipe(ChainArgs a, ChainLayout L) {
     static_assert(!PRE_ADD || (SRC == SRC_X && VEC), "the pre-add form stages f32 rows with vector loads");
     static_assert(!FQ || (VEC && !PRE_ADD), "the quantising form needs whole 32-element blocks");
     constexpr int NL = PRE_ADD ? 3 : 1;  // loader warps 1..NL; writers NL+1..7
@@ -944,22 +948,39 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
         float *sc = scales + (i % NS) * 64;
         float ss = 0.0f;
         if constexpr (FQ) {
-            const float *rrow =
-                reinterpret_cast<const float *>(slot(i) + (size_t)G * L.xstride + (size_t)lane * L.rstride);
-            float ss2 = 0.0f;
+            if (fq_resid) {
+                // x + resid is what gets quantised: a second chain over it
+                const float *rrow =
+                    reinterpret_cast<const float *>(slot(i) + (size_t)G * L.xstride + (size_t)lane * L.rstride);
+                float ss2 = 0.0f;
 #pragma unroll 4
-            for (int c = 0; c < dim; c += 8) {
-                float v[8];
-                decode_staged<SRC, 8>(row, dim, c, v);
+                for (int c = 0; c < dim; c += 8) {
+                    float v[8];
+                    decode_staged<SRC, 8>(row, dim, c, v);
+                    const float4 r0v = *reinterpret_cast<const float4 *>(rrow + c);
+                    const float4 r1v = *reinterpret_cast<const float4 *>(rrow + c + 4);
+                    const float rv[8] = {r0v.x, r0v.y, r0v.z, r0v.w, r1v.x, r1v.y, r1v.z, r1v.w};
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    ss = add_rn(ss, mul_rn(v[e], v[e]));
-                    const float xo = fq_resid ? add_rn(v[e], rrow[c + e]) : v[e];
-                    ss2 = add_rn(ss2, mul_rn(xo, xo));
+                    for (int e = 0; e < 8; ++e) {
+                        ss = add_rn(ss, mul_rn(v[e], v[e]));
+                        const float xo = add_rn(v[e], rv[e]);
+                        ss2 = add_rn(ss2, mul_rn(xo, xo));
+                    }
                 }
+                sc[lane] = rms_scale(ss, (float)dim, a.eps);
+                sc[32 + lane] = rms_scale(ss2, (float)dim, a.final_eps);
+            } else {
+                // the quantised row is x itself: both norms share one sum
+#pragma unroll 4
+                for (int c = 0; c < dim; c += 8) {
+                    float v[8];
+                    decode_staged<SRC, 8>(row, dim, c, v);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
+                }
+                sc[lane] = rms_scale(ss, (float)dim, a.eps);
+                sc[32 + lane] = rms_scale(ss, (float)dim, a.final_eps);
             }
-            sc[lane] = rms_scale(ss, (float)dim, a.eps);
-            sc[32 + lane] = rms_scale(ss2, (float)dim, a.final_eps);
             return;
         } else if constexpr (VEC) {
 #pragma unroll 4
@@ -1119,6 +1140,679 @@ __global__ void __launch_bounds__(kThreads, 2) k_norm_pipe(ChainArgs a, ChainLay
         }
         __syncthreads();
     }
+}
+
+// --- bulk-copy (TMA) staging with mbarrier completion --------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// One arrival that also announces `bytes` of bulk copies to come.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Global -> shared bulk copy (no tensor map, no multicast); 16-byte aligned
+// addresses, size a multiple of 16.  Completion is counted on `bar`.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_addr(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with this parity to complete, for at most ~1 s of SM
+// clock; false if it did not.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > (1ll << 31)) return false;
+    return true;
+}
+
+struct TiledLayout {
+    int G;          // rows per group (<= 32: one summing lane per row)
+    int TC;         // columns per tile; the last tile may be shorter
+    int T;          // tiles per row
+    int xstride;    // bytes per staged row tile (+ Q8 block scales), an odd multiple of 16
+    int srstride;   // bytes per f32 residual row tile in a sum slot, or 0
+    int wrstride;   // bytes per f32 residual row tile in a write slot, or 0
+    int sslot;      // bytes per sum slot: G * (xstride + srstride)
+    int wslot;      // bytes per write slot: G * (xstride + wrstride)
+    size_t smem;
+};
+
+constexpr int kTiledThreads = 512;  // 16 warps
+constexpr int kTiledSlots = 3;      // per ring: staging two units ahead
+constexpr int kTiledWriters = 12;   // warps off the summing warp's sub-partition
+constexpr bool kTiledBulk = true;  // stage with bulk copies (else 16-byte cp.async)
+
+// The norm stage as a column-tiled pipeline fed by bulk copies, one CTA per
+// SM.  A CTA's rows come in groups of G; a group's rows are cut into T column
+// tiles, and a unit is one tile of one group.  Two rings of three slots, each
+// slot with an mbarrier that counts its copies' bytes:
+//   sum ring    unit u's tiles of x (and of resid where the sums need it);
+//   write ring  the same tiles again, one group later, for the writers (and
+//               resid where the outputs need it); the x tiles then come from
+//               L2, where the sum ring's copies left them.
+// In iteration u:
+//   warp 4    issues the copies of sum unit u+2 and of write unit u+2-T,
+//             lane r those of row r, after lane 0 announced the bytes;
+//   warp 0    waits for sum unit u and continues its rows' sums over the tile,
+//             lane r for row r, left to right: the reference's order
+//             (reference.rs:167-170), carried across tiles in a register;
+//             after the last tile it stores the group's scales;
+//   writers   (12 warps on the other three sub-partitions) wait for write
+//             unit u-T, tile t of the previous group, whose scales are known,
+//             and write xb, x (+ resid), or the Q8_0 codes from shared memory.
+// Warps 8 and 12 only keep the barrier count, so the summing warp shares its
+// sub-partition with the copy issuer alone.  Every global read is a bulk
+// copy; the writers' only global traffic is their stores.
+//
+// PRE_ADD: the sums are of x + resid (the driver's add_in_place -> rms_norm,
+// llama.rs:762-765), and the writers store x = x + resid and xb.  FQ: a
+// second sum of x (+ resid) for the final norm, and the writers quantise it
+// to Q8_0 (quant.rs:856-874).
+template <int SRC, bool PRE_ADD, bool FQ>
+__global__ void __launch_bounds__(kTiledThreads, 1) k_norm_tiled(ChainArgs a, TiledLayout L) {
+    static_assert(!PRE_ADD || SRC == SRC_X, "the pre-add form reads f32 x");
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int dim = a.dim, G = L.G, T = L.T, TC = L.TC;
+    const int ngroups = (a.rows + G - 1) / G;
+    const int nmine = (int)blockIdx.x < ngroups ? (ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    const int units = nmine * T;
+    unsigned char *sring = smem;
+    unsigned char *wring = smem + kTiledSlots * (size_t)L.sslot;
+    float *scales = reinterpret_cast<float *>(wring + kTiledSlots * (size_t)L.wslot);  // [2][64]
+    uint64_t *sbar = reinterpret_cast<uint64_t *>(scales + 128);                       // [kTiledSlots]
+    uint64_t *wbar = sbar + kTiledSlots;                                               // [kTiledSlots]
+    __shared__ int s_abort;
+    const bool has_resid = a.resid != nullptr;
+    const bool sum_resid = PRE_ADD || (FQ && has_resid);
+    const bool write_resid = has_resid && (PRE_ADD || FQ || a.x_out);
+
+    auto first_row = [&](int g) { return (int)(blockIdx.x + (unsigned)g * gridDim.x) * G; };
+
+    if (tid == 0) {
+        s_abort = 0;
+        for (int i = 0; i < 2 * kTiledSlots; ++i) mbar_init(&sbar[i], kTiledBulk ? 1 : 32);
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    // Copies of unit u into a slot of one ring, by warp 4 (lane r: row r).
+    auto issue = [&](int u, unsigned char *slot, uint64_t *bar, int rstride, bool resid) {
+        const int g = u / T, t = u - g * T;
+        const int r0 = first_row(g), gr = min(G, a.rows - r0);
+        const int c0 = t * TC, tc = min(TC, dim - c0);
+        const uint32_t xbytes = (uint32_t)src_row_bytes<SRC>(tc), sbytes = SRC == SRC_Q8 ? (uint32_t)(tc / 8) : 0u;
+        const uint32_t rbytes = resid ? (uint32_t)tc * 4u : 0u;
+        const unsigned char *sp = nullptr;
+        int tok = 0;
+        uint32_t mine = 0;
+        if (lane < gr) {
+            if constexpr (SRC == SRC_X) {
+                sp = reinterpret_cast<const unsigned char *>(a.x_in + (size_t)(r0 + lane) * dim + c0);
+            } else {
+                tok = a.tokens[r0 + lane];
+                if ((unsigned)tok < (unsigned)a.vocab)
+                    sp = static_cast<const unsigned char *>(a.table) +
+                         (size_t)tok * (size_t)src_row_bytes<SRC>(dim) + src_row_bytes<SRC>(c0);
+                else if (t == 0)
+                    set_err(a.err, ERR_TOKEN);
+            }
+            mine = (sp ? xbytes + sbytes : 0u) + rbytes;
+        }
+        if constexpr (kTiledBulk) {
+            uint32_t total = mine;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFull, total, o);
+            if (lane == 0) mbar_arrive_expect_tx(bar, total);
+            __syncwarp();
+            if (lane < gr) {
+                unsigned char *dst = slot + (size_t)lane * L.xstride;
+                if (sp) {
+                    bulk_load(dst, sp, xbytes, bar);
+                    if constexpr (SRC == SRC_Q8)
+                        bulk_load(dst + align16(TC), a.tscales + (size_t)tok * (dim >> 5) + (c0 >> 5), sbytes, bar);
+                }
+                if (resid)
+                    bulk_load(slot + (size_t)G * L.xstride + (size_t)lane * rstride,
+                              a.resid + (size_t)(r0 + lane) * dim + c0, rbytes, bar);
+            }
+        } else {
+            // 16-byte cp.async by the whole warp, row by row; each lane's
+            // arrival on the mbarrier fires when its own copies have landed.
+            for (int r = 0; r < gr; ++r) {
+                const unsigned char *rsp = (const unsigned char *)__shfl_sync(kFull, (unsigned long long)sp, r);
+                const int rtok = __shfl_sync(kFull, tok, r);
+                unsigned char *dst = slot + (size_t)r * L.xstride;
+                if (rsp) {
+                    for (int k = lane; k < (int)(xbytes >> 4); k += 32) cp_async16(dst + 16 * k, rsp + 16 * k);
+                    if constexpr (SRC == SRC_Q8) {
+                        const float *ssp = a.tscales + (size_t)rtok * (dim >> 5) + (c0 >> 5);
+                        for (int k = lane; k < (int)(sbytes >> 4); k += 32)
+                            cp_async16(dst + align16(TC) + 16 * k, ssp + 4 * k);
+                    }
+                }
+                if (resid) {
+                    const float *rsrc = a.resid + (size_t)(r0 + r) * dim + c0;
+                    unsigned char *rdst = slot + (size_t)G * L.xstride + (size_t)r * rstride;
+                    for (int k = lane; k < (int)(rbytes >> 4); k += 32) cp_async16(rdst + 16 * k, rsrc + 4 * k);
+                }
+            }
+            asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+        }
+    };
+    auto issue_sum = [&](int u) {
+        issue(u, sring + (size_t)(u % kTiledSlots) * L.sslot, &sbar[u % kTiledSlots], L.srstride, sum_resid);
+    };
+    auto issue_write = [&](int u) {
+        issue(u, wring + (size_t)(u % kTiledSlots) * L.wslot, &wbar[u % kTiledSlots], L.wrstride, write_resid);
+    };
+    // Waits for a slot's copies; a wait that runs out reports it, and the
+    // CTA stops waiting (its results are then not valid).
+    auto wait = [&](uint64_t *bar, int u) {
+        if (s_abort) return false;
+        if (mbar_wait_bounded(bar, (uint32_t)(u / kTiledSlots) & 1u)) return true;
+        if (lane == 0) {
+            set_err(a.err, ERR_TIMEOUT);
+            s_abort = 1;
+        }
+        return false;
+    };
+
+    float ss = 0.0f, ss2 = 0.0f;  // summing lanes: the running sums of their rows
+    auto sum = [&](int u) {
+        const int g = u / T, t = u - g * T;
+        const int r0 = first_row(g), gr = min(G, a.rows - r0);
+        const int c0 = t * TC, tc = min(TC, dim - c0);
+        const unsigned char *slot = sring + (size_t)(u % kTiledSlots) * L.sslot;
+        if (wait(&sbar[u % kTiledSlots], u) && lane < gr) {
+            bool valid = true;
+            if constexpr (SRC != SRC_X) valid = (unsigned)a.tokens[r0 + lane] < (unsigned)a.vocab;
+            const unsigned char *xr = slot + (size_t)lane * L.xstride;
+            const float *rr = reinterpret_cast<const float *>(slot + (size_t)G * L.xstride + (size_t)lane * L.srstride);
+            if (PRE_ADD) {
+#pragma unroll 2
+                for (int c = 0; c < tc; c += 8) {
+                    float v[8];
+                    decode_staged<SRC, 8>(xr, TC, c, v);
+                    const float4 p = *reinterpret_cast<const float4 *>(rr + c), q = *reinterpret_cast<const float4 *>(rr + c + 4);
+                    const float rv[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float xo = add_rn(v[e], rv[e]);
+                        ss = add_rn(ss, mul_rn(xo, xo));
+                    }
+                }
+            } else if (FQ && has_resid) {
+#pragma unroll 2
+                for (int c = 0; c < tc; c += 8) {
+                    float v[8];
+                    decode_staged<SRC, 8>(xr, TC, c, v);
+                    if (!valid)
+                        for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+                    const float4 p = *reinterpret_cast<const float4 *>(rr + c), q = *reinterpret_cast<const float4 *>(rr + c + 4);
+                    const float rv[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        ss = add_rn(ss, mul_rn(v[e], v[e]));
+                        const float xo = add_rn(v[e], rv[e]);
+                        ss2 = add_rn(ss2, mul_rn(xo, xo));
+                    }
+                }
+            } else if (valid) {
+#pragma unroll 4
+                for (int c = 0; c < tc; c += 8) {
+                    float v[8];
+                    decode_staged<SRC, 8>(xr, TC, c, v);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
+                }
+            }
+        }
+        if (t == T - 1) {
+            if (lane < gr) {
+                float *sc = scales + (g & 1) * 64;
+                sc[lane] = rms_scale(ss, (float)dim, a.eps);
+                if (FQ) sc[32 + lane] = rms_scale(has_resid ? ss2 : ss, (float)dim, a.final_eps);
+            }
+            ss = 0.0f;
+            ss2 = 0.0f;
+        }
+    };
+
+    // Write unit u (tile t of group g) from its write slot, by the writer
+    // warps (wi = 0..11): float4 items in row-major order over the tile.
+    const int wi = warp - 1 - (warp >> 2);
+    auto write = [&](int u) {
+        const int g = u / T, t = u - g * T;
+        const int r0 = first_row(g), gr = min(G, a.rows - r0);
+        const int c0 = t * TC, tc = min(TC, dim - c0);
+        const unsigned char *slot = wring + (size_t)(u % kTiledSlots) * L.wslot;
+        if (!wait(&wbar[u % kTiledSlots], u)) return;
+        const float *sc = scales + (g & 1) * 64;
+        const int q = tc >> 2, total = gr * q;
+        const int nwt = kTiledWriters * 32;
+        const int dr = nwt / q, dc = nwt - dr * q;
+        const int wt = wi * 32 + lane;
+        int r = wt / q, c4 = wt - r * q;
+        int vr = -1;
+        bool vok = true;  // row vr's token is inside the table (its slot rows were not copied otherwise)
+        auto xval = [&](int rr_, int cc, float *v) {  // cc: column within the tile
+            decode_staged<SRC, 4>(slot + (size_t)rr_ * L.xstride, TC, cc, v);
+            if constexpr (SRC != SRC_X) {
+                if (rr_ != vr) {
+                    vr = rr_;
+                    vok = (unsigned)a.tokens[r0 + rr_] < (unsigned)a.vocab;
+                }
+                if (!vok) v[0] = v[1] = v[2] = v[3] = 0.0f;
+            }
+        };
+        auto rval = [&](int rr_, int cc) {
+            return *reinterpret_cast<const float4 *>(slot + (size_t)G * L.xstride + (size_t)rr_ * L.wrstride + 4 * cc);
+        };
+        if constexpr (FQ) {
+            // eight lanes per 32-element block; q % 8 == 0 and a warp's items
+            // are consecutive, so each block's lanes share a warp.
+            for (int i = wt; i - lane < total; i += nwt) {
+                const bool ok = i < total;
+                const int cc = 4 * c4, c = c0 + cc, row = r0 + r;
+                float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (ok) {
+                    float v[4];
+                    xval(r, cc, v);
+                    const size_t o = (size_t)row * dim + c;
+                    if (a.xb) {
+                        const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
+                        const float s1 = sc[r];
+                        st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s1, v[0])), mul_rn(w.y, mul_rn(s1, v[1])),
+                                                  mul_rn(w.z, mul_rn(s1, v[2])), mul_rn(w.w, mul_rn(s1, v[3]))));
+                    }
+                    float4 xo = make_float4(v[0], v[1], v[2], v[3]);
+                    if (has_resid) {
+                        const float4 rv = rval(r, cc);
+                        xo = make_float4(add_rn(v[0], rv.x), add_rn(v[1], rv.y), add_rn(v[2], rv.z), add_rn(v[3], rv.w));
+                    }
+                    if (a.x_out) st4(a.x_out + o, xo);
+                    const float4 wf = __ldg(reinterpret_cast<const float4 *>(a.w_final + c));
+                    const float s2 = sc[32 + r];
+                    y = make_float4(mul_rn(wf.x, mul_rn(s2, xo.x)), mul_rn(wf.y, mul_rn(s2, xo.y)),
+                                    mul_rn(wf.z, mul_rn(s2, xo.z)), mul_rn(wf.w, mul_rn(s2, xo.w)));
+                }
+                float am = fmaxf(fmaxf(fmaxf(0.0f, fabsf(y.x)), fmaxf(0.0f, fabsf(y.y))),
+                                 fmaxf(fmaxf(0.0f, fabsf(y.z)), fmaxf(0.0f, fabsf(y.w))));
+                am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
+                am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
+                am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
+                if (ok) {
+                    const int nb = dim >> 5;
+                    const float d = div_rn(am, 127.0f);
+                    const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+                    const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y.x, inv)) |
+                                            ((uint32_t)(uint8_t)q8_code(mul_rn(y.y, inv)) << 8) |
+                                            ((uint32_t)(uint8_t)q8_code(mul_rn(y.z, inv)) << 16) |
+                                            ((uint32_t)(uint8_t)q8_code(mul_rn(y.w, inv)) << 24);
+                    *reinterpret_cast<uint32_t *>(a.codes + (size_t)row * dim + c) = packed;
+                    if ((c4 & 7) == 0) {
+                        a.scales[(size_t)row * nb + (c >> 5)] = d;
+                        if (a.scales16) a.scales16[(size_t)row * nb + (c >> 5)] = f16_bits(d);
+                    }
+                }
+                c4 += dc;
+                r += dr;
+                if (c4 >= q) {
+                    c4 -= q;
+                    ++r;
+                }
+            }
+            return;
+        }
+        for (int i = wt; i < total; i += nwt) {
+            const int cc = 4 * c4, c = c0 + cc;
+            const size_t o = (size_t)(r0 + r) * dim + c;
+            float v[4];
+            xval(r, cc, v);
+            float4 rv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (write_resid) rv = rval(r, cc);
+            if (PRE_ADD) {
+                v[0] = add_rn(v[0], rv.x); v[1] = add_rn(v[1], rv.y);
+                v[2] = add_rn(v[2], rv.z); v[3] = add_rn(v[3], rv.w);
+            }
+            if (a.xb) {
+                const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
+                const float s = sc[r];
+                st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[0])), mul_rn(w.y, mul_rn(s, v[1])),
+                                          mul_rn(w.z, mul_rn(s, v[2])), mul_rn(w.w, mul_rn(s, v[3]))));
+            }
+            if (a.x_out) {
+                float4 xo = make_float4(v[0], v[1], v[2], v[3]);
+                if (!PRE_ADD && has_resid)
+                    xo = make_float4(add_rn(v[0], rv.x), add_rn(v[1], rv.y), add_rn(v[2], rv.z), add_rn(v[3], rv.w));
+                st4(a.x_out + o, xo);
+            }
+            c4 += dc;
+            r += dr;
+            if (c4 >= q) {
+                c4 -= q;
+                ++r;
+            }
+        }
+    };
+
+    // warp 4's counts of units issued into each ring
+    int s_issued = 0, w_issued = 0;
+    if (warp == 4)
+        for (; s_issued < min(units, kTiledSlots - 1); ++s_issued) issue_sum(s_issued);
+    for (int u = 0; u < units + T; ++u) {
+        if (warp == 4) {
+            if (!__shfl_sync(kFull, s_abort, 0)) {
+                if (s_issued < units) issue_sum(s_issued++);
+                // write unit u+S-1-T lands in the slot the writers left in iteration u-1
+                if (u + kTiledSlots - 1 - T >= 0 && w_issued < units) issue_write(w_issued++);
+            }
+        } else if (warp == 0) {
+            if (u < units) sum(u);
+        } else if ((warp & 3) != 0) {
+            if (u >= T) write(u - T);
+        }
+        __syncthreads();
+    }
+    // Every copy issued was waited for unless a wait ran out; then wait (again
+    // bounded) for the last copies into each slot before the CTA's memory goes.
+    if (warp == 4 && lane == 0 && s_abort) {
+        for (int u = max(0, s_issued - kTiledSlots); u < s_issued; ++u)
+            mbar_wait_bounded(&sbar[u % kTiledSlots], (uint32_t)(u / kTiledSlots) & 1u);
+        for (int u = max(0, w_issued - kTiledSlots); u < w_issued; ++u)
+            mbar_wait_bounded(&wbar[u % kTiledSlots], (uint32_t)(u / kTiledSlots) & 1u);
+    }
+}
+
+struct RowsLayout {
+    int G;        // rows per group (<= 32)
+    int xstride;  // bytes per staged row (+ Q8 block scales), an odd multiple of 16
+    int rstride;  // bytes per staged f32 residual row, or 0
+    int slot;     // G * (xstride + rstride)
+    size_t smem;
+};
+
+// The norm stage over whole staged rows, one 16-warp CTA per SM, three slots
+// of G rows, each filled by one bulk copy per row (a full row is big enough
+// that the copy engine's per-request cost stays far below the row's
+// traffic).  In iteration i:
+//   warp 4    issues group i+1's copies into slot (i+1)%3, lane r those of
+//             row r (its x or embedding row, Q8 block scales, and the f32
+//             resid row when the quantised norm sums x + resid), counted on
+//             the slot's mbarrier;
+//   warp 0    waits for group i and sums it, lane r row r left to right (the
+//             reference's order, reference.rs:167-170);
+//   writers   (12 warps on the other sub-partitions) write group i-1 from its
+//             slot: xb = w*(scale*x), x + resid (resid from global memory,
+//             eight float4 loads in flight per lane), or the Q8_0 codes.
+// Warps 8 and 12 only keep the barrier count.  FQ is the final RMSNorm fused
+// with Q8_0 quantisation (quant.rs:856-874).
+template <int SRC, bool FQ>
+__global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, RowsLayout L) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int dim = a.dim, G = L.G;
+    const int ngroups = (a.rows + G - 1) / G;
+    const int nmine = (int)blockIdx.x < ngroups ? (ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    float *scales = reinterpret_cast<float *>(smem + 3 * (size_t)L.slot);  // [3][64]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(scales + 192);           // [3]
+    __shared__ int s_abort;
+    const bool has_resid = a.resid != nullptr;
+    const bool stage_resid = FQ && has_resid;
+    const int rb = src_row_bytes<SRC>(dim);
+
+    auto first_row = [&](int g) { return (int)(blockIdx.x + (unsigned)g * gridDim.x) * G; };
+    auto slot = [&](int g) { return smem + (size_t)(g % 3) * L.slot; };
+
+    if (tid == 0) {
+        s_abort = 0;
+        for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    auto issue = [&](int g) {  // warp 4
+        const int r0 = first_row(g), gr = min(G, a.rows - r0);
+        const unsigned char *sp = nullptr;
+        int tok = 0;
+        uint32_t mine = 0;
+        if (lane < gr) {
+            if constexpr (SRC == SRC_X) {
+                sp = reinterpret_cast<const unsigned char *>(a.x_in + (size_t)(r0 + lane) * dim);
+            } else {
+                tok = a.tokens[r0 + lane];
+                if ((unsigned)tok < (unsigned)a.vocab)
+                    sp = static_cast<const unsigned char *>(a.table) + (size_t)tok * (size_t)rb;
+                else
+                    set_err(a.err, ERR_TOKEN);
+            }
+            mine = (sp ? (uint32_t)rb + (SRC == SRC_Q8 ? (uint32_t)(dim / 8) : 0u) : 0u) +
+                   (stage_resid ? (uint32_t)dim * 4u : 0u);
+        }
+        uint32_t total = mine;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFull, total, o);
+        uint64_t *bar = &bars[g % 3];
+        if (lane == 0) mbar_arrive_expect_tx(bar, total);
+        __syncwarp();
+        if (lane < gr) {
+            unsigned char *dst = slot(g) + (size_t)lane * L.xstride;
+            if (sp) {
+                bulk_load(dst, sp, (uint32_t)rb, bar);
+                if constexpr (SRC == SRC_Q8)
+                    bulk_load(dst + align16(dim), a.tscales + (size_t)tok * (dim >> 5), (uint32_t)(dim / 8), bar);
+            }
+            if (stage_resid)
+                bulk_load(slot(g) + (size_t)G * L.xstride + (size_t)lane * L.rstride, a.resid + (size_t)(r0 + lane) * dim,
+                          (uint32_t)dim * 4u, bar);
+        }
+    };
+
+    auto sum = [&](int g) {  // warp 0
+        const int r0 = first_row(g), gr = min(G, a.rows - r0);
+        if (s_abort) return;
+        if (!mbar_wait_bounded(&bars[g % 3], (uint32_t)(g / 3) & 1u)) {
+            if (lane == 0) {
+                set_err(a.err, ERR_TIMEOUT);
+                s_abort = 1;
+            }
+            return;
+        }
+        if (lane >= gr) return;
+        bool valid = true;
+        if constexpr (SRC != SRC_X) valid = (unsigned)a.tokens[r0 + lane] < (unsigned)a.vocab;
+        const unsigned char *xr = slot(g) + (size_t)lane * L.xstride;
+        float *sc = scales + (g % 3) * 64;
+        float ss = 0.0f;
+        if (FQ && stage_resid) {
+            const float *rr = reinterpret_cast<const float *>(slot(g) + (size_t)G * L.xstride + (size_t)lane * L.rstride);
+            float ss2 = 0.0f;
+#pragma unroll 2
+            for (int c = 0; c < dim; c += 8) {
+                float v[8];
+                decode_staged<SRC, 8>(xr, dim, c, v);
+                if (!valid)
+                    for (int e = 0; e < 8; ++e) v[e] = 0.0f;
+                const float4 p = *reinterpret_cast<const float4 *>(rr + c), q = *reinterpret_cast<const float4 *>(rr + c + 4);
+                const float rv[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    ss = add_rn(ss, mul_rn(v[e], v[e]));
+                    const float xo = add_rn(v[e], rv[e]);
+                    ss2 = add_rn(ss2, mul_rn(xo, xo));
+                }
+            }
+            sc[lane] = rms_scale(ss, (float)dim, a.eps);
+            sc[32 + lane] = rms_scale(ss2, (float)dim, a.final_eps);
+            return;
+        }
+        if (valid) {
+#pragma unroll 4
+            for (int c = 0; c < dim; c += 8) {
+                float v[8];
+                decode_staged<SRC, 8>(xr, dim, c, v);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
+            }
+        }
+        sc[lane] = rms_scale(ss, (float)dim, a.eps);
+        if (FQ) sc[32 + lane] = rms_scale(ss, (float)dim, a.final_eps);
+    };
+
+    const int wi = warp - 1 - (warp >> 2);
+    auto write = [&](int g) {  // 12 writer warps
+        if (s_abort) return;
+        const int r0 = first_row(g), gr = min(G, a.rows - r0);
+        const unsigned char *base = slot(g);
+        const float *sc = scales + (g % 3) * 64;
+        const int q = dim >> 2, total = gr * q;
+        const int nwt = kTiledWriters * 32;
+        const int dr = nwt / q, dc = nwt - dr * q;
+        const int wt = wi * 32 + lane;
+        int r = wt / q, c4 = wt - r * q;
+        int vr = -1;
+        bool vok = true;
+        auto xval = [&](int rr_, int c, float *v) {
+            decode_staged<SRC, 4>(base + (size_t)rr_ * L.xstride, dim, c, v);
+            if constexpr (SRC != SRC_X) {
+                if (rr_ != vr) {
+                    vr = rr_;
+                    vok = (unsigned)a.tokens[r0 + rr_] < (unsigned)a.vocab;
+                }
+                if (!vok) v[0] = v[1] = v[2] = v[3] = 0.0f;
+            }
+        };
+        auto step = [&]() {
+            c4 += dc;
+            r += dr;
+            if (c4 >= q) {
+                c4 -= q;
+                ++r;
+            }
+        };
+        if constexpr (FQ) {
+            for (int i = wt; i - lane < total; i += nwt) {
+                const bool ok = i < total;
+                const int c = 4 * c4, row = r0 + r;
+                float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (ok) {
+                    float v[4];
+                    xval(r, c, v);
+                    const size_t o = (size_t)row * dim + c;
+                    if (a.xb) {
+                        const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
+                        const float s1 = sc[r];
+                        st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s1, v[0])), mul_rn(w.y, mul_rn(s1, v[1])),
+                                                  mul_rn(w.z, mul_rn(s1, v[2])), mul_rn(w.w, mul_rn(s1, v[3]))));
+                    }
+                    float4 xo = make_float4(v[0], v[1], v[2], v[3]);
+                    if (has_resid) {
+                        const float4 rv = *reinterpret_cast<const float4 *>(base + (size_t)G * L.xstride +
+                                                                            (size_t)r * L.rstride + 4 * c);
+                        xo = make_float4(add_rn(v[0], rv.x), add_rn(v[1], rv.y), add_rn(v[2], rv.z), add_rn(v[3], rv.w));
+                    }
+                    if (a.x_out) st4(a.x_out + o, xo);
+                    const float4 wf = __ldg(reinterpret_cast<const float4 *>(a.w_final + c));
+                    const float s2 = sc[32 + r];
+                    y = make_float4(mul_rn(wf.x, mul_rn(s2, xo.x)), mul_rn(wf.y, mul_rn(s2, xo.y)),
+                                    mul_rn(wf.z, mul_rn(s2, xo.z)), mul_rn(wf.w, mul_rn(s2, xo.w)));
+                }
+                float am = fmaxf(fmaxf(fmaxf(0.0f, fabsf(y.x)), fmaxf(0.0f, fabsf(y.y))),
+                                 fmaxf(fmaxf(0.0f, fabsf(y.z)), fmaxf(0.0f, fabsf(y.w))));
+                am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
+                am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
+                am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
+                if (ok) {
+                    const int nb = dim >> 5;
+                    const float d = div_rn(am, 127.0f);
+                    const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+                    const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y.x, inv)) |
+                                            ((uint32_t)(uint8_t)q8_code(mul_rn(y.y, inv)) << 8) |
+                                            ((uint32_t)(uint8_t)q8_code(mul_rn(y.z, inv)) << 16) |
+                                            ((uint32_t)(uint8_t)q8_code(mul_rn(y.w, inv)) << 24);
+                    *reinterpret_cast<uint32_t *>(a.codes + (size_t)row * dim + c) = packed;
+                    if ((c4 & 7) == 0) {
+                        a.scales[(size_t)row * nb + (c >> 5)] = d;
+                        if (a.scales16) a.scales16[(size_t)row * nb + (c >> 5)] = f16_bits(d);
+                    }
+                }
+                step();
+            }
+            return;
+        }
+        constexpr int U = 8;
+        for (int i = wt; i < total; i += U * nwt) {
+            int rs[U], cs[U];
+            float4 rv[U];
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                rs[k] = r;
+                cs[k] = 4 * c4;
+                if (has_resid && a.x_out && i + k * nwt < total) rv[k] = ld4(a.resid + (size_t)(r0 + r) * dim + cs[k]);
+                step();
+            }
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                if (i + k * nwt >= total) break;
+                const size_t o = (size_t)(r0 + rs[k]) * dim + cs[k];
+                float v[4];
+                xval(rs[k], cs[k], v);
+                if (a.xb) {
+                    const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + cs[k]));
+                    const float s = sc[rs[k]];
+                    st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[0])), mul_rn(w.y, mul_rn(s, v[1])),
+                                              mul_rn(w.z, mul_rn(s, v[2])), mul_rn(w.w, mul_rn(s, v[3]))));
+                }
+                if (a.x_out) {
+                    float4 xo = make_float4(v[0], v[1], v[2], v[3]);
+                    if (has_resid)
+                        xo = make_float4(add_rn(v[0], rv[k].x), add_rn(v[1], rv[k].y), add_rn(v[2], rv[k].z),
+                                         add_rn(v[3], rv[k].w));
+                    st4(a.x_out + o, xo);
+                }
+            }
+        }
+    };
+
+    int issued = 0;  // warp 4's count of groups issued
+    if (warp == 4 && nmine > 0) issue(issued++);
+    for (int i = 0; i <= nmine; ++i) {
+        if (warp == 4) {
+            if (issued < nmine && issued == i + 1 && !__shfl_sync(kFull, s_abort, 0)) issue(issued++);
+        } else if (warp == 0) {
+            if (i < nmine) sum(i);
+        } else if ((warp & 3) != 0) {
+            if (i >= 1) write(i - 1);
+        }
+        __syncthreads();
+    }
+    if (warp == 4 && lane == 0 && s_abort)
+        for (int g = max(0, issued - 3); g < issued; ++g) mbar_wait_bounded(&bars[g % 3], (uint32_t)(g / 3) & 1u);
 }
 
 // The chain's pure streams (RoPE on Q and K, SwiGLU) over all rows: no
@@ -1734,10 +2428,10 @@ QkLaunch qk_launch_config(K kern, int width, int head, int rows) {
     return c;
 }
 
-// The norm stage as the persistent pipeline: rows per group from the shared
-// memory that lets two CTAs share an SM, fewer when the rows would give a CTA
-// under eight groups.  Contiguous f32 rows are re-read by the writers (two
-// slots); gathered or quantising rows are written from their slot (three).
+// The norm stage as the persistent pipeline, one CTA per SM: rows per group
+// from the SM's shared memory, fewer when the rows would give a CTA under
+// eight groups.  Contiguous f32 rows are re-read by the writers (two slots);
+// gathered or quantising rows are written from their slot (three).
 template <int SRC, bool VEC, bool PRE_ADD = false, bool FQ = false>
 cudaError_t launch_norm_pipe(const ChainArgs &a, cudaStream_t s) {
     constexpr bool RR = SRC == SRC_X && !FQ;
@@ -1746,12 +2440,12 @@ cudaError_t launch_norm_pipe(const ChainArgs &a, cudaStream_t s) {
     const int rb = SRC == SRC_BF16 ? a.dim * 2 : (SRC == SRC_Q8 ? a.dim : a.dim * 4);
     L.xstride = align16(rb) + (SRC == SRC_Q8 ? align16((a.dim / 32) * 4) : 0) + 16;
     L.rstride = (FQ && a.resid) ? align16(a.dim * 4) + 16 : 0;
-    const size_t budget = 110 * 1024 - NS * 64 * sizeof(float);
+    const size_t budget = 224 * 1024 - NS * 64 * sizeof(float);
     int G = (int)(budget / (NS * (size_t)(L.xstride + L.rstride)));
     if (G > 32) G = 32;
     if (G < 1) G = 1;
     const int sms = device_sms();
-    const long want = ((long)a.rows + (long)sms * 2 * 8 - 1) / ((long)sms * 2 * 8);
+    const long want = ((long)a.rows + (long)sms * 8 - 1) / ((long)sms * 8);
     if (want < G) G = (int)(want > 0 ? want : 1);
     L.G = G;
     L.smem = NS * (size_t)G * (L.xstride + L.rstride) + NS * 64 * sizeof(float);
@@ -1760,13 +2454,117 @@ cudaError_t launch_norm_pipe(const ChainArgs &a, cudaStream_t s) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
     if (e != cudaSuccess) return e;
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, L.smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kPipeThreads, L.smem);
     if (e != cudaSuccess) return e;
     const long groups = ((long)a.rows + G - 1) / G;
     long grid = (long)sms * (per_sm > 0 ? per_sm : 1);
     if (grid > groups) grid = groups;
-    kern<<<(unsigned)grid, kThreads, L.smem, s>>>(a, L);
+    kern<<<(unsigned)grid, kPipeThreads, L.smem, s>>>(a, L);
     return launched();
+}
+
+// The column-tiled norm pipeline where its bulk copies apply: every staged
+// address and size 16-byte aligned (dim % 8, % 32 when quantising, % 128 for
+// Q8_0 sources), so every tile boundary is too.  Rows per group come from
+// the L2 the writers' re-reads may hold (48 MB over all CTAs, two groups
+// each), the tile width from the shared memory of three slots.  Returns
+// false (nothing launched) where it does not apply.
+inline bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
+
+template <int SRC, bool PRE_ADD, bool FQ>
+bool try_norm_tiled(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
+    const int esz = SRC == SRC_BF16 ? 2 : (SRC == SRC_Q8 ? 1 : 4);
+    const int gran = SRC == SRC_Q8 ? 128 : (FQ ? 32 : 8);
+    if (a.rows <= 0 || a.dim <= 0 || a.dim % gran) return false;
+    const void *src = SRC == SRC_X ? (const void *)a.x_in : a.table;
+    if (!al16(src) || (SRC == SRC_Q8 && !al16(a.tscales)) || (a.resid && !al16(a.resid)) ||
+        (a.x_out && !al16(a.x_out)) || (a.xb && !al16(a.xb)) || (a.w_att && !al16(a.w_att)) ||
+        (FQ && (!al16(a.w_final) || ((uintptr_t)a.codes & 3u))))
+        return false;
+    const bool sum_resid = PRE_ADD || (FQ && a.resid);
+    const bool write_resid = a.resid && (PRE_ADD || FQ || a.x_out);
+    const int sms = device_sms();
+    // the write ring's copies of x (and of a summed resid) come from L2
+    const size_t reread = (size_t)a.dim * esz + (sum_resid ? (size_t)a.dim * 4 : 0);
+    long G = (long)((48ull << 20) / (2 * reread * (size_t)sms));
+    if (G > 32) G = 32;
+    if (G < 1) G = 1;
+    const long per_cta = ((long)a.rows + sms - 1) / sms;
+    if (G > per_cta) G = per_cta;
+    // shared memory per column of one row, over both rings
+    const double xcol = esz + (SRC == SRC_Q8 ? 0.125 : 0.0);
+    const double per_col = kTiledSlots * (2 * xcol + (sum_resid ? 4.0 : 0.0) + (write_resid ? 4.0 : 0.0));
+    const long per_row = (long)((208u << 10) / (size_t)G) - kTiledSlots * 4 * 48;
+    long tcmax = (long)(per_row / per_col) / gran * gran;
+    if (tcmax < gran) return false;
+    const int T = (int)((a.dim + tcmax - 1) / tcmax);
+    const int TC = (int)(((a.dim + T - 1) / T + gran - 1) / gran * gran);
+    TiledLayout L{};
+    L.G = (int)G;
+    L.TC = TC;
+    L.T = (a.dim + TC - 1) / TC;
+    // odd multiples of 16 bytes: the summing lanes' 16-byte loads of one
+    // column fall in distinct banks
+    const int xb = TC * esz + (SRC == SRC_Q8 ? align16(TC / 8) : 0);
+    L.xstride = ((xb + 31) & ~31) + 16;
+    const int rs = ((TC * 4 + 31) & ~31) + 16;
+    L.srstride = sum_resid ? rs : 0;
+    L.wrstride = write_resid ? rs : 0;
+    L.sslot = L.G * (L.xstride + L.srstride);
+    L.wslot = L.G * (L.xstride + L.wrstride);
+    L.smem = (size_t)kTiledSlots * (L.sslot + L.wslot) + 128 * sizeof(float) + 2 * kTiledSlots * sizeof(uint64_t);
+    if (L.smem > 226 * 1024) return false;
+    auto kern = k_norm_tiled<SRC, PRE_ADD, FQ>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
+    if (e != cudaSuccess) {
+        *err = e;
+        return true;
+    }
+    const long groups = ((long)a.rows + L.G - 1) / L.G;
+    const long grid = groups < sms ? groups : sms;
+    kern<<<(unsigned)grid, kTiledThreads, L.smem, s>>>(a, L);
+    *err = launched();
+    return true;
+}
+
+// The whole-row pipeline where its bulk copies apply (16-byte aligned rows:
+// dim % 8, % 32 when quantising, % 128 for Q8_0 sources) and three slots of
+// at least four rows fit in shared memory.  Returns false (nothing launched)
+// otherwise.
+template <int SRC, bool FQ>
+bool try_norm_rows(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
+    const int gran = SRC == SRC_Q8 ? 128 : (FQ ? 32 : 8);
+    if (a.rows <= 0 || a.dim <= 0 || a.dim % gran) return false;
+    const void *src = SRC == SRC_X ? (const void *)a.x_in : a.table;
+    if (!al16(src) || (SRC == SRC_Q8 && !al16(a.tscales)) || (a.resid && !al16(a.resid)) ||
+        (a.x_out && !al16(a.x_out)) || (a.xb && !al16(a.xb)) || (a.w_att && !al16(a.w_att)) ||
+        (FQ && (!al16(a.w_final) || ((uintptr_t)a.codes & 3u))))
+        return false;
+    const int esz = SRC == SRC_BF16 ? 2 : (SRC == SRC_Q8 ? 1 : 4);
+    RowsLayout L{};
+    const int xb = a.dim * esz + (SRC == SRC_Q8 ? align16(a.dim / 8) : 0);
+    L.xstride = ((xb + 31) & ~31) + 16;
+    L.rstride = (FQ && a.resid) ? ((a.dim * 4 + 31) & ~31) + 16 : 0;
+    long G = (long)((214u << 10) / (3 * (size_t)(L.xstride + L.rstride)));
+    if (G > 32) G = 32;
+    if (G < 4) return false;
+    const int sms = device_sms();
+    const long per_cta = ((long)a.rows + sms - 1) / sms;
+    if (G > per_cta) G = per_cta;
+    L.G = (int)G;
+    L.slot = L.G * (L.xstride + L.rstride);
+    L.smem = 3 * (size_t)L.slot + 192 * sizeof(float) + 3 * sizeof(uint64_t);
+    auto kern = k_norm_rows<SRC, FQ>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
+    if (e != cudaSuccess) {
+        *err = e;
+        return true;
+    }
+    const long groups = ((long)a.rows + L.G - 1) / L.G;
+    const long grid = groups < sms ? groups : sms;
+    kern<<<(unsigned)grid, kTiledThreads, L.smem, s>>>(a, L);
+    *err = launched();
+    return true;
 }
 
 template <int SRC>
@@ -1804,10 +2602,13 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
     cudaError_t e = cudaSuccess;
     if (fq_pipe) {
         mark(hook, STAGE_NORM);
-        e = launch_norm_pipe<SRC, true, false, true>(a, s);
+        if (!try_norm_rows<SRC, true>(a, s, &e)) e = launch_norm_pipe<SRC, true, false, true>(a, s);
     } else if (a.xb || a.x_out) {
         mark(hook, STAGE_NORM);
-        e = vec ? launch_norm_pipe<SRC, true>(a, s) : launch_norm_pipe<SRC, false>(a, s);
+        // f32 x rows: the column-tiled pipeline keeps more rows' sums in flight
+        const bool done = vec && (SRC == SRC_X ? try_norm_tiled<SRC, false, false>(a, s, &e)
+                                               : try_norm_rows<SRC, false>(a, s, &e));
+        if (!done) e = vec ? launch_norm_pipe<SRC, true>(a, s) : launch_norm_pipe<SRC, false>(a, s);
     }
     if (e != cudaSuccess) return e;
     if (any_stream && qk_stream) {
@@ -1912,6 +2713,8 @@ cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows,
 cudaError_t launch_add_rms_norm(const ChainArgs &a, cudaStream_t s) {
     if (a.rows <= 0) return cudaSuccess;
     if (a.dim % 8 != 0) return cudaErrorInvalidValue;
+    cudaError_t e = cudaSuccess;
+    if (try_norm_tiled<SRC_X, true, false>(a, s, &e)) return e;
     return launch_norm_pipe<SRC_X, true, true, false>(a, s);
 }
 

@@ -10,7 +10,7 @@
 namespace krt {
 
 // Bits of the device error word (checked by the host at every barrier).
-enum : int { ERR_TOKEN = 1, ERR_POSITION = 2 };
+enum : int { ERR_TOKEN = 1, ERR_POSITION = 2, ERR_TIMEOUT = 4 };
 
 // Kernels this library has launched in this process, and the counter hook
 // every launcher calls.

@@ -7,6 +7,7 @@ configurations plus ragged/odd sizes that take the kernels' scalar paths.
 import numpy as np
 import pytest
 
+import kernrt_b200
 from tests import _data
 from tests._parity import assert_bits_equal, assert_close_rel
 
@@ -95,15 +96,39 @@ def test_embed_rejects_bad_token_and_offset(gpu, oracle):
 
 # --- rms_norm (reference.rs:161-178) ---------------------------------------------------
 
+# Enough rows for several row groups per CTA and several column tiles per row
+# in the tiled pipeline (5000x2048, 3001x576, 2000x8192), few rows, and widths
+# that take the unaligned fallback.
 @pytest.mark.parametrize("rows,dim,eps", [(1, 2048, 1e-5), (7, 576, 1e-5), (33, 1536, 1e-6),
                                           (5, 37, 1e-5), (64, 1024, 1e-6), (3, 8192, 1e-5),
-                                          (2, 12, 0.0), (100, 2048, 1e-5)])
+                                          (2, 12, 0.0), (100, 2048, 1e-5), (5000, 2048, 1e-5),
+                                          (3001, 576, 1e-6), (2000, 8192, 1e-5)])
 def test_rms_norm(gpu, oracle, rows, dim, eps):
     x = _data.lcg_normal(rows * dim, 10 + dim).reshape(rows, dim)
     w = _data.lcg_normal(dim, 11, 1.0, 0.1)
     hx, hw, ho = up(gpu, x), up(gpu, w), gpu.alloc(rows * dim)
     gpu.rms_norm(ho, hx, hw, rows, dim, eps)
     assert_bits_equal(rd(gpu, ho, (rows, dim)), oracle.rms_norm(x, w, eps), f"rms {rows}x{dim}")
+
+
+@pytest.mark.parametrize("rows,dim", [(4000, 2048), (300, 1536), (7, 64), (9, 20)])
+def test_add_in_place_then_rms_norm_fuses(gpu, oracle, rows, dim):
+    """The driver's add_in_place(x, o) -> rms_norm(xb, x) pair (llama.rs:762-765)
+    runs as one launch (for rows of whole float4 pairs) and matches the two ops
+    in order."""
+    x = _data.lcg_normal(rows * dim, 13 + dim).reshape(rows, dim)
+    o = _data.lcg_normal(rows * dim, 14 + dim).reshape(rows, dim)
+    w = _data.lcg_normal(dim, 15, 1.0, 0.1)
+    hx, ho, hw, hxb = up(gpu, x), up(gpu, o), up(gpu, w), gpu.alloc(rows * dim)
+    gpu.synchronize()
+    n0 = kernrt_b200.kernel_launches()
+    gpu.add_in_place(hx, ho, rows * dim)
+    gpu.rms_norm(hxb, hx, hw, rows, dim, 1e-5)
+    gpu.synchronize()
+    assert kernrt_b200.kernel_launches() - n0 == (1 if dim % 8 == 0 else 2)
+    xs = oracle.add_in_place(x, o)
+    assert_bits_equal(rd(gpu, hx, (rows, dim)), xs, "x + o")
+    assert_bits_equal(rd(gpu, hxb, (rows, dim)), oracle.rms_norm(xs, w, 1e-5), "xb")
 
 
 def test_rms_norm_partial_rows_leave_the_rest(gpu, oracle):
@@ -290,7 +315,8 @@ def test_quantize_q8_0(gpu, oracle, rows, dim):
     assert_bits_equal(gpu.read_bytes(hh, rows * nb * 2, np.uint16).reshape(rows, -1), wh, "f16 scales")
 
 
-@pytest.mark.parametrize("rows,dim,eps", [(256, 1024, 1e-6), (5, 2048, 1e-5), (3, 40, 1e-5)])
+@pytest.mark.parametrize("rows,dim,eps", [(256, 1024, 1e-6), (5, 2048, 1e-5), (3, 40, 1e-5),
+                                          (5000, 1024, 1e-6), (1000, 4096, 1e-5), (333, 96, 1e-5)])
 def test_rms_norm_q8_0_fused(gpu, oracle, rows, dim, eps):
     x = _data.lcg_normal(rows * dim, 70 + dim).reshape(rows, dim)
     w = _data.lcg_normal(dim, 71, 1.0, 0.1)
