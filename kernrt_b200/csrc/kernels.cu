@@ -14,6 +14,7 @@
 // No kernel asserts or traps: bad token ids / positions set a bit in a device
 // error word that the host checks at its next barrier.
 #include "kernels.cuh"
+#include "q8_math.cuh"
 
 #include <cuda_fp16.h>
 
@@ -54,15 +55,6 @@ __device__ __forceinline__ float rms_scale(float ss, float n, float eps) {
     ss = div_rn(ss, n);
     ss = add_rn(ss, eps);
     return div_rn(1.0f, __fsqrt_rn(ss));
-}
-
-// quant.rs:871: (v * inv).round().clamp(-127, 127) as i8 — round half away
-// from zero, NaN -> 0.
-__device__ __forceinline__ int8_t q8_code(float v) {
-    float r = roundf(v);
-    r = (r < -127.0f) ? -127.0f : r;
-    r = (r > 127.0f) ? 127.0f : r;
-    return (r != r) ? (int8_t)0 : (int8_t)__float2int_rz(r);
 }
 
 // quant.rs:722-758 is IEEE binary16 round-to-nearest-even; the block scale it
@@ -783,8 +775,8 @@ __global__ void __launch_bounds__(kThreads, 3) k_chain(ChainArgs a, ChainLayout 
                 float am = fmaxf(0.0f, fabsf(y));
 #pragma unroll
                 for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(kFull, am, off));
-                const float d = div_rn(am, 127.0f);
-                const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+                const float d = q8_scale(am);
+                const float inv = d > 0.0f ? q8_inv(d) : 0.0f;
                 a.codes[(size_t)row * nb * 32 + i] = ok ? q8_code(mul_rn(y, inv)) : (int8_t)0;
                 if (lane == 0) {
                     a.scales[(size_t)row * nb + b] = d;
@@ -1052,8 +1044,8 @@ __global__ void __launch_bounds__(kPipeThreads, 1) k_norm_pipe(ChainArgs a, Chai
                 am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
                 am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
                 if (!ok) continue;
-                const float d = div_rn(am, 127.0f);
-                const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+                const float d = q8_scale(am);
+                const float inv = d > 0.0f ? q8_inv(d) : 0.0f;
                 const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y.x, inv)) |
                                         ((uint32_t)(uint8_t)q8_code(mul_rn(y.y, inv)) << 8) |
                                         ((uint32_t)(uint8_t)q8_code(mul_rn(y.z, inv)) << 16) |
@@ -1167,6 +1159,11 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
                      smem_addr(dst)),
                  "l"(src), "r"(bytes), "r"(smem_addr(bar))
                  : "memory");
+}
+
+// Bulk prefetch of global memory into L2 (no shared memory, no completion).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
@@ -1468,8 +1465,8 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_tiled(ChainArgs a, Ti
                 am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
                 if (ok) {
                     const int nb = dim >> 5;
-                    const float d = div_rn(am, 127.0f);
-                    const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+                    const float d = q8_scale(am);
+                    const float inv = d > 0.0f ? q8_inv(d) : 0.0f;
                     const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y.x, inv)) |
                                             ((uint32_t)(uint8_t)q8_code(mul_rn(y.y, inv)) << 8) |
                                             ((uint32_t)(uint8_t)q8_code(mul_rn(y.z, inv)) << 16) |
@@ -1749,8 +1746,8 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
                 am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
                 if (ok) {
                     const int nb = dim >> 5;
-                    const float d = div_rn(am, 127.0f);
-                    const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+                    const float d = q8_scale(am);
+                    const float inv = d > 0.0f ? q8_inv(d) : 0.0f;
                     const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y.x, inv)) |
                                             ((uint32_t)(uint8_t)q8_code(mul_rn(y.y, inv)) << 8) |
                                             ((uint32_t)(uint8_t)q8_code(mul_rn(y.z, inv)) << 16) |
@@ -1799,11 +1796,21 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
         }
     };
 
+    // The writers' residual rows (read from global memory) are prefetched
+    // into L2 one iteration before they are written, so their loads wait on
+    // L2 rather than HBM.
+    auto prefetch_resid = [&](int g) {  // warp 4
+        const int r0 = first_row(g), gr = min(G, a.rows - r0);
+        if (lane < gr) bulk_prefetch_l2(a.resid + (size_t)(r0 + lane) * dim, (uint32_t)dim * 4u);
+    };
+    const bool fetch_resid = has_resid && !stage_resid && a.x_out;
+
     int issued = 0;  // warp 4's count of groups issued
     if (warp == 4 && nmine > 0) issue(issued++);
     for (int i = 0; i <= nmine; ++i) {
         if (warp == 4) {
             if (issued < nmine && issued == i + 1 && !__shfl_sync(kFull, s_abort, 0)) issue(issued++);
+            if (fetch_resid && i < nmine) prefetch_resid(i);
         } else if (warp == 0) {
             if (i < nmine) sum(i);
         } else if ((warp & 3) != 0) {
@@ -2241,8 +2248,8 @@ __global__ void __launch_bounds__(kThreads) k_quantize_q8(const float *__restric
         float am = fmaxf(0.0f, fabsf(y));
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) am = fmaxf(am, __shfl_xor_sync(kFull, am, off));
-        const float d = div_rn(am, 127.0f);
-        const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+        const float d = q8_scale(am);
+        const float inv = d > 0.0f ? q8_inv(d) : 0.0f;
         codes[(size_t)row * nb * 32 + i] = ok ? q8_code(mul_rn(y, inv)) : (int8_t)0;
         if (lane == 0) {
             scales[(size_t)row * nb + b] = d;
@@ -2280,8 +2287,8 @@ __global__ void __launch_bounds__(kThreads) k_quantize_q8v(const float *__restri
             am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
             am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
             if (idx >= items) continue;
-            const float d = div_rn(am, 127.0f);
-            const float inv = d > 0.0f ? div_rn(1.0f, d) : 0.0f;
+            const float d = q8_scale(am);
+            const float inv = d > 0.0f ? q8_inv(d) : 0.0f;
             const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y[k].x, inv)) |
                                     ((uint32_t)(uint8_t)q8_code(mul_rn(y[k].y, inv)) << 8) |
                                     ((uint32_t)(uint8_t)q8_code(mul_rn(y[k].z, inv)) << 16) |

@@ -1,0 +1,47 @@
+// Q8_0 block arithmetic (quant.rs:856-874), shared by the kernels and by the
+// exhaustive check in tests/cuda/q8_math_check.cu.  Compiled with -fmad=false;
+// the fused multiply-adds below are explicit.
+#pragma once
+#include <cstdint>
+
+namespace krt {
+
+// d = amax / 127, correctly rounded, for amax >= +0 (a fold of fmaxf from
+// +0.0, so never -0 or NaN).  The product with the rounded reciprocal c of 127
+// is corrected once by its exact residual r = amax - 127 q0 (computed exactly
+// by the fused multiply-add): q1 = q0 + r c (P. Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990).  +inf passes through.  Checked against the correctly
+// rounded division for every non-negative f32.
+__device__ __forceinline__ float q8_scale(float amax) {
+    const float c = 1.0f / 127.0f;
+    const float q0 = __fmul_rn(amax, c);
+    const float r = __fmaf_rn(-q0, 127.0f, amax);
+    const float q1 = __fmaf_rn(r, c, q0);
+    return amax < __int_as_float(0x7f800000) ? q1 : amax;
+}
+
+// 1 / d, correctly rounded, for d > 0: the hardware reciprocal approximation
+// y0 refined by one Newton-Raphson step y1 = y0 + y0 (1 - d y0) with fused
+// multiply-adds (Markstein 1990, as above).  Quotients that overflow
+// (d <= 2^-128) or fall into the subnormals (d > 2^126, or +inf) take the
+// correctly rounded division; d = amax / 127 never exceeds 2^122 for finite
+// amax.  Checked against the correctly rounded division for every positive
+// f32.
+__device__ __forceinline__ float q8_inv(float d) {
+    if (d <= 0x1p-128f || d > 0x1p126f) return __fdiv_rn(1.0f, d);
+    float y0;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(y0) : "f"(d));
+    const float e = __fmaf_rn(-d, y0, 1.0f);
+    return __fmaf_rn(e, y0, y0);
+}
+
+// quant.rs:871: (v * inv).round().clamp(-127, 127) as i8 -- round half away
+// from zero, NaN -> 0.  The float-to-int conversion saturates and maps NaN to
+// 0, so the clamp can run on the integer.
+__device__ __forceinline__ int8_t q8_code(float v) {
+    const int i = __float2int_rz(roundf(v));
+    return (int8_t)max(-127, min(127, i));
+}
+
+}  // namespace krt
