@@ -1546,6 +1546,8 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_tiled(ChainArgs a, Ti
     }
 }
 
+constexpr int kRowsSlots = 4;  // writing, summing, and two staged ahead
+
 struct RowsLayout {
     int G;        // rows per group (<= 32)
     int xstride;  // bytes per staged row (+ Q8 block scales), an odd multiple of 16
@@ -1554,11 +1556,11 @@ struct RowsLayout {
     size_t smem;
 };
 
-// The norm stage over whole staged rows, one 16-warp CTA per SM, three slots
+// The norm stage over whole staged rows, one 16-warp CTA per SM, four slots
 // of G rows, each filled by one bulk copy per row (a full row is big enough
 // that the copy engine's per-request cost stays far below the row's
 // traffic).  In iteration i:
-//   warp 4    issues group i+1's copies into slot (i+1)%3, lane r those of
+//   warp 4    issues group i+2's copies into slot (i+2)%4, lane r those of
 //             row r (its x or embedding row, Q8 block scales, and the f32
 //             resid row when the quantised norm sums x + resid), counted on
 //             the slot's mbarrier;
@@ -1567,8 +1569,10 @@ struct RowsLayout {
 //   writers   (12 warps on the other sub-partitions) write group i-1 from its
 //             slot: xb = w*(scale*x), x + resid (resid from global memory,
 //             eight float4 loads in flight per lane), or the Q8_0 codes.
-// Warps 8 and 12 only keep the barrier count.  FQ is the final RMSNorm fused
-// with Q8_0 quantisation (quant.rs:856-874).
+// Staging two groups ahead keeps a group's copies in flight for two
+// iterations, longer than their HBM latency under load.  Warps 8 and 12 only
+// keep the barrier count.  FQ is the final RMSNorm fused with Q8_0
+// quantisation (quant.rs:856-874).
 template <int SRC, bool FQ>
 __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, RowsLayout L) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -1576,19 +1580,20 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
     const int dim = a.dim, G = L.G;
     const int ngroups = (a.rows + G - 1) / G;
     const int nmine = (int)blockIdx.x < ngroups ? (ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
-    float *scales = reinterpret_cast<float *>(smem + 3 * (size_t)L.slot);  // [3][64]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(scales + 192);           // [3]
+    constexpr int NS = kRowsSlots;
+    float *scales = reinterpret_cast<float *>(smem + NS * (size_t)L.slot);  // [NS][64]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(scales + NS * 64);        // [NS]
     __shared__ int s_abort;
     const bool has_resid = a.resid != nullptr;
     const bool stage_resid = FQ && has_resid;
     const int rb = src_row_bytes<SRC>(dim);
 
     auto first_row = [&](int g) { return (int)(blockIdx.x + (unsigned)g * gridDim.x) * G; };
-    auto slot = [&](int g) { return smem + (size_t)(g % 3) * L.slot; };
+    auto slot = [&](int g) { return smem + (size_t)(g % NS) * L.slot; };
 
     if (tid == 0) {
         s_abort = 0;
-        for (int i = 0; i < 3; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -1614,7 +1619,7 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
         uint32_t total = mine;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFull, total, o);
-        uint64_t *bar = &bars[g % 3];
+        uint64_t *bar = &bars[g % NS];
         if (lane == 0) mbar_arrive_expect_tx(bar, total);
         __syncwarp();
         if (lane < gr) {
@@ -1633,7 +1638,7 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
     auto sum = [&](int g) {  // warp 0
         const int r0 = first_row(g), gr = min(G, a.rows - r0);
         if (s_abort) return;
-        if (!mbar_wait_bounded(&bars[g % 3], (uint32_t)(g / 3) & 1u)) {
+        if (!mbar_wait_bounded(&bars[g % NS], (uint32_t)(g / NS) & 1u)) {
             if (lane == 0) {
                 set_err(a.err, ERR_TIMEOUT);
                 s_abort = 1;
@@ -1644,7 +1649,7 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
         bool valid = true;
         if constexpr (SRC != SRC_X) valid = (unsigned)a.tokens[r0 + lane] < (unsigned)a.vocab;
         const unsigned char *xr = slot(g) + (size_t)lane * L.xstride;
-        float *sc = scales + (g % 3) * 64;
+        float *sc = scales + (g % NS) * 64;
         float ss = 0.0f;
         if (FQ && stage_resid) {
             const float *rr = reinterpret_cast<const float *>(slot(g) + (size_t)G * L.xstride + (size_t)lane * L.rstride);
@@ -1686,7 +1691,7 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
         if (s_abort) return;
         const int r0 = first_row(g), gr = min(G, a.rows - r0);
         const unsigned char *base = slot(g);
-        const float *sc = scales + (g % 3) * 64;
+        const float *sc = scales + (g % NS) * 64;
         const int q = dim >> 2, total = gr * q;
         const int nwt = kTiledWriters * 32;
         const int dr = nwt / q, dc = nwt - dr * q;
@@ -1805,11 +1810,15 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
     };
     const bool fetch_resid = has_resid && !stage_resid && a.x_out;
 
+    // warp 4 stages LA = NS - 2 groups ahead of the sums: group i + LA goes
+    // into the slot the writers left in iteration i - 1
+    constexpr int LA = NS - 2;
     int issued = 0;  // warp 4's count of groups issued
-    if (warp == 4 && nmine > 0) issue(issued++);
+    if (warp == 4)
+        while (issued < min(nmine, LA)) issue(issued++);
     for (int i = 0; i <= nmine; ++i) {
         if (warp == 4) {
-            if (issued < nmine && issued == i + 1 && !__shfl_sync(kFull, s_abort, 0)) issue(issued++);
+            if (issued < nmine && issued == i + LA && !__shfl_sync(kFull, s_abort, 0)) issue(issued++);
             if (fetch_resid && i < nmine) prefetch_resid(i);
         } else if (warp == 0) {
             if (i < nmine) sum(i);
@@ -1819,7 +1828,7 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
         __syncthreads();
     }
     if (warp == 4 && lane == 0 && s_abort)
-        for (int g = max(0, issued - 3); g < issued; ++g) mbar_wait_bounded(&bars[g % 3], (uint32_t)(g / 3) & 1u);
+        for (int g = max(0, issued - NS); g < issued; ++g) mbar_wait_bounded(&bars[g % NS], (uint32_t)(g / NS) & 1u);
 }
 
 // The chain's pure streams (RoPE on Q and K, SwiGLU) over all rows: no
@@ -2535,7 +2544,7 @@ bool try_norm_tiled(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
 }
 
 // The whole-row pipeline where its bulk copies apply (16-byte aligned rows:
-// dim % 8, % 32 when quantising, % 128 for Q8_0 sources) and three slots of
+// dim % 8, % 32 when quantising, % 128 for Q8_0 sources) and four slots of
 // at least four rows fit in shared memory.  Returns false (nothing launched)
 // otherwise.
 template <int SRC, bool FQ>
@@ -2552,7 +2561,7 @@ bool try_norm_rows(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
     const int xb = a.dim * esz + (SRC == SRC_Q8 ? align16(a.dim / 8) : 0);
     L.xstride = ((xb + 31) & ~31) + 16;
     L.rstride = (FQ && a.resid) ? ((a.dim * 4 + 31) & ~31) + 16 : 0;
-    long G = (long)((214u << 10) / (3 * (size_t)(L.xstride + L.rstride)));
+    long G = (long)((214u << 10) / (kRowsSlots * (size_t)(L.xstride + L.rstride)));
     if (G > 32) G = 32;
     if (G < 4) return false;
     const int sms = device_sms();
@@ -2560,7 +2569,7 @@ bool try_norm_rows(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
     if (G > per_cta) G = per_cta;
     L.G = (int)G;
     L.slot = L.G * (L.xstride + L.rstride);
-    L.smem = 3 * (size_t)L.slot + 192 * sizeof(float) + 3 * sizeof(uint64_t);
+    L.smem = kRowsSlots * ((size_t)L.slot + 64 * sizeof(float) + sizeof(uint64_t));
     auto kern = k_norm_rows<SRC, FQ>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
     if (e != cudaSuccess) {

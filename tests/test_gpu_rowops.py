@@ -102,7 +102,8 @@ def test_embed_rejects_bad_token_and_offset(gpu, oracle):
 @pytest.mark.parametrize("rows,dim,eps", [(1, 2048, 1e-5), (7, 576, 1e-5), (33, 1536, 1e-6),
                                           (5, 37, 1e-5), (64, 1024, 1e-6), (3, 8192, 1e-5),
                                           (2, 12, 0.0), (100, 2048, 1e-5), (5000, 2048, 1e-5),
-                                          (3001, 576, 1e-6), (2000, 8192, 1e-5)])
+                                          (3001, 576, 1e-6), (2000, 8192, 1e-5), (700, 1000, 1e-5),
+                                          (1200, 96, 1e-6)])
 def test_rms_norm(gpu, oracle, rows, dim, eps):
     x = _data.lcg_normal(rows * dim, 10 + dim).reshape(rows, dim)
     w = _data.lcg_normal(dim, 11, 1.0, 0.1)
@@ -111,7 +112,7 @@ def test_rms_norm(gpu, oracle, rows, dim, eps):
     assert_bits_equal(rd(gpu, ho, (rows, dim)), oracle.rms_norm(x, w, eps), f"rms {rows}x{dim}")
 
 
-@pytest.mark.parametrize("rows,dim", [(4000, 2048), (300, 1536), (7, 64), (9, 20)])
+@pytest.mark.parametrize("rows,dim", [(4000, 2048), (300, 1536), (7, 64), (9, 20), (640, 1000), (2000, 64)])
 def test_add_in_place_then_rms_norm_fuses(gpu, oracle, rows, dim):
     """The driver's add_in_place(x, o) -> rms_norm(xb, x) pair (llama.rs:762-765)
     runs as one launch (for rows of whole float4 pairs) and matches the two ops
@@ -316,7 +317,8 @@ def test_quantize_q8_0(gpu, oracle, rows, dim):
 
 
 @pytest.mark.parametrize("rows,dim,eps", [(256, 1024, 1e-6), (5, 2048, 1e-5), (3, 40, 1e-5),
-                                          (5000, 1024, 1e-6), (1000, 4096, 1e-5), (333, 96, 1e-5)])
+                                          (5000, 1024, 1e-6), (1000, 4096, 1e-5), (333, 96, 1e-5),
+                                          (800, 96, 1e-5), (700, 1536, 1e-6)])
 def test_rms_norm_q8_0_fused(gpu, oracle, rows, dim, eps):
     x = _data.lcg_normal(rows * dim, 70 + dim).reshape(rows, dim)
     w = _data.lcg_normal(dim, 71, 1.0, 0.1)
