@@ -345,13 +345,14 @@ class CudaBackend:
             setattr(a, name, v)
         _ok(self._lib.kernrt_cuda_layer_chain_host(self._ctx, C.byref(a)))
 
-    STAGES = ("k_norm_pipe", "k_stream", "k_chain")
+    # the norm stage is k_norm_rows, k_norm_tiled or k_norm_pipe by source and width
+    STAGES = ("norm", "stream", "fused")
 
     def stage_timing(self, enable: bool) -> None:
         _ok(self._lib.kernrt_cuda_stage_timing(self._ctx, int(bool(enable))))
 
     def stage_times(self) -> dict:
-        """{kernel: (total device ms, launches)} since stage timing was enabled."""
+        """{stage: (total device ms, launches)} since stage timing was enabled."""
         ms = (C.c_double * 3)()
         n = (C.c_uint64 * 3)()
         _ok(self._lib.kernrt_cuda_stage_times(self._ctx, ms, n))

@@ -68,11 +68,11 @@ class Workload:
         return b
 
     def stage_bytes_per_row(self) -> dict:
-        """The same compulsory bytes split by the kernel that moves them when
-        the chain runs as the norm pipeline plus the RoPE/SwiGLU stream."""
+        """The same compulsory bytes split by the stage that moves them when
+        the chain runs as the norm stage plus the RoPE/SwiGLU stream."""
         f = 4
         stream = 2 * f * self.q_dim + 2 * f * self.kv_dim + 3 * f * self.hidden
-        return {"k_norm_pipe": self.bytes_per_row() - stream, "k_stream": stream}
+        return {"norm": self.bytes_per_row() - stream, "stream": stream}
 
 
 SMOLLM2_135M = Workload("smollm2-135m-prefill128", 49152, 576, 9, 3, 64, 1536, 1e5, 1e-5, "bf16",

@@ -271,8 +271,8 @@ def test_stage_timing_records_each_kernel(gpu):
     gpu_chain(gpu, wl, d)
     t = gpu.stage_times()
     gpu.stage_timing(False)
-    assert t["k_norm_pipe"][1] == 2 and t["k_stream"][1] == 2 and t["k_chain"][1] == 0
-    assert t["k_norm_pipe"][0] > 0 and t["k_stream"][0] > 0
+    assert t["norm"][1] == 2 and t["stream"][1] == 2 and t["fused"][1] == 0
+    assert t["norm"][0] > 0 and t["stream"][0] > 0
 
 
 @pytest.mark.parametrize("wl,chunk", [(W.SMOLLM2_135M, 37), (W.QWEN3_06B_Q8, 0), (W.LFM2_700M, 100),
