@@ -2603,6 +2603,7 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
     // q/k norms or pair-mode RoPE go through the row-staged stream kernel.
     const bool qk_stream = has_qk || (has_rope && a.rope_mode == 2);
     const bool qk_ok = ((a.head | a.q_dim | a.kv_dim) & 3) == 0 && a.head > 0 &&
+                       (a.rope_mode != 1 || (a.head & 7) == 0) &&
                        (a.rope_mode != 2 || (a.q_dim % a.head == 0 && a.kv_dim % a.head == 0));
     const bool streams_vec = ((a.half | a.q_dim | a.kv_dim | a.hidden) & 3) == 0;
     const bool any_stream = has_qk || has_rope || a.gate;
@@ -2738,7 +2739,8 @@ cudaError_t launch_qk_rope(float *q, float *k, int q_width, int kv_width, int ro
                            const float *wk, float eps, const int32_t *pos, const float *cos_t, const float *sin_t,
                            int max_pos, int interleaved, int *err, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
-    const bool whole = !interleaved || (q_width % head == 0 && kv_width % head == 0);
+    // float4 runs of a half head need head % 8; interleaved pairs need whole heads
+    const bool whole = (head & 7) == 0 && (!interleaved || (q_width % head == 0 && kv_width % head == 0));
     const QkLaunch c = whole ? qk_launch_config(k_qk_rope_smem, q_width > kv_width ? q_width : kv_width, head, rows)
                              : QkLaunch{};
     if (c.warps && ((q_width | kv_width) & 3) == 0) {

@@ -131,7 +131,7 @@ def test_chain_lfm2_attention_block(gpu, oracle):
 
 
 @pytest.mark.parametrize("rows,dim,q,kv,head,hidden", [(37, 40, 48, 16, 8, 20), (3, 36, 12, 12, 6, 7),
-                                                       (70, 96, 96, 32, 32, 64)])
+                                                       (70, 96, 96, 32, 32, 64), (21, 40, 12, 8, 4, 20)])
 def test_chain_ragged_shapes(gpu, oracle, rows, dim, q, kv, head, hidden):
     wl = W.Workload("ragged", 50, dim, q // head, kv // head, head, hidden, 1e4, 1e-5, "bf16",
                     rows=rows, seq_len=17, qk_norm=True, final_q8=True)

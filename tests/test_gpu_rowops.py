@@ -157,13 +157,43 @@ def test_rms_norm_rejects_aliasing(gpu):
 
 @pytest.mark.parametrize("rows,width,head", [(5, 1024, 128), (3, 2048, 64), (2, 1536, 64),
                                              (4, 512, 64), (3, 24, 6), (2, 4096, 64),
-                                             (2, 100, 32), (1, 2048, 128)])
+                                             (2, 100, 32), (1, 2048, 128), (3000, 2048, 128),
+                                             (1200, 1536, 64), (500, 16, 4)])
 def test_qk_norm(gpu, oracle, rows, width, head):
     v = _data.lcg_normal(rows * width, 20 + width).reshape(rows, width)
     w = _data.lcg_normal(head, 21, 1.0, 0.1)
     hv, hw = up(gpu, v), up(gpu, w)
     gpu.qk_norm(hv, rows, width, head, hw, 1e-6)
     assert_bits_equal(rd(gpu, hv, (rows, width)), oracle.qk_norm(v, head, w, 1e-6), "qk_norm")
+
+
+# The driver's qk_norm(q), qk_norm(k), rope(q, k) sequence runs as one launch;
+# large row counts give every warp several staged rows, small heads and the
+# interleaved form take their own paths.
+QK_ROPE_SHAPES = [(3000, 2048, 1024, 128, 1e6), (2500, 1536, 512, 64, 1e6), (7, 2048, 1024, 128, 1e6),
+                  (300, 64, 32, 8, 1e4), (40, 8, 8, 4, 1e4), (33, 12, 12, 6, 1e4)]
+
+
+@pytest.mark.parametrize("interleaved", [False, True])
+@pytest.mark.parametrize("rows,qw,kvw,head,theta", QK_ROPE_SHAPES)
+def test_qk_norm_then_rope_fused(gpu, oracle, rows, qw, kvw, head, theta, interleaved):
+    q = _data.lcg_normal(rows * qw, 35 + qw).reshape(rows, qw)
+    k = _data.lcg_normal(rows * kvw, 36 + kvw).reshape(rows, kvw)
+    wq = _data.lcg_normal(head, 37, 1.0, 0.1)
+    wk = _data.lcg_normal(head, 38, 1.0, 0.1)
+    pos = (np.arange(rows, dtype=np.uint64) * 7) % 4096
+    hq, hk, hwq, hwk = up(gpu, q), up(gpu, k), up(gpu, wq), up(gpu, wk)
+    gpu.synchronize()
+    n0 = kernrt_b200.kernel_launches()
+    gpu.qk_norm(hq, rows, qw, head, hwq, 1e-6)
+    gpu.qk_norm(hk, rows, kvw, head, hwk, 1e-6)
+    gpu.rope(hq, hk, qw, kvw, rows, pos, head, theta, interleaved)
+    gpu.synchronize()
+    assert kernrt_b200.kernel_launches() - n0 == 1
+    nq, nk = oracle.qk_norm(q, head, wq, 1e-6), oracle.qk_norm(k, head, wk, 1e-6)
+    want_q, want_k = oracle.rope(nq, nk, pos, head, theta, interleaved)
+    assert_bits_equal(rd(gpu, hq, (rows, qw)), want_q, "q")
+    assert_bits_equal(rd(gpu, hk, (rows, kvw)), want_k, "k")
 
 
 # --- rope (reference.rs:209-257) -----------------------------------------------------------
