@@ -250,6 +250,53 @@ int kernrt_cuda_stage_times(kernrt_cuda_ctx *ctx, double ms[3], uint64_t launche
 int kernrt_cuda_lfm2_conv_block(kernrt_cuda_ctx *ctx, kernrt_buf bcx, kernrt_buf kernel,
                                 kernrt_buf ring, kernrt_buf cy, size_t rows, size_t dim, size_t k);
 
+/* --- Contractions: Backend::project / logits / kv_write / attention ----------
+ * The reference backend's arithmetic order (reference.rs:73-79 dot, one f32
+ * accumulator left to right, multiply then add): projections, logits and the
+ * cache write are bit-identical to it; attention differs only through expf. */
+
+/* A weight matrix prepared once (the weights Backend::prepare receives,
+ * mod.rs:268-273): handle = index + 1. */
+typedef uint64_t kernrt_mat;
+
+/* Uploads W [out_dim, in_dim] in its stored format (kinds and layouts as for
+ * kernrt_cuda_prepare_embedding; Matrix, quant.rs:502-520). */
+int kernrt_cuda_prepare_matrix(kernrt_cuda_ctx *ctx, int kind, const void *data, const float *scales,
+                               size_t out_dim, size_t in_dim, kernrt_mat *out);
+
+/* Backend::project (mod.rs:318; reference.rs:259-274): y[r, o] =
+ * dot(decode_row(W, o), x[r]) for rows r; x [rows, in_dim], y [rows, out_dim].
+ * The trait's project_qkv / project_gate_up defaults (mod.rs:326-337) are
+ * three / two of these calls. */
+int kernrt_cuda_project(kernrt_cuda_ctx *ctx, kernrt_mat w, kernrt_buf x, kernrt_buf y, size_t rows);
+
+/* Backend::logits (mod.rs:403; reference.rs:402-416): the classifier W over
+ * row 0 of x. */
+int kernrt_cuda_logits(kernrt_cuda_ctx *ctx, kernrt_mat w, kernrt_buf x, kernrt_buf y);
+
+/* The key/value caches of a KvSpec (mod.rs:169-177), [n_layers][seq_len]
+ * [kv_dim] f32 each, zero-filled; Backend::prepare's cache half. */
+int kernrt_cuda_kv_prepare(kernrt_cuda_ctx *ctx, size_t n_layers, size_t kv_dim, size_t seq_len);
+
+/* Backend::kv_write (mod.rs:344; reference.rs:151-159): rows
+ * min(rows, n_slots) of k and v [rows, kv_dim] into slots[i] of `layer`. */
+int kernrt_cuda_kv_write(kernrt_cuda_ctx *ctx, size_t layer, const uint64_t *slots, size_t n_slots,
+                         kernrt_buf k, kernrt_buf v, size_t rows);
+
+/* One query row's causal window (Window, mod.rs:179-188): its own slots
+ * att_start..=slot and the extra range [shared_start, shared_end). */
+typedef struct {
+    uint64_t att_start, slot, shared_start, shared_end;
+} kernrt_window;
+
+/* Backend::attention (mod.rs:351-359; reference.rs:276-306, 418-482) with
+ * AttnSpec {n_heads, kv_mul, head_size, kv_dim, seq_len} (mod.rs:158-167):
+ * q and out [n_windows, n_heads * head_size], att [n_windows, n_heads,
+ * seq_len] (each head's first `count` scores are written). */
+int kernrt_cuda_attention(kernrt_cuda_ctx *ctx, kernrt_buf q, kernrt_buf out, kernrt_buf att, size_t layer,
+                          const kernrt_window *windows, size_t n_windows, size_t n_heads, size_t kv_mul,
+                          size_t head_size, size_t kv_dim, size_t seq_len);
+
 /* --- Embedding gather without allocation --------------------------------------
  * No counterpart in the reference: KernRT's backends allocate their own memory.
  * Some callers of this library cannot let it allocate device memory: a host

@@ -61,6 +61,13 @@ class ChainArgs(C.Structure):
     ]
 
 
+class Window(C.Structure):
+    """Mirror of ``kernrt_window``: one query row's causal window."""
+
+    _fields_ = [("att_start", C.c_uint64), ("slot", C.c_uint64), ("shared_start", C.c_uint64),
+                ("shared_end", C.c_uint64)]
+
+
 class ChainHostArgs(C.Structure):
     """Mirror of ``kernrt_chain_host_args`` (include/kernrt_cuda.h)."""
 
@@ -113,6 +120,12 @@ SIGNATURES = {
     "kernrt_cuda_layer_chain_host": (C.c_int, [P, C.POINTER(ChainHostArgs)]),
     "kernrt_cuda_stage_timing": (C.c_int, [P, C.c_int]),
     "kernrt_cuda_stage_times": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
+    "kernrt_cuda_prepare_matrix": (C.c_int, [P, C.c_int, P, P, SZ, SZ, C.POINTER(C.c_uint64)]),
+    "kernrt_cuda_project": (C.c_int, [P, C.c_uint64, Buf, Buf, SZ]),
+    "kernrt_cuda_logits": (C.c_int, [P, C.c_uint64, Buf, Buf]),
+    "kernrt_cuda_kv_prepare": (C.c_int, [P, SZ, SZ, SZ]),
+    "kernrt_cuda_kv_write": (C.c_int, [P, SZ, P, SZ, Buf, Buf, SZ]),
+    "kernrt_cuda_attention": (C.c_int, [P, Buf, Buf, Buf, SZ, C.POINTER(Window), SZ, SZ, SZ, SZ, SZ, SZ]),
     "kernrt_cuda_embed_rows_noalloc": (C.c_int, [C.c_int, C.c_int, P, P, SZ, SZ, P, SZ, P, P]),
 }
 
@@ -357,6 +370,37 @@ class CudaBackend:
         n = (C.c_uint64 * 3)()
         _ok(self._lib.kernrt_cuda_stage_times(self._ctx, ms, n))
         return {k: (ms[i], n[i]) for i, k in enumerate(self.STAGES)}
+
+    # -- contractions (reference.rs:151-159, 259-306, 402-416) ----------------------
+    def prepare_matrix(self, kind: int, data: np.ndarray, scales: np.ndarray | None, out_dim: int,
+                       in_dim: int) -> int:
+        """Uploads W [out_dim, in_dim] in its stored format; returns its handle."""
+        data = np.ascontiguousarray(data)
+        sc = None if scales is None else np.ascontiguousarray(scales, dtype=np.float32)
+        h = C.c_uint64()
+        _ok(self._lib.kernrt_cuda_prepare_matrix(self._ctx, kind, _ptr(data), None if sc is None else _ptr(sc),
+                                                 out_dim, in_dim, C.byref(h)))
+        return h.value
+
+    def project(self, w: int, x: int, y: int, rows: int) -> None:
+        _ok(self._lib.kernrt_cuda_project(self._ctx, w, x, y, rows))
+
+    def logits(self, w: int, x: int, y: int) -> None:
+        _ok(self._lib.kernrt_cuda_logits(self._ctx, w, x, y))
+
+    def kv_prepare(self, n_layers: int, kv_dim: int, seq_len: int) -> None:
+        _ok(self._lib.kernrt_cuda_kv_prepare(self._ctx, n_layers, kv_dim, seq_len))
+
+    def kv_write(self, layer: int, slots, k: int, v: int, rows: int) -> None:
+        sl = np.ascontiguousarray(slots, dtype=np.uint64)
+        _ok(self._lib.kernrt_cuda_kv_write(self._ctx, layer, _ptr(sl), sl.size, k, v, rows))
+
+    def attention(self, q: int, out: int, att: int, layer: int, windows, n_heads: int, kv_mul: int,
+                  head_size: int, kv_dim: int, seq_len: int) -> None:
+        """windows: sequence of (att_start, slot, shared_start, shared_end)."""
+        ws = (Window * max(1, len(windows)))(*[Window(*map(int, w)) for w in windows])
+        _ok(self._lib.kernrt_cuda_attention(self._ctx, q, out, att, layer, ws, len(windows), n_heads, kv_mul,
+                                            head_size, kv_dim, seq_len))
 
     def lfm2_conv_block(self, bcx: int, kernel: int, ring: int, cy: int, rows: int, dim: int,
                         k: int) -> None:

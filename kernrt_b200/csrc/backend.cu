@@ -76,6 +76,12 @@ public:
         }
         cudaFree(emb_data_);
         cudaFree(emb_scales_);
+        for (auto &m : mats_) {
+            cudaFree(m.data);
+            cudaFree(m.scales);
+        }
+        cudaFree(kc_);
+        cudaFree(vc_);
         cudaFree(d_err_);
         cudaFreeHost(h_err_);
         cudaFreeHost(stage_host_);
@@ -231,6 +237,177 @@ public:
         flush_deferred();
         if (!pending_.empty() && pending_.back().out != out) flush();
         pending_.push_back({(int32_t)token, out, (int64_t)offset});
+    }
+
+    // ---- contractions (reference.rs:151-159, 259-306, 402-416) ---------------
+    struct DevMatrix {
+        int src = SRC_F32;
+        void *data = nullptr;
+        float *scales = nullptr;
+        size_t out_dim = 0, in_dim = 0;
+    };
+
+    // A weight matrix [out_dim, in_dim] in its stored format, kept on the
+    // device in the form the kernels read (Q8_0x4 de-interleaved to Q8_0 with
+    // widened scales, the repack quant.rs:646-652 gives device backends).
+    uint64_t prepare_matrix(int kind, const void *data, const float *scales, size_t out_dim, size_t in_dim) {
+        if (!data || out_dim == 0 || in_dim == 0) fail(KERNRT_E_INVALID, "empty matrix");
+        if (kind < KERNRT_F32 || kind > KERNRT_Q8_0X4) fail(KERNRT_E_INVALID, "unknown storage kind");
+        if ((kind == KERNRT_Q8_0 || kind == KERNRT_Q8_0X4) && in_dim % 32 != 0)
+            fail(KERNRT_E_INVALID, "Q8_0 rows must be a whole number of 32-element blocks");
+        if (kind == KERNRT_Q8_0X4 && out_dim % 4 != 0) fail(KERNRT_E_INVALID, "Q8_0x4 matrices hold a multiple of four rows");
+        if (kind == KERNRT_Q8_0 && !scales) fail(KERNRT_E_INVALID, "Q8_0 matrix needs its scales");
+        if (out_dim > (size_t)INT32_MAX || in_dim > (size_t)INT32_MAX || out_dim * in_dim > ((size_t)1 << 40))
+            fail(KERNRT_E_INVALID, "matrix too large");
+        flush();
+        DevMatrix m;
+        m.out_dim = out_dim;
+        m.in_dim = in_dim;
+        const size_t n = out_dim * in_dim;
+        try {
+            if (kind == KERNRT_F32 || kind == KERNRT_BF16) {
+                const size_t bytes = n * (kind == KERNRT_F32 ? 4 : 2);
+                check(cudaMalloc(&m.data, bytes), "cudaMalloc(matrix)");
+                check(cudaMemcpy(m.data, data, bytes, cudaMemcpyHostToDevice), "upload matrix");
+                m.src = kind == KERNRT_F32 ? SRC_F32 : SRC_BF16;
+            } else {
+                check(cudaMalloc(&m.data, n), "cudaMalloc(matrix)");
+                check(cudaMalloc(&m.scales, (n / 32) * sizeof(float)), "cudaMalloc(matrix scales)");
+                if (kind == KERNRT_Q8_0) {
+                    check(cudaMemcpy(m.data, data, n, cudaMemcpyHostToDevice), "upload matrix");
+                    check(cudaMemcpy(m.scales, scales, (n / 32) * sizeof(float), cudaMemcpyHostToDevice),
+                          "upload matrix scales");
+                } else {
+                    const size_t blk_bytes = (out_dim / 4) * (in_dim / 32) * 136;
+                    void *tmp = nullptr;
+                    check(cudaMalloc(&tmp, blk_bytes), "cudaMalloc(q8_0x4 staging)");
+                    cudaError_t e = cudaMemcpy(tmp, data, blk_bytes, cudaMemcpyHostToDevice);
+                    if (e == cudaSuccess)
+                        e = launch_q8x4_to_row_major(static_cast<const uint8_t *>(tmp), (int)out_dim, (int)in_dim,
+                                                     static_cast<int8_t *>(m.data), m.scales, stream_);
+                    if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
+                    cudaFree(tmp);
+                    check(e, "Q8_0x4 de-interleave");
+                }
+                m.src = SRC_Q8;
+            }
+        } catch (...) {
+            cudaFree(m.data);
+            cudaFree(m.scales);
+            throw;
+        }
+        mats_.push_back(m);
+        return (uint64_t)mats_.size();  // handle = index + 1
+    }
+
+    const DevMatrix &mat(uint64_t h) const {
+        if (h == 0 || h > mats_.size()) fail(KERNRT_E_INVALID, "invalid matrix handle " + std::to_string(h));
+        return mats_[h - 1];
+    }
+
+    // reference.rs:259-274: y[r, o] = dot(decode_row(W, o), x[r]).
+    void project(uint64_t w, kernrt_buf x, kernrt_buf y, size_t rows) {
+        const DevMatrix &m = mat(w);
+        distinct(x, y);
+        Buffer &xb = buf(x), &yb = buf(y);
+        span(xb, 0, rows * m.in_dim, "project x");
+        span(yb, 0, rows * m.out_dim, "project y");
+        fits_int(rows * std::max(m.in_dim, m.out_dim), "project");
+        flush();
+        if (rows == 0) return;
+        launch_or_fail(launch_project(m.src, m.data, m.scales, (int)m.out_dim, (int)m.in_dim, f(xb), (int)rows, f(yb),
+                                      stream_),
+                       "project");
+    }
+
+    // reference.rs:402-416: the classifier over row 0 of x.
+    void logits(uint64_t w, kernrt_buf x, kernrt_buf y) { project(w, x, y, 1); }
+
+    // The key/value caches, [n_layers][seq_len][kv_dim] f32 each, zeroed
+    // (KvSpec, mod.rs:169-177).
+    void kv_prepare(size_t n_layers, size_t kv_dim, size_t seq_len) {
+        if (n_layers == 0 || kv_dim == 0 || seq_len == 0) fail(KERNRT_E_INVALID, "empty key/value cache");
+        if (seq_len > (size_t)INT32_MAX || kv_dim > (size_t)INT32_MAX || n_layers * seq_len > (size_t)INT32_MAX)
+            fail(KERNRT_E_INVALID, "key/value cache too large");
+        flush();
+        check(cudaStreamSynchronize(stream_), "synchronize");
+        cudaFree(kc_);
+        cudaFree(vc_);
+        kc_ = vc_ = nullptr;
+        const size_t bytes = n_layers * seq_len * kv_dim * sizeof(float);
+        check(cudaMalloc(&kc_, bytes), "cudaMalloc(key cache)");
+        check(cudaMalloc(&vc_, bytes), "cudaMalloc(value cache)");
+        check(cudaMemsetAsync(kc_, 0, bytes, stream_), "cudaMemset");
+        check(cudaMemsetAsync(vc_, 0, bytes, stream_), "cudaMemset");
+        kv_layers_ = n_layers;
+        kv_dim_ = kv_dim;
+        kv_seq_ = seq_len;
+    }
+
+    // reference.rs:151-159: row i of k and v into slot slots[i] of `layer`.
+    void kv_write(size_t layer, const uint64_t *slots, size_t n_slots, kernrt_buf k, kernrt_buf v, size_t rows) {
+        if (!kc_) fail(KERNRT_E_STATE, "kv_prepare() runs before kv_write");
+        if (layer >= kv_layers_) fail(KERNRT_E_INVALID, "layer out of range of the key/value cache");
+        distinct(k, v);
+        rows = std::min(rows, n_slots);
+        Buffer &kb = buf(k), &vb = buf(v);
+        span(kb, 0, rows * kv_dim_, "kv_write k");
+        span(vb, 0, rows * kv_dim_, "kv_write v");
+        flush();
+        if (rows == 0) return;
+        if (!slots) fail(KERNRT_E_INVALID, "null slots");
+        std::vector<int32_t> dst(rows);
+        for (size_t i = 0; i < rows; ++i) {
+            if (slots[i] >= kv_seq_) fail(KERNRT_E_INVALID, "slot " + std::to_string(slots[i]) + " out of range");
+            dst[i] = (int32_t)(layer * kv_seq_ + slots[i]);
+        }
+        const int32_t *d = static_cast<const int32_t *>(stage(dst.data(), rows * sizeof(int32_t)));
+        launch_or_fail(launch_kv_write(kc_, vc_, (int)kv_dim_, d, f(kb), f(vb), (int)rows, stream_), "kv_write");
+    }
+
+    // reference.rs:276-306: one query row per window; scores to att
+    // [row][head][seq_len], output [row][n_heads * head_size].
+    void attention(kernrt_buf q, kernrt_buf out, kernrt_buf att, size_t layer, const kernrt_window *windows,
+                   size_t n_windows, size_t n_heads, size_t kv_mul, size_t head_size, size_t kv_dim,
+                   size_t seq_len) {
+        if (!kc_) fail(KERNRT_E_STATE, "kv_prepare() runs before attention");
+        if (layer >= kv_layers_) fail(KERNRT_E_INVALID, "layer out of range of the key/value cache");
+        if (kv_dim != kv_dim_ || seq_len != kv_seq_) fail(KERNRT_E_INVALID, "attention spec does not match the cache");
+        if (n_heads == 0 || head_size == 0 || kv_mul == 0) fail(KERNRT_E_INVALID, "empty attention spec");
+        if (((n_heads - 1) / kv_mul + 1) * head_size > kv_dim)
+            fail(KERNRT_E_INVALID, "key/value heads exceed kv_dim");
+        distinct(q, out);
+        if (att == q || att == out) fail(KERNRT_E_INVALID, "buffers must be distinct");
+        const size_t width = n_heads * head_size;
+        Buffer &qb = buf(q), &ob = buf(out), &ab = buf(att);
+        span(qb, 0, n_windows * width, "attention q");
+        span(ob, 0, n_windows * width, "attention out");
+        span(ab, 0, n_windows * n_heads * seq_len, "attention att");
+        fits_int(n_windows * n_heads, "attention");
+        flush();
+        if (n_windows == 0) return;
+        if (!windows) fail(KERNRT_E_INVALID, "null windows");
+        std::vector<int32_t> win(4 * n_windows);
+        size_t max_count = 0;
+        for (size_t i = 0; i < n_windows; ++i) {
+            const kernrt_window &w = windows[i];
+            if (w.slot < w.att_start || w.shared_end < w.shared_start || w.slot >= seq_len || w.shared_end > seq_len)
+                fail(KERNRT_E_INVALID, "window " + std::to_string(i) + " out of range");
+            const size_t count = (size_t)(w.shared_end - w.shared_start) + (size_t)(w.slot - w.att_start) + 1;
+            if (count > seq_len) fail(KERNRT_E_INVALID, "window " + std::to_string(i) + " longer than seq_len");
+            max_count = std::max(max_count, count);
+            win[4 * i] = (int32_t)w.att_start;
+            win[4 * i + 1] = (int32_t)w.slot;
+            win[4 * i + 2] = (int32_t)w.shared_start;
+            win[4 * i + 3] = (int32_t)w.shared_end;
+        }
+        if (attention_smem_bytes((int)head_size, (int)max_count) > 200 * 1024)
+            fail(KERNRT_E_INVALID, "attention window too long for one SM's shared memory");
+        const int32_t *d = static_cast<const int32_t *>(stage(win.data(), win.size() * sizeof(int32_t)));
+        launch_or_fail(launch_attention(f(qb), f(ob), f(ab), kc_, vc_, d, (int)n_windows, (int)n_heads, (int)kv_mul,
+                                        (int)head_size, (int)kv_dim, (int)seq_len, layer * seq_len * kv_dim,
+                                        (int)max_count, stream_),
+                       "attention");
     }
 
     // ---- row ops ----------------------------------------------------------------
@@ -1085,6 +1262,9 @@ private:
     std::vector<Buffer> bufs_;
     std::vector<RopeTable> ropes_;
     std::vector<Pending> pending_;
+    std::vector<DevMatrix> mats_;
+    float *kc_ = nullptr, *vc_ = nullptr;
+    size_t kv_layers_ = 0, kv_dim_ = 0, kv_seq_ = 0;
     int emb_kind_ = -1;
     int emb_src_ = SRC_F32;
     size_t vocab_ = 0, dim_ = 0;
@@ -1350,6 +1530,40 @@ int kernrt_cuda_stage_times(kernrt_cuda_ctx *ctx, double *ms, uint64_t *launches
 int kernrt_cuda_lfm2_conv_block(kernrt_cuda_ctx *ctx, kernrt_buf bcx, kernrt_buf kernel, kernrt_buf ring,
                                 kernrt_buf cy, size_t rows, size_t dim, size_t k) {
     return guard(ctx, [&](krt::Backend &b) { b.lfm2_conv_block(bcx, kernel, ring, cy, rows, dim, k); });
+}
+
+int kernrt_cuda_prepare_matrix(kernrt_cuda_ctx *ctx, int kind, const void *data, const float *scales, size_t out_dim,
+                               size_t in_dim, kernrt_mat *out) {
+    if (!out) {
+        g_last_error = "null output pointer";
+        return KERNRT_E_INVALID;
+    }
+    return guard(ctx, [&](krt::Backend &b) { *out = b.prepare_matrix(kind, data, scales, out_dim, in_dim); });
+}
+
+int kernrt_cuda_project(kernrt_cuda_ctx *ctx, kernrt_mat w, kernrt_buf x, kernrt_buf y, size_t rows) {
+    return guard(ctx, [&](krt::Backend &b) { b.project(w, x, y, rows); });
+}
+
+int kernrt_cuda_logits(kernrt_cuda_ctx *ctx, kernrt_mat w, kernrt_buf x, kernrt_buf y) {
+    return guard(ctx, [&](krt::Backend &b) { b.logits(w, x, y); });
+}
+
+int kernrt_cuda_kv_prepare(kernrt_cuda_ctx *ctx, size_t n_layers, size_t kv_dim, size_t seq_len) {
+    return guard(ctx, [&](krt::Backend &b) { b.kv_prepare(n_layers, kv_dim, seq_len); });
+}
+
+int kernrt_cuda_kv_write(kernrt_cuda_ctx *ctx, size_t layer, const uint64_t *slots, size_t n_slots, kernrt_buf k,
+                         kernrt_buf v, size_t rows) {
+    return guard(ctx, [&](krt::Backend &b) { b.kv_write(layer, slots, n_slots, k, v, rows); });
+}
+
+int kernrt_cuda_attention(kernrt_cuda_ctx *ctx, kernrt_buf q, kernrt_buf out, kernrt_buf att, size_t layer,
+                          const kernrt_window *windows, size_t n_windows, size_t n_heads, size_t kv_mul,
+                          size_t head_size, size_t kv_dim, size_t seq_len) {
+    return guard(ctx, [&](krt::Backend &b) {
+        b.attention(q, out, att, layer, windows, n_windows, n_heads, kv_mul, head_size, kv_dim, seq_len);
+    });
 }
 
 }  // extern "C"

@@ -1,0 +1,306 @@
+// The reference backend's contractions on the device, in its arithmetic order
+// (src/backends/reference.rs:73-79, 151-159, 259-306, 402-482): projections
+// and logits as y[r, o] = dot(decode_row(W, o), x[r]) with one f32 accumulator
+// per output running over k left to right, multiply then add; the key/value
+// cache write; causal attention with the reference's score, softmax and
+// weighted-sum order.  Every operation is an explicit _rn intrinsic (the
+// library builds with -fmad=false), so projections, logits and the cache are
+// bit-identical to the reference; attention differs only through expf.
+#include "kernels.cuh"
+
+#include <cuda_fp16.h>
+
+namespace krt {
+namespace {
+
+constexpr unsigned kFullMask = 0xffffffffu;
+
+__device__ __forceinline__ float mul_rn(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add_rn(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float bf16f(uint32_t bits16) { return __uint_as_float(bits16 << 16); }
+
+cudaError_t launched() {
+    count_launch();
+    return cudaGetLastError();
+}
+
+// ---- projections --------------------------------------------------------------
+
+constexpr int kBK = 32;   // k per staged chunk (one Q8_0 block)
+constexpr int kBN = 64;   // outputs per CTA: 16 threads x 4
+constexpr int kPad = 4;   // floats of padding per staged k-row
+
+// A CTA computes a BM x 64 tile of y with 16 x 16 threads, TM rows x 4 outputs
+// each.  Per chunk of 32 k it stages x[rows, k] and the decoded W[outputs, k]
+// transposed in shared memory; every accumulator then takes the chunk's k in
+// order, so each output is the reference's sequential dot.  k past in_dim is
+// staged as zeros: 0*0 added to a partial sum that starts at +0 and never
+// becomes -0 leaves it unchanged.  Requires in_dim % 8 == 0 (% 32 for Q8_0).
+template <int SRC, int TM>
+__global__ void __launch_bounds__(256) k_project(const void *__restrict__ w, const float *__restrict__ wsc,
+                                                 int out_dim, int in_dim, const float *__restrict__ x, int rows,
+                                                 float *__restrict__ y) {
+    constexpr int BM = 16 * TM;
+    __shared__ __align__(16) float xs[kBK][BM + kPad];
+    __shared__ __align__(16) float ws[kBK][kBN + kPad];
+    const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+    const int o0 = blockIdx.x * kBN, r0 = blockIdx.y * BM;
+    float acc[TM][4];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+
+    for (int k0 = 0; k0 < in_dim; k0 += kBK) {
+        // x chunk: BM rows x 32 k as float4, stored k-major
+        for (int idx = tid; idx < BM * (kBK / 4); idx += 256) {
+            const int r = idx >> 3, c = (idx & 7) << 2;
+            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (r0 + r < rows && k0 + c < in_dim)
+                v = __ldg(reinterpret_cast<const float4 *>(x + (size_t)(r0 + r) * in_dim + k0 + c));
+            xs[c][r] = v.x;
+            xs[c + 1][r] = v.y;
+            xs[c + 2][r] = v.z;
+            xs[c + 3][r] = v.w;
+        }
+        // W chunk: 64 outputs x 32 k, decoded as Matrix::decode_row does
+        if constexpr (SRC == SRC_BF16) {
+            const int o = tid >> 2, c = (tid & 3) << 3;
+            uint4 t = make_uint4(0u, 0u, 0u, 0u);
+            if (o0 + o < out_dim && k0 + c < in_dim)
+                t = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(w) +
+                                                          (size_t)(o0 + o) * in_dim + k0 + c));
+            const uint32_t p[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                ws[c + 2 * e][o] = bf16f(p[e] & 0xffffu);
+                ws[c + 2 * e + 1][o] = bf16f(p[e] >> 16);
+            }
+        } else if constexpr (SRC == SRC_Q8) {
+            if (tid < 128) {
+                const int o = tid >> 1, c = (tid & 1) << 4;
+                uint4 t = make_uint4(0u, 0u, 0u, 0u);
+                float sc = 0.0f;
+                if (o0 + o < out_dim && k0 + c < in_dim) {
+                    t = __ldg(reinterpret_cast<const uint4 *>(static_cast<const int8_t *>(w) +
+                                                              (size_t)(o0 + o) * in_dim + k0 + c));
+                    sc = __ldg(wsc + (size_t)(o0 + o) * (in_dim >> 5) + (k0 >> 5));
+                }
+                const uint32_t p[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    ws[c + e][o] = mul_rn((float)(int8_t)((p[e >> 2] >> (8 * (e & 3))) & 0xffu), sc);
+            }
+        } else {
+            for (int idx = tid; idx < kBN * (kBK / 4); idx += 256) {
+                const int o = idx >> 3, c = (idx & 7) << 2;
+                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (o0 + o < out_dim && k0 + c < in_dim)
+                    v = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(w) +
+                                                               (size_t)(o0 + o) * in_dim + k0 + c));
+                ws[c][o] = v.x;
+                ws[c + 1][o] = v.y;
+                ws[c + 2][o] = v.z;
+                ws[c + 3][o] = v.w;
+            }
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < kBK; ++kk) {
+            float a[TM];
+            if constexpr (TM == 4) {
+                const float4 t = *reinterpret_cast<const float4 *>(&xs[kk][ty * 4]);
+                a[0] = t.x; a[1] = t.y; a[2] = t.z; a[3] = t.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < TM; ++i) a[i] = xs[kk][ty * TM + i];
+            }
+            const float4 b = *reinterpret_cast<const float4 *>(&ws[kk][tx * 4]);
+#pragma unroll
+            for (int i = 0; i < TM; ++i) {
+                acc[i][0] = add_rn(acc[i][0], mul_rn(b.x, a[i]));
+                acc[i][1] = add_rn(acc[i][1], mul_rn(b.y, a[i]));
+                acc[i][2] = add_rn(acc[i][2], mul_rn(b.z, a[i]));
+                acc[i][3] = add_rn(acc[i][3], mul_rn(b.w, a[i]));
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const int r = r0 + ty * TM + i;
+        if (r >= rows) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int o = o0 + tx * 4 + j;
+            if (o < out_dim) y[(size_t)r * out_dim + o] = acc[i][j];
+        }
+    }
+}
+
+// Any shape: one thread per output, the dot in order, decoding each weight.
+template <int SRC>
+__global__ void __launch_bounds__(256) k_project_scalar(const void *__restrict__ w, const float *__restrict__ wsc,
+                                                        int out_dim, int in_dim, const float *__restrict__ x,
+                                                        int rows, float *__restrict__ y) {
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= (long long)rows * out_dim) return;
+    const int r = (int)(i / out_dim), o = (int)(i - (long long)r * out_dim);
+    const float *xr = x + (size_t)r * in_dim;
+    float sum = 0.0f;
+    for (int k = 0; k < in_dim; ++k) {
+        float wv;
+        if constexpr (SRC == SRC_BF16) wv = bf16f(static_cast<const uint16_t *>(w)[(size_t)o * in_dim + k]);
+        else if constexpr (SRC == SRC_Q8)
+            wv = mul_rn((float)static_cast<const int8_t *>(w)[(size_t)o * in_dim + k],
+                        wsc[(size_t)o * (in_dim >> 5) + (k >> 5)]);
+        else wv = static_cast<const float *>(w)[(size_t)o * in_dim + k];
+        sum = add_rn(sum, mul_rn(wv, xr[k]));
+    }
+    y[i] = sum;
+}
+
+template <int SRC>
+cudaError_t project_src(const void *w, const float *wsc, int out_dim, int in_dim, const float *x, int rows, float *y,
+                        cudaStream_t s) {
+    const bool tiled = in_dim % (SRC == SRC_Q8 ? 32 : 8) == 0 && ((uintptr_t)x & 15) == 0 &&
+                       ((uintptr_t)w & 15) == 0;
+    if (!tiled) {
+        const long long n = (long long)rows * out_dim;
+        k_project_scalar<SRC><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(w, wsc, out_dim, in_dim, x, rows, y);
+        return launched();
+    }
+    const unsigned gx = (unsigned)((out_dim + kBN - 1) / kBN);
+    if (rows >= 64) {
+        k_project<SRC, 4><<<dim3(gx, (unsigned)((rows + 63) / 64)), 256, 0, s>>>(w, wsc, out_dim, in_dim, x, rows, y);
+    } else {
+        k_project<SRC, 1><<<dim3(gx, (unsigned)((rows + 15) / 16)), 256, 0, s>>>(w, wsc, out_dim, in_dim, x, rows, y);
+    }
+    return launched();
+}
+
+// ---- key/value cache ------------------------------------------------------------
+
+// reference.rs:151-159: row i of k and v into cache row dst_rows[i]
+// (layer * seq_len + slot).
+__global__ void __launch_bounds__(256) k_kv_write(float *__restrict__ kc, float *__restrict__ vc, int kv_dim,
+                                                  const int32_t *__restrict__ dst_rows, const float *__restrict__ k,
+                                                  const float *__restrict__ v, int rows) {
+    const long long n = (long long)rows * kv_dim;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / kv_dim), e = (int)(i - (long long)r * kv_dim);
+        const size_t d = (size_t)dst_rows[r] * kv_dim + e;
+        kc[d] = k[i];
+        vc[d] = v[i];
+    }
+}
+
+// ---- attention ------------------------------------------------------------------
+
+// reference.rs:418-482 for one (query row, head): a CTA of 128 threads.
+//   scores: thread per position, each a sequential dot over head_size, times
+//           1/sqrt(head_size);
+//   softmax: the maximum (order-free), exp(s - max), the sum by one thread in
+//            position order, then s / sum (written to att);
+//   output: thread per element, accumulated over positions in order.
+// Window: positions shared_start..shared_end, then att_start..=slot.
+__global__ void __launch_bounds__(128) k_attention(const float *__restrict__ q, float *__restrict__ out,
+                                                   float *__restrict__ att, const float *__restrict__ kc,
+                                                   const float *__restrict__ vc, const int32_t *__restrict__ win,
+                                                   int n_heads, int kv_mul, int head_size, int kv_dim, int seq_len,
+                                                   size_t loff) {
+    extern __shared__ __align__(16) float asm_[];
+    const int row = blockIdx.x / n_heads, h = blockIdx.x - row * n_heads;
+    const int tid = threadIdx.x;
+    const int att_start = win[4 * row], slot = win[4 * row + 1], ss = win[4 * row + 2], se = win[4 * row + 3];
+    const int n_shared = se - ss, count = n_shared + slot - att_start + 1;
+    float *qh = asm_;                       // [head_size]
+    float *sc = asm_ + ((head_size + 3) & ~3);  // [count]
+    __shared__ float red[4];
+    __shared__ float total;
+    const int width = n_heads * head_size;
+    const float *qg = q + (size_t)row * width + (size_t)h * head_size;
+    for (int e = tid; e < head_size; e += 128) qh[e] = qg[e];
+    __syncthreads();
+    const size_t kv = (size_t)(h / kv_mul) * head_size;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)head_size));
+    auto pos_of = [&](int i) { return i < n_shared ? ss + i : att_start + (i - n_shared); };
+    for (int i = tid; i < count; i += 128) {
+        const float *kr = kc + loff + (size_t)pos_of(i) * kv_dim + kv;
+        float d = 0.0f;
+        for (int e = 0; e < head_size; ++e) d = add_rn(d, mul_rn(qh[e], kr[e]));
+        sc[i] = mul_rn(d, scale);
+    }
+    __syncthreads();
+    // the maximum over positions, NaN scores skipped as the reference's `>` does
+    float m = -INFINITY;
+    for (int i = tid; i < count; i += 128) m = fmaxf(m, sc[i]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, o));
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    for (int i = tid; i < count; i += 128) sc[i] = expf(__fsub_rn(sc[i], m));
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.0f;
+        for (int i = 0; i < count; ++i) sum = add_rn(sum, sc[i]);
+        total = sum;
+    }
+    __syncthreads();
+    const float sum = total;
+    float *ag = att + ((size_t)row * n_heads + h) * seq_len;
+    for (int i = tid; i < count; i += 128) {
+        const float a = __fdiv_rn(sc[i], sum);
+        sc[i] = a;
+        ag[i] = a;
+    }
+    __syncthreads();
+    float *og = out + (size_t)row * width + (size_t)h * head_size;
+    for (int e = tid; e < head_size; e += 128) {
+        float o = 0.0f;
+        for (int i = 0; i < count; ++i) o = add_rn(o, mul_rn(sc[i], vc[loff + (size_t)pos_of(i) * kv_dim + kv + e]));
+        og[e] = o;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_project(int src, const void *w, const float *wsc, int out_dim, int in_dim, const float *x,
+                           int rows, float *y, cudaStream_t s) {
+    if (rows <= 0 || out_dim <= 0) return cudaSuccess;
+    switch (src) {
+    case SRC_BF16: return project_src<SRC_BF16>(w, wsc, out_dim, in_dim, x, rows, y, s);
+    case SRC_Q8: return project_src<SRC_Q8>(w, wsc, out_dim, in_dim, x, rows, y, s);
+    default: return project_src<SRC_F32>(w, wsc, out_dim, in_dim, x, rows, y, s);
+    }
+}
+
+cudaError_t launch_kv_write(float *kc, float *vc, int kv_dim, const int32_t *dst_rows, const float *k, const float *v,
+                            int rows, cudaStream_t s) {
+    if (rows <= 0 || kv_dim <= 0) return cudaSuccess;
+    const long long n = (long long)rows * kv_dim;
+    long long grid = (n + 255) / 256;
+    if (grid > 148 * 16) grid = 148 * 16;
+    k_kv_write<<<(unsigned)grid, 256, 0, s>>>(kc, vc, kv_dim, dst_rows, k, v, rows);
+    return launched();
+}
+
+size_t attention_smem_bytes(int head_size, int max_count) {
+    return (size_t)(((head_size + 3) & ~3) + max_count) * sizeof(float);
+}
+
+cudaError_t launch_attention(const float *q, float *out, float *att, const float *kc, const float *vc,
+                             const int32_t *win, int n_rows, int n_heads, int kv_mul, int head_size, int kv_dim,
+                             int seq_len, size_t loff, int max_count, cudaStream_t s) {
+    if (n_rows <= 0 || n_heads <= 0) return cudaSuccess;
+    const size_t smem = attention_smem_bytes(head_size, max_count);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    k_attention<<<(unsigned)(n_rows * n_heads), 128, smem, s>>>(q, out, att, kc, vc, win, n_heads, kv_mul, head_size,
+                                                                kv_dim, seq_len, loff);
+    return launched();
+}
+
+}  // namespace krt

@@ -91,4 +91,20 @@ cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes,
 cudaError_t launch_q8x4_to_row_major(const uint8_t *blocks, int out_dim, int in_dim,
                                      int8_t *quants, float *scales, cudaStream_t s);
 
+
+// ---- contractions (contract.cu) ----
+// y[r, o] = dot(decode_row(W, o), x[r]) in the reference's order; W stored
+// [out_dim, in_dim] as SRC_F32 / SRC_BF16 / SRC_Q8 (+ block scales).
+cudaError_t launch_project(int src, const void *w, const float *wsc, int out_dim, int in_dim, const float *x,
+                           int rows, float *y, cudaStream_t s);
+// Row i of k and v into cache row dst_rows[i] of caches [rows_total, kv_dim].
+cudaError_t launch_kv_write(float *kc, float *vc, int kv_dim, const int32_t *dst_rows, const float *k, const float *v,
+                            int rows, cudaStream_t s);
+// win: [n_rows][4] = att_start, slot, shared_start, shared_end; max_count the
+// largest window; loff the layer's first cache element.
+size_t attention_smem_bytes(int head_size, int max_count);
+cudaError_t launch_attention(const float *q, float *out, float *att, const float *kc, const float *vc,
+                             const int32_t *win, int n_rows, int n_heads, int kv_mul, int head_size, int kv_dim,
+                             int seq_len, size_t loff, int max_count, cudaStream_t s);
+
 }  // namespace krt

@@ -529,3 +529,129 @@ int kro_max_threads(void) {
     long n = sysconf(_SC_NPROCESSORS_ONLN);
     return n > 0 ? (int)n : 1;
 }
+
+/* ------------------------------------------------------------------ */
+/* Contractions (the reference backend's, src/backends/reference.rs)   */
+/* ------------------------------------------------------------------ */
+
+/* reference.rs:73-79 dot: one f32 accumulator, left to right, multiply then
+ * add (no fused multiply-add). */
+static float dot_seq(const float *a, const float *b, size_t n) {
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; ++i) sum += a[i] * b[i];
+    return sum;
+}
+
+typedef struct {
+    kro_table w;
+    size_t out_dim, in_dim, rows, r0, r1;
+    const float *x;
+    float *y;
+} kro_project_job;
+
+static void *project_worker(void *arg) {
+    kro_project_job *j = (kro_project_job *)arg;
+    float *row = (float *)malloc(j->in_dim * sizeof(float));
+    if (!row) return NULL;
+    /* reference.rs:259-274: for each row, decode each weight row and dot it */
+    for (size_t r = j->r0; r < j->r1; ++r)
+        for (size_t o = 0; o < j->out_dim; ++o) {
+            kro_embed(&j->w, o, row);
+            j->y[r * j->out_dim + o] = dot_seq(row, j->x + r * j->in_dim, j->in_dim);
+        }
+    free(row);
+    return NULL;
+}
+
+/* reference.rs:259-274 project (and :402-416 logits, one row): y[r, o] =
+ * dot(decode_row(W, o), x[r]) with W of `kind` stored [out_dim, in_dim].
+ * Rows split over `threads` host threads (each row is independent). */
+void kro_project(int kind, const void *data, const float *scales, size_t out_dim, size_t in_dim,
+                 const float *x, size_t rows, float *y, int threads) {
+    if (threads < 1) threads = 1;
+    if ((size_t)threads > rows) threads = rows > 0 ? (int)rows : 1;
+    kro_project_job jobs[64];
+    pthread_t tid[64];
+    if (threads > 64) threads = 64;
+    for (int t = 0; t < threads; ++t) {
+        kro_project_job *j = &jobs[t];
+        j->w.kind = kind; j->w.vocab = out_dim; j->w.dim = in_dim; j->w.data = data; j->w.scales = scales;
+        j->out_dim = out_dim; j->in_dim = in_dim; j->rows = rows; j->x = x; j->y = y;
+        j->r0 = rows * (size_t)t / (size_t)threads;
+        j->r1 = rows * (size_t)(t + 1) / (size_t)threads;
+    }
+    for (int t = 1; t < threads; ++t) pthread_create(&tid[t], NULL, project_worker, &jobs[t]);
+    project_worker(&jobs[0]);
+    for (int t = 1; t < threads; ++t) pthread_join(tid[t], NULL);
+}
+
+/* reference.rs:151-159 kv_write: row i of k and v into slot slots[i] of
+ * `layer` in caches laid out [layer][seq_len][kv_dim]. */
+void kro_kv_write(float *key_cache, float *value_cache, size_t kv_dim, size_t seq_len, size_t layer,
+                  const uint64_t *slots, size_t n_slots, const float *k, const float *v, size_t rows) {
+    for (size_t row = 0; row < n_slots && row < rows; ++row) {
+        size_t at = (layer * seq_len + (size_t)slots[row]) * kv_dim;
+        memcpy(key_cache + at, k + row * kv_dim, kv_dim * sizeof(float));
+        memcpy(value_cache + at, v + row * kv_dim, kv_dim * sizeof(float));
+    }
+}
+
+/* One query row's window (src/backends/mod.rs:179-188): its own slots
+ * att_start..=slot and the shared range [shared_start, shared_end). */
+typedef struct {
+    uint64_t att_start, slot, shared_start, shared_end;
+} kro_window;
+
+/* reference.rs:418-482 attention_rows for one query row. */
+static void attention_row(const float *q, const float *key_cache, const float *value_cache, float *out,
+                          float *att, size_t loff, const kro_window *w, size_t n_heads, size_t kv_mul,
+                          size_t head_size, size_t kv_dim, size_t seq_len) {
+    size_t n_shared = (size_t)(w->shared_end - w->shared_start);
+    size_t count = n_shared + (size_t)(w->slot - w->att_start) + 1;
+    float scale = 1.0f / sqrtf((float)head_size);
+    for (size_t h = 0; h < n_heads; ++h) {
+        const float *qh = q + h * head_size;
+        float *scores = att + h * seq_len;
+        size_t kv = (h / kv_mul) * head_size;
+        size_t i = 0;
+        for (uint64_t t = w->shared_start; t < w->shared_end; ++t, ++i)
+            scores[i] = dot_seq(qh, key_cache + loff + (size_t)t * kv_dim + kv, head_size) * scale;
+        for (uint64_t t = w->att_start; t <= w->slot; ++t, ++i)
+            scores[n_shared + (size_t)(t - w->att_start)] =
+                dot_seq(qh, key_cache + loff + (size_t)t * kv_dim + kv, head_size) * scale;
+        float max = -INFINITY;
+        for (size_t s = 0; s < count; ++s)
+            if (scores[s] > max) max = scores[s];
+        float sum = 0.0f;
+        for (size_t s = 0; s < count; ++s) {
+            scores[s] = expf(scores[s] - max);
+            sum += scores[s];
+        }
+        for (size_t s = 0; s < count; ++s) scores[s] /= sum;
+        float *o = out + h * head_size;
+        for (size_t e = 0; e < head_size; ++e) o[e] = 0.0f;
+        i = 0;
+        for (uint64_t t = w->shared_start; t < w->shared_end; ++t, ++i) {
+            const float *vv = value_cache + loff + (size_t)t * kv_dim + kv;
+            float a = scores[i];
+            for (size_t e = 0; e < head_size; ++e) o[e] += a * vv[e];
+        }
+        for (uint64_t t = w->att_start; t <= w->slot; ++t) {
+            const float *vv = value_cache + loff + (size_t)t * kv_dim + kv;
+            float a = scores[n_shared + (size_t)(t - w->att_start)];
+            for (size_t e = 0; e < head_size; ++e) o[e] += a * vv[e];
+        }
+    }
+}
+
+/* reference.rs:276-306 attention: every window's row, scores at
+ * att[row][head][seq_len], output [row][n_heads * head_size]. */
+void kro_attention(const float *q, float *out, float *att, const float *key_cache, const float *value_cache,
+                   size_t layer, const kro_window *windows, size_t n_windows, size_t n_heads, size_t kv_mul,
+                   size_t head_size, size_t kv_dim, size_t seq_len) {
+    size_t loff = layer * seq_len * kv_dim;
+    size_t width = n_heads * head_size;
+    for (size_t row = 0; row < n_windows; ++row)
+        attention_row(q + row * width, key_cache, value_cache, out + row * width, att + row * n_heads * seq_len,
+                      loff, &windows[row], n_heads, kv_mul, head_size, kv_dim, seq_len);
+}

@@ -84,6 +84,9 @@ def _declare(L: C.CDLL) -> None:
     L.kro_conv_prefill.argtypes = [P, P, P, SZ, SZ, SZ]
     L.kro_conv_decode.argtypes = [P, P, P, P, SZ, SZ]
     L.kro_lfm2_conv_block.argtypes = [P, P, P, P, P, P, SZ, SZ, SZ]
+    L.kro_project.argtypes = [C.c_int, P, P, SZ, SZ, P, SZ, P, C.c_int]
+    L.kro_kv_write.argtypes = [P, P, SZ, SZ, SZ, P, SZ, P, P, SZ]
+    L.kro_attention.argtypes = [P, P, P, P, P, SZ, P, SZ, SZ, SZ, SZ, SZ, SZ]
     L.kro_chain_run.argtypes = [C.POINTER(Chain)]
     L.kro_chain_run_mt.argtypes = [C.POINTER(Chain), C.c_int]
     L.kro_chain_struct_size.restype = SZ
@@ -332,3 +335,43 @@ def chain(*, dim, q_dim, kv_dim, hidden, head, eps, theta, positions, w_att, q, 
 
 def max_threads() -> int:
     return lib().kro_max_threads()
+
+
+# --- contractions (reference.rs:73-79, 151-159, 259-306, 402-482) -----------------------
+
+def project(kind: int, data: np.ndarray, scales, out_dim: int, in_dim: int, x, threads: int = 0) -> np.ndarray:
+    """y[r, o] = dot(decode_row(W, o), x[r]) in the reference's order; x is
+    [rows, in_dim] f32.  `threads` 0 = every host thread."""
+    x = np.ascontiguousarray(f32(x)).reshape(-1, in_dim)
+    y = np.zeros((x.shape[0], out_dim), np.float32)
+    data = np.ascontiguousarray(data)
+    sc = None if scales is None else np.ascontiguousarray(f32(scales))
+    lib().kro_project(kind, _p(data), _p(sc), out_dim, in_dim, _p(x), x.shape[0], _p(y),
+                      threads or max_threads())
+    return y
+
+
+def kv_write(key_cache: np.ndarray, value_cache: np.ndarray, kv_dim: int, seq_len: int, layer: int,
+             slots, k, v, rows: int):
+    """Writes rows of k and v into the caches (updated in place and returned)."""
+    slots = np.ascontiguousarray(slots, dtype=np.uint64)
+    k, v = np.ascontiguousarray(f32(k)), np.ascontiguousarray(f32(v))
+    lib().kro_kv_write(_p(key_cache), _p(value_cache), kv_dim, seq_len, layer, _p(slots), slots.size,
+                       _p(k), _p(v), rows)
+    return key_cache, value_cache
+
+
+def attention(q, key_cache, value_cache, layer: int, windows, n_heads: int, kv_mul: int, head_size: int,
+              kv_dim: int, seq_len: int, att=None):
+    """(out, att): windows is a sequence of (att_start, slot, shared_start,
+    shared_end); att (rows x n_heads x seq_len) keeps what the call does not
+    write."""
+    w = np.ascontiguousarray(windows, dtype=np.uint64).reshape(-1, 4)
+    rows = w.shape[0]
+    q = np.ascontiguousarray(f32(q)).reshape(rows, n_heads * head_size)
+    out = np.zeros((rows, n_heads * head_size), np.float32)
+    att = np.zeros((rows, n_heads, seq_len), np.float32) if att is None else np.array(att, np.float32)
+    lib().kro_attention(_p(q), _p(out), _p(att), _p(np.ascontiguousarray(key_cache)),
+                        _p(np.ascontiguousarray(value_cache)), layer, _p(w), rows, n_heads, kv_mul, head_size,
+                        kv_dim, seq_len)
+    return out, att

@@ -1,0 +1,128 @@
+"""Device contractions against the oracle (reference.rs:73-79, 151-159,
+259-306, 402-482): projections, logits and the key/value cache write are
+bit-identical to the reference backend's sequential dot; attention differs only
+through CUDA's expf, held to |g - r| <= 1e-5 * max|V| for the outputs and the
+SwiGLU tolerance (1e-5 relative) for the softmax weights."""
+import numpy as np
+import pytest
+
+import kernrt_b200
+from tests import _data
+from tests._parity import assert_bits_equal, assert_close_rel
+
+pytestmark = pytest.mark.gpu
+f32 = np.float32
+
+
+def weights(kind, out_dim, in_dim, seed, oracle):
+    """(device kind, host data, scales, oracle kind) for W [out_dim, in_dim]."""
+    if kind == "f32":
+        return kernrt_b200.F32, _data.lcg_normal(out_dim * in_dim, seed, 0.0, 0.05).reshape(out_dim, in_dim), None, \
+            oracle.F32
+    if kind == "bf16":
+        return kernrt_b200.BF16, _data.bf16_table(out_dim, in_dim, seed, 0.05), None, oracle.BF16
+    codes, scales = _data.q8_table(out_dim, in_dim, seed)
+    if kind == "q8_0":
+        return kernrt_b200.Q8_0, codes, scales, oracle.Q8_0
+    w = oracle.embed_rows(oracle.Q8_0, codes, scales, out_dim, in_dim, np.arange(out_dim, dtype=np.int32))
+    blocks = oracle.q8_0x4_pack(w)
+    return kernrt_b200.Q8_0X4, blocks, None, oracle.Q8_0X4
+
+
+# tiled kernel for in_dim % 8 == 0 (% 32 for Q8_0), edges in every direction,
+# decode (1 row) and prefill (>= 64 rows) tiles, the scalar kernel otherwise
+SHAPES = [(96, 64, 1), (2048, 2048, 1), (256, 512, 100), (130, 72, 5), (64, 32, 64), (33, 36, 3), (7, 8, 70)]
+
+
+@pytest.mark.parametrize("kind", ["f32", "bf16", "q8_0", "q8_0x4"])
+@pytest.mark.parametrize("out_dim,in_dim,rows", SHAPES)
+def test_project_matches_reference_dot(gpu, oracle, kind, out_dim, in_dim, rows):
+    if kind.startswith("q8") and in_dim % 32:
+        pytest.skip("Q8_0 rows are whole 32-element blocks")
+    if kind == "q8_0x4" and out_dim % 4:
+        pytest.skip("Q8_0x4 holds a multiple of four rows")
+    dk, data, scales, ok = weights(kind, out_dim, in_dim, 90 + in_dim, oracle)
+    x = _data.lcg_normal(rows * in_dim, 91 + rows).reshape(rows, in_dim)
+    m = gpu.prepare_matrix(dk, data, scales, out_dim, in_dim)
+    hx, hy = gpu.upload(x), gpu.alloc(rows * out_dim)
+    gpu.project(m, hx, hy, rows)
+    want = oracle.project(ok, data, scales, out_dim, in_dim, x)
+    assert_bits_equal(gpu.read(hy, rows * out_dim).reshape(rows, out_dim), want, f"project {kind}")
+
+
+def test_logits_is_the_classifier_over_row_zero(gpu, oracle):
+    vocab, dim = 3000, 256
+    table = _data.bf16_table(vocab, dim, 95)
+    x = _data.lcg_normal(3 * dim, 96).reshape(3, dim)
+    m = gpu.prepare_matrix(kernrt_b200.BF16, table, None, vocab, dim)
+    hx, hy = gpu.upload(x), gpu.alloc(vocab)
+    gpu.logits(m, hx, hy)
+    want = oracle.project(oracle.BF16, table, None, vocab, dim, x[:1])
+    assert_bits_equal(gpu.read(hy, vocab), want[0], "logits")
+
+
+def attention_case(gpu, oracle, n_layers, n_heads, n_kv, head, seq_len, layer, writes, windows, seed):
+    kv_dim = n_kv * head
+    kv_mul = n_heads // n_kv
+    gpu.kv_prepare(n_layers, kv_dim, seq_len)
+    kc = np.zeros(n_layers * seq_len * kv_dim, f32)
+    vc = np.zeros_like(kc)
+    for i, (lay, slots) in enumerate(writes):
+        rows = len(slots)
+        k = _data.lcg_normal(rows * kv_dim, seed + 2 * i).reshape(rows, kv_dim)
+        v = _data.lcg_normal(rows * kv_dim, seed + 2 * i + 1).reshape(rows, kv_dim)
+        hk, hv = gpu.upload(k), gpu.upload(v)
+        gpu.kv_write(lay, slots, hk, hv, rows)
+        oracle.kv_write(kc, vc, kv_dim, seq_len, lay, slots, k, v, rows)
+    width = n_heads * head
+    q = _data.lcg_normal(len(windows) * width, seed + 50).reshape(len(windows), width)
+    hq, ho = gpu.upload(q), gpu.alloc(len(windows) * width)
+    ha = gpu.alloc(len(windows) * n_heads * seq_len)
+    gpu.attention(hq, ho, ha, layer, windows, n_heads, kv_mul, head, kv_dim, seq_len)
+    want_o, want_a = oracle.attention(q, kc, vc, layer, windows, n_heads, kv_mul, head, kv_dim, seq_len)
+    got_o = gpu.read(ho, len(windows) * width).reshape(want_o.shape)
+    got_a = gpu.read(ha, want_a.size).reshape(want_a.shape)
+    bound = 1e-5 * float(np.abs(vc).max())
+    err = np.abs(got_o.astype(np.float64) - want_o)
+    assert err.max() <= bound, f"attention out: max error {err.max()} above {bound}"
+    assert_close_rel(got_a, want_a, what="attention weights")
+
+
+def test_attention_decode_and_gqa(gpu, oracle):
+    # one query at position 40 over slots 0..40, 8 query heads on 2 kv heads
+    attention_case(gpu, oracle, 2, 8, 2, 64, 128, 1, [(1, list(range(41))), (0, [3, 4])], [(0, 40, 0, 0)], 300)
+
+
+def test_attention_prefill_causal_rows(gpu, oracle):
+    rows = 37
+    wins = [(0, r, 0, 0) for r in range(rows)]
+    attention_case(gpu, oracle, 1, 4, 4, 32, 64, 0, [(0, list(range(rows)))], wins, 310)
+
+
+def test_attention_shared_range_and_window_start(gpu, oracle):
+    # rows attending a shared prefix [0, 6) plus their own sliding range
+    wins = [(10, 12, 0, 6), (11, 14, 0, 6), (20, 20, 2, 5)]
+    attention_case(gpu, oracle, 3, 6, 3, 16, 32, 2, [(2, list(range(32)))], wins, 320)
+
+
+def test_attention_long_window(gpu, oracle):
+    attention_case(gpu, oracle, 1, 2, 1, 128, 4096, 0, [(0, list(range(4096)))], [(0, 4095, 0, 0)], 330)
+
+
+def test_contraction_errors(gpu):
+    with pytest.raises(kernrt_b200.KernrtCudaError) as e:
+        gpu.project(12345, gpu.alloc(8), gpu.alloc(8), 1)
+    assert "invalid matrix handle" in str(e.value)
+    b = kernrt_b200.CudaBackend(0)
+    with pytest.raises(kernrt_b200.KernrtCudaError) as e:
+        b.kv_write(0, [0], b.alloc(8), b.alloc(8), 1)
+    assert e.value.code == kernrt_b200.E_STATE
+    b.kv_prepare(1, 8, 16)
+    with pytest.raises(kernrt_b200.KernrtCudaError) as e:
+        b.kv_write(0, [16], b.alloc(8), b.alloc(8), 1)
+    assert "out of range" in str(e.value)
+    with pytest.raises(kernrt_b200.KernrtCudaError) as e:
+        b.attention(b.alloc(8), b.alloc(8), b.alloc(16), 0, [(5, 3, 0, 0)], 1, 1, 8, 8, 16)
+    assert "window 0 out of range" in str(e.value)
+    b.synchronize()
+    b.close()
