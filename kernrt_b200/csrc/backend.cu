@@ -316,7 +316,7 @@ public:
         flush();
         if (rows == 0) return;
         launch_or_fail(launch_project(m.src, m.data, m.scales, (int)m.out_dim, (int)m.in_dim, f(xb), (int)rows, f(yb),
-                                      stream_),
+                                      d_err_, stream_),
                        "project");
     }
 

@@ -7,6 +7,7 @@
 // library builds with -fmad=false), so projections, logits and the cache are
 // bit-identical to the reference; attention differs only through expf.
 #include "kernels.cuh"
+#include "bulk.cuh"
 
 #include <cuda_fp16.h>
 
@@ -160,9 +161,151 @@ __global__ void __launch_bounds__(256) k_project_scalar(const void *__restrict__
     y[i] = sum;
 }
 
+// Decode projections (R <= 4 rows): one warp per 32 outputs, lane o running
+// output o's dots for the R rows.  The warp's 32 weight rows and the R x rows
+// stream through three shared-memory stages of CK columns, one bulk copy per
+// row per stage (lane o copies row o), two stages ahead of the sums, so the
+// weight bytes arrive while the lanes run their sequential accumulations.
+// Row slots are padded to an odd number of 16-byte units: the lanes' 16-byte
+// reads of one column land in distinct banks.  Requires in_dim % 8 (% 128
+// for Q8_0, whose block scales then move in 16-byte units too).
+constexpr int kGemvCK = 512;
+constexpr int kGemvStages = 3;
+
+template <int SRC>
+struct GemvGeom {
+    static constexpr int esz = SRC == SRC_BF16 ? 2 : (SRC == SRC_Q8 ? 1 : 4);
+    static constexpr int wrow = kGemvCK * esz + (SRC == SRC_Q8 ? kGemvCK / 8 : 0);  // codes (+ scales)
+    static constexpr int wstride = ((wrow + 31) & ~31) + 16;                          // odd x 16 B
+    template <int R>
+    __host__ __device__ static constexpr int stage_bytes() { return 32 * wstride + R * kGemvCK * 4; }
+};
+
+template <int SRC, int R>
+__global__ void __launch_bounds__(32) k_gemv(const void *__restrict__ w, const float *__restrict__ wsc, int out_dim,
+                                             int in_dim, const float *__restrict__ x, float *__restrict__ y,
+                                             int *err) {
+    using Geo = GemvGeom<SRC>;
+    constexpr int SB = Geo::template stage_bytes<R>();
+    extern __shared__ __align__(16) unsigned char gsm[];
+    __shared__ __align__(8) uint64_t bar[kGemvStages];
+    const int lane = threadIdx.x, o = blockIdx.x * 32 + lane;
+    const bool live = o < out_dim;
+    const int nlive = min(32, out_dim - (int)blockIdx.x * 32);
+    const int nchunks = (in_dim + kGemvCK - 1) / kGemvCK;
+    if (lane == 0) {
+        for (int i = 0; i < kGemvStages; ++i) mbar_init(&bar[i], 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+    auto stage = [&](int c) { return gsm + (size_t)(c % kGemvStages) * SB; };
+    auto issue = [&](int c) {
+        const int k0 = c * kGemvCK, tc = min(kGemvCK, in_dim - k0);
+        const uint32_t wb = (uint32_t)(tc * Geo::esz), sb = SRC == SRC_Q8 ? (uint32_t)(tc / 8) : 0u;
+        const uint32_t total = (uint32_t)nlive * (wb + sb) + (uint32_t)(R * tc * 4);
+        uint64_t *b = &bar[c % kGemvStages];
+        if (lane == 0) mbar_arrive_expect_tx(b, total);
+        __syncwarp();
+        unsigned char *st = stage(c);
+        if (live) {
+            bulk_load(st + (size_t)lane * Geo::wstride,
+                      static_cast<const unsigned char *>(w) + ((size_t)o * in_dim + k0) * Geo::esz, wb, b);
+            if constexpr (SRC == SRC_Q8)
+                bulk_load(st + (size_t)lane * Geo::wstride + kGemvCK, wsc + (size_t)o * (in_dim >> 5) + (k0 >> 5), sb, b);
+        }
+        if (lane < R) bulk_load(st + 32 * Geo::wstride + (size_t)lane * kGemvCK * 4, x + (size_t)lane * in_dim + k0,
+                                (uint32_t)(tc * 4), b);
+    };
+    int issued = 0;  // warp-uniform count of chunks issued
+    while (issued < min(nchunks, kGemvStages - 1)) issue(issued++);
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c) {
+        if (!__all_sync(kFullMask, mbar_wait_bounded(&bar[c % kGemvStages], (uint32_t)(c / kGemvStages) & 1u))) {
+            if (lane == 0) atomicOr(err, ERR_TIMEOUT);
+            ok = false;
+            break;
+        }
+        // the stage that chunk c - 1 used is free: chunk c + 2 goes there
+        if (issued < nchunks) issue(issued++);
+        const unsigned char *st = stage(c);
+        const unsigned char *wr = st + (size_t)lane * Geo::wstride;
+        const float *xs = reinterpret_cast<const float *>(st + 32 * Geo::wstride);
+        const int tc = min(kGemvCK, in_dim - c * kGemvCK);
+        if (live) {
+#pragma unroll 2
+            for (int k = 0; k < tc; k += 8) {
+                float wv[8];
+                if constexpr (SRC == SRC_BF16) {
+                    const uint4 t = *reinterpret_cast<const uint4 *>(wr + 2 * k);
+                    const uint32_t p[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        wv[2 * e] = bf16f(p[e] & 0xffffu);
+                        wv[2 * e + 1] = bf16f(p[e] >> 16);
+                    }
+                } else if constexpr (SRC == SRC_Q8) {
+                    const uint2 t = *reinterpret_cast<const uint2 *>(wr + k);
+                    const float sc = reinterpret_cast<const float *>(wr + kGemvCK)[k >> 5];
+                    const uint32_t p[2] = {t.x, t.y};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) wv[e] = mul_rn((float)(int8_t)((p[e >> 2] >> (8 * (e & 3))) & 0xffu), sc);
+                } else {
+                    const float4 a = *reinterpret_cast<const float4 *>(wr + 4 * k);
+                    const float4 b2 = *reinterpret_cast<const float4 *>(wr + 4 * k + 16);
+                    wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+                    wv[4] = b2.x; wv[5] = b2.y; wv[6] = b2.z; wv[7] = b2.w;
+                }
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const float4 x0 = *reinterpret_cast<const float4 *>(xs + r * kGemvCK + k);
+                    const float4 x1 = *reinterpret_cast<const float4 *>(xs + r * kGemvCK + k + 4);
+                    const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[r] = add_rn(acc[r], mul_rn(wv[e], xv[e]));
+                }
+            }
+        }
+        // every lane's reads of this stage are done before it is refilled
+        __syncwarp();
+    }
+    if (!ok) {
+        // copies still in flight: wait for them (bounded) before the memory goes
+        if (lane == 0)
+            for (int c = max(0, issued - kGemvStages); c < issued; ++c)
+                mbar_wait_bounded(&bar[c % kGemvStages], (uint32_t)(c / kGemvStages) & 1u);
+        return;
+    }
+    if (live)
+#pragma unroll
+        for (int r = 0; r < R; ++r) y[(size_t)r * out_dim + o] = acc[r];
+}
+
+template <int SRC, int R>
+cudaError_t launch_gemv(const void *w, const float *wsc, int out_dim, int in_dim, const float *x, float *y, int *err,
+                        cudaStream_t s) {
+    const size_t smem = (size_t)kGemvStages * GemvGeom<SRC>::template stage_bytes<R>();
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<SRC, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k_gemv<SRC, R><<<(unsigned)((out_dim + 31) / 32), 32, smem, s>>>(w, wsc, out_dim, in_dim, x, y, err);
+    return launched();
+}
+
 template <int SRC>
 cudaError_t project_src(const void *w, const float *wsc, int out_dim, int in_dim, const float *x, int rows, float *y,
-                        cudaStream_t s) {
+                        int *err, cudaStream_t s) {
+    const bool gemv = rows <= 4 && in_dim % (SRC == SRC_Q8 ? 128 : 8) == 0 && ((uintptr_t)x & 15) == 0 &&
+                      ((uintptr_t)w & 15) == 0 && (SRC != SRC_Q8 || ((uintptr_t)wsc & 15) == 0);
+    if (gemv) {
+        switch (rows) {
+        case 1: return launch_gemv<SRC, 1>(w, wsc, out_dim, in_dim, x, y, err, s);
+        case 2: return launch_gemv<SRC, 2>(w, wsc, out_dim, in_dim, x, y, err, s);
+        case 3: return launch_gemv<SRC, 3>(w, wsc, out_dim, in_dim, x, y, err, s);
+        default: return launch_gemv<SRC, 4>(w, wsc, out_dim, in_dim, x, y, err, s);
+        }
+    }
     const bool tiled = in_dim % (SRC == SRC_Q8 ? 32 : 8) == 0 && ((uintptr_t)x & 15) == 0 &&
                        ((uintptr_t)w & 15) == 0;
     if (!tiled) {
@@ -266,12 +409,12 @@ __global__ void __launch_bounds__(128) k_attention(const float *__restrict__ q, 
 }  // namespace
 
 cudaError_t launch_project(int src, const void *w, const float *wsc, int out_dim, int in_dim, const float *x,
-                           int rows, float *y, cudaStream_t s) {
+                           int rows, float *y, int *err, cudaStream_t s) {
     if (rows <= 0 || out_dim <= 0) return cudaSuccess;
     switch (src) {
-    case SRC_BF16: return project_src<SRC_BF16>(w, wsc, out_dim, in_dim, x, rows, y, s);
-    case SRC_Q8: return project_src<SRC_Q8>(w, wsc, out_dim, in_dim, x, rows, y, s);
-    default: return project_src<SRC_F32>(w, wsc, out_dim, in_dim, x, rows, y, s);
+    case SRC_BF16: return project_src<SRC_BF16>(w, wsc, out_dim, in_dim, x, rows, y, err, s);
+    case SRC_Q8: return project_src<SRC_Q8>(w, wsc, out_dim, in_dim, x, rows, y, err, s);
+    default: return project_src<SRC_F32>(w, wsc, out_dim, in_dim, x, rows, y, err, s);
     }
 }
 

@@ -96,7 +96,7 @@ cudaError_t launch_q8x4_to_row_major(const uint8_t *blocks, int out_dim, int in_
 // y[r, o] = dot(decode_row(W, o), x[r]) in the reference's order; W stored
 // [out_dim, in_dim] as SRC_F32 / SRC_BF16 / SRC_Q8 (+ block scales).
 cudaError_t launch_project(int src, const void *w, const float *wsc, int out_dim, int in_dim, const float *x,
-                           int rows, float *y, cudaStream_t s);
+                           int rows, float *y, int *err, cudaStream_t s);
 // Row i of k and v into cache row dst_rows[i] of caches [rows_total, kv_dim].
 cudaError_t launch_kv_write(float *kc, float *vc, int kv_dim, const int32_t *dst_rows, const float *k, const float *v,
                             int rows, cudaStream_t s);

@@ -213,6 +213,10 @@ def run(reps: int, only: str | None = None):
         B.time("rms_norm_q8_0 65536x1024 (fused)", lambda: b.rms_norm_q8_0(xq, wq8, R, qd8, 1e-6, c8, s8, h8),
                R * (4 * qd8 + qd8 + 6 * nb))
 
+    # --- contractions (exact order; SmolLM2-1.7B and Qwen3-0.6B shapes)
+    if B.want("project", "logits", "attention", "kv_write"):
+        contractions(B)
+
     # --- the chain on every workload
     for wk in (W.SMOLLM2_135M, W.SMOLLM2_17B_PREFILL, W.QWEN3_06B_Q8, W.LFM2_700M, W.SMOLLM2_17B_65K):
         if B.want(f"chain: {wk.name}"):
@@ -222,6 +226,61 @@ def run(reps: int, only: str | None = None):
     if B.want("decode step"):
         decode_latency(B)
     return B
+
+
+# FP32 multiply + add pairs per second a B200 issues on its CUDA cores
+# (148 SMs x 128 lanes x 1.965 GHz / 2 instructions per pair): the ceiling of
+# an exact-order dot, which cannot fuse the multiply into the add.
+EXACT_MAC_PEAK = 148 * 128 * 1.965e9 / 2
+
+
+def contractions(B):
+    b = B.b
+    rng = np.random.default_rng(5)
+    H = 2048
+    wq = rng.standard_normal((H, H), dtype=np.float32) * np.float32(0.02)
+    wq16 = (wq.view(np.uint32) >> 16).astype(np.uint16)  # bf16 by truncation: any bit pattern will do
+    mq = b.prepare_matrix(BF16, wq16, None, H, H)
+    for rows in (1, 512):
+        x, y = B.buf(rows * H), b.alloc(rows * H)
+        macs = rows * H * H
+        r = B.time(f"project bf16 {H}x{H}, {rows} row{'s' if rows > 1 else ''}", lambda: b.project(mq, x, y, rows),
+                   H * H * 2 + rows * H * 8,
+                   note="HBM-bound (weights once)" if rows == 1 else "")
+        if r is not None and rows > 1:
+            r["note"] = f"{macs / (r['ms'] / 1e3) / 1e12:.2f} T MAC/s = {macs / (r['ms'] / 1e3) / EXACT_MAC_PEAK:.2f} of the exact-order FP32 ceiling"
+    codes = rng.integers(-127, 128, size=(3072, 1024), dtype=np.int8)
+    sc = rng.uniform(1e-4, 1e-2, size=(3072, 32)).astype(np.float32)
+    mg = b.prepare_matrix(Q8_0, codes, sc, 3072, 1024)
+    x1, y1 = B.buf(1024), b.alloc(3072)
+    B.time("project q8_0 3072x1024, 1 row (Qwen3 gate)", lambda: b.project(mg, x1, y1, 1), 3072 * (1024 + 128) + 1024 * 4)
+    vocab = 49152
+    emb = (rng.standard_normal((vocab, H), dtype=np.float32) * np.float32(0.02)).view(np.uint32) >> 16
+    ml = b.prepare_matrix(BF16, emb.astype(np.uint16), None, vocab, H)
+    xl, yl = B.buf(H), b.alloc(vocab)
+    B.time(f"logits bf16 {vocab}x{H}", lambda: b.logits(ml, xl, yl), vocab * H * 2 + vocab * 4)
+    # attention: 32 heads x 64, the cache of one layer, seq 4096
+    n_heads, head, seq = 32, 64, 4096
+    kv_dim = n_heads * head
+    b.kv_prepare(1, kv_dim, seq)
+    kx, vx = B.buf(512 * kv_dim), B.buf(512 * kv_dim)
+    slots = np.arange(512, dtype=np.uint64)
+    B.time("kv_write 512 rows x 2048", lambda: b.kv_write(0, slots, kx, vx, 512), 512 * kv_dim * 16)
+    for s0 in range(0, seq, 512):
+        b.kv_write(0, slots + s0, kx, vx, 512)
+    q1, o1, a1 = B.buf(kv_dim), b.alloc(kv_dim), b.alloc(n_heads * seq)
+    B.time("attention decode, 1 row at pos 511 (32x64)", lambda: b.attention(q1, o1, a1, 0, [(0, 511, 0, 0)], n_heads, 1,
+                                                                           head, kv_dim, seq),
+           512 * kv_dim * 8 + 32 * 512 * 4)
+    B.time("attention decode, 1 row at pos 4095 (32x64)",
+           lambda: b.attention(q1, o1, a1, 0, [(0, 4095, 0, 0)], n_heads, 1, head, kv_dim, seq),
+           4096 * kv_dim * 8 + 32 * 4096 * 4)
+    rows = 512
+    qp, op, ap = B.buf(rows * kv_dim), b.alloc(rows * kv_dim), b.alloc(rows * n_heads * seq)
+    wins = [(0, r, 0, 0) for r in range(rows)]
+    B.time("attention prefill, 512 causal rows (32x64)",
+           lambda: b.attention(qp, op, ap, 0, wins, n_heads, 1, head, kv_dim, seq), None,
+           note="per-(row, head) CTAs; scores and sums in order")
 
 
 def chain_time(B, wk):
