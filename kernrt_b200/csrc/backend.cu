@@ -82,6 +82,7 @@ public:
         }
         cudaFree(kc_);
         cudaFree(vc_);
+        cudaFree(att_scratch_);
         cudaFree(d_err_);
         cudaFreeHost(h_err_);
         cudaFreeHost(stage_host_);
@@ -403,10 +404,20 @@ public:
         }
         if (attention_smem_bytes((int)head_size, (int)max_count) > 200 * 1024)
             fail(KERNRT_E_INVALID, "attention window too long for one SM's shared memory");
+        // raw scores go to a scratch the backend keeps (grown, never shrunk)
+        const size_t need = attention_scratch_floats((int)n_windows, (int)n_heads, (int)max_count) * sizeof(float);
+        if (need > att_scratch_bytes_) {
+            check(cudaStreamSynchronize(stream_), "synchronize");
+            cudaFree(att_scratch_);
+            att_scratch_ = nullptr;
+            att_scratch_bytes_ = 0;
+            check(cudaMalloc(&att_scratch_, need), "cudaMalloc(attention scratch)");
+            att_scratch_bytes_ = need;
+        }
         const int32_t *d = static_cast<const int32_t *>(stage(win.data(), win.size() * sizeof(int32_t)));
         launch_or_fail(launch_attention(f(qb), f(ob), f(ab), kc_, vc_, d, (int)n_windows, (int)n_heads, (int)kv_mul,
                                         (int)head_size, (int)kv_dim, (int)seq_len, layer * seq_len * kv_dim,
-                                        (int)max_count, stream_),
+                                        (int)max_count, att_scratch_, stream_),
                        "attention");
     }
 
@@ -1264,6 +1275,8 @@ private:
     std::vector<Pending> pending_;
     std::vector<DevMatrix> mats_;
     float *kc_ = nullptr, *vc_ = nullptr;
+    float *att_scratch_ = nullptr;
+    size_t att_scratch_bytes_ = 0;
     size_t kv_layers_ = 0, kv_dim_ = 0, kv_seq_ = 0;
     int emb_kind_ = -1;
     int emb_src_ = SRC_F32;

@@ -340,6 +340,28 @@ __global__ void __launch_bounds__(256) k_kv_write(float *__restrict__ kc, float 
 
 // ---- attention ------------------------------------------------------------------
 
+// sum_{i < n} v[i] from shared memory in index order, one thread: sixteen
+// values loaded ahead of their adds, so the loads stay off the add chain.
+__device__ __forceinline__ float seq_sum_smem(const float *v, int n) {
+    float sum = 0.0f;
+    int i = 0;
+    if (((uintptr_t)v & 15) == 0)
+        for (; i + 16 <= n; i += 16) {
+            float4 t[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) t[j] = *reinterpret_cast<const float4 *>(v + i + 4 * j);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                sum = add_rn(sum, t[j].x);
+                sum = add_rn(sum, t[j].y);
+                sum = add_rn(sum, t[j].z);
+                sum = add_rn(sum, t[j].w);
+            }
+        }
+    for (; i < n; ++i) sum = add_rn(sum, v[i]);
+    return sum;
+}
+
 // reference.rs:418-482 for one (query row, head): a CTA of 128 threads.
 //   scores: thread per position, each a sequential dot over head_size, times
 //           1/sqrt(head_size);
@@ -384,11 +406,7 @@ __global__ void __launch_bounds__(128) k_attention(const float *__restrict__ q, 
     m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
     for (int i = tid; i < count; i += 128) sc[i] = expf(__fsub_rn(sc[i], m));
     __syncthreads();
-    if (tid == 0) {
-        float sum = 0.0f;
-        for (int i = 0; i < count; ++i) sum = add_rn(sum, sc[i]);
-        total = sum;
-    }
+    if (tid == 0) total = seq_sum_smem(sc, count);
     __syncthreads();
     const float sum = total;
     float *ag = att + ((size_t)row * n_heads + h) * seq_len;
@@ -404,6 +422,159 @@ __global__ void __launch_bounds__(128) k_attention(const float *__restrict__ q, 
         for (int i = 0; i < count; ++i) o = add_rn(o, mul_rn(sc[i], vc[loff + (size_t)pos_of(i) * kv_dim + kv + e]));
         og[e] = o;
     }
+}
+
+// ---- attention in two kernels ---------------------------------------------------
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// Window position i of a row: the shared range first, then the row's own.
+__device__ __forceinline__ int win_pos(const int32_t *w, int i) {
+    const int n_shared = w[3] - w[2];
+    return i < n_shared ? w[2] + i : w[0] + (i - n_shared);
+}
+
+// Scores (reference.rs:439-446): raw[row][h][i] = dot(q_h, k_pos) * scale,
+// thread per position, each dot over head_size in order, into scratch rows of
+// `stride` floats.  Grid (row x head, position blocks of 128).
+__global__ void __launch_bounds__(128) k_att_scores(const float *__restrict__ q, float *__restrict__ raw,
+                                                    const float *__restrict__ kc, const int32_t *__restrict__ win,
+                                                    int n_heads, int kv_mul, int head_size, int kv_dim, int stride,
+                                                    size_t loff) {
+    extern __shared__ __align__(16) float qsh[];
+    const int row = blockIdx.x / n_heads, h = blockIdx.x - row * n_heads;
+    const int32_t *w = win + 4 * row;
+    const int count = (w[3] - w[2]) + w[1] - w[0] + 1;
+    const int i = blockIdx.y * 128 + threadIdx.x;
+    if ((int)blockIdx.y * 128 >= count) return;
+    const float *qg = q + ((size_t)row * n_heads + h) * head_size;
+    for (int e = threadIdx.x; e < head_size; e += 128) qsh[e] = qg[e];
+    __syncthreads();
+    if (i >= count) return;
+    const float *kr = kc + loff + (size_t)win_pos(w, i) * kv_dim + (size_t)(h / kv_mul) * head_size;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)head_size));
+    float d = 0.0f;
+    if ((head_size & 3) == 0 && ((uintptr_t)kr & 15) == 0) {
+        // eight float4 of the key in flight, then their products in order
+        for (int e0 = 0; e0 < head_size; e0 += 32) {
+            float4 kv4[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (e0 + 4 * j < head_size) kv4[j] = __ldg(reinterpret_cast<const float4 *>(kr + e0 + 4 * j));
+            float4 q4[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (e0 + 4 * j < head_size) q4[j] = *reinterpret_cast<const float4 *>(qsh + e0 + 4 * j);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (e0 + 4 * j >= head_size) break;
+                d = add_rn(d, mul_rn(q4[j].x, kv4[j].x));
+                d = add_rn(d, mul_rn(q4[j].y, kv4[j].y));
+                d = add_rn(d, mul_rn(q4[j].z, kv4[j].z));
+                d = add_rn(d, mul_rn(q4[j].w, kv4[j].w));
+            }
+        }
+    } else {
+        for (int e = 0; e < head_size; ++e) d = add_rn(d, mul_rn(qsh[e], kr[e]));
+    }
+    raw[((size_t)row * n_heads + h) * stride + i] = mul_rn(d, scale);
+}
+
+// Softmax and output (reference.rs:448-480) for one (row, head) and a slice
+// of `sw` output elements: the raw scores, their maximum (order-free),
+// exp(s - max), the sum by one thread in position order, s / sum (slice 0
+// writes these to att); then thread e of the slice runs out[e] = sum_i a_i *
+// v_pos(i)[e] in position order.  Slices of one head repeat the softmax,
+// which is cheap next to the value rows they stream.  The slice's value
+// columns move through shared memory in tiles of 2048 / sw positions,
+// kAttStages - 1 tiles ahead, every thread issuing 16-byte cp.async copies.
+constexpr int kAttTileFloats = 2048;  // positions x slice width per stage (8 KB)
+
+template <int kAttStages>
+__global__ void __launch_bounds__(128) k_att_out(float *__restrict__ out, float *__restrict__ att,
+                                                 const float *__restrict__ raw, const float *__restrict__ vc,
+                                                 const int32_t *__restrict__ win, int n_heads, int kv_mul,
+                                                 int head_size, int kv_dim, int seq_len, size_t loff, int stride,
+                                                 int sw) {
+    extern __shared__ __align__(16) float osm[];
+    const int nsl = (head_size + sw - 1) / sw, tp = kAttTileFloats / sw;
+    const int rh = blockIdx.x / nsl, sl = blockIdx.x - rh * nsl;
+    const int row = rh / n_heads, h = rh - row * n_heads;
+    const int tid = threadIdx.x;
+    const int32_t *w = win + 4 * row;
+    const int count = (w[3] - w[2]) + w[1] - w[0] + 1;
+    const int e0 = sl * sw, ne = min(sw, head_size - e0);
+    float *sc = osm;                             // [stride]
+    float *tiles = osm + ((stride + 3) & ~3);    // [kAttStages][tp][sw]
+    __shared__ float red[4];
+    __shared__ float total;
+    const float *rg = raw + (size_t)rh * stride;
+    for (int i = tid; i < count; i += 128) sc[i] = rg[i];
+    __syncthreads();
+    float m = -INFINITY;  // NaN scores skipped, as the reference's `>` does
+    for (int i = tid; i < count; i += 128) m = fmaxf(m, sc[i]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, o));
+    if ((tid & 31) == 0) red[tid >> 5] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    for (int i = tid; i < count; i += 128) sc[i] = expf(__fsub_rn(sc[i], m));
+    __syncthreads();
+    if (tid == 0) total = seq_sum_smem(sc, count);
+    __syncthreads();
+    const float sum = total;
+    float *ag = att + (size_t)rh * seq_len;
+    for (int i = tid; i < count; i += 128) {
+        const float a = __fdiv_rn(sc[i], sum);
+        sc[i] = a;
+        if (sl == 0) ag[i] = a;
+    }
+    const size_t vo = loff + (size_t)(h / kv_mul) * head_size + e0;
+    const int chunks = ne >> 2;  // 16-byte pieces of a position's slice
+    const int ntiles = (count + tp - 1) / tp;
+    auto load_tile = [&](int t) {
+        float *dst = tiles + (size_t)(t % kAttStages) * kAttTileFloats;
+        const int p0 = t * tp, np = min(tp, count - p0);
+        for (int c = tid; c < np * chunks; c += 128) {
+            const int p = c / chunks, j = c - p * chunks;
+            cp_async16(dst + p * sw + 4 * j, vc + vo + (size_t)win_pos(w, p0 + p) * kv_dim + 4 * j);
+        }
+    };
+    for (int t = 0; t < kAttStages - 1; ++t) {
+        if (t < ntiles) load_tile(t);
+        cp_async_commit();
+    }
+    float o = 0.0f;
+    for (int t = 0; t < ntiles; ++t) {
+        cp_async_wait<kAttStages - 2>();  // tile t has landed (for this thread's copies)
+        __syncthreads();                  // ... and every thread's
+        // the stage tile t - 1 used is free: tile t + S - 1 goes there
+        if (t + kAttStages - 1 < ntiles) load_tile(t + kAttStages - 1);
+        cp_async_commit();
+        if (tid < ne) {
+            const float *tile = tiles + (size_t)(t % kAttStages) * kAttTileFloats;
+            const int p0 = t * tp, np = min(tp, count - p0);
+            int p = 0;
+            // eight weights and values loaded ahead of their products in order
+            for (; p + 8 <= np; p += 8) {
+                float a[8], v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    a[j] = sc[p0 + p + j];
+                    v[j] = tile[(p + j) * sw + tid];
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o = add_rn(o, mul_rn(a[j], v[j]));
+            }
+            for (; p < np; ++p) o = add_rn(o, mul_rn(sc[p0 + p], tile[p * sw + tid]));
+        }
+    }
+    cp_async_wait<0>();
+    if (tid < ne) out[(size_t)rh * head_size + e0 + tid] = o;
 }
 
 }  // namespace
@@ -432,10 +603,43 @@ size_t attention_smem_bytes(int head_size, int max_count) {
     return (size_t)(((head_size + 3) & ~3) + max_count) * sizeof(float);
 }
 
+size_t attention_scratch_floats(int n_rows, int n_heads, int max_count) {
+    return (size_t)n_rows * n_heads * (size_t)((max_count + 3) & ~3);
+}
+
 cudaError_t launch_attention(const float *q, float *out, float *att, const float *kc, const float *vc,
                              const int32_t *win, int n_rows, int n_heads, int kv_mul, int head_size, int kv_dim,
-                             int seq_len, size_t loff, int max_count, cudaStream_t s) {
+                             int seq_len, size_t loff, int max_count, float *raw, cudaStream_t s) {
     if (n_rows <= 0 || n_heads <= 0) return cudaSuccess;
+    // Two kernels where the value slices move in 16-byte pieces and a scratch
+    // for the raw scores is given: parallel scores, then per (row, head,
+    // slice) the softmax and the output chains with the value rows streamed.
+    const int stride = (max_count + 3) & ~3;
+    // Few (row, head) pairs (decode): slices of 32 elements and twelve stages
+    // spread a long window's value rows over more SMs and keep ~90 KB of them
+    // in flight per CTA.  Many pairs (prefill) fill the GPU by themselves: one
+    // slice per head, three stages, several CTAs per SM.
+    const bool few = n_rows * n_heads < 2 * 148;
+    const int stages = few ? 12 : 3;
+    const size_t out_smem = (size_t)(stride + stages * kAttTileFloats) * sizeof(float);
+    const bool split = raw && (head_size & 3) == 0 && (kv_dim & 3) == 0 && out_smem <= 200 * 1024;
+    if (split) {
+        k_att_scores<<<dim3((unsigned)(n_rows * n_heads), (unsigned)((max_count + 127) / 128)), 128,
+                       (size_t)head_size * sizeof(float), s>>>(q, raw, kc, win, n_heads, kv_mul, head_size, kv_dim,
+                                                               stride, loff);
+        cudaError_t e = launched();
+        if (e != cudaSuccess) return e;
+        const int sw = few ? 32 : (head_size > 128 ? 128 : head_size);
+        const int nsl = (head_size + sw - 1) / sw;
+        auto kern = few ? k_att_out<12> : k_att_out<3>;
+        if (out_smem > 48 * 1024) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)out_smem);
+            if (e != cudaSuccess) return e;
+        }
+        kern<<<(unsigned)(n_rows * n_heads * nsl), 128, out_smem, s>>>(out, att, raw, vc, win, n_heads, kv_mul,
+                                                                       head_size, kv_dim, seq_len, loff, stride, sw);
+        return launched();
+    }
     const size_t smem = attention_smem_bytes(head_size, max_count);
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -102,9 +102,12 @@ cudaError_t launch_kv_write(float *kc, float *vc, int kv_dim, const int32_t *dst
                             int rows, cudaStream_t s);
 // win: [n_rows][4] = att_start, slot, shared_start, shared_end; max_count the
 // largest window; loff the layer's first cache element.
+// raw: scratch of attention_scratch_floats() for the raw scores (null: the
+// single-kernel form).
 size_t attention_smem_bytes(int head_size, int max_count);
+size_t attention_scratch_floats(int n_rows, int n_heads, int max_count);
 cudaError_t launch_attention(const float *q, float *out, float *att, const float *kc, const float *vc,
                              const int32_t *win, int n_rows, int n_heads, int kv_mul, int head_size, int kv_dim,
-                             int seq_len, size_t loff, int max_count, cudaStream_t s);
+                             int seq_len, size_t loff, int max_count, float *raw, cudaStream_t s);
 
 }  // namespace krt

@@ -127,3 +127,8 @@ def test_contraction_errors(gpu):
     assert "window 0 out of range" in str(e.value)
     b.synchronize()
     b.close()
+
+
+def test_attention_odd_head_size(gpu, oracle):
+    # head_size 6 takes the single-kernel path
+    attention_case(gpu, oracle, 1, 3, 3, 6, 16, 0, [(0, list(range(10)))], [(0, 9, 0, 0), (2, 5, 0, 2)], 340)
