@@ -225,7 +225,82 @@ def run(reps: int, only: str | None = None):
     # --- decode latency: one row through the trait ops, read() each step
     if B.want("decode step"):
         decode_latency(B)
+    if B.want("decode token"):
+        model_decode(B)
     return B
+
+
+def model_decode(B, n_layers: int = 24, pos: int = 511, samples: int = 50):
+    """A whole SmolLM2-1.7B decode step on the device through the trait ops in
+    the driver's order (llama.rs decode: per layer rms_norm, q/k/v projections,
+    RoPE, kv_write, attention, o projection, residual add, rms_norm, gate/up
+    projections, SwiGLU, down projection, residual add; then the final norm,
+    the tied classifier and read()), random bf16 weights, the cache filled to
+    `pos`.  Host wall clock per token."""
+    import torch
+
+    b = B.b
+    wk = W.SMOLLM2_17B_DECODE
+    H, Q, KV, I, hd = wk.dim, wk.q_dim, wk.kv_dim, wk.hidden, wk.head
+    g = torch.Generator(device="cuda:0").manual_seed(11)
+
+    def mat(o, i):
+        t = (torch.randn(o, i, device="cuda:0", generator=g) * (1.0 / i ** 0.5)).to(torch.bfloat16)
+        return b.prepare_matrix(BF16, t.view(torch.int16).cpu().numpy().view(np.uint16), None, o, i)
+
+    layers = [dict(q=mat(Q, H), k=mat(KV, H), v=mat(KV, H), o=mat(H, Q), gate=mat(I, H), up=mat(I, H),
+                   down=mat(H, I)) for _ in range(n_layers)]
+    emb = (torch.randn(wk.vocab, H, device="cuda:0", generator=g) * 0.02).to(torch.bfloat16)
+    emb_h = emb.view(torch.int16).cpu().numpy().view(np.uint16)
+    b.prepare_embedding(BF16, emb_h, None, wk.vocab, H)
+    cls = b.prepare_matrix(BF16, emb_h, None, wk.vocab, H)
+    seq = 4096
+    b.kv_prepare(n_layers, KV, seq)
+    ones = b.upload(np.ones(H, np.float32))
+    x, xb, q, k, v, att_o, o = (b.alloc(n) for n in (H, H, Q, KV, KV, Q, H))
+    gt, up, dn = b.alloc(I), b.alloc(I), b.alloc(H)
+    att = b.alloc(wk.n_heads * seq)
+    logits = b.alloc(wk.vocab)
+    kf, vf = B.buf(pos * KV), B.buf(pos * KV)
+    for layer in range(n_layers):  # the cache up to pos - 1
+        b.kv_write(layer, np.arange(pos, dtype=np.uint64), kf, vf, pos)
+    out = np.empty(wk.vocab, np.float32)
+    kv_mul = wk.n_heads // wk.n_kv_heads
+
+    def step(p):
+        b.embed(7, x, 0)
+        for L in layers:
+            b.rms_norm(xb, x, ones, 1, H, wk.eps)
+            b.project(L["q"], xb, q, 1)
+            b.project(L["k"], xb, k, 1)
+            b.project(L["v"], xb, v, 1)
+            b.rope(q, k, Q, KV, 1, [p], hd, wk.theta, False)
+            b.kv_write(layers.index(L), [p], k, v, 1)
+            b.attention(q, att_o, att, layers.index(L), [(0, p, 0, 0)], wk.n_heads, kv_mul, hd, KV, seq)
+            b.project(L["o"], att_o, o, 1)
+            b.add_in_place(x, o, H)
+            b.rms_norm(xb, x, ones, 1, H, wk.eps)
+            b.project(L["gate"], xb, gt, 1)
+            b.project(L["up"], xb, up, 1)
+            b.silu_mul(gt, up, I)
+            b.project(L["down"], gt, dn, 1)
+            b.add_in_place(x, dn, H)
+        b.rms_norm(xb, x, ones, 1, H, wk.eps)
+        b.logits(cls, xb, logits)
+        b.read_into(logits, out)
+
+    for _ in range(3):
+        step(pos)
+    times = []
+    for _ in range(samples):
+        t0 = time.perf_counter()
+        step(pos)
+        times.append((time.perf_counter() - t0) * 1e3)
+    times.sort()
+    B.rows.append({"name": f"decode token, SmolLM2-1.7B ({n_layers} layers, bf16, pos {pos}): trait ops + read()",
+                   "ms": None, "us_p10": times[len(times) // 10] * 1e3, "us_median": times[len(times) // 2] * 1e3,
+                   "gbs": None, "frac": None, "launches": None,
+                   "note": f"host wall clock, {samples} samples; {1e3 / times[len(times) // 2]:.0f} tokens/s"})
 
 
 # FP32 multiply + add pairs per second a B200 issues on its CUDA cores
