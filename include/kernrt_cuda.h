@@ -270,6 +270,15 @@ int kernrt_cuda_prepare_matrix(kernrt_cuda_ctx *ctx, int kind, const void *data,
  * three / two of these calls. */
 int kernrt_cuda_project(kernrt_cuda_ctx *ctx, kernrt_mat w, kernrt_buf x, kernrt_buf y, size_t rows);
 
+/* Backend::project_qkv / project_gate_up (mod.rs:320-337): the same
+ * projections of one x as three / two kernrt_cuda_project calls, in one
+ * launch where the matrices share storage and in_dim (the override the
+ * trait's comment invites: decode projections run side by side). */
+int kernrt_cuda_project_qkv(kernrt_cuda_ctx *ctx, kernrt_mat wq, kernrt_mat wk, kernrt_mat wv, kernrt_buf x,
+                            kernrt_buf q, kernrt_buf k, kernrt_buf v, size_t rows);
+int kernrt_cuda_project_gate_up(kernrt_cuda_ctx *ctx, kernrt_mat wg, kernrt_mat wu, kernrt_buf x,
+                                kernrt_buf gate, kernrt_buf up, size_t rows);
+
 /* Backend::logits (mod.rs:403; reference.rs:402-416): the classifier W over
  * row 0 of x. */
 int kernrt_cuda_logits(kernrt_cuda_ctx *ctx, kernrt_mat w, kernrt_buf x, kernrt_buf y);

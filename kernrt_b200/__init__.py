@@ -122,6 +122,8 @@ SIGNATURES = {
     "kernrt_cuda_stage_times": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
     "kernrt_cuda_prepare_matrix": (C.c_int, [P, C.c_int, P, P, SZ, SZ, C.POINTER(C.c_uint64)]),
     "kernrt_cuda_project": (C.c_int, [P, C.c_uint64, Buf, Buf, SZ]),
+    "kernrt_cuda_project_qkv": (C.c_int, [P, C.c_uint64, C.c_uint64, C.c_uint64, Buf, Buf, Buf, Buf, SZ]),
+    "kernrt_cuda_project_gate_up": (C.c_int, [P, C.c_uint64, C.c_uint64, Buf, Buf, Buf, SZ]),
     "kernrt_cuda_logits": (C.c_int, [P, C.c_uint64, Buf, Buf]),
     "kernrt_cuda_kv_prepare": (C.c_int, [P, SZ, SZ, SZ]),
     "kernrt_cuda_kv_write": (C.c_int, [P, SZ, P, SZ, Buf, Buf, SZ]),
@@ -384,6 +386,12 @@ class CudaBackend:
 
     def project(self, w: int, x: int, y: int, rows: int) -> None:
         _ok(self._lib.kernrt_cuda_project(self._ctx, w, x, y, rows))
+
+    def project_qkv(self, wq: int, wk: int, wv: int, x: int, q: int, k: int, v: int, rows: int) -> None:
+        _ok(self._lib.kernrt_cuda_project_qkv(self._ctx, wq, wk, wv, x, q, k, v, rows))
+
+    def project_gate_up(self, wg: int, wu: int, x: int, gate: int, up: int, rows: int) -> None:
+        _ok(self._lib.kernrt_cuda_project_gate_up(self._ctx, wg, wu, x, gate, up, rows))
 
     def logits(self, w: int, x: int, y: int) -> None:
         _ok(self._lib.kernrt_cuda_logits(self._ctx, w, x, y))

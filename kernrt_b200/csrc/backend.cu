@@ -321,6 +321,45 @@ public:
                        "project");
     }
 
+    // mod.rs:320-337 project_qkv / project_gate_up: n projections of one x,
+    // in one launch where the shapes allow (same storage and in_dim).
+    void project_set(int n, const uint64_t *ws, kernrt_buf x, const kernrt_buf *ys, size_t rows) {
+        const void *wp[3];
+        const float *sp[3];
+        int outs[3];
+        float *yp[3];
+        const DevMatrix &m0 = mat(ws[0]);
+        bool same = true;
+        for (int i = 0; i < n; ++i) {
+            const DevMatrix &m = mat(ws[i]);
+            distinct(x, ys[i]);
+            for (int j = 0; j < i; ++j)
+                if (ys[j] == ys[i]) fail(KERNRT_E_INVALID, "buffers must be distinct");
+            same = same && m.src == m0.src && m.in_dim == m0.in_dim;
+        }
+        if (!same) {
+            for (int i = 0; i < n; ++i) project(ws[i], x, ys[i], rows);
+            return;
+        }
+        Buffer &xb = buf(x);
+        span(xb, 0, rows * m0.in_dim, "project x");
+        for (int i = 0; i < n; ++i) {
+            const DevMatrix &m = mat(ws[i]);
+            Buffer &yb = buf(ys[i]);
+            span(yb, 0, rows * m.out_dim, "project y");
+            fits_int(rows * std::max(m.in_dim, m.out_dim), "project");
+            wp[i] = m.data;
+            sp[i] = m.scales;
+            outs[i] = (int)m.out_dim;
+            yp[i] = f(yb);
+        }
+        flush();
+        if (rows == 0) return;
+        launch_or_fail(launch_project_set(m0.src, n, wp, sp, outs, (int)m0.in_dim, f(xb), (int)rows, yp, d_err_,
+                                          stream_),
+                       "project");
+    }
+
     // reference.rs:402-416: the classifier over row 0 of x.
     void logits(uint64_t w, kernrt_buf x, kernrt_buf y) { project(w, x, y, 1); }
 
@@ -1556,6 +1595,24 @@ int kernrt_cuda_prepare_matrix(kernrt_cuda_ctx *ctx, int kind, const void *data,
 
 int kernrt_cuda_project(kernrt_cuda_ctx *ctx, kernrt_mat w, kernrt_buf x, kernrt_buf y, size_t rows) {
     return guard(ctx, [&](krt::Backend &b) { b.project(w, x, y, rows); });
+}
+
+int kernrt_cuda_project_qkv(kernrt_cuda_ctx *ctx, kernrt_mat wq, kernrt_mat wk, kernrt_mat wv, kernrt_buf x,
+                            kernrt_buf q, kernrt_buf k, kernrt_buf v, size_t rows) {
+    return guard(ctx, [&](krt::Backend &b) {
+        const uint64_t ws[3] = {wq, wk, wv};
+        const kernrt_buf ys[3] = {q, k, v};
+        b.project_set(3, ws, x, ys, rows);
+    });
+}
+
+int kernrt_cuda_project_gate_up(kernrt_cuda_ctx *ctx, kernrt_mat wg, kernrt_mat wu, kernrt_buf x, kernrt_buf gate,
+                                kernrt_buf up, size_t rows) {
+    return guard(ctx, [&](krt::Backend &b) {
+        const uint64_t ws[2] = {wg, wu};
+        const kernrt_buf ys[2] = {gate, up};
+        b.project_set(2, ws, x, ys, rows);
+    });
 }
 
 int kernrt_cuda_logits(kernrt_cuda_ctx *ctx, kernrt_mat w, kernrt_buf x, kernrt_buf y) {

@@ -181,17 +181,34 @@ struct GemvGeom {
     __host__ __device__ static constexpr int stage_bytes() { return 32 * wstride + R * kGemvCK * 4; }
 };
 
+// Up to three matrices sharing x and in_dim in one launch (the trait's
+// project_qkv / project_gate_up, mod.rs:320-337): their CTAs run side by side
+// instead of one projection after another.
+struct GemvSet {
+    const void *w[3];
+    const float *wsc[3];
+    float *y[3];
+    int out_dim[3];
+    int cta_end[3];  // exclusive prefix sums of each matrix's CTAs
+    int n;
+};
+
 template <int SRC, int R>
-__global__ void __launch_bounds__(32) k_gemv(const void *__restrict__ w, const float *__restrict__ wsc, int out_dim,
-                                             int in_dim, const float *__restrict__ x, float *__restrict__ y,
-                                             int *err) {
+__global__ void __launch_bounds__(32) k_gemv(GemvSet set, int in_dim, const float *__restrict__ x, int *err) {
     using Geo = GemvGeom<SRC>;
     constexpr int SB = Geo::template stage_bytes<R>();
     extern __shared__ __align__(16) unsigned char gsm[];
     __shared__ __align__(8) uint64_t bar[kGemvStages];
-    const int lane = threadIdx.x, o = blockIdx.x * 32 + lane;
+    int m = 0;
+    while (m + 1 < set.n && (int)blockIdx.x >= set.cta_end[m]) ++m;
+    const int blk = (int)blockIdx.x - (m ? set.cta_end[m - 1] : 0);
+    const void *__restrict__ w = set.w[m];
+    const float *__restrict__ wsc = set.wsc[m];
+    float *__restrict__ y = set.y[m];
+    const int out_dim = set.out_dim[m];
+    const int lane = threadIdx.x, o = blk * 32 + lane;
     const bool live = o < out_dim;
-    const int nlive = min(32, out_dim - (int)blockIdx.x * 32);
+    const int nlive = min(32, out_dim - blk * 32);
     const int nchunks = (in_dim + kGemvCK - 1) / kGemvCK;
     if (lane == 0) {
         for (int i = 0; i < kGemvStages; ++i) mbar_init(&bar[i], 1);
@@ -284,27 +301,42 @@ __global__ void __launch_bounds__(32) k_gemv(const void *__restrict__ w, const f
 }
 
 template <int SRC, int R>
-cudaError_t launch_gemv(const void *w, const float *wsc, int out_dim, int in_dim, const float *x, float *y, int *err,
-                        cudaStream_t s) {
+cudaError_t launch_gemv(const GemvSet &set, int in_dim, const float *x, int *err, cudaStream_t s) {
     const size_t smem = (size_t)kGemvStages * GemvGeom<SRC>::template stage_bytes<R>();
     cudaError_t e = cudaFuncSetAttribute(k_gemv<SRC, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    k_gemv<SRC, R><<<(unsigned)((out_dim + 31) / 32), 32, smem, s>>>(w, wsc, out_dim, in_dim, x, y, err);
+    k_gemv<SRC, R><<<(unsigned)set.cta_end[set.n - 1], 32, smem, s>>>(set, in_dim, x, err);
     return launched();
+}
+
+template <int SRC>
+cudaError_t gemv_rows(const GemvSet &set, int in_dim, const float *x, int rows, int *err, cudaStream_t s) {
+    switch (rows) {
+    case 1: return launch_gemv<SRC, 1>(set, in_dim, x, err, s);
+    case 2: return launch_gemv<SRC, 2>(set, in_dim, x, err, s);
+    case 3: return launch_gemv<SRC, 3>(set, in_dim, x, err, s);
+    default: return launch_gemv<SRC, 4>(set, in_dim, x, err, s);
+    }
+}
+
+template <int SRC>
+bool gemv_fits(const void *w, const float *wsc, int in_dim, const float *x, int rows) {
+    return rows <= 4 && in_dim % (SRC == SRC_Q8 ? 128 : 8) == 0 && ((uintptr_t)x & 15) == 0 &&
+           ((uintptr_t)w & 15) == 0 && (SRC != SRC_Q8 || ((uintptr_t)wsc & 15) == 0);
 }
 
 template <int SRC>
 cudaError_t project_src(const void *w, const float *wsc, int out_dim, int in_dim, const float *x, int rows, float *y,
                         int *err, cudaStream_t s) {
-    const bool gemv = rows <= 4 && in_dim % (SRC == SRC_Q8 ? 128 : 8) == 0 && ((uintptr_t)x & 15) == 0 &&
-                      ((uintptr_t)w & 15) == 0 && (SRC != SRC_Q8 || ((uintptr_t)wsc & 15) == 0);
-    if (gemv) {
-        switch (rows) {
-        case 1: return launch_gemv<SRC, 1>(w, wsc, out_dim, in_dim, x, y, err, s);
-        case 2: return launch_gemv<SRC, 2>(w, wsc, out_dim, in_dim, x, y, err, s);
-        case 3: return launch_gemv<SRC, 3>(w, wsc, out_dim, in_dim, x, y, err, s);
-        default: return launch_gemv<SRC, 4>(w, wsc, out_dim, in_dim, x, y, err, s);
-        }
+    if (gemv_fits<SRC>(w, wsc, in_dim, x, rows)) {
+        GemvSet set{};
+        set.w[0] = w;
+        set.wsc[0] = wsc;
+        set.y[0] = y;
+        set.out_dim[0] = out_dim;
+        set.cta_end[0] = (out_dim + 31) / 32;
+        set.n = 1;
+        return gemv_rows<SRC>(set, in_dim, x, rows, err, s);
     }
     const bool tiled = in_dim % (SRC == SRC_Q8 ? 32 : 8) == 0 && ((uintptr_t)x & 15) == 0 &&
                        ((uintptr_t)w & 15) == 0;
@@ -586,6 +618,42 @@ cudaError_t launch_project(int src, const void *w, const float *wsc, int out_dim
     case SRC_BF16: return project_src<SRC_BF16>(w, wsc, out_dim, in_dim, x, rows, y, err, s);
     case SRC_Q8: return project_src<SRC_Q8>(w, wsc, out_dim, in_dim, x, rows, y, err, s);
     default: return project_src<SRC_F32>(w, wsc, out_dim, in_dim, x, rows, y, err, s);
+    }
+}
+
+cudaError_t launch_project_set(int src, int n, const void *const *w, const float *const *wsc, const int *out_dim,
+                               int in_dim, const float *x, int rows, float *const *y, int *err, cudaStream_t s) {
+    if (rows <= 0 || n <= 0) return cudaSuccess;
+    bool one = n <= 3 && rows <= 4;
+    for (int i = 0; one && i < n; ++i) {
+        switch (src) {
+        case SRC_BF16: one = gemv_fits<SRC_BF16>(w[i], wsc[i], in_dim, x, rows); break;
+        case SRC_Q8: one = gemv_fits<SRC_Q8>(w[i], wsc[i], in_dim, x, rows); break;
+        default: one = gemv_fits<SRC_F32>(w[i], wsc[i], in_dim, x, rows); break;
+        }
+    }
+    if (!one) {  // one projection after another
+        for (int i = 0; i < n; ++i) {
+            const cudaError_t e = launch_project(src, w[i], wsc[i], out_dim[i], in_dim, x, rows, y[i], err, s);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    }
+    GemvSet set{};
+    int ctas = 0;
+    for (int i = 0; i < n; ++i) {
+        set.w[i] = w[i];
+        set.wsc[i] = wsc[i];
+        set.y[i] = y[i];
+        set.out_dim[i] = out_dim[i];
+        ctas += (out_dim[i] + 31) / 32;
+        set.cta_end[i] = ctas;
+    }
+    set.n = n;
+    switch (src) {
+    case SRC_BF16: return gemv_rows<SRC_BF16>(set, in_dim, x, rows, err, s);
+    case SRC_Q8: return gemv_rows<SRC_Q8>(set, in_dim, x, rows, err, s);
+    default: return gemv_rows<SRC_F32>(set, in_dim, x, rows, err, s);
     }
 }
 

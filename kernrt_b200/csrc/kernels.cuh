@@ -97,6 +97,10 @@ cudaError_t launch_q8x4_to_row_major(const uint8_t *blocks, int out_dim, int in_
 // [out_dim, in_dim] as SRC_F32 / SRC_BF16 / SRC_Q8 (+ block scales).
 cudaError_t launch_project(int src, const void *w, const float *wsc, int out_dim, int in_dim, const float *x,
                            int rows, float *y, int *err, cudaStream_t s);
+// n (<= 3) projections of the same x and in_dim, one launch where the decode
+// kernel takes them all (the trait's project_qkv / project_gate_up).
+cudaError_t launch_project_set(int src, int n, const void *const *w, const float *const *wsc, const int *out_dim,
+                               int in_dim, const float *x, int rows, float *const *y, int *err, cudaStream_t s);
 // Row i of k and v into cache row dst_rows[i] of caches [rows_total, kv_dim].
 cudaError_t launch_kv_write(float *kc, float *vc, int kv_dim, const int32_t *dst_rows, const float *k, const float *v,
                             int rows, cudaStream_t s);

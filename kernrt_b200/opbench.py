@@ -232,9 +232,9 @@ def run(reps: int, only: str | None = None):
 
 def model_decode(B, n_layers: int = 24, pos: int = 511, samples: int = 50):
     """A whole SmolLM2-1.7B decode step on the device through the trait ops in
-    the driver's order (llama.rs decode: per layer rms_norm, q/k/v projections,
-    RoPE, kv_write, attention, o projection, residual add, rms_norm, gate/up
-    projections, SwiGLU, down projection, residual add; then the final norm,
+    the driver's order (llama.rs decode: per layer rms_norm, project_qkv, RoPE,
+    kv_write, attention, o projection, residual add, rms_norm, project_gate_up,
+    SwiGLU, down projection, residual add; then the final norm,
     the tied classifier and read()), random bf16 weights, the cache filled to
     `pos`.  Host wall clock per token."""
     import torch
@@ -271,17 +271,14 @@ def model_decode(B, n_layers: int = 24, pos: int = 511, samples: int = 50):
         b.embed(7, x, 0)
         for L in layers:
             b.rms_norm(xb, x, ones, 1, H, wk.eps)
-            b.project(L["q"], xb, q, 1)
-            b.project(L["k"], xb, k, 1)
-            b.project(L["v"], xb, v, 1)
+            b.project_qkv(L["q"], L["k"], L["v"], xb, q, k, v, 1)
             b.rope(q, k, Q, KV, 1, [p], hd, wk.theta, False)
             b.kv_write(layers.index(L), [p], k, v, 1)
             b.attention(q, att_o, att, layers.index(L), [(0, p, 0, 0)], wk.n_heads, kv_mul, hd, KV, seq)
             b.project(L["o"], att_o, o, 1)
             b.add_in_place(x, o, H)
             b.rms_norm(xb, x, ones, 1, H, wk.eps)
-            b.project(L["gate"], xb, gt, 1)
-            b.project(L["up"], xb, up, 1)
+            b.project_gate_up(L["gate"], L["up"], xb, gt, up, 1)
             b.silu_mul(gt, up, I)
             b.project(L["down"], gt, dn, 1)
             b.add_in_place(x, dn, H)
@@ -321,7 +318,7 @@ def contractions(B):
         macs = rows * H * H
         r = B.time(f"project bf16 {H}x{H}, {rows} row{'s' if rows > 1 else ''}", lambda: b.project(mq, x, y, rows),
                    H * H * 2 + rows * H * 8,
-                   note="HBM-bound (weights once)" if rows == 1 else "")
+                   note="bound by each output's 2048-long add chain" if rows == 1 else "")
         if r is not None and rows > 1:
             r["note"] = f"{macs / (r['ms'] / 1e3) / 1e12:.2f} T MAC/s = {macs / (r['ms'] / 1e3) / EXACT_MAC_PEAK:.2f} of the exact-order FP32 ceiling"
     codes = rng.integers(-127, 128, size=(3072, 1024), dtype=np.int8)

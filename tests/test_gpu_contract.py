@@ -132,3 +132,31 @@ def test_contraction_errors(gpu):
 def test_attention_odd_head_size(gpu, oracle):
     # head_size 6 takes the single-kernel path
     attention_case(gpu, oracle, 1, 3, 3, 6, 16, 0, [(0, list(range(10)))], [(0, 9, 0, 0), (2, 5, 0, 2)], 340)
+
+
+@pytest.mark.parametrize("rows", [1, 3, 6])
+def test_project_qkv_and_gate_up_equal_the_separate_projections(gpu, oracle, rows):
+    """mod.rs:320-337: the fused calls give each projection's own bits, in one
+    launch for decode rows, one after another otherwise or when storages differ."""
+    dim = 256
+    mats = []
+    for i, (kind, out) in enumerate([("bf16", 256), ("bf16", 64), ("bf16", 64), ("q8_0", 512), ("q8_0", 512)]):
+        dk, data, scales, ok = weights(kind, out, dim, 400 + i, oracle)
+        mats.append((gpu.prepare_matrix(dk, data, scales, out, dim), data, scales, ok, out))
+    x = _data.lcg_normal(rows * dim, 410 + rows).reshape(rows, dim)
+    hx = gpu.upload(x)
+    outs = [gpu.alloc(rows * m[4]) for m in mats]
+    gpu.synchronize()
+    n0 = kernrt_b200.kernel_launches()
+    gpu.project_qkv(mats[0][0], mats[1][0], mats[2][0], hx, outs[0], outs[1], outs[2], rows)
+    gpu.project_gate_up(mats[3][0], mats[4][0], hx, outs[3], outs[4], rows)
+    gpu.synchronize()
+    assert kernrt_b200.kernel_launches() - n0 == (2 if rows <= 4 else 5)
+    for (h, data, scales, ok, out), ho in zip(mats, outs):
+        want = oracle.project(ok, data, scales, out, dim, x)
+        assert_bits_equal(gpu.read(ho, rows * out).reshape(rows, out), want, "fused projection")
+    # storages that differ take the separate launches, same bits
+    dk, data, _, ok = weights("f32", 64, dim, 420, oracle)
+    mf = gpu.prepare_matrix(dk, data, None, 64, dim)
+    gpu.project_qkv(mats[0][0], mf, mats[2][0], hx, outs[0], outs[1], outs[2], rows)
+    assert_bits_equal(gpu.read(outs[1], rows * 64).reshape(rows, 64), oracle.project(ok, data, None, 64, dim, x), "k")
