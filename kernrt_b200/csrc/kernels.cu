@@ -152,11 +152,12 @@ __device__ void qk_norm_row_warp(float *v, int width, int head, const float *__r
 
 // reference.rs:239-254 half-split RoPE of `nh` heads of one row.
 // ct/st: the table row of this row's position, `half` entries each.
+// `lane` of `nl` cooperating threads (a warp, or several warps on one row).
 __device__ void rope_half_row(float *v, int nh, int head, int half, const float *__restrict__ ct,
-                              const float *__restrict__ st, bool vec, int lane) {
+                              const float *__restrict__ st, bool vec, int lane, int nl = 32) {
     if (vec) {
         const int per = half >> 2, n = nh * per;
-        for (int t = lane; t < n; t += 32) {
+        for (int t = lane; t < n; t += nl) {
             const int h = t / per;
             const int j = (t - h * per) << 2;
             float *b = v + h * head;
@@ -178,7 +179,7 @@ __device__ void rope_half_row(float *v, int nh, int head, int half, const float 
         }
     } else {
         const int n = nh * half;
-        for (int t = lane; t < n; t += 32) {
+        for (int t = lane; t < n; t += nl) {
             const int h = t / half, j = t - h * half;
             float *b = v + h * head;
             const float lo = b[j], hi = b[j + half], c = ct[j], s = st[j];
@@ -191,10 +192,10 @@ __device__ void rope_half_row(float *v, int nh, int head, int half, const float 
 // reference.rs:220-237 adjacent-pair RoPE over `npairs` pairs of one row;
 // pair i uses the frequency of head_dim = (2*i) % head.
 __device__ void rope_pair_row(float *v, int npairs, int head, const float *__restrict__ ct,
-                              const float *__restrict__ st, bool vec, int lane) {
+                              const float *__restrict__ st, bool vec, int lane, int nl = 32) {
     if (vec) {  // two pairs per float4; head % 4 == 0 keeps them in one head
         const int n = npairs >> 1;
-        for (int t = lane; t < n; t += 32) {
+        for (int t = lane; t < n; t += nl) {
             const int i = t << 2;
             const int j = (i % head) >> 1;
             float4 x = *reinterpret_cast<float4 *>(v + i);
@@ -208,7 +209,7 @@ __device__ void rope_pair_row(float *v, int npairs, int head, const float *__res
             *reinterpret_cast<float4 *>(v + i) = x;
         }
     } else {
-        for (int p = lane; p < npairs; p += 32) {
+        for (int p = lane; p < npairs; p += nl) {
             const int i = 2 * p;
             const int j = (i % head) >> 1;
             const float x0 = v[i], x1 = v[i + 1], c = ct[j], s = st[j];
@@ -1780,6 +1781,57 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
         for (int g = max(0, issued - NS); g < issued; ++g) mbar_wait_bounded(&bars[g % NS], (uint32_t)(g / NS) & 1u);
 }
 
+// The norm stage for a few f32 rows (decode): a CTA per row stages the row
+// (x + resid with PRE_ADD, written back as x) in shared memory with all its
+// loads in flight at once, one thread runs the row's squares left to right
+// (reference.rs:167-170) with sixteen values loaded ahead of their adds, and
+// the CTA writes xb = w*(scale*x).  Latency: one load round trip, the
+// dependent add chain, one store round.  dim % 4 == 0.
+template <bool PRE_ADD>
+__global__ void __launch_bounds__(256) k_norm_small(ChainArgs a) {
+    extern __shared__ __align__(16) float row_s[];
+    __shared__ float scale_s;
+    const int r = blockIdx.x, dim = a.dim, n4 = dim >> 2;
+    const float *xr = a.x_in + (size_t)r * dim;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        float4 v = *reinterpret_cast<const float4 *>(xr + 4 * i);
+        if constexpr (PRE_ADD) {
+            const float4 rr = *reinterpret_cast<const float4 *>(a.resid + (size_t)r * dim + 4 * i);
+            v = make_float4(add_rn(v.x, rr.x), add_rn(v.y, rr.y), add_rn(v.z, rr.z), add_rn(v.w, rr.w));
+            *reinterpret_cast<float4 *>(a.x_out + (size_t)r * dim + 4 * i) = v;
+        }
+        *reinterpret_cast<float4 *>(row_s + 4 * i) = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float ss = 0.0f;
+        int i = 0;
+        for (; i + 16 <= dim; i += 16) {
+            float4 t[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) t[j] = *reinterpret_cast<const float4 *>(row_s + i + 4 * j);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                ss = add_rn(ss, mul_rn(t[j].x, t[j].x));
+                ss = add_rn(ss, mul_rn(t[j].y, t[j].y));
+                ss = add_rn(ss, mul_rn(t[j].z, t[j].z));
+                ss = add_rn(ss, mul_rn(t[j].w, t[j].w));
+            }
+        }
+        for (; i < dim; ++i) ss = add_rn(ss, mul_rn(row_s[i], row_s[i]));
+        scale_s = rms_scale(ss, (float)dim, a.eps);
+    }
+    __syncthreads();
+    const float sc = scale_s;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 v = *reinterpret_cast<const float4 *>(row_s + 4 * i);
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + 4 * i));
+        *reinterpret_cast<float4 *>(a.xb + (size_t)r * dim + 4 * i) =
+            make_float4(mul_rn(w.x, mul_rn(sc, v.x)), mul_rn(w.y, mul_rn(sc, v.y)), mul_rn(w.z, mul_rn(sc, v.z)),
+                        mul_rn(w.w, mul_rn(sc, v.w)));
+    }
+}
+
 // The chain's pure streams (RoPE on Q and K, SwiGLU) over all rows: no
 // shared memory and few registers, so an SM holds many more warps than the
 // norm stage's CTAs allow.  Grid-stride over one flat index space.
@@ -1809,9 +1861,11 @@ __global__ void __launch_bounds__(kThreads) k_qk_norm(float *v, int rows, int wi
 __global__ void __launch_bounds__(kThreads) k_rope(float *q, float *k, int q_width, int kv_width,
                                                    int rows, int head, const int32_t *pos,
                                                    const float *cos_t, const float *sin_t,
-                                                   int max_pos, int interleaved, int *err) {
-    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
+                                                   int max_pos, int interleaved, int *err, int wpr) {
+    // wpr warps per row: a few rows (decode) still spread over many threads
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int row = gw / wpr;
+    const int lane = (gw - row * wpr) * 32 + (threadIdx.x & 31), nl = 32 * wpr;
     if (row >= rows) return;
     const int p = pos[row];
     if ((unsigned)p >= (unsigned)max_pos) {
@@ -1823,13 +1877,13 @@ __global__ void __launch_bounds__(kThreads) k_rope(float *q, float *k, int q_wid
     float *qr = q + (size_t)row * q_width, *kr = k + (size_t)row * kv_width;
     if (!interleaved) {
         const bool vec = ((half | q_width | kv_width) & 3) == 0;
-        rope_half_row(qr, q_width / head, head, half, ct, st, vec, lane);
-        rope_half_row(kr, kv_width / head, head, half, ct, st, vec, lane);
+        rope_half_row(qr, q_width / head, head, half, ct, st, vec, lane, nl);
+        rope_half_row(kr, kv_width / head, head, half, ct, st, vec, lane, nl);
     } else {
         const bool vec = ((head | q_width | kv_width) & 3) == 0;
         const int kp = k_pairs_interleaved(q_width, kv_width);
-        rope_pair_row(qr, q_width / 2, head, ct, st, vec && (q_width / 2) % 2 == 0, lane);
-        rope_pair_row(kr, kp, head, ct, st, vec && kp % 2 == 0, lane);
+        rope_pair_row(qr, q_width / 2, head, ct, st, vec && (q_width / 2) % 2 == 0, lane, nl);
+        rope_pair_row(kr, kp, head, ct, st, vec && kp % 2 == 0, lane, nl);
     }
 }
 
@@ -2436,6 +2490,20 @@ cudaError_t launch_norm_pipe(const ChainArgs &a, cudaStream_t s) {
 // false (nothing launched) where it does not apply.
 inline bool al16(const void *p) { return ((uintptr_t)p & 15u) == 0; }
 
+// A CTA per row for a few contiguous f32 rows (fewer than half the SMs):
+// shorter than any pipeline's fill.  rms_norm (xb only) or, with PRE_ADD, the
+// add_in_place -> rms_norm pair; 16-byte aligned rows that fit in 48 KB.
+template <bool PRE_ADD>
+bool try_norm_small(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
+    if (a.rows <= 0 || a.rows * 2 > device_sms() || a.dim <= 0 || a.dim % 4 || a.dim > 12288) return false;
+    if (!a.xb || (!PRE_ADD && a.x_out) || (PRE_ADD && (!a.resid || !a.x_out)) || a.w_final) return false;
+    if (!al16(a.x_in) || !al16(a.xb) || !al16(a.w_att) || (PRE_ADD && (!al16(a.resid) || !al16(a.x_out))))
+        return false;
+    k_norm_small<PRE_ADD><<<(unsigned)a.rows, 256, (size_t)a.dim * sizeof(float), s>>>(a);
+    *err = launched();
+    return true;
+}
+
 template <int SRC, bool PRE_ADD, bool FQ>
 bool try_norm_tiled(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
     const int esz = SRC == SRC_BF16 ? 2 : (SRC == SRC_Q8 ? 1 : 4);
@@ -2571,9 +2639,11 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
         if (!try_norm_rows<SRC, true>(a, s, &e)) e = launch_norm_pipe<SRC, true, false, true>(a, s);
     } else if (a.xb || a.x_out) {
         mark(hook, STAGE_NORM);
-        // f32 x rows: the column-tiled pipeline keeps more rows' sums in flight
-        const bool done = vec && (SRC == SRC_X ? try_norm_tiled<SRC, false, false>(a, s, &e)
-                                               : try_norm_rows<SRC, false>(a, s, &e));
+        // f32 x rows: a CTA per row for a few, else the column-tiled pipeline
+        // keeps more rows' sums in flight
+        const bool done =
+            vec && (SRC == SRC_X ? (try_norm_small<false>(a, s, &e) || try_norm_tiled<SRC, false, false>(a, s, &e))
+                                 : try_norm_rows<SRC, false>(a, s, &e));
         if (!done) e = vec ? launch_norm_pipe<SRC, true>(a, s) : launch_norm_pipe<SRC, false>(a, s);
     }
     if (e != cudaSuccess) return e;
@@ -2671,8 +2741,11 @@ cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows,
                         const int32_t *pos, const float *cos_t, const float *sin_t, int max_pos,
                         int interleaved, int *err, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
-    k_rope<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(
-        q, k, q_width, kv_width, rows, head, pos, cos_t, sin_t, max_pos, interleaved, err);
+    // up to 8 warps per row while the rows alone would not fill the SMs
+    int wpr = 1;
+    while (wpr < 8 && (long)rows * 32 * wpr * 2 <= (long)device_sms() * kThreads) wpr *= 2;
+    k_rope<<<grid_for((size_t)rows * 32 * wpr, kThreads), kThreads, 0, s>>>(
+        q, k, q_width, kv_width, rows, head, pos, cos_t, sin_t, max_pos, interleaved, err, wpr);
     return launched();
 }
 
@@ -2680,7 +2753,7 @@ cudaError_t launch_add_rms_norm(const ChainArgs &a, cudaStream_t s) {
     if (a.rows <= 0) return cudaSuccess;
     if (a.dim % 8 != 0) return cudaErrorInvalidValue;
     cudaError_t e = cudaSuccess;
-    if (try_norm_tiled<SRC_X, true, false>(a, s, &e)) return e;
+    if (try_norm_small<true>(a, s, &e) || try_norm_tiled<SRC_X, true, false>(a, s, &e)) return e;
     return launch_norm_pipe<SRC_X, true, true, false>(a, s);
 }
 
