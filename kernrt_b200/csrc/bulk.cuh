@@ -24,6 +24,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                  : "memory");
 }
 
+// One plain arrival (a consumer handing a stage back to its producer).
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // Global -> shared bulk copy (no tensor map, no multicast); 16-byte aligned
 // addresses, size a multiple of 16.  Completion is counted on `bar`.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

@@ -161,16 +161,19 @@ __global__ void __launch_bounds__(256) k_project_scalar(const void *__restrict__
     y[i] = sum;
 }
 
-// Decode projections (R <= 4 rows): one warp per 32 outputs, lane o running
-// output o's dots for the R rows.  The warp's 32 weight rows and the R x rows
-// stream through three shared-memory stages of CK columns, one bulk copy per
-// row per stage (lane o copies row o), two stages ahead of the sums, so the
-// weight bytes arrive while the lanes run their sequential accumulations.
+// Decode projections (R <= 4 rows): one consumer warp per 32 outputs, lane o
+// running output o's dots for the R rows, and one producer warp that streams
+// the 32 weight rows and the R x rows through kGemvStages shared-memory stages
+// of CK columns, one bulk copy per row per stage (producer lane o copies row
+// o).  The copy engine takes the 32 requests of a stage one after another
+// (about a microsecond per stage); with its own warp issuing them that time
+// overlaps the consumer's sequential accumulations instead of adding to them.
+// full[s] counts a stage's bytes in, empty[s] hands it back to the producer.
 // Row slots are padded to an odd number of 16-byte units: the lanes' 16-byte
 // reads of one column land in distinct banks.  Requires in_dim % 8 (% 128
 // for Q8_0, whose block scales then move in 16-byte units too).
 constexpr int kGemvCK = 512;
-constexpr int kGemvStages = 3;
+constexpr int kGemvStages = 2;
 
 template <int SRC>
 struct GemvGeom {
@@ -193,111 +196,127 @@ struct GemvSet {
     int n;
 };
 
+// a[m] for a kernel-parameter array with constant indices only (a runtime
+// index would copy the whole parameter struct to local memory)
+template <class T>
+__device__ __forceinline__ T pick3(const T (&a)[3], int m) {
+    return m == 0 ? a[0] : (m == 1 ? a[1] : a[2]);
+}
+
 template <int SRC, int R>
-__global__ void __launch_bounds__(32) k_gemv(GemvSet set, int in_dim, const float *__restrict__ x, int *err) {
+__global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const float *__restrict__ x, int *err) {
     using Geo = GemvGeom<SRC>;
+    constexpr int NS = kGemvStages;
     constexpr int SB = Geo::template stage_bytes<R>();
     extern __shared__ __align__(16) unsigned char gsm[];
-    __shared__ __align__(8) uint64_t bar[kGemvStages];
+    __shared__ __align__(8) uint64_t full[NS], empty[NS];
+    __shared__ int issued_sh;
     int m = 0;
-    while (m + 1 < set.n && (int)blockIdx.x >= set.cta_end[m]) ++m;
-    const int blk = (int)blockIdx.x - (m ? set.cta_end[m - 1] : 0);
-    const void *__restrict__ w = set.w[m];
-    const float *__restrict__ wsc = set.wsc[m];
-    float *__restrict__ y = set.y[m];
-    const int out_dim = set.out_dim[m];
-    const int lane = threadIdx.x, o = blk * 32 + lane;
+    if (set.n > 1 && (int)blockIdx.x >= set.cta_end[0]) m = (set.n > 2 && (int)blockIdx.x >= set.cta_end[1]) ? 2 : 1;
+    const int blk = (int)blockIdx.x - (m == 0 ? 0 : (m == 1 ? set.cta_end[0] : set.cta_end[1]));
+    const int out_dim = pick3(set.out_dim, m);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, o = blk * 32 + lane;
     const bool live = o < out_dim;
     const int nlive = min(32, out_dim - blk * 32);
     const int nchunks = (in_dim + kGemvCK - 1) / kGemvCK;
-    if (lane == 0) {
-        for (int i = 0; i < kGemvStages; ++i) mbar_init(&bar[i], 1);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
         mbar_fence_init();
     }
-    __syncwarp();
-    auto stage = [&](int c) { return gsm + (size_t)(c % kGemvStages) * SB; };
-    auto issue = [&](int c) {
-        const int k0 = c * kGemvCK, tc = min(kGemvCK, in_dim - k0);
-        const uint32_t wb = (uint32_t)(tc * Geo::esz), sb = SRC == SRC_Q8 ? (uint32_t)(tc / 8) : 0u;
-        const uint32_t total = (uint32_t)nlive * (wb + sb) + (uint32_t)(R * tc * 4);
-        uint64_t *b = &bar[c % kGemvStages];
-        if (lane == 0) mbar_arrive_expect_tx(b, total);
-        __syncwarp();
-        unsigned char *st = stage(c);
-        if (live) {
-            bulk_load(st + (size_t)lane * Geo::wstride,
-                      static_cast<const unsigned char *>(w) + ((size_t)o * in_dim + k0) * Geo::esz, wb, b);
-            if constexpr (SRC == SRC_Q8)
-                bulk_load(st + (size_t)lane * Geo::wstride + kGemvCK, wsc + (size_t)o * (in_dim >> 5) + (k0 >> 5), sb, b);
-        }
-        if (lane < R) bulk_load(st + 32 * Geo::wstride + (size_t)lane * kGemvCK * 4, x + (size_t)lane * in_dim + k0,
-                                (uint32_t)(tc * 4), b);
-    };
-    int issued = 0;  // warp-uniform count of chunks issued
-    while (issued < min(nchunks, kGemvStages - 1)) issue(issued++);
-    float acc[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+    __syncthreads();
     bool ok = true;
-    for (int c = 0; c < nchunks; ++c) {
-        if (!__all_sync(kFullMask, mbar_wait_bounded(&bar[c % kGemvStages], (uint32_t)(c / kGemvStages) & 1u))) {
-            if (lane == 0) atomicOr(err, ERR_TIMEOUT);
-            ok = false;
-            break;
+    int consumed = 0;
+    if (warp == 1) {
+        // producer: chunk c into stage c % NS once chunk c - NS has been consumed
+        const void *__restrict__ w = pick3(set.w, m);
+        const float *__restrict__ wsc = pick3(set.wsc, m);
+        int issued = 0;
+        for (; issued < nchunks; ++issued) {
+            const int c = issued, k0 = c * kGemvCK, tc = min(kGemvCK, in_dim - k0);
+            if (c >= NS && !__all_sync(kFullMask, mbar_wait_bounded(&empty[c % NS], (uint32_t)(c / NS - 1) & 1u)))
+                break;  // the consumer stopped: issue nothing more
+            const uint32_t wb = (uint32_t)(tc * Geo::esz), sb = SRC == SRC_Q8 ? (uint32_t)(tc / 8) : 0u;
+            uint64_t *b = &full[c % NS];
+            if (lane == 0) mbar_arrive_expect_tx(b, (uint32_t)nlive * (wb + sb) + (uint32_t)(R * tc * 4));
+            __syncwarp();
+            unsigned char *st = gsm + (size_t)(c % NS) * SB;
+            if (live) {
+                bulk_load(st + (size_t)lane * Geo::wstride,
+                          static_cast<const unsigned char *>(w) + ((size_t)o * in_dim + k0) * Geo::esz, wb, b);
+                if constexpr (SRC == SRC_Q8)
+                    bulk_load(st + (size_t)lane * Geo::wstride + kGemvCK, wsc + (size_t)o * (in_dim >> 5) + (k0 >> 5),
+                              sb, b);
+            }
+            if (lane < R)
+                bulk_load(st + 32 * Geo::wstride + (size_t)lane * kGemvCK * 4, x + (size_t)lane * in_dim + k0,
+                          (uint32_t)(tc * 4), b);
         }
-        // the stage that chunk c - 1 used is free: chunk c + 2 goes there
-        if (issued < nchunks) issue(issued++);
-        const unsigned char *st = stage(c);
-        const unsigned char *wr = st + (size_t)lane * Geo::wstride;
-        const float *xs = reinterpret_cast<const float *>(st + 32 * Geo::wstride);
-        const int tc = min(kGemvCK, in_dim - c * kGemvCK);
-        if (live) {
+        if (lane == 0) issued_sh = issued;
+    } else {
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+        for (int c = 0; c < nchunks; ++c) {
+            if (!__all_sync(kFullMask, mbar_wait_bounded(&full[c % NS], (uint32_t)(c / NS) & 1u))) {
+                if (lane == 0) atomicOr(err, ERR_TIMEOUT);
+                ok = false;
+                break;
+            }
+            const unsigned char *st = gsm + (size_t)(c % NS) * SB;
+            const unsigned char *wr = st + (size_t)lane * Geo::wstride;
+            const float *xs = reinterpret_cast<const float *>(st + 32 * Geo::wstride);
+            const int tc = min(kGemvCK, in_dim - c * kGemvCK);
+            if (live) {
 #pragma unroll 2
-            for (int k = 0; k < tc; k += 8) {
-                float wv[8];
-                if constexpr (SRC == SRC_BF16) {
-                    const uint4 t = *reinterpret_cast<const uint4 *>(wr + 2 * k);
-                    const uint32_t p[4] = {t.x, t.y, t.z, t.w};
+                for (int k = 0; k < tc; k += 8) {
+                    float wv[8];
+                    if constexpr (SRC == SRC_BF16) {
+                        const uint4 t = *reinterpret_cast<const uint4 *>(wr + 2 * k);
+                        const uint32_t p[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        wv[2 * e] = bf16f(p[e] & 0xffffu);
-                        wv[2 * e + 1] = bf16f(p[e] >> 16);
+                        for (int e = 0; e < 4; ++e) {
+                            wv[2 * e] = __uint_as_float(p[e] << 16);
+                            wv[2 * e + 1] = __uint_as_float(p[e] & 0xffff0000u);
+                        }
+                    } else if constexpr (SRC == SRC_Q8) {
+                        const uint2 t = *reinterpret_cast<const uint2 *>(wr + k);
+                        const float sc = reinterpret_cast<const float *>(wr + kGemvCK)[k >> 5];
+                        const uint32_t p[2] = {t.x, t.y};
+#pragma unroll
+                        for (int e = 0; e < 8; ++e)
+                            wv[e] = mul_rn((float)(int8_t)((p[e >> 2] >> (8 * (e & 3))) & 0xffu), sc);
+                    } else {
+                        const float4 a = *reinterpret_cast<const float4 *>(wr + 4 * k);
+                        const float4 b2 = *reinterpret_cast<const float4 *>(wr + 4 * k + 16);
+                        wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
+                        wv[4] = b2.x; wv[5] = b2.y; wv[6] = b2.z; wv[7] = b2.w;
                     }
-                } else if constexpr (SRC == SRC_Q8) {
-                    const uint2 t = *reinterpret_cast<const uint2 *>(wr + k);
-                    const float sc = reinterpret_cast<const float *>(wr + kGemvCK)[k >> 5];
-                    const uint32_t p[2] = {t.x, t.y};
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) wv[e] = mul_rn((float)(int8_t)((p[e >> 2] >> (8 * (e & 3))) & 0xffu), sc);
-                } else {
-                    const float4 a = *reinterpret_cast<const float4 *>(wr + 4 * k);
-                    const float4 b2 = *reinterpret_cast<const float4 *>(wr + 4 * k + 16);
-                    wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
-                    wv[4] = b2.x; wv[5] = b2.y; wv[6] = b2.z; wv[7] = b2.w;
-                }
+                    for (int r = 0; r < R; ++r) {
+                        const float4 x0 = *reinterpret_cast<const float4 *>(xs + r * kGemvCK + k);
+                        const float4 x1 = *reinterpret_cast<const float4 *>(xs + r * kGemvCK + k + 4);
+                        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const float4 x0 = *reinterpret_cast<const float4 *>(xs + r * kGemvCK + k);
-                    const float4 x1 = *reinterpret_cast<const float4 *>(xs + r * kGemvCK + k + 4);
-                    const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[r] = add_rn(acc[r], mul_rn(wv[e], xv[e]));
+                        for (int e = 0; e < 8; ++e) acc[r] = add_rn(acc[r], mul_rn(wv[e], xv[e]));
+                    }
                 }
             }
+            // every lane's reads of this stage are done before it goes back
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[c % NS]);
+            consumed = c + 1;
         }
-        // every lane's reads of this stage are done before it is refilled
-        __syncwarp();
-    }
-    if (!ok) {
-        // copies still in flight: wait for them (bounded) before the memory goes
-        if (lane == 0)
-            for (int c = max(0, issued - kGemvStages); c < issued; ++c)
-                mbar_wait_bounded(&bar[c % kGemvStages], (uint32_t)(c / kGemvStages) & 1u);
-        return;
-    }
-    if (live)
+        if (ok && live)
 #pragma unroll
-        for (int r = 0; r < R; ++r) y[(size_t)r * out_dim + o] = acc[r];
+            for (int r = 0; r < R; ++r) pick3(set.y, m)[(size_t)r * out_dim + o] = acc[r];
+    }
+    __syncthreads();
+    if (!ok && threadIdx.x == 0)
+        // copies still in flight: wait for them (bounded) before the memory goes
+        for (int c = consumed; c < issued_sh; ++c) mbar_wait_bounded(&full[c % NS], (uint32_t)(c / NS) & 1u);
 }
 
 template <int SRC, int R>
@@ -305,7 +324,7 @@ cudaError_t launch_gemv(const GemvSet &set, int in_dim, const float *x, int *err
     const size_t smem = (size_t)kGemvStages * GemvGeom<SRC>::template stage_bytes<R>();
     cudaError_t e = cudaFuncSetAttribute(k_gemv<SRC, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    k_gemv<SRC, R><<<(unsigned)set.cta_end[set.n - 1], 32, smem, s>>>(set, in_dim, x, err);
+    k_gemv<SRC, R><<<(unsigned)set.cta_end[set.n - 1], 64, smem, s>>>(set, in_dim, x, err);
     return launched();
 }
 
@@ -321,8 +340,10 @@ cudaError_t gemv_rows(const GemvSet &set, int in_dim, const float *x, int rows, 
 
 template <int SRC>
 bool gemv_fits(const void *w, const float *wsc, int in_dim, const float *x, int rows) {
-    return rows <= 4 && in_dim % (SRC == SRC_Q8 ? 128 : 8) == 0 && ((uintptr_t)x & 15) == 0 &&
-           ((uintptr_t)w & 15) == 0 && (SRC != SRC_Q8 || ((uintptr_t)wsc & 15) == 0);
+    // the stages plus a little static shared memory within the 227 KB opt-in limit
+    const size_t smem = (size_t)kGemvStages * (32 * GemvGeom<SRC>::wstride + (size_t)rows * kGemvCK * 4);
+    return rows <= 4 && smem + 256 <= 232448 && in_dim % (SRC == SRC_Q8 ? 128 : 8) == 0 &&
+           ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 && (SRC != SRC_Q8 || ((uintptr_t)wsc & 15) == 0);
 }
 
 template <int SRC>

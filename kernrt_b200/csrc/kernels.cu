@@ -2636,7 +2636,10 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
     cudaError_t e = cudaSuccess;
     if (fq_pipe) {
         mark(hook, STAGE_NORM);
-        if (!try_norm_rows<SRC, true>(a, s, &e)) e = launch_norm_pipe<SRC, true, false, true>(a, s);
+        // f32 x rows: the column-tiled pipeline (32 rows' sums in flight);
+        // whole staged rows of f32 leave room for fewer
+        const bool done = (SRC == SRC_X && try_norm_tiled<SRC, false, true>(a, s, &e)) || try_norm_rows<SRC, true>(a, s, &e);
+        if (!done) e = launch_norm_pipe<SRC, true, false, true>(a, s);
     } else if (a.xb || a.x_out) {
         mark(hook, STAGE_NORM);
         // f32 x rows: a CTA per row for a few, else the column-tiled pipeline

@@ -202,7 +202,7 @@ def run(reps: int, only: str | None = None):
     if B.want("conv_decode"):
         xr, kern, st = B.buf(d), B.buf(d * 3), B.buf(2 * d)
         B.time("conv_decode 1x1536 (latency)", lambda: b.conv_decode(xr, xr, kern, st, d, 3), None)
-    if B.want("q8_0"):
+    if B.want("quantize_q8_0", "rms_norm_q8_0"):
         qd8 = 1024
         xq = B.buf(R * qd8)
         nb = qd8 // 32
@@ -321,6 +321,24 @@ def contractions(B):
                    note="bound by each output's 2048-long add chain" if rows == 1 else "")
         if r is not None and rows > 1:
             r["note"] = f"{macs / (r['ms'] / 1e3) / 1e12:.2f} T MAC/s = {macs / (r['ms'] / 1e3) / EXACT_MAC_PEAK:.2f} of the exact-order FP32 ceiling"
+    # the decode projections of one SmolLM2-1.7B layer (fused q/k/v and gate/up)
+    wk = W.SMOLLM2_17B_DECODE
+
+    def bf16_mat(o, i):
+        m = (rng.standard_normal((o, i), dtype=np.float32) * np.float32(0.02)).view(np.uint32) >> 16
+        return b.prepare_matrix(BF16, m.astype(np.uint16), None, o, i)
+
+    mqkv = [bf16_mat(wk.q_dim, H), bf16_mat(wk.kv_dim, H), bf16_mat(wk.kv_dim, H)]
+    mgu = [bf16_mat(wk.hidden, H), bf16_mat(wk.hidden, H)]
+    mdown = bf16_mat(H, wk.hidden)
+    xd = B.buf(wk.hidden)
+    yq, yk, yv, yg, yu, yd = (b.alloc(n) for n in (wk.q_dim, wk.kv_dim, wk.kv_dim, wk.hidden, wk.hidden, H))
+    B.time("project_qkv decode (3 x 2048x2048 bf16)", lambda: b.project_qkv(*mqkv, xd, yq, yk, yv, 1),
+           3 * H * H * 2, note="one launch; chains of 2048")
+    B.time("project_gate_up decode (2 x 8192x2048 bf16)", lambda: b.project_gate_up(*mgu, xd, yg, yu, 1),
+           2 * wk.hidden * H * 2, note="one launch; chains of 2048")
+    B.time("project down decode (2048x8192 bf16)", lambda: b.project(mdown, xd, yd, 1), H * wk.hidden * 2,
+           note="chains of 8192")
     codes = rng.integers(-127, 128, size=(3072, 1024), dtype=np.int8)
     sc = rng.uniform(1e-4, 1e-2, size=(3072, 32)).astype(np.float32)
     mg = b.prepare_matrix(Q8_0, codes, sc, 3072, 1024)
