@@ -237,9 +237,9 @@ int kernrt_cuda_layer_chain_host(kernrt_cuda_ctx *ctx, const kernrt_chain_host_a
  * (kernrt_cuda_rms_norm, _rms_norm_q8_0, _layer_chain) records a CUDA event
  * around each kernel it issues.  kernrt_cuda_stage_times completes pending
  * work and returns, per stage, the device milliseconds and launch count since
- * timing was enabled: [0] the norm stage (k_norm_rows for gathered or
- * quantised rows, k_norm_tiled for f32 rows, k_norm_pipe for widths the bulk
- * copies cannot take), [1] the RoPE/SwiGLU stream (k_stream), [2] the single
+ * timing was enabled: [0] the norm stage (k_norm_rows for gathered rows,
+ * k_norm_cols for f32 rows, k_norm_small for a few f32 rows, k_norm_pipe for
+ * widths the bulk copies cannot take), [1] the RoPE/SwiGLU stream (k_stream), [2] the single
  * fused kernel (k_chain).  Enabling clears the record. */
 int kernrt_cuda_stage_timing(kernrt_cuda_ctx *ctx, int enable);
 int kernrt_cuda_stage_times(kernrt_cuda_ctx *ctx, double ms[3], uint64_t launches[3]);

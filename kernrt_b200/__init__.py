@@ -360,7 +360,7 @@ class CudaBackend:
             setattr(a, name, v)
         _ok(self._lib.kernrt_cuda_layer_chain_host(self._ctx, C.byref(a)))
 
-    # the norm stage is k_norm_rows, k_norm_tiled or k_norm_pipe by source and width
+    # the norm stage is k_norm_rows, k_norm_cols, k_norm_small or k_norm_pipe by source, rows and width
     STAGES = ("norm", "stream", "fused")
 
     def stage_timing(self, enable: bool) -> None:

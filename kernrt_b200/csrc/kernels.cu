@@ -1136,364 +1136,313 @@ __global__ void __launch_bounds__(kPipeThreads, 1) k_norm_pipe(ChainArgs a, Chai
     }
 }
 
-struct TiledLayout {
-    int G;          // rows per group (<= 32: one summing lane per row)
-    int TC;         // columns per tile; the last tile may be shorter
-    int T;          // tiles per row
-    int xstride;    // bytes per staged row tile (+ Q8 block scales), an odd multiple of 16
-    int srstride;   // bytes per f32 residual row tile in a sum slot, or 0
-    int wrstride;   // bytes per f32 residual row tile in a write slot, or 0
-    int sslot;      // bytes per sum slot: G * (xstride + srstride)
-    int wslot;      // bytes per write slot: G * (xstride + wrstride)
+constexpr int kTiledThreads = 512;  // 16 warps
+constexpr int kTiledWriters = 12;   // warps off the summing warp's sub-partition
+
+// f32 x rows with the three roles decoupled: one 16-warp CTA per SM, its
+// rows in groups of G, a group's rows cut into T column tiles of TC columns
+// (a unit = one tile of one group).
+//   warp 4    issues unit u's bulk copies (lane r: row r's x tile, and its
+//             resid tile where the sums need it) into slot u % S of a ring
+//             of S slots once the summing warp has handed that slot back;
+//   warp 0    sums unit after unit, lane r row r left to right (the
+//             reference's order, reference.rs:167-170) carried across tiles
+//             in a register, hands each slot back, and after a group's last
+//             tile stores its scales into one of two buffers;
+//   writers   (the warps off warp 0's sub-partition) take group after group
+//             once its scales are stored and write xb, x (+ resid) or the
+//             Q8_0 codes from x (and resid) loaded from L2, where the ring's
+//             copies left them a group earlier: eight 16-byte loads in flight
+//             per lane, no barrier between tiles.
+// mbarriers connect the roles (full/empty per slot, ready/freed per scale
+// buffer), so each runs at its own rate: the summing lanes' chains, the copy
+// engine and the writers' L2 traffic overlap instead of meeting at a CTA
+// barrier per tile.  The other warps of warp 0's sub-partition only wait at
+// the end.
+// PRE_ADD: the sums are of x + resid (the driver's add_in_place -> rms_norm,
+// llama.rs:762-765) and the writers store x = x + resid and xb.  FQ: a second
+// sum of x (+ resid) for the final norm, and the writers quantise it to Q8_0
+// (quant.rs:856-874).
+constexpr int kColsSlots = 4;
+// The quantising form runs 24 warps (18 writers, at most 85 registers
+// each, four items per batch): its writers' dependent block arithmetic needs
+// more warps to hide than the plain forms' loads and stores, which run 16
+// warps (12 writers, eight items per batch).
+template <bool FQ>
+struct ColsShape {
+    static constexpr int threads = FQ ? 768 : 512;
+    static constexpr int writers = threads / 32 * 3 / 4;  // the warps off sub-partition 0
+    static constexpr int U = FQ ? 4 : 8;                  // items per writer lane and batch
+};
+constexpr unsigned kColsSleepNs = 128;  // poll interval of the issuer's and the writers' waits
+
+struct ColsLayout {
+    int G;       // rows per group (<= 32: one summing lane per row)
+    int TC;      // columns per tile; the last tile may be shorter
+    int T;       // tiles per row
+    int stride;  // bytes per staged row: x tile (+ resid tile), an odd multiple of 16
+    int rofs;    // byte offset of the resid tile in a staged row
+    int slot;    // G * stride
     size_t smem;
 };
 
-constexpr int kTiledThreads = 512;  // 16 warps
-constexpr int kTiledSlots = 3;      // per ring: staging two units ahead
-constexpr int kTiledWriters = 12;   // warps off the summing warp's sub-partition
-constexpr bool kTiledBulk = true;  // stage with bulk copies (else 16-byte cp.async)
-
-// The norm stage as a column-tiled pipeline fed by bulk copies, one CTA per
-// SM.  A CTA's rows come in groups of G; a group's rows are cut into T column
-// tiles, and a unit is one tile of one group.  Two rings of three slots, each
-// slot with an mbarrier that counts its copies' bytes:
-//   sum ring    unit u's tiles of x (and of resid where the sums need it);
-//   write ring  the same tiles again, one group later, for the writers (and
-//               resid where the outputs need it); the x tiles then come from
-//               L2, where the sum ring's copies left them.
-// In iteration u:
-//   warp 4    issues the copies of sum unit u+2 and of write unit u+2-T,
-//             lane r those of row r, after lane 0 announced the bytes;
-//   warp 0    waits for sum unit u and continues its rows' sums over the tile,
-//             lane r for row r, left to right: the reference's order
-//             (reference.rs:167-170), carried across tiles in a register;
-//             after the last tile it stores the group's scales;
-//   writers   (12 warps on the other three sub-partitions) wait for write
-//             unit u-T, tile t of the previous group, whose scales are known,
-//             and write xb, x (+ resid), or the Q8_0 codes from shared memory.
-// Warps 8 and 12 only keep the barrier count, so the summing warp shares its
-// sub-partition with the copy issuer alone.  Every global read is a bulk
-// copy; the writers' only global traffic is their stores.
-//
-// PRE_ADD: the sums are of x + resid (the driver's add_in_place -> rms_norm,
-// llama.rs:762-765), and the writers store x = x + resid and xb.  FQ: a
-// second sum of x (+ resid) for the final norm, and the writers quantise it
-// to Q8_0 (quant.rs:856-874).
-template <int SRC, bool PRE_ADD, bool FQ>
-__global__ void __launch_bounds__(kTiledThreads, 1) k_norm_tiled(ChainArgs a, TiledLayout L) {
-    static_assert(!PRE_ADD || SRC == SRC_X, "the pre-add form reads f32 x");
+template <bool PRE_ADD, bool FQ>
+__global__ void __launch_bounds__(ColsShape<FQ>::threads, 1) k_norm_cols(ChainArgs a, ColsLayout L) {
     extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int NS = kColsSlots;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int dim = a.dim, G = L.G, T = L.T, TC = L.TC;
     const int ngroups = (a.rows + G - 1) / G;
     const int nmine = (int)blockIdx.x < ngroups ? (ngroups - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
     const int units = nmine * T;
-    unsigned char *sring = smem;
-    unsigned char *wring = smem + kTiledSlots * (size_t)L.sslot;
-    float *scales = reinterpret_cast<float *>(wring + kTiledSlots * (size_t)L.wslot);  // [2][64]
-    uint64_t *sbar = reinterpret_cast<uint64_t *>(scales + 128);                       // [kTiledSlots]
-    uint64_t *wbar = sbar + kTiledSlots;                                               // [kTiledSlots]
-    __shared__ int s_abort;
+    float *scales = reinterpret_cast<float *>(smem + NS * (size_t)L.slot);  // [2][64]
+    uint64_t *full = reinterpret_cast<uint64_t *>(scales + 128);            // [NS] a slot's bytes landed
+    uint64_t *empty = full + NS;                                            // [NS] a slot summed
+    uint64_t *ready = empty + NS;                                           // [2] a group's scales stored
+    uint64_t *freed = ready + 2;                                            // [2] a group written
+    __shared__ volatile int s_abort;
+    __shared__ int s_issued, s_consumed;
     const bool has_resid = a.resid != nullptr;
     const bool sum_resid = PRE_ADD || (FQ && has_resid);
     const bool write_resid = has_resid && (PRE_ADD || FQ || a.x_out);
-
     auto first_row = [&](int g) { return (int)(blockIdx.x + (unsigned)g * gridDim.x) * G; };
 
     if (tid == 0) {
         s_abort = 0;
-        for (int i = 0; i < 2 * kTiledSlots; ++i) mbar_init(&sbar[i], kTiledBulk ? 1 : 32);
+        s_issued = s_consumed = 0;
+        for (int i = 0; i < NS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&ready[i], 1);
+            mbar_init(&freed[i], ColsShape<FQ>::writers);
+        }
         mbar_fence_init();
     }
     __syncthreads();
 
-    // Copies of unit u into a slot of one ring, by warp 4 (lane r: row r).
-    auto issue = [&](int u, unsigned char *slot, uint64_t *bar, int rstride, bool resid) {
-        const int g = u / T, t = u - g * T;
-        const int r0 = first_row(g), gr = min(G, a.rows - r0);
-        const int c0 = t * TC, tc = min(TC, dim - c0);
-        const uint32_t xbytes = (uint32_t)src_row_bytes<SRC>(tc), sbytes = SRC == SRC_Q8 ? (uint32_t)(tc / 8) : 0u;
-        const uint32_t rbytes = resid ? (uint32_t)tc * 4u : 0u;
-        const unsigned char *sp = nullptr;
-        int tok = 0;
-        uint32_t mine = 0;
-        if (lane < gr) {
-            if constexpr (SRC == SRC_X) {
-                sp = reinterpret_cast<const unsigned char *>(a.x_in + (size_t)(r0 + lane) * dim + c0);
-            } else {
-                tok = a.tokens[r0 + lane];
-                if ((unsigned)tok < (unsigned)a.vocab)
-                    sp = static_cast<const unsigned char *>(a.table) +
-                         (size_t)tok * (size_t)src_row_bytes<SRC>(dim) + src_row_bytes<SRC>(c0);
-                else if (t == 0)
-                    set_err(a.err, ERR_TOKEN);
+    // A bounded wait that also gives up once another role has given up; the
+    // warp agrees on the outcome.  Roles whose waits are not on the critical
+    // path (the copy issuer shares warp 0's sub-partition) sleep between
+    // polls, leaving the issue slots to the warps that work.
+    auto wait = [&](uint64_t *bar, uint32_t parity, unsigned sleep_ns) {
+        bool ok = mbar_try_wait(bar, parity);
+        if (!ok) {
+            const long long t0 = clock64();
+            while (!(ok = mbar_try_wait(bar, parity))) {
+                if (sleep_ns) __nanosleep(sleep_ns);
+                if (s_abort) break;
+                if (clock64() - t0 > (1ll << 31)) {
+                    set_err(a.err, ERR_TIMEOUT);
+                    s_abort = 1;
+                    break;
+                }
             }
-            mine = (sp ? xbytes + sbytes : 0u) + rbytes;
         }
-        if constexpr (kTiledBulk) {
-            uint32_t total = mine;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFull, total, o);
-            if (lane == 0) mbar_arrive_expect_tx(bar, total);
+        return __all_sync(kFull, ok);
+    };
+
+    if (warp == 4) {
+        // the writers read these rows again a group later: keep them in L2
+        const uint64_t keep = l2_evict_last();
+        int u = 0;
+        for (; u < units; ++u) {
+            if (u >= NS && !wait(&empty[u % NS], (uint32_t)(u / NS - 1) & 1u, kColsSleepNs)) break;
+            const int g = u / T, t = u - g * T;
+            const int r0 = first_row(g), gr = min(G, a.rows - r0);
+            const int c0 = t * TC, tc = min(TC, dim - c0);
+            uint64_t *bar = &full[u % NS];
+            if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)gr * (uint32_t)tc * (sum_resid ? 8u : 4u));
             __syncwarp();
             if (lane < gr) {
-                unsigned char *dst = slot + (size_t)lane * L.xstride;
-                if (sp) {
-                    bulk_load(dst, sp, xbytes, bar);
-                    if constexpr (SRC == SRC_Q8)
-                        bulk_load(dst + align16(TC), a.tscales + (size_t)tok * (dim >> 5) + (c0 >> 5), sbytes, bar);
-                }
-                if (resid)
-                    bulk_load(slot + (size_t)G * L.xstride + (size_t)lane * rstride,
-                              a.resid + (size_t)(r0 + lane) * dim + c0, rbytes, bar);
-            }
-        } else {
-            // 16-byte cp.async by the whole warp, row by row; each lane's
-            // arrival on the mbarrier fires when its own copies have landed.
-            for (int r = 0; r < gr; ++r) {
-                const unsigned char *rsp = (const unsigned char *)__shfl_sync(kFull, (unsigned long long)sp, r);
-                const int rtok = __shfl_sync(kFull, tok, r);
-                unsigned char *dst = slot + (size_t)r * L.xstride;
-                if (rsp) {
-                    for (int k = lane; k < (int)(xbytes >> 4); k += 32) cp_async16(dst + 16 * k, rsp + 16 * k);
-                    if constexpr (SRC == SRC_Q8) {
-                        const float *ssp = a.tscales + (size_t)rtok * (dim >> 5) + (c0 >> 5);
-                        for (int k = lane; k < (int)(sbytes >> 4); k += 32)
-                            cp_async16(dst + align16(TC) + 16 * k, ssp + 4 * k);
-                    }
-                }
-                if (resid) {
-                    const float *rsrc = a.resid + (size_t)(r0 + r) * dim + c0;
-                    unsigned char *rdst = slot + (size_t)G * L.xstride + (size_t)r * rstride;
-                    for (int k = lane; k < (int)(rbytes >> 4); k += 32) cp_async16(rdst + 16 * k, rsrc + 4 * k);
-                }
-            }
-            asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
-        }
-    };
-    auto issue_sum = [&](int u) {
-        issue(u, sring + (size_t)(u % kTiledSlots) * L.sslot, &sbar[u % kTiledSlots], L.srstride, sum_resid);
-    };
-    auto issue_write = [&](int u) {
-        issue(u, wring + (size_t)(u % kTiledSlots) * L.wslot, &wbar[u % kTiledSlots], L.wrstride, write_resid);
-    };
-    // Waits for a slot's copies; a wait that runs out reports it, and the
-    // CTA stops waiting (its results are then not valid).
-    auto wait = [&](uint64_t *bar, int u) {
-        if (s_abort) return false;
-        if (mbar_wait_bounded(bar, (uint32_t)(u / kTiledSlots) & 1u)) return true;
-        if (lane == 0) {
-            set_err(a.err, ERR_TIMEOUT);
-            s_abort = 1;
-        }
-        return false;
-    };
-
-    float ss = 0.0f, ss2 = 0.0f;  // summing lanes: the running sums of their rows
-    auto sum = [&](int u) {
-        const int g = u / T, t = u - g * T;
-        const int r0 = first_row(g), gr = min(G, a.rows - r0);
-        const int c0 = t * TC, tc = min(TC, dim - c0);
-        const unsigned char *slot = sring + (size_t)(u % kTiledSlots) * L.sslot;
-        if (wait(&sbar[u % kTiledSlots], u) && lane < gr) {
-            bool valid = true;
-            if constexpr (SRC != SRC_X) valid = (unsigned)a.tokens[r0 + lane] < (unsigned)a.vocab;
-            const unsigned char *xr = slot + (size_t)lane * L.xstride;
-            const float *rr = reinterpret_cast<const float *>(slot + (size_t)G * L.xstride + (size_t)lane * L.srstride);
-            if (PRE_ADD) {
-#pragma unroll 2
-                for (int c = 0; c < tc; c += 8) {
-                    float v[8];
-                    decode_staged<SRC, 8>(xr, TC, c, v);
-                    const float4 p = *reinterpret_cast<const float4 *>(rr + c), q = *reinterpret_cast<const float4 *>(rr + c + 4);
-                    const float rv[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float xo = add_rn(v[e], rv[e]);
-                        ss = add_rn(ss, mul_rn(xo, xo));
-                    }
-                }
-            } else if (FQ && has_resid) {
-#pragma unroll 2
-                for (int c = 0; c < tc; c += 8) {
-                    float v[8];
-                    decode_staged<SRC, 8>(xr, TC, c, v);
-                    if (!valid)
-                        for (int e = 0; e < 8; ++e) v[e] = 0.0f;
-                    const float4 p = *reinterpret_cast<const float4 *>(rr + c), q = *reinterpret_cast<const float4 *>(rr + c + 4);
-                    const float rv[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        ss = add_rn(ss, mul_rn(v[e], v[e]));
-                        const float xo = add_rn(v[e], rv[e]);
-                        ss2 = add_rn(ss2, mul_rn(xo, xo));
-                    }
-                }
-            } else if (valid) {
-#pragma unroll 4
-                for (int c = 0; c < tc; c += 8) {
-                    float v[8];
-                    decode_staged<SRC, 8>(xr, TC, c, v);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
-                }
+                unsigned char *dst = smem + (size_t)(u % NS) * L.slot + (size_t)lane * L.stride;
+                const size_t o = (size_t)(r0 + lane) * dim + c0;
+                bulk_load_hint(dst, a.x_in + o, (uint32_t)tc * 4u, bar, keep);
+                if (sum_resid) bulk_load_hint(dst + L.rofs, a.resid + o, (uint32_t)tc * 4u, bar, keep);
             }
         }
-        if (t == T - 1) {
+        if (lane == 0) s_issued = u;
+    } else if (warp == 0) {
+        float ss = 0.0f, ss2 = 0.0f;
+        int u = 0;
+        bool ok = true;
+        for (; u < units && ok; ++u) {
+            const int g = u / T, t = u - g * T;
+            const int r0 = first_row(g), gr = min(G, a.rows - r0);
+            const int tc = min(TC, dim - t * TC);
+            if (!wait(&full[u % NS], (uint32_t)(u / NS) & 1u, 0)) break;
             if (lane < gr) {
-                float *sc = scales + (g & 1) * 64;
-                sc[lane] = rms_scale(ss, (float)dim, a.eps);
-                if (FQ) sc[32 + lane] = rms_scale(has_resid ? ss2 : ss, (float)dim, a.final_eps);
+                const unsigned char *row = smem + (size_t)(u % NS) * L.slot + (size_t)lane * L.stride;
+                const float *xr = reinterpret_cast<const float *>(row);
+                const float *rr = reinterpret_cast<const float *>(row + L.rofs);
+                // one step of eight columns loaded ahead of the step being
+                // added, so the shared-memory latency stays off the chain
+                auto ld8 = [&](const float *p, int c, float *v) {
+                    const float4 p0 = *reinterpret_cast<const float4 *>(p + c), p1 = *reinterpret_cast<const float4 *>(p + c + 4);
+                    v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+                    v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+                };
+                float v[8], rv[8] = {}, nv[8], nrv[8] = {};
+                ld8(xr, 0, v);
+                if (sum_resid) ld8(rr, 0, rv);
+#pragma unroll 2
+                for (int c = 0; c < tc; c += 8) {
+                    const int cn = c + 8 < tc ? c + 8 : c;
+                    ld8(xr, cn, nv);
+                    if (sum_resid) ld8(rr, cn, nrv);
+                    if (PRE_ADD) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const float xo = add_rn(v[e], rv[e]);
+                            ss = add_rn(ss, mul_rn(xo, xo));
+                        }
+                    } else if (FQ && has_resid) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            ss = add_rn(ss, mul_rn(v[e], v[e]));
+                            const float xo = add_rn(v[e], rv[e]);
+                            ss2 = add_rn(ss2, mul_rn(xo, xo));
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        v[e] = nv[e];
+                        rv[e] = nrv[e];
+                    }
+                }
             }
-            ss = 0.0f;
-            ss2 = 0.0f;
+            // every lane's reads of the slot are done before it goes back
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[u % NS]);
+            if (t == T - 1) {
+                // group g's scales go to buffer g % 2 once the writers are
+                // done with group g - 2
+                if (g >= 2 && !wait(&freed[g & 1], (uint32_t)((g - 2) >> 1) & 1u, 0)) ok = false;
+                if (ok) {
+                    float *sc = scales + (g & 1) * 64;
+                    if (lane < gr) {
+                        sc[lane] = rms_scale(ss, (float)dim, a.eps);
+                        if (FQ) sc[32 + lane] = rms_scale(has_resid ? ss2 : ss, (float)dim, a.final_eps);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&ready[g & 1]);
+                }
+                ss = 0.0f;
+                ss2 = 0.0f;
+            }
         }
-    };
-
-    // Write unit u (tile t of group g) from its write slot, by the writer
-    // warps (wi = 0..11): float4 items in row-major order over the tile.
-    const int wi = warp - 1 - (warp >> 2);
-    auto write = [&](int u) {
-        const int g = u / T, t = u - g * T;
-        const int r0 = first_row(g), gr = min(G, a.rows - r0);
-        const int c0 = t * TC, tc = min(TC, dim - c0);
-        const unsigned char *slot = wring + (size_t)(u % kTiledSlots) * L.wslot;
-        if (!wait(&wbar[u % kTiledSlots], u)) return;
-        const float *sc = scales + (g & 1) * 64;
-        const int q = tc >> 2, total = gr * q;
-        const int nwt = kTiledWriters * 32;
+        // units whose copies were waited for
+        if (lane == 0) s_consumed = u;
+    } else if (warp & 3) {
+        const int wi = warp - 1 - (warp >> 2);  // 0..11
+        const int nwt = ColsShape<FQ>::writers * 32, wt = wi * 32 + lane;
+        const int q = dim >> 2;                 // float4 items per row
         const int dr = nwt / q, dc = nwt - dr * q;
-        const int wt = wi * 32 + lane;
-        int r = wt / q, c4 = wt - r * q;
-        int vr = -1;
-        bool vok = true;  // row vr's token is inside the table (its slot rows were not copied otherwise)
-        auto xval = [&](int rr_, int cc, float *v) {  // cc: column within the tile
-            decode_staged<SRC, 4>(slot + (size_t)rr_ * L.xstride, TC, cc, v);
-            if constexpr (SRC != SRC_X) {
-                if (rr_ != vr) {
-                    vr = rr_;
-                    vok = (unsigned)a.tokens[r0 + rr_] < (unsigned)a.vocab;
+        for (int g = 0; g < nmine; ++g) {
+            if (!wait(&ready[g & 1], (uint32_t)(g >> 1) & 1u, kColsSleepNs)) break;
+            const float *sc = scales + (g & 1) * 64;
+            const int r0 = first_row(g), gr = min(G, a.rows - r0);
+            const int total = gr * q;  // the group's float4 items, row-major
+            int r = wt / q, c4 = wt - r * q;
+            constexpr int U = ColsShape<FQ>::U;
+            for (int i = wt; i - lane < total; i += U * nwt) {
+                int rs[U], cs[U];
+                float4 xv[U], rv[U];
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    rs[k] = r;
+                    cs[k] = 4 * c4;
+                    xv[k] = rv[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (i + k * nwt < total) {
+                        const size_t o = (size_t)(r0 + r) * dim + cs[k];
+                        xv[k] = ld4(a.x_in + o);
+                        if (write_resid) rv[k] = ld4(a.resid + o);
+                    }
+                    c4 += dc;
+                    r += dr;
+                    if (c4 >= q) {
+                        c4 -= q;
+                        ++r;
+                    }
                 }
-                if (!vok) v[0] = v[1] = v[2] = v[3] = 0.0f;
-            }
-        };
-        auto rval = [&](int rr_, int cc) {
-            return *reinterpret_cast<const float4 *>(slot + (size_t)G * L.xstride + (size_t)rr_ * L.wrstride + 4 * cc);
-        };
-        if constexpr (FQ) {
-            // eight lanes per 32-element block; q % 8 == 0 and a warp's items
-            // are consecutive, so each block's lanes share a warp.
-            for (int i = wt; i - lane < total; i += nwt) {
-                const bool ok = i < total;
-                const int cc = 4 * c4, c = c0 + cc, row = r0 + r;
-                float4 y = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (ok) {
-                    float v[4];
-                    xval(r, cc, v);
-                    const size_t o = (size_t)row * dim + c;
-                    if (a.xb) {
+                // outputs in phases over the U items, so their latencies
+                // (shuffles, loads of weights) overlap
+                float4 y[U];
+                float am[U];
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    const bool ok = i + k * nwt < total;
+                    const int c = cs[k];
+                    const size_t o = (size_t)(r0 + rs[k]) * dim + c;
+                    float4 v = xv[k];
+                    if (PRE_ADD)
+                        v = make_float4(add_rn(v.x, rv[k].x), add_rn(v.y, rv[k].y), add_rn(v.z, rv[k].z),
+                                        add_rn(v.w, rv[k].w));
+                    if (a.xb && ok) {
                         const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
-                        const float s1 = sc[r];
-                        st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s1, v[0])), mul_rn(w.y, mul_rn(s1, v[1])),
-                                                  mul_rn(w.z, mul_rn(s1, v[2])), mul_rn(w.w, mul_rn(s1, v[3]))));
+                        const float s1 = sc[rs[k]];
+                        st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s1, v.x)), mul_rn(w.y, mul_rn(s1, v.y)),
+                                                  mul_rn(w.z, mul_rn(s1, v.z)), mul_rn(w.w, mul_rn(s1, v.w))));
                     }
-                    float4 xo = make_float4(v[0], v[1], v[2], v[3]);
-                    if (has_resid) {
-                        const float4 rv = rval(r, cc);
-                        xo = make_float4(add_rn(v[0], rv.x), add_rn(v[1], rv.y), add_rn(v[2], rv.z), add_rn(v[3], rv.w));
+                    float4 xo = v;
+                    if (!PRE_ADD && has_resid && (FQ || a.x_out))
+                        xo = make_float4(add_rn(v.x, rv[k].x), add_rn(v.y, rv[k].y), add_rn(v.z, rv[k].z),
+                                         add_rn(v.w, rv[k].w));
+                    if (a.x_out && ok) st4(a.x_out + o, xo);
+                    if constexpr (FQ) {
+                        y[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        if (ok) {
+                            const float4 wf = __ldg(reinterpret_cast<const float4 *>(a.w_final + c));
+                            const float s2 = sc[32 + rs[k]];
+                            y[k] = make_float4(mul_rn(wf.x, mul_rn(s2, xo.x)), mul_rn(wf.y, mul_rn(s2, xo.y)),
+                                               mul_rn(wf.z, mul_rn(s2, xo.z)), mul_rn(wf.w, mul_rn(s2, xo.w)));
+                        }
+                        am[k] = fmaxf(fmaxf(fmaxf(0.0f, fabsf(y[k].x)), fmaxf(0.0f, fabsf(y[k].y))),
+                                      fmaxf(fmaxf(0.0f, fabsf(y[k].z)), fmaxf(0.0f, fabsf(y[k].w))));
                     }
-                    if (a.x_out) st4(a.x_out + o, xo);
-                    const float4 wf = __ldg(reinterpret_cast<const float4 *>(a.w_final + c));
-                    const float s2 = sc[32 + r];
-                    y = make_float4(mul_rn(wf.x, mul_rn(s2, xo.x)), mul_rn(wf.y, mul_rn(s2, xo.y)),
-                                    mul_rn(wf.z, mul_rn(s2, xo.z)), mul_rn(wf.w, mul_rn(s2, xo.w)));
                 }
-                float am = fmaxf(fmaxf(fmaxf(0.0f, fabsf(y.x)), fmaxf(0.0f, fabsf(y.y))),
-                                 fmaxf(fmaxf(0.0f, fabsf(y.z)), fmaxf(0.0f, fabsf(y.w))));
-                am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
-                am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
-                am = fmaxf(am, __shfl_xor_sync(kFull, am, 4));
-                if (ok) {
+                if constexpr (FQ) {
+                    // eight lanes per 32-element block: q % 8 == 0 and a
+                    // warp's 32 items are consecutive, so a block's lanes
+                    // share a warp and a row
+#pragma unroll
+                    for (int m = 1; m < 8; m <<= 1)
+#pragma unroll
+                        for (int k = 0; k < U; ++k) am[k] = fmaxf(am[k], __shfl_xor_sync(kFull, am[k], m));
                     const int nb = dim >> 5;
-                    const float d = q8_scale(am);
-                    const float inv = d > 0.0f ? q8_inv(d) : 0.0f;
-                    const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y.x, inv)) |
-                                            ((uint32_t)(uint8_t)q8_code(mul_rn(y.y, inv)) << 8) |
-                                            ((uint32_t)(uint8_t)q8_code(mul_rn(y.z, inv)) << 16) |
-                                            ((uint32_t)(uint8_t)q8_code(mul_rn(y.w, inv)) << 24);
-                    *reinterpret_cast<uint32_t *>(a.codes + (size_t)row * dim + c) = packed;
-                    if ((c4 & 7) == 0) {
-                        a.scales[(size_t)row * nb + (c >> 5)] = d;
-                        if (a.scales16) a.scales16[(size_t)row * nb + (c >> 5)] = f16_bits(d);
+#pragma unroll
+                    for (int k = 0; k < U; ++k) {
+                        if (i + k * nwt >= total) continue;
+                        const int c = cs[k];
+                        const float d = q8_scale(am[k]);
+                        const float inv = d > 0.0f ? q8_inv(d) : 0.0f;
+                        const uint32_t packed = (uint32_t)(uint8_t)q8_code(mul_rn(y[k].x, inv)) |
+                                                ((uint32_t)(uint8_t)q8_code(mul_rn(y[k].y, inv)) << 8) |
+                                                ((uint32_t)(uint8_t)q8_code(mul_rn(y[k].z, inv)) << 16) |
+                                                ((uint32_t)(uint8_t)q8_code(mul_rn(y[k].w, inv)) << 24);
+                        const size_t ro = (size_t)(r0 + rs[k]);
+                        *reinterpret_cast<uint32_t *>(a.codes + ro * dim + c) = packed;
+                        if ((c & 31) == 0) {
+                            a.scales[ro * nb + (c >> 5)] = d;
+                            if (a.scales16) a.scales16[ro * nb + (c >> 5)] = f16_bits(d);
+                        }
                     }
                 }
-                c4 += dc;
-                r += dr;
-                if (c4 >= q) {
-                    c4 -= q;
-                    ++r;
-                }
             }
-            return;
+            // this warp's reads of the group's scales are done
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&freed[g & 1]);
         }
-        for (int i = wt; i < total; i += nwt) {
-            const int cc = 4 * c4, c = c0 + cc;
-            const size_t o = (size_t)(r0 + r) * dim + c;
-            float v[4];
-            xval(r, cc, v);
-            float4 rv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (write_resid) rv = rval(r, cc);
-            if (PRE_ADD) {
-                v[0] = add_rn(v[0], rv.x); v[1] = add_rn(v[1], rv.y);
-                v[2] = add_rn(v[2], rv.z); v[3] = add_rn(v[3], rv.w);
-            }
-            if (a.xb) {
-                const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c));
-                const float s = sc[r];
-                st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[0])), mul_rn(w.y, mul_rn(s, v[1])),
-                                          mul_rn(w.z, mul_rn(s, v[2])), mul_rn(w.w, mul_rn(s, v[3]))));
-            }
-            if (a.x_out) {
-                float4 xo = make_float4(v[0], v[1], v[2], v[3]);
-                if (!PRE_ADD && has_resid)
-                    xo = make_float4(add_rn(v[0], rv.x), add_rn(v[1], rv.y), add_rn(v[2], rv.z), add_rn(v[3], rv.w));
-                st4(a.x_out + o, xo);
-            }
-            c4 += dc;
-            r += dr;
-            if (c4 >= q) {
-                c4 -= q;
-                ++r;
-            }
-        }
-    };
-
-    // warp 4's counts of units issued into each ring
-    int s_issued = 0, w_issued = 0;
-    if (warp == 4)
-        for (; s_issued < min(units, kTiledSlots - 1); ++s_issued) issue_sum(s_issued);
-    for (int u = 0; u < units + T; ++u) {
-        if (warp == 4) {
-            if (!__shfl_sync(kFull, s_abort, 0)) {
-                if (s_issued < units) issue_sum(s_issued++);
-                // write unit u+S-1-T lands in the slot the writers left in iteration u-1
-                if (u + kTiledSlots - 1 - T >= 0 && w_issued < units) issue_write(w_issued++);
-            }
-        } else if (warp == 0) {
-            if (u < units) sum(u);
-        } else if ((warp & 3) != 0) {
-            if (u >= T) write(u - T);
-        }
-        __syncthreads();
     }
-    // Every copy issued was waited for unless a wait ran out; then wait (again
-    // bounded) for the last copies into each slot before the CTA's memory goes.
-    if (warp == 4 && lane == 0 && s_abort) {
-        for (int u = max(0, s_issued - kTiledSlots); u < s_issued; ++u)
-            mbar_wait_bounded(&sbar[u % kTiledSlots], (uint32_t)(u / kTiledSlots) & 1u);
-        for (int u = max(0, w_issued - kTiledSlots); u < w_issued; ++u)
-            mbar_wait_bounded(&wbar[u % kTiledSlots], (uint32_t)(u / kTiledSlots) & 1u);
-    }
+    __syncthreads();
+    // Every copy issued was waited for unless a role gave up; then wait
+    // (again bounded) for the copies still in flight before the memory goes.
+    if (tid == 0 && s_abort)
+        for (int u = s_consumed; u < s_issued; ++u) mbar_wait_bounded(&full[u % NS], (uint32_t)(u / NS) & 1u);
 }
 
 constexpr int kRowsSlots = 4;  // writing, summing, and two staged ahead
@@ -2504,50 +2453,49 @@ bool try_norm_small(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
     return true;
 }
 
-template <int SRC, bool PRE_ADD, bool FQ>
-bool try_norm_tiled(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
-    const int esz = SRC == SRC_BF16 ? 2 : (SRC == SRC_Q8 ? 1 : 4);
-    const int gran = SRC == SRC_Q8 ? 128 : (FQ ? 32 : 8);
+// The decoupled column-tiled pipeline for f32 x rows (dim % 8, % 32 when
+// quantising; 16-byte aligned rows).  Returns false (nothing launched) when it
+// does not apply.
+template <bool PRE_ADD, bool FQ>
+bool try_norm_cols(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
+    const int gran = FQ ? 32 : 8;
     if (a.rows <= 0 || a.dim <= 0 || a.dim % gran) return false;
-    const void *src = SRC == SRC_X ? (const void *)a.x_in : a.table;
-    if (!al16(src) || (SRC == SRC_Q8 && !al16(a.tscales)) || (a.resid && !al16(a.resid)) ||
-        (a.x_out && !al16(a.x_out)) || (a.xb && !al16(a.xb)) || (a.w_att && !al16(a.w_att)) ||
-        (FQ && (!al16(a.w_final) || ((uintptr_t)a.codes & 3u))))
+    if (!al16(a.x_in) || (a.resid && !al16(a.resid)) || (a.x_out && !al16(a.x_out)) || (a.xb && !al16(a.xb)) ||
+        (a.w_att && !al16(a.w_att)) || (FQ && (!al16(a.w_final) || ((uintptr_t)a.codes & 3u))))
         return false;
+    if (PRE_ADD && !a.resid) return false;
     const bool sum_resid = PRE_ADD || (FQ && a.resid);
-    const bool write_resid = a.resid && (PRE_ADD || FQ || a.x_out);
     const int sms = device_sms();
-    // the write ring's copies of x (and of a summed resid) come from L2
-    const size_t reread = (size_t)a.dim * esz + (sum_resid ? (size_t)a.dim * 4 : 0);
-    long G = (long)((48ull << 20) / (2 * reread * (size_t)sms));
+    // the writers' loads of x (and of a summed resid) come from L2, a group
+    // after the ring's copies brought them in: two groups per SM in flight.
+    // More rows per group keep more exact-order sums in flight; fewer keep
+    // more of the writers' loads in L2.  The sums of x + resid cost more per
+    // element, so that form takes more rows (measured optimum on B200: about
+    // 40 MB of such rows in flight, 60 MB for x + resid).
+    const size_t reread = (size_t)a.dim * 4 * (sum_resid ? 2 : 1);
+    const size_t budget = (sum_resid ? 60ull : 40ull) << 20;
+    long G = (long)(budget / (2 * reread * (size_t)sms));
     if (G > 32) G = 32;
     if (G < 1) G = 1;
     const long per_cta = ((long)a.rows + sms - 1) / sms;
     if (G > per_cta) G = per_cta;
-    // shared memory per column of one row, over both rings
-    const double xcol = esz + (SRC == SRC_Q8 ? 0.125 : 0.0);
-    const double per_col = kTiledSlots * (2 * xcol + (sum_resid ? 4.0 : 0.0) + (write_resid ? 4.0 : 0.0));
-    const long per_row = (long)((208u << 10) / (size_t)G) - kTiledSlots * 4 * 48;
-    long tcmax = (long)(per_row / per_col) / gran * gran;
+    // ring slots of G staged rows, each row x (+ resid) tiles of TC columns
+    const int per_row = (int)((212u << 10) / (kColsSlots * (size_t)G)) - 32;
+    long tcmax = (long)(per_row / (4 * (sum_resid ? 2 : 1))) / gran * gran;
     if (tcmax < gran) return false;
-    const int T = (int)((a.dim + tcmax - 1) / tcmax);
-    const int TC = (int)(((a.dim + T - 1) / T + gran - 1) / gran * gran);
-    TiledLayout L{};
+    const int T0 = (int)((a.dim + tcmax - 1) / tcmax);
+    ColsLayout L{};
     L.G = (int)G;
-    L.TC = TC;
-    L.T = (a.dim + TC - 1) / TC;
-    // odd multiples of 16 bytes: the summing lanes' 16-byte loads of one
+    L.TC = (int)(((a.dim + T0 - 1) / T0 + gran - 1) / gran * gran);
+    L.T = (a.dim + L.TC - 1) / L.TC;
+    L.rofs = L.TC * 4;
+    // an odd multiple of 16 bytes: the summing lanes' 16-byte loads of one
     // column fall in distinct banks
-    const int xb = TC * esz + (SRC == SRC_Q8 ? align16(TC / 8) : 0);
-    L.xstride = ((xb + 31) & ~31) + 16;
-    const int rs = ((TC * 4 + 31) & ~31) + 16;
-    L.srstride = sum_resid ? rs : 0;
-    L.wrstride = write_resid ? rs : 0;
-    L.sslot = L.G * (L.xstride + L.srstride);
-    L.wslot = L.G * (L.xstride + L.wrstride);
-    L.smem = (size_t)kTiledSlots * (L.sslot + L.wslot) + 128 * sizeof(float) + 2 * kTiledSlots * sizeof(uint64_t);
+    L.stride = ((L.TC * 4 * (sum_resid ? 2 : 1) + 31) & ~31) + 16;
+    L.slot = L.G * L.stride;
+    L.smem = (size_t)kColsSlots * L.slot + 128 * sizeof(float) + (2 * kColsSlots + 4) * sizeof(uint64_t);
     if (L.smem > 226 * 1024) return false;
-    auto kern = k_norm_tiled<SRC, PRE_ADD, FQ>;
+    auto kern = k_norm_cols<PRE_ADD, FQ>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
     if (e != cudaSuccess) {
         *err = e;
@@ -2555,7 +2503,7 @@ bool try_norm_tiled(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
     }
     const long groups = ((long)a.rows + L.G - 1) / L.G;
     const long grid = groups < sms ? groups : sms;
-    kern<<<(unsigned)grid, kTiledThreads, L.smem, s>>>(a, L);
+    kern<<<(unsigned)grid, ColsShape<FQ>::threads, L.smem, s>>>(a, L);
     *err = launched();
     return true;
 }
@@ -2638,14 +2586,14 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
         mark(hook, STAGE_NORM);
         // f32 x rows: the column-tiled pipeline (32 rows' sums in flight);
         // whole staged rows of f32 leave room for fewer
-        const bool done = (SRC == SRC_X && try_norm_tiled<SRC, false, true>(a, s, &e)) || try_norm_rows<SRC, true>(a, s, &e);
+        const bool done = (SRC == SRC_X && try_norm_cols<false, true>(a, s, &e)) || try_norm_rows<SRC, true>(a, s, &e);
         if (!done) e = launch_norm_pipe<SRC, true, false, true>(a, s);
     } else if (a.xb || a.x_out) {
         mark(hook, STAGE_NORM);
         // f32 x rows: a CTA per row for a few, else the column-tiled pipeline
         // keeps more rows' sums in flight
         const bool done =
-            vec && (SRC == SRC_X ? (try_norm_small<false>(a, s, &e) || try_norm_tiled<SRC, false, false>(a, s, &e))
+            vec && (SRC == SRC_X ? (try_norm_small<false>(a, s, &e) || try_norm_cols<false, false>(a, s, &e))
                                  : try_norm_rows<SRC, false>(a, s, &e));
         if (!done) e = vec ? launch_norm_pipe<SRC, true>(a, s) : launch_norm_pipe<SRC, false>(a, s);
     }
@@ -2756,7 +2704,7 @@ cudaError_t launch_add_rms_norm(const ChainArgs &a, cudaStream_t s) {
     if (a.rows <= 0) return cudaSuccess;
     if (a.dim % 8 != 0) return cudaErrorInvalidValue;
     cudaError_t e = cudaSuccess;
-    if (try_norm_small<true>(a, s, &e) || try_norm_tiled<SRC_X, true, false>(a, s, &e)) return e;
+    if (try_norm_small<true>(a, s, &e) || try_norm_cols<true, false>(a, s, &e)) return e;
     return launch_norm_pipe<SRC_X, true, true, false>(a, s);
 }
 
