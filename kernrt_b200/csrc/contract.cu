@@ -270,9 +270,10 @@ __global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const floa
             const float *xs = reinterpret_cast<const float *>(st + 32 * Geo::wstride);
             const int tc = min(kGemvCK, in_dim - c * kGemvCK);
             if (live) {
-#pragma unroll 2
-                for (int k = 0; k < tc; k += 8) {
-                    float wv[8];
+                // step k's eight weights (decoded) and x values; the next
+                // step is loaded and decoded ahead of the current step's adds,
+                // so shared-memory latency and decoding stay off the chain
+                auto ldw = [&](int k, float *wv) {
                     if constexpr (SRC == SRC_BF16) {
                         const uint4 t = *reinterpret_cast<const uint4 *>(wr + 2 * k);
                         const uint32_t p[4] = {t.x, t.y, t.z, t.w};
@@ -294,13 +295,33 @@ __global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const floa
                         wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w;
                         wv[4] = b2.x; wv[5] = b2.y; wv[6] = b2.z; wv[7] = b2.w;
                     }
+                };
+                auto ldx = [&](int k, float (*xv)[8]) {
 #pragma unroll
                     for (int r = 0; r < R; ++r) {
                         const float4 x0 = *reinterpret_cast<const float4 *>(xs + r * kGemvCK + k);
                         const float4 x1 = *reinterpret_cast<const float4 *>(xs + r * kGemvCK + k + 4);
-                        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                        xv[r][0] = x0.x; xv[r][1] = x0.y; xv[r][2] = x0.z; xv[r][3] = x0.w;
+                        xv[r][4] = x1.x; xv[r][5] = x1.y; xv[r][6] = x1.z; xv[r][7] = x1.w;
+                    }
+                };
+                float wv[8], xv[R][8], nwv[8], nxv[R][8];
+                ldw(0, wv);
+                ldx(0, xv);
+#pragma unroll 2
+                for (int k = 0; k < tc; k += 8) {
+                    const int kn = k + 8 < tc ? k + 8 : k;
+                    ldw(kn, nwv);
+                    ldx(kn, nxv);
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) acc[r] = add_rn(acc[r], mul_rn(wv[e], xv[e]));
+                    for (int r = 0; r < R; ++r)
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[r] = add_rn(acc[r], mul_rn(wv[e], xv[r][e]));
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        wv[e] = nwv[e];
+#pragma unroll
+                        for (int r = 0; r < R; ++r) xv[r][e] = nxv[r][e];
                     }
                 }
             }
