@@ -172,16 +172,20 @@ __global__ void __launch_bounds__(256) k_project_scalar(const void *__restrict__
 // Row slots are padded to an odd number of 16-byte units: the lanes' 16-byte
 // reads of one column land in distinct banks.  Requires in_dim % 8 (% 128
 // for Q8_0, whose block scales then move in 16-byte units too).
+// Chunks of CK = 512 columns, or 1024 when the matrix has fewer warps of
+// outputs than the GPU has SMs: each SM then runs one CTA, whose copy engine
+// takes a stage's 32 requests one after another, and wider requests move more
+// bytes per request.
 constexpr int kGemvCK = 512;
+constexpr int kGemvCKWide = 1024;
 constexpr int kGemvStages = 2;
 
-template <int SRC>
+template <int SRC, int CK>
 struct GemvGeom {
     static constexpr int esz = SRC == SRC_BF16 ? 2 : (SRC == SRC_Q8 ? 1 : 4);
-    static constexpr int wrow = kGemvCK * esz + (SRC == SRC_Q8 ? kGemvCK / 8 : 0);  // codes (+ scales)
-    static constexpr int wstride = ((wrow + 31) & ~31) + 16;                          // odd x 16 B
-    template <int R>
-    __host__ __device__ static constexpr int stage_bytes() { return 32 * wstride + R * kGemvCK * 4; }
+    static constexpr int wrow = CK * esz + (SRC == SRC_Q8 ? CK / 8 : 0);  // codes (+ scales)
+    static constexpr int wstride = ((wrow + 31) & ~31) + 16;              // odd x 16 B
+    __host__ __device__ static constexpr size_t stage_bytes(int rows) { return 32 * (size_t)wstride + (size_t)rows * CK * 4; }
 };
 
 // Up to three matrices sharing x and in_dim in one launch (the trait's
@@ -203,11 +207,11 @@ __device__ __forceinline__ T pick3(const T (&a)[3], int m) {
     return m == 0 ? a[0] : (m == 1 ? a[1] : a[2]);
 }
 
-template <int SRC, int R>
+template <int SRC, int R, int CK>
 __global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const float *__restrict__ x, int *err) {
-    using Geo = GemvGeom<SRC>;
+    using Geo = GemvGeom<SRC, CK>;
     constexpr int NS = kGemvStages;
-    constexpr int SB = Geo::template stage_bytes<R>();
+    constexpr int SB = (int)Geo::stage_bytes(R);
     extern __shared__ __align__(16) unsigned char gsm[];
     __shared__ __align__(8) uint64_t full[NS], empty[NS];
     __shared__ int issued_sh;
@@ -218,7 +222,7 @@ __global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const floa
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, o = blk * 32 + lane;
     const bool live = o < out_dim;
     const int nlive = min(32, out_dim - blk * 32);
-    const int nchunks = (in_dim + kGemvCK - 1) / kGemvCK;
+    const int nchunks = (in_dim + CK - 1) / CK;
     if (threadIdx.x == 0) {
         for (int i = 0; i < NS; ++i) {
             mbar_init(&full[i], 1);
@@ -235,7 +239,7 @@ __global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const floa
         const float *__restrict__ wsc = pick3(set.wsc, m);
         int issued = 0;
         for (; issued < nchunks; ++issued) {
-            const int c = issued, k0 = c * kGemvCK, tc = min(kGemvCK, in_dim - k0);
+            const int c = issued, k0 = c * CK, tc = min(CK, in_dim - k0);
             if (c >= NS && !__all_sync(kFullMask, mbar_wait_bounded(&empty[c % NS], (uint32_t)(c / NS - 1) & 1u)))
                 break;  // the consumer stopped: issue nothing more
             const uint32_t wb = (uint32_t)(tc * Geo::esz), sb = SRC == SRC_Q8 ? (uint32_t)(tc / 8) : 0u;
@@ -247,11 +251,11 @@ __global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const floa
                 bulk_load(st + (size_t)lane * Geo::wstride,
                           static_cast<const unsigned char *>(w) + ((size_t)o * in_dim + k0) * Geo::esz, wb, b);
                 if constexpr (SRC == SRC_Q8)
-                    bulk_load(st + (size_t)lane * Geo::wstride + kGemvCK, wsc + (size_t)o * (in_dim >> 5) + (k0 >> 5),
+                    bulk_load(st + (size_t)lane * Geo::wstride + CK, wsc + (size_t)o * (in_dim >> 5) + (k0 >> 5),
                               sb, b);
             }
             if (lane < R)
-                bulk_load(st + 32 * Geo::wstride + (size_t)lane * kGemvCK * 4, x + (size_t)lane * in_dim + k0,
+                bulk_load(st + 32 * Geo::wstride + (size_t)lane * CK * 4, x + (size_t)lane * in_dim + k0,
                           (uint32_t)(tc * 4), b);
         }
         if (lane == 0) issued_sh = issued;
@@ -268,7 +272,7 @@ __global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const floa
             const unsigned char *st = gsm + (size_t)(c % NS) * SB;
             const unsigned char *wr = st + (size_t)lane * Geo::wstride;
             const float *xs = reinterpret_cast<const float *>(st + 32 * Geo::wstride);
-            const int tc = min(kGemvCK, in_dim - c * kGemvCK);
+            const int tc = min(CK, in_dim - c * CK);
             if (live) {
                 // step k's eight weights (decoded) and x values; the next
                 // step is loaded and decoded ahead of the current step's adds,
@@ -284,7 +288,7 @@ __global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const floa
                         }
                     } else if constexpr (SRC == SRC_Q8) {
                         const uint2 t = *reinterpret_cast<const uint2 *>(wr + k);
-                        const float sc = reinterpret_cast<const float *>(wr + kGemvCK)[k >> 5];
+                        const float sc = reinterpret_cast<const float *>(wr + CK)[k >> 5];
                         const uint32_t p[2] = {t.x, t.y};
 #pragma unroll
                         for (int e = 0; e < 8; ++e)
@@ -299,8 +303,8 @@ __global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const floa
                 auto ldx = [&](int k, float (*xv)[8]) {
 #pragma unroll
                     for (int r = 0; r < R; ++r) {
-                        const float4 x0 = *reinterpret_cast<const float4 *>(xs + r * kGemvCK + k);
-                        const float4 x1 = *reinterpret_cast<const float4 *>(xs + r * kGemvCK + k + 4);
+                        const float4 x0 = *reinterpret_cast<const float4 *>(xs + r * CK + k);
+                        const float4 x1 = *reinterpret_cast<const float4 *>(xs + r * CK + k + 4);
                         xv[r][0] = x0.x; xv[r][1] = x0.y; xv[r][2] = x0.z; xv[r][3] = x0.w;
                         xv[r][4] = x1.x; xv[r][5] = x1.y; xv[r][6] = x1.z; xv[r][7] = x1.w;
                     }
@@ -340,13 +344,26 @@ __global__ void __launch_bounds__(64) k_gemv(GemvSet set, int in_dim, const floa
         for (int c = consumed; c < issued_sh; ++c) mbar_wait_bounded(&full[c % NS], (uint32_t)(c / NS) & 1u);
 }
 
+// the stages plus a little static shared memory within the 227 KB opt-in limit
+template <int SRC, int CK>
+bool gemv_smem_fits(int rows) {
+    return (size_t)kGemvStages * GemvGeom<SRC, CK>::stage_bytes(rows) + 256 <= 232448;
+}
+
+template <int SRC, int R, int CK>
+cudaError_t launch_gemv_ck(const GemvSet &set, int in_dim, const float *x, int *err, cudaStream_t s) {
+    const size_t smem = (size_t)kGemvStages * GemvGeom<SRC, CK>::stage_bytes(R);
+    cudaError_t e = cudaFuncSetAttribute(k_gemv<SRC, R, CK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k_gemv<SRC, R, CK><<<(unsigned)set.cta_end[set.n - 1], 64, smem, s>>>(set, in_dim, x, err);
+    return launched();
+}
+
 template <int SRC, int R>
 cudaError_t launch_gemv(const GemvSet &set, int in_dim, const float *x, int *err, cudaStream_t s) {
-    const size_t smem = (size_t)kGemvStages * GemvGeom<SRC>::template stage_bytes<R>();
-    cudaError_t e = cudaFuncSetAttribute(k_gemv<SRC, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    k_gemv<SRC, R><<<(unsigned)set.cta_end[set.n - 1], 64, smem, s>>>(set, in_dim, x, err);
-    return launched();
+    const bool wide = set.cta_end[set.n - 1] < device_sms() && in_dim > kGemvCK && gemv_smem_fits<SRC, kGemvCKWide>(R);
+    return wide ? launch_gemv_ck<SRC, R, kGemvCKWide>(set, in_dim, x, err, s)
+                : launch_gemv_ck<SRC, R, kGemvCK>(set, in_dim, x, err, s);
 }
 
 template <int SRC>
@@ -361,9 +378,7 @@ cudaError_t gemv_rows(const GemvSet &set, int in_dim, const float *x, int rows, 
 
 template <int SRC>
 bool gemv_fits(const void *w, const float *wsc, int in_dim, const float *x, int rows) {
-    // the stages plus a little static shared memory within the 227 KB opt-in limit
-    const size_t smem = (size_t)kGemvStages * (32 * GemvGeom<SRC>::wstride + (size_t)rows * kGemvCK * 4);
-    return rows <= 4 && smem + 256 <= 232448 && in_dim % (SRC == SRC_Q8 ? 128 : 8) == 0 &&
+    return rows <= 4 && gemv_smem_fits<SRC, kGemvCK>(rows) && in_dim % (SRC == SRC_Q8 ? 128 : 8) == 0 &&
            ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 && (SRC != SRC_Q8 || ((uintptr_t)wsc & 15) == 0);
 }
 

@@ -2350,17 +2350,6 @@ cudaError_t launch_chain_t(const ChainArgs &a, cudaStream_t s) {
     return launched();
 }
 
-int device_sms() {
-    static int sms[64] = {0};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (!sms[dev]) {
-        int n = 148;
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        sms[dev] = n > 0 ? n : 148;
-    }
-    return sms[dev];
-}
 
 // Warps per CTA and grid for the row-staged q/k kernels; 0 warps when a row
 // does not fit, so the caller keeps the unstaged form.
@@ -2635,6 +2624,19 @@ cudaError_t launch_chain_src_fused(const ChainArgs &a, cudaStream_t s) {
 }
 
 }  // namespace
+
+// SM count of the current device, cached per device.
+int device_sms() {
+    static int sms[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!sms[dev]) {
+        int n = 148;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        sms[dev] = n > 0 ? n : 148;
+    }
+    return sms[dev];
+}
 
 cudaError_t launch_embed_gather(int kind, bool vec, const GatherArgs &a, cudaStream_t s) {
     if (a.n <= 0) return cudaSuccess;

@@ -57,6 +57,8 @@ struct LaunchHook {
     void *user;
 };
 // Chooses rows-per-CTA and shared memory, then launches.
+// SM count of the current device (148 if it cannot be read).
+int device_sms();
 cudaError_t launch_chain(int src, const ChainArgs &a, cudaStream_t s, const LaunchHook *hook = nullptr);
 // Shared memory a chain launch would need for one row group (to report limits).
 size_t chain_smem_bytes(int src, const ChainArgs &a, int rows_per_cta);
