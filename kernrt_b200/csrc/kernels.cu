@@ -263,44 +263,98 @@ __device__ void qk_rope_row_smem(float *v, int width, int head, const float *__r
         return make_float4(mul_rn(ww.x, mul_rn(s, x.x)), mul_rn(ww.y, mul_rn(s, x.y)), mul_rn(ww.z, mul_rn(s, x.z)),
                            mul_rn(ww.w, mul_rn(s, x.w)));
     };
+    auto scale4 = [&](float4 x, float s, float4 ww) {
+        return make_float4(mul_rn(ww.x, mul_rn(s, x.x)), mul_rn(ww.y, mul_rn(s, x.y)), mul_rn(ww.z, mul_rn(s, x.z)),
+                           mul_rn(ww.w, mul_rn(s, x.w)));
+    };
+    auto rot_half = [&](float4 lo, float4 hi, float4 c, float4 s, float *dlo, float *dhi) {
+        float4 nl, nhv;
+        nl.x = sub_rn(mul_rn(lo.x, c.x), mul_rn(hi.x, s.x));
+        nl.y = sub_rn(mul_rn(lo.y, c.y), mul_rn(hi.y, s.y));
+        nl.z = sub_rn(mul_rn(lo.z, c.z), mul_rn(hi.z, s.z));
+        nl.w = sub_rn(mul_rn(lo.w, c.w), mul_rn(hi.w, s.w));
+        nhv.x = add_rn(mul_rn(lo.x, s.x), mul_rn(hi.x, c.x));
+        nhv.y = add_rn(mul_rn(lo.y, s.y), mul_rn(hi.y, c.y));
+        nhv.z = add_rn(mul_rn(lo.z, s.z), mul_rn(hi.z, c.z));
+        nhv.w = add_rn(mul_rn(lo.w, s.w), mul_rn(hi.w, c.w));
+        *reinterpret_cast<float4 *>(dlo) = nl;
+        *reinterpret_cast<float4 *>(dhi) = nhv;
+    };
     if (mode == 1) {
         const int ph = half >> 2;  // float4 items per head (lo half)
-        for (int t = lane; t < nh * ph; t += 32) {
-            const int h = t / ph, j = (t - h * ph) << 2;
-            const float4 lo = norm4(*reinterpret_cast<const float4 *>(sm + h * hs + j), h, j);
-            const float4 hi = norm4(*reinterpret_cast<const float4 *>(sm + h * hs + half + j), h, half + j);
+        if (32 % ph == 0) {
+            // every item of a lane has the same column j: its weights and its
+            // cos/sin are loaded once per row, not once per item
+            const int j = (lane % ph) << 2, hstep = 32 / ph;
             const float4 c = __ldg(reinterpret_cast<const float4 *>(ct + j));
-            const float4 s = __ldg(reinterpret_cast<const float4 *>(st + j));
-            float4 nl, nhv;
-            nl.x = sub_rn(mul_rn(lo.x, c.x), mul_rn(hi.x, s.x));
-            nl.y = sub_rn(mul_rn(lo.y, c.y), mul_rn(hi.y, s.y));
-            nl.z = sub_rn(mul_rn(lo.z, c.z), mul_rn(hi.z, s.z));
-            nl.w = sub_rn(mul_rn(lo.w, c.w), mul_rn(hi.w, s.w));
-            nhv.x = add_rn(mul_rn(lo.x, s.x), mul_rn(hi.x, c.x));
-            nhv.y = add_rn(mul_rn(lo.y, s.y), mul_rn(hi.y, c.y));
-            nhv.z = add_rn(mul_rn(lo.z, s.z), mul_rn(hi.z, c.z));
-            nhv.w = add_rn(mul_rn(lo.w, s.w), mul_rn(hi.w, c.w));
-            *reinterpret_cast<float4 *>(v + h * head + j) = nl;
-            *reinterpret_cast<float4 *>(v + h * head + half + j) = nhv;
+            const float4 sn = __ldg(reinterpret_cast<const float4 *>(st + j));
+            float4 wl = make_float4(0.0f, 0.0f, 0.0f, 0.0f), wh = wl;
+            if (w) {
+                wl = __ldg(reinterpret_cast<const float4 *>(w + j));
+                wh = __ldg(reinterpret_cast<const float4 *>(w + half + j));
+            }
+#pragma unroll 4
+            for (int h = lane / ph; h < nh; h += hstep) {
+                float4 lo = *reinterpret_cast<const float4 *>(sm + h * hs + j);
+                float4 hi = *reinterpret_cast<const float4 *>(sm + h * hs + half + j);
+                if (w) {
+                    const float s1 = sc[h];
+                    lo = scale4(lo, s1, wl);
+                    hi = scale4(hi, s1, wh);
+                }
+                rot_half(lo, hi, c, sn, v + h * head + j, v + h * head + half + j);
+            }
+        } else {
+            for (int t = lane; t < nh * ph; t += 32) {
+                const int h = t / ph, j = (t - h * ph) << 2;
+                const float4 lo = norm4(*reinterpret_cast<const float4 *>(sm + h * hs + j), h, j);
+                const float4 hi = norm4(*reinterpret_cast<const float4 *>(sm + h * hs + half + j), h, half + j);
+                const float4 c = __ldg(reinterpret_cast<const float4 *>(ct + j));
+                const float4 sn = __ldg(reinterpret_cast<const float4 *>(st + j));
+                rot_half(lo, hi, c, sn, v + h * head + j, v + h * head + half + j);
+            }
         }
     } else {
-        for (int t = lane; t < n4; t += 32) {
-            const int h = t / per, j = (t - h * per) << 2;
-            float4 x = norm4(*reinterpret_cast<const float4 *>(sm + h * hs + j), h, j);
-            const int i = 4 * t;  // element index in the row = pair 2t, 2t+1
+        auto pair_rot = [&](float4 x, int t, float2 c, float2 sn) {
             if (mode == 2 && 2 * t < npairs) {
-                const int jj = j >> 1;  // (i % head) / 2, with i % head == j
-                const float2 c = __ldg(reinterpret_cast<const float2 *>(ct + jj));
-                const float2 s = __ldg(reinterpret_cast<const float2 *>(st + jj));
                 const float x0 = x.x, x1 = x.y, x2 = x.z, x3 = x.w;
-                x.x = sub_rn(mul_rn(x0, c.x), mul_rn(x1, s.x));
-                x.y = add_rn(mul_rn(x0, s.x), mul_rn(x1, c.x));
+                x.x = sub_rn(mul_rn(x0, c.x), mul_rn(x1, sn.x));
+                x.y = add_rn(mul_rn(x0, sn.x), mul_rn(x1, c.x));
                 if (2 * t + 1 < npairs) {
-                    x.z = sub_rn(mul_rn(x2, c.y), mul_rn(x3, s.y));
-                    x.w = add_rn(mul_rn(x2, s.y), mul_rn(x3, c.y));
+                    x.z = sub_rn(mul_rn(x2, c.y), mul_rn(x3, sn.y));
+                    x.w = add_rn(mul_rn(x2, sn.y), mul_rn(x3, c.y));
                 }
             }
-            *reinterpret_cast<float4 *>(v + i) = x;
+            return x;
+        };
+        if (32 % per == 0) {
+            // a lane's items share the column j (see above)
+            const int j = (lane % per) << 2, hstep = 32 / per;
+            float2 c = make_float2(0.0f, 0.0f), sn = c;
+            if (mode == 2) {
+                c = __ldg(reinterpret_cast<const float2 *>(ct + (j >> 1)));
+                sn = __ldg(reinterpret_cast<const float2 *>(st + (j >> 1)));
+            }
+            float4 ww = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (w) ww = __ldg(reinterpret_cast<const float4 *>(w + j));
+#pragma unroll 4
+            for (int h = lane / per; h < nh; h += hstep) {
+                const int t = h * per + (lane % per);
+                float4 x = *reinterpret_cast<const float4 *>(sm + h * hs + j);
+                if (w) x = scale4(x, sc[h], ww);
+                *reinterpret_cast<float4 *>(v + 4 * t) = pair_rot(x, t, c, sn);
+            }
+        } else {
+            for (int t = lane; t < n4; t += 32) {
+                const int h = t / per, j = (t - h * per) << 2;
+                const float4 x = norm4(*reinterpret_cast<const float4 *>(sm + h * hs + j), h, j);
+                float2 c = make_float2(0.0f, 0.0f), sn = c;
+                if (mode == 2 && 2 * t < npairs) {
+                    c = __ldg(reinterpret_cast<const float2 *>(ct + (j >> 1)));
+                    sn = __ldg(reinterpret_cast<const float2 *>(st + (j >> 1)));
+                }
+                *reinterpret_cast<float4 *>(v + 4 * t) = pair_rot(x, t, c, sn);
+            }
         }
     }
     __syncwarp();
