@@ -88,6 +88,15 @@ __device__ __forceinline__ void set_err(int *err, int code) {
 __device__ __forceinline__ float4 ld4(const float *p) { return __ldcs(reinterpret_cast<const float4 *>(p)); }
 __device__ __forceinline__ void st4(float *p, float4 v) { __stcs(reinterpret_cast<float4 *>(p), v); }
 
+// 16-byte global -> shared copies that need no registers: a warp issues all
+// of a row's copies back to back and waits once.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 // --------------------------------------------------------------------------
 // Row-local building blocks (one warp per row)
 // --------------------------------------------------------------------------
@@ -238,19 +247,24 @@ __device__ void qk_rope_row_smem(float *v, int width, int head, const float *__r
     const int n4 = (nh * head) >> 2, per = head >> 2;
     for (int t = lane; t < n4; t += 32) {
         const int h = t / per, j = (t - h * per) << 2;
-        *reinterpret_cast<float4 *>(sm + h * hs + j) = *reinterpret_cast<const float4 *>(v + 4 * t);
+        cp_async16(sm + h * hs + j, v + 4 * t);
     }
+    cp_async_wait_all();
     __syncwarp();
     if (w) {
         for (int h = lane; h < nh; h += 32) {
             const float *p = sm + h * hs;
             float ss = 0.0f;
+            // the next four values are loaded ahead of the current four's adds
+            float4 t4 = *reinterpret_cast<const float4 *>(p);
+#pragma unroll 4
             for (int j = 0; j < head; j += 4) {
-                const float4 t4 = *reinterpret_cast<const float4 *>(p + j);
+                const float4 n4v = *reinterpret_cast<const float4 *>(p + (j + 4 < head ? j + 4 : j));
                 ss = add_rn(ss, mul_rn(t4.x, t4.x));
                 ss = add_rn(ss, mul_rn(t4.y, t4.y));
                 ss = add_rn(ss, mul_rn(t4.z, t4.z));
                 ss = add_rn(ss, mul_rn(t4.w, t4.w));
+                t4 = n4v;
             }
             sc[h] = rms_scale(ss, (float)head, eps);
         }
@@ -619,12 +633,6 @@ struct ChainLayout {
     size_t smem;
 };
 
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
-    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 template <int SRC, bool FQ, bool VEC>
 __global__ void __launch_bounds__(kThreads, 3) k_chain(ChainArgs a, ChainLayout L) {
