@@ -427,6 +427,19 @@ __global__ void __launch_bounds__(256) k_kv_write(float *__restrict__ kc, float 
     }
 }
 
+// The same with 16-byte items (kv_dim % 4, 16-byte aligned buffers): q4
+// float4 per row, n4 items in all.
+__global__ void __launch_bounds__(256) k_kv_write4(float *__restrict__ kc, float *__restrict__ vc, int q4,
+                                                   const int32_t *__restrict__ dst_rows, const float *__restrict__ k,
+                                                   const float *__restrict__ v, int n4) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+        const int r = i / q4, e = i - r * q4;
+        const size_t d = ((size_t)dst_rows[r] * q4 + e) * 4;
+        *reinterpret_cast<float4 *>(kc + d) = *reinterpret_cast<const float4 *>(k + (size_t)i * 4);
+        *reinterpret_cast<float4 *>(vc + d) = *reinterpret_cast<const float4 *>(v + (size_t)i * 4);
+    }
+}
+
 // ---- attention ------------------------------------------------------------------
 
 // sum_{i < n} v[i] from shared memory in index order, one thread: sixteen
@@ -718,6 +731,13 @@ cudaError_t launch_kv_write(float *kc, float *vc, int kv_dim, const int32_t *dst
                             int rows, cudaStream_t s) {
     if (rows <= 0 || kv_dim <= 0) return cudaSuccess;
     const long long n = (long long)rows * kv_dim;
+    if ((kv_dim & 3) == 0 && ((((uintptr_t)kc) | ((uintptr_t)vc) | ((uintptr_t)k) | ((uintptr_t)v)) & 15) == 0 &&
+        n / 4 < (1ll << 31)) {
+        const int n4 = (int)(n / 4);
+        const int grid = (n4 + 255) / 256 < 148 * 16 ? (n4 + 255) / 256 : 148 * 16;
+        k_kv_write4<<<(unsigned)grid, 256, 0, s>>>(kc, vc, kv_dim >> 2, dst_rows, k, v, n4);
+        return launched();
+    }
     long long grid = (n + 255) / 256;
     if (grid > 148 * 16) grid = 148 * 16;
     k_kv_write<<<(unsigned)grid, 256, 0, s>>>(kc, vc, kv_dim, dst_rows, k, v, rows);
