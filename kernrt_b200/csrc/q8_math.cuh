@@ -37,10 +37,15 @@ __device__ __forceinline__ float q8_inv(float d) {
 }
 
 // quant.rs:871: (v * inv).round().clamp(-127, 127) as i8 -- round half away
-// from zero, NaN -> 0.  The float-to-int conversion saturates and maps NaN to
-// 0, so the clamp can run on the integer.
+// from zero, NaN -> 0.  Half away from zero is sign(v) floor(|v| + 1/2); the
+// sum |v| + 1/2 rounded toward zero has the same floor as the exact sum
+// (integers below 2^24 are floats, so rounding down never crosses one, and
+// above 2^23 the sum is |v| itself), and the conversion's truncation takes
+// that floor.  The conversion saturates and maps NaN to 0, so the clamp can
+// run on the integer.  Checked against roundf for every f32.
 __device__ __forceinline__ int8_t q8_code(float v) {
-    const int i = __float2int_rz(roundf(v));
+    const float half = __int_as_float((__float_as_int(v) & (int)0x80000000u) | 0x3f000000);  // copysign(1/2, v)
+    const int i = __float2int_rz(__fadd_rz(v, half));
     return (int8_t)max(-127, min(127, i));
 }
 
