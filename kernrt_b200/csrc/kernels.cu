@@ -1198,8 +1198,16 @@ __global__ void __launch_bounds__(kPipeThreads, 1) k_norm_pipe(ChainArgs a, Chai
     }
 }
 
-constexpr int kTiledThreads = 512;  // 16 warps
-constexpr int kTiledWriters = 12;   // warps off the summing warp's sub-partition
+constexpr int kRowsThreadsPlain = 640;
+// k_norm_rows: 16 warps (12 writers) in the quantising form, 20 (15 writers,
+// at most 102 registers each) otherwise, where the writers' residual loads
+// and stores want more warps in flight (measured: 0.340 -> 0.321 ms for the
+// 65 536-row chain's norm stage; 24 warps no better, 32 spill).
+template <bool FQ>
+struct RowsShape {
+    static constexpr int threads = FQ ? 512 : kRowsThreadsPlain;
+    static constexpr int writers = threads / 32 * 3 / 4;  // the warps off sub-partition 0
+};
 
 // f32 x rows with the three roles decoupled: one 16-warp CTA per SM, its
 // rows in groups of G, a group's rows cut into T column tiles of TC columns
@@ -1517,7 +1525,7 @@ struct RowsLayout {
     size_t smem;
 };
 
-// The norm stage over whole staged rows, one 16-warp CTA per SM, four slots
+// The norm stage over whole staged rows, one CTA per SM (RowsShape), four slots
 // of G rows, each filled by one bulk copy per row (a full row is big enough
 // that the copy engine's per-request cost stays far below the row's
 // traffic).  In iteration i:
@@ -1527,15 +1535,15 @@ struct RowsLayout {
 //             the slot's mbarrier;
 //   warp 0    waits for group i and sums it, lane r row r left to right (the
 //             reference's order, reference.rs:167-170);
-//   writers   (12 warps on the other sub-partitions) write group i-1 from its
+//   writers   (the warps off warp 0's sub-partition) write group i-1 from its
 //             slot: xb = w*(scale*x), x + resid (resid from global memory,
 //             eight float4 loads in flight per lane), or the Q8_0 codes.
 // Staging two groups ahead keeps a group's copies in flight for two
-// iterations, longer than their HBM latency under load.  Warps 8 and 12 only
-// keep the barrier count.  FQ is the final RMSNorm fused with Q8_0
-// quantisation (quant.rs:856-874).
+// iterations, longer than their HBM latency under load.  The other warps of
+// warp 0's sub-partition only keep the barrier count.  FQ is the final
+// RMSNorm fused with Q8_0 quantisation (quant.rs:856-874).
 template <int SRC, bool FQ>
-__global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, RowsLayout L) {
+__global__ void __launch_bounds__(RowsShape<FQ>::threads, 1) k_norm_rows(ChainArgs a, RowsLayout L) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int dim = a.dim, G = L.G;
@@ -1648,13 +1656,13 @@ __global__ void __launch_bounds__(kTiledThreads, 1) k_norm_rows(ChainArgs a, Row
     };
 
     const int wi = warp - 1 - (warp >> 2);
-    auto write = [&](int g) {  // 12 writer warps
+    auto write = [&](int g) {  // the writer warps
         if (s_abort) return;
         const int r0 = first_row(g), gr = min(G, a.rows - r0);
         const unsigned char *base = slot(g);
         const float *sc = scales + (g % NS) * 64;
         const int q = dim >> 2, total = gr * q;
-        const int nwt = kTiledWriters * 32;
+        const int nwt = RowsShape<FQ>::writers * 32;
         const int dr = nwt / q, dc = nwt - dr * q;
         const int wt = wi * 32 + lane;
         int r = wt / q, c4 = wt - r * q;
@@ -2594,7 +2602,7 @@ bool try_norm_rows(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
     }
     const long groups = ((long)a.rows + L.G - 1) / L.G;
     const long grid = groups < sms ? groups : sms;
-    kern<<<(unsigned)grid, kTiledThreads, L.smem, s>>>(a, L);
+    kern<<<(unsigned)grid, RowsShape<FQ>::threads, L.smem, s>>>(a, L);
     *err = launched();
     return true;
 }
