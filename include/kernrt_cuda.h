@@ -81,6 +81,32 @@ int kernrt_cuda_stream(kernrt_cuda_ctx *ctx, void **stream);
 int kernrt_cuda_prepare_embedding(kernrt_cuda_ctx *ctx, int kind, const void *data,
                                   const float *scales, size_t vocab, size_t dim);
 
+/* --- Weights from a safetensors file (src/formats/safetensors.rs) ----------
+ * A tensor's entry in a safetensors file, read and checked on the host only
+ * (no device): the header is validated as read_with does
+ * (safetensors.rs:161-257: header length, strict JSON, every entry's dtype,
+ * shape and byte range), and the message of a failure is the reference's
+ * SafeTensorsError text (safetensors.rs:46-68) in kernrt_cuda_last_error. */
+enum { KERNRT_ST_F32 = 0, KERNRT_ST_BF16 = 1, KERNRT_ST_F16 = 2 };
+typedef struct {
+    int dtype;             /* KERNRT_ST_* */
+    int rank;
+    uint64_t shape[8];     /* the first min(rank, 8) dimensions */
+    uint64_t file_offset;  /* byte offset of the payload in the file */
+    uint64_t bytes;        /* payload bytes */
+} kernrt_st_tensor;
+int kernrt_cuda_safetensors_tensor(const char *path, const char *name, kernrt_st_tensor *out);
+
+/* Backend::prepare's token embedding taken from a file, as the HF loaders take
+ * "model.embed_tokens.weight" (take_matrix_raw, hf.rs:141-147, llama.rs:281,
+ * lfm2.rs:174): the payload goes from the file to the device as stored and is
+ * converted there by matrix_from_raw's rules (hf.rs:151-191) for `storage`
+ * (KERNRT_F32 / _BF16 / _Q8_0 / _Q8_0X4): a bf16 payload is handed over as it
+ * is for bf16 storage, and no f32 copy of it is made on the host.  The rank-2
+ * tensor becomes the `[vocab, dim]` table kernrt_cuda_prepare_embedding would
+ * install; kernrt_cuda_storage then names the storage the rules produced. */
+int kernrt_cuda_prepare_embedding_file(kernrt_cuda_ctx *ctx, const char *path, const char *name, int storage);
+
 /* --- buffers: Backend::alloc / upload / read (mod.rs:275-282) --------------- */
 /* `len` f32 elements.  Zero-filled (the trait says uninitialised; zeroing is
  * what the LFM2 ring seeding relies on, lfm2.rs:311-318). */

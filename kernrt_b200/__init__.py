@@ -68,6 +68,13 @@ class Window(C.Structure):
                 ("shared_end", C.c_uint64)]
 
 
+class StTensor(C.Structure):
+    """Mirror of ``kernrt_st_tensor``: one tensor's entry in a safetensors file."""
+
+    _fields_ = [("dtype", C.c_int), ("rank", C.c_int), ("shape", C.c_uint64 * 8),
+                ("file_offset", C.c_uint64), ("bytes", C.c_uint64)]
+
+
 class ChainHostArgs(C.Structure):
     """Mirror of ``kernrt_chain_host_args`` (include/kernrt_cuda.h)."""
 
@@ -129,7 +136,13 @@ SIGNATURES = {
     "kernrt_cuda_kv_write": (C.c_int, [P, SZ, P, SZ, Buf, Buf, SZ]),
     "kernrt_cuda_attention": (C.c_int, [P, Buf, Buf, Buf, SZ, C.POINTER(Window), SZ, SZ, SZ, SZ, SZ, SZ]),
     "kernrt_cuda_embed_rows_noalloc": (C.c_int, [C.c_int, C.c_int, P, P, SZ, SZ, P, SZ, P, P]),
+    "kernrt_cuda_safetensors_tensor": (C.c_int, [C.c_char_p, C.c_char_p, C.POINTER(StTensor)]),
+    "kernrt_cuda_prepare_embedding_file": (C.c_int, [P, C.c_char_p, C.c_char_p, C.c_int]),
 }
+
+# safetensors dtypes (kernrt_st_tensor.dtype)
+ST_F32, ST_BF16, ST_F16 = 0, 1, 2
+ST_DTYPES = {ST_F32: "F32", ST_BF16: "BF16", ST_F16: "F16"}
 
 NOALLOC_MAX_ROWS = 65536
 
@@ -169,6 +182,16 @@ def kernel_launches() -> int:
     n = C.c_uint64(0)
     _ok(load().kernrt_cuda_kernel_launches(C.byref(n)))
     return n.value
+
+
+def safetensors_tensor(path: str, name: str) -> dict:
+    """One tensor's entry in a safetensors file, read and validated on the host
+    as src/formats/safetensors.rs:161-257 does (no device involved): dtype name,
+    shape, and the payload's byte range in the file."""
+    t = StTensor()
+    _ok(load().kernrt_cuda_safetensors_tensor(os.fsencode(path), name.encode(), C.byref(t)))
+    return {"dtype": ST_DTYPES[t.dtype], "shape": tuple(t.shape[i] for i in range(min(t.rank, 8))),
+            "offset": t.file_offset, "bytes": t.bytes}
 
 
 def _ptr(a: np.ndarray):
@@ -224,6 +247,14 @@ class CudaBackend:
         _ok(self._lib.kernrt_cuda_prepare_embedding(self._ctx, kind, _ptr(data),
                                                     None if sc is None else _ptr(sc), vocab, dim))
         self._keep = (data, sc)
+
+    def prepare_embedding_file(self, path: str, name: str = "model.embed_tokens.weight",
+                               storage: int = 1) -> None:
+        """The token embedding straight from a safetensors file (hf.rs:141-191):
+        the stored payload goes to the device and is converted there into the
+        storage matrix_from_raw picks for ``storage`` (default bf16)."""
+        _ok(self._lib.kernrt_cuda_prepare_embedding_file(self._ctx, os.fsencode(path), name.encode(),
+                                                         int(storage)))
 
     # -- buffers ---------------------------------------------------------------------
     def alloc(self, length: int) -> int:

@@ -16,13 +16,18 @@
 // and returned as KERNRT_E_INVALID with a message.
 #include "../../include/kernrt_cuda.h"
 #include "kernels.cuh"
+#include "safetensors.h"
 
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cerrno>
 #include <cstdlib>
+#include <fcntl.h>
+#include <unistd.h>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <utility>
 #include <vector>
 
@@ -92,6 +97,10 @@ public:
             cudaFree(r.second);
         }
         for (auto e : events_) cudaEventDestroy(e);
+        for (int k = 0; k < 2; ++k) {
+            if (file_ev_[k]) cudaEventDestroy(file_ev_[k]);
+            cudaFreeHost(file_pin_[k]);
+        }
         cudaStreamSynchronize(h2d_);
         cudaStreamSynchronize(d2h_);
         for (auto &set : sets_) {
@@ -159,6 +168,178 @@ public:
         vocab_ = vocab;
         dim_ = dim;
         storage_ = kind_name(kind);
+    }
+
+    // Backend::prepare's embedding read from a safetensors file
+    // (hf.rs:141-191 take_matrix_raw / matrix_from_raw over the raw reader,
+    // safetensors.rs:129-135): the tensor's payload goes from the file to the
+    // device as stored (page-locked chunks, reads overlapped with the copies)
+    // and is converted there into the storage the reference's rules pick:
+    // bf16 bits as they are for bf16 storage; bf16 widened and quantised for
+    // block-aligned Q8_0 / Q8_0x4; f32 or f16 widened, then kept as f32,
+    // quantised for aligned Q8_0x4, and otherwise narrowed to bf16 by
+    // dropping the low half.
+    void prepare_embedding_file(const char *path, const char *name, int storage) {
+        if (!path || !name) fail(KERNRT_E_INVALID, "null path or tensor name");
+        if (storage < KERNRT_F32 || storage > KERNRT_Q8_0X4) fail(KERNRT_E_INVALID, "unknown storage kind");
+        StHeader h;
+        const std::string err = st_read_header(path, &h);
+        if (!err.empty()) fail(KERNRT_E_INVALID, err);
+        const auto it = h.tensors.find(name);
+        if (it == h.tensors.end()) fail(KERNRT_E_INVALID, "weight file is missing \"" + std::string(name) + "\"");
+        const StTensor &t = it->second;
+        if (t.shape.size() != 2) fail(KERNRT_E_INVALID, "a weight matrix was not rank 2");
+        const size_t vocab = (size_t)t.shape[0], dim = (size_t)t.shape[1];
+        if (vocab == 0 || dim == 0) fail(KERNRT_E_INVALID, "empty embedding table");
+        if (vocab > (size_t)INT32_MAX || dim > (1u << 24) || vocab * dim > (size_t)INT32_MAX * 4)
+            fail(KERNRT_E_INVALID, "embedding table too large");
+        const bool aligned_q8 = dim % 32 == 0, aligned_q8x4 = aligned_q8 && vocab % 4 == 0;
+        enum { BF16_BITS, TO_F32, TO_Q8, TO_Q8X4, TO_BF16 } route;
+        if (t.dtype == ST_BF16 && storage == KERNRT_BF16) route = BF16_BITS;
+        else if (t.dtype == ST_BF16 && storage == KERNRT_Q8_0 && aligned_q8) route = TO_Q8;
+        else if (t.dtype == ST_BF16 && storage == KERNRT_Q8_0X4 && aligned_q8x4) route = TO_Q8X4;
+        else if (storage == KERNRT_F32) route = TO_F32;
+        else if (storage == KERNRT_Q8_0X4 && aligned_q8x4) route = TO_Q8X4;
+        else route = TO_BF16;
+
+        flush();
+        check(cudaStreamSynchronize(stream_), "synchronize");
+        const size_t n = vocab * dim, nb = n / 32;
+        struct Dev {
+            void *p = nullptr;
+            ~Dev() { cudaFree(p); }
+        } payload, wide, table, scales, scales16;
+        check(cudaMalloc(&payload.p, std::max<size_t>(t.end - t.start, 16)), "cudaMalloc(file payload)");
+        read_file(path, h.data_offset + t.start, t.end - t.start, payload.p);
+        // f32 values of the table, where the route needs them
+        const float *f = nullptr;
+        if (route != BF16_BITS) {
+            if (t.dtype == ST_F32) {
+                f = static_cast<const float *>(payload.p);
+            } else {
+                check(cudaMalloc(&wide.p, n * sizeof(float)), "cudaMalloc(widened table)");
+                check(launch_widen_f32(t.dtype == ST_BF16 ? 1 : 2, static_cast<const uint16_t *>(payload.p),
+                                       static_cast<float *>(wide.p), n, stream_),
+                      "widen table");
+                f = static_cast<const float *>(wide.p);
+            }
+        }
+        int kind, src;
+        switch (route) {
+        case BF16_BITS:
+            std::swap(table.p, payload.p);
+            kind = KERNRT_BF16, src = SRC_BF16;
+            break;
+        case TO_F32:
+            if (f == payload.p) std::swap(table.p, payload.p);
+            else std::swap(table.p, wide.p);
+            kind = KERNRT_F32, src = SRC_F32;
+            break;
+        case TO_BF16:
+            check(cudaMalloc(&table.p, n * 2), "cudaMalloc(embedding)");
+            check(launch_narrow_bf16(f, static_cast<uint16_t *>(table.p), n, stream_), "narrow table");
+            kind = KERNRT_BF16, src = SRC_BF16;
+            break;
+        default:  // TO_Q8, TO_Q8X4: Q8Vec::quantize's blocks (quant.rs:544-557, 124-165)
+            check(cudaMalloc(&table.p, n), "cudaMalloc(embedding)");
+            check(cudaMalloc(&scales.p, nb * sizeof(float)), "cudaMalloc(embedding scales)");
+            check(cudaMalloc(&scales16.p, nb * sizeof(uint16_t)), "cudaMalloc(f16 scales)");
+            check(launch_quantize_q8(f, (int)vocab, (int)dim, static_cast<int8_t *>(table.p),
+                                     static_cast<float *>(scales.p), static_cast<uint16_t *>(scales16.p), stream_),
+                  "quantize table");
+            // Q8_0x4 keeps f16 scales and widens them on read (quant.rs:198-220, 764-769)
+            if (route == TO_Q8X4)
+                check(launch_f16_scales_to_f32(static_cast<const uint16_t *>(scales16.p),
+                                               static_cast<float *>(scales.p), nb, stream_),
+                      "widen f16 scales");
+            kind = route == TO_Q8 ? KERNRT_Q8_0 : KERNRT_Q8_0X4, src = SRC_Q8;
+            break;
+        }
+        check(cudaStreamSynchronize(stream_), "load embedding");
+        cudaFree(emb_data_);
+        cudaFree(emb_scales_);
+        emb_data_ = table.p;
+        emb_scales_ = static_cast<float *>(scales.p);
+        table.p = scales.p = nullptr;
+        emb_src_ = src;
+        emb_kind_ = kind;
+        vocab_ = vocab;
+        dim_ = dim;
+        storage_ = kind_name(kind);
+    }
+
+    // `bytes` of `path` from `offset` into device memory through two
+    // page-locked 64 MB chunks (allocated on the first load and kept): each
+    // chunk is filled by several reader threads while the other's copy runs.
+    static constexpr size_t kFileChunk = 64u << 20;
+
+    void read_file(const char *path, uint64_t offset, uint64_t bytes, void *dst) {
+        if (bytes == 0) return;
+        const int fd = ::open(path, O_RDONLY | O_CLOEXEC);
+        if (fd < 0) fail(KERNRT_E_INVALID, std::string("i/o error: ") + std::strerror(errno));
+        std::string why;
+        int code = KERNRT_E_CUDA;
+        for (int k = 0; k < 2 && why.empty(); ++k) {
+            if (!file_pin_[k] && cudaHostAlloc(&file_pin_[k], kFileChunk, cudaHostAllocDefault) != cudaSuccess) {
+                file_pin_[k] = nullptr;
+                why = "cudaHostAlloc(file staging)";
+            } else if (!file_ev_[k] && cudaEventCreateWithFlags(&file_ev_[k], cudaEventDisableTiming) != cudaSuccess) {
+                file_ev_[k] = nullptr;
+                why = "cudaEventCreate";
+            }
+        }
+        const unsigned hw = std::thread::hardware_concurrency();
+        const int nthreads = (int)std::max(1u, std::min(8u, hw ? hw : 1u));
+        // pread [lo, lo + len) of the file into p; false on a short read
+        auto fill = [&](char *p, uint64_t lo, size_t len) {
+            std::vector<std::thread> pool;
+            std::vector<char> ok((size_t)nthreads, 1);
+            const size_t part = (len + nthreads - 1) / nthreads;
+            for (int t = 0; t < nthreads; ++t) {
+                const size_t a = std::min(len, (size_t)t * part), z = std::min(len, a + part);
+                if (a >= z) break;
+                pool.emplace_back([&, t, a, z] {
+                    size_t got = a;
+                    while (got < z) {
+                        const ssize_t r = ::pread(fd, p + got, z - got, (off_t)(lo + got));
+                        if (r < 0 && errno == EINTR) continue;
+                        if (r <= 0) break;
+                        got += (size_t)r;
+                    }
+                    ok[(size_t)t] = got == z;
+                });
+            }
+            for (auto &th : pool) th.join();
+            for (char c : ok)
+                if (!c) return false;
+            return true;
+        };
+        bool used[2] = {false, false};
+        uint64_t done = 0;
+        for (int k = 0; why.empty() && done < bytes; k ^= 1) {
+            const size_t len = (size_t)std::min<uint64_t>(bytes - done, kFileChunk);
+            if (used[k] && cudaEventSynchronize(file_ev_[k]) != cudaSuccess) {
+                why = "file staging copy";
+                break;
+            }
+            if (!fill(static_cast<char *>(file_pin_[k]), offset + done, len)) {
+                why = "i/o error: short read of a tensor payload";
+                code = KERNRT_E_INVALID;
+                break;
+            }
+            if (cudaMemcpyAsync(static_cast<char *>(dst) + done, file_pin_[k], len, cudaMemcpyHostToDevice,
+                                stream_) != cudaSuccess ||
+                cudaEventRecord(file_ev_[k], stream_) != cudaSuccess) {
+                why = "upload of a tensor payload";
+                break;
+            }
+            used[k] = true;
+            done += len;
+        }
+        const cudaError_t e = cudaStreamSynchronize(stream_);
+        if (why.empty() && e != cudaSuccess) why = "upload of a tensor payload";
+        ::close(fd);
+        if (!why.empty()) fail(code, why);
     }
 
     // ---- buffers ------------------------------------------------------------
@@ -1324,6 +1505,8 @@ private:
     size_t vocab_ = 0, dim_ = 0;
     void *emb_data_ = nullptr;
     float *emb_scales_ = nullptr;
+    void *file_pin_[2] = {nullptr, nullptr};  // page-locked file staging, kept across loads
+    cudaEvent_t file_ev_[2] = {nullptr, nullptr};
     const char *storage_ = "f32";
     int *d_err_ = nullptr;
     int *h_err_ = nullptr;
@@ -1371,6 +1554,36 @@ static int guard(kernrt_cuda_ctx *ctx, F &&fn) {
 extern "C" {
 
 const char *kernrt_cuda_last_error(void) { return g_last_error.c_str(); }
+
+int kernrt_cuda_safetensors_tensor(const char *path, const char *name, kernrt_st_tensor *out) {
+    if (!path || !name || !out) {
+        g_last_error = "null argument";
+        return KERNRT_E_INVALID;
+    }
+    krt::StHeader h;
+    const std::string err = krt::st_read_header(path, &h);
+    if (!err.empty()) {
+        g_last_error = err;
+        return KERNRT_E_INVALID;
+    }
+    const auto it = h.tensors.find(name);
+    if (it == h.tensors.end()) {
+        g_last_error = "weight file is missing \"" + std::string(name) + "\"";
+        return KERNRT_E_INVALID;
+    }
+    const krt::StTensor &t = it->second;
+    std::memset(out, 0, sizeof *out);
+    out->dtype = t.dtype;
+    out->rank = (int)t.shape.size();
+    for (size_t i = 0; i < t.shape.size() && i < 8; ++i) out->shape[i] = t.shape[i];
+    out->file_offset = h.data_offset + t.start;
+    out->bytes = t.end - t.start;
+    return KERNRT_OK;
+}
+
+int kernrt_cuda_prepare_embedding_file(kernrt_cuda_ctx *ctx, const char *path, const char *name, int storage) {
+    return guard(ctx, [&](krt::Backend &b) { b.prepare_embedding_file(path, name, storage); });
+}
 
 int kernrt_cuda_kernel_launches(uint64_t *count) {
     if (!count) {

@@ -2341,6 +2341,36 @@ __device__ __forceinline__ float f16_scale_to_f32(uint16_t bits) {
     return __uint_as_float(sign | ((exp + 112u) << 23) | (mant << 13));
 }
 
+// src/formats/safetensors.rs:365-385 f16_to_f32_local: IEEE binary16 to
+// binary32.  A subnormal m * 2^-24 (m < 1024) is exact in f32, which is what
+// the reference's normalising loop produces; NaN keeps its payload bits.
+__device__ __forceinline__ float f16_to_f32_exact(uint16_t bits) {
+    const uint32_t sign = (uint32_t)(bits >> 15) << 31;
+    const uint32_t exp = (bits >> 10) & 0x1fu, mant = bits & 0x3ffu;
+    if (exp == 0) return __uint_as_float(sign | __float_as_uint(__uint2float_rn(mant) * 0x1p-24f));
+    if (exp == 0x1f) return __uint_as_float(sign | 0x7f800000u | (mant << 13));
+    return __uint_as_float(sign | ((exp + 112u) << 23) | (mant << 13));
+}
+
+__global__ void __launch_bounds__(kThreads) k_widen_f32(int dtype, const uint16_t *__restrict__ src,
+                                                        float *__restrict__ dst, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = dtype == 1 ? bf16f(src[i]) : f16_to_f32_exact(src[i]);
+}
+
+// hf.rs:182-188: (v.to_bits() >> 16) as u16, truncation (not rounding)
+__global__ void __launch_bounds__(kThreads) k_narrow_bf16(const float *__restrict__ src, uint16_t *__restrict__ dst,
+                                                          size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = (uint16_t)(__float_as_uint(src[i]) >> 16);
+}
+
+__global__ void __launch_bounds__(kThreads) k_f16_scales_to_f32(const uint16_t *__restrict__ src,
+                                                                float *__restrict__ dst, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = f16_scale_to_f32(src[i]);
+}
+
 __global__ void __launch_bounds__(kThreads) k_q8x4_to_row_major(const uint8_t *__restrict__ blocks,
                                                                 int out_dim, int in_dim,
                                                                 int8_t *quants, float *scales) {
@@ -2892,6 +2922,25 @@ cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes,
     }
     k_quantize_q8<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(x, rows, dim, codes, scales,
                                                                               scales16);
+    return launched();
+}
+
+cudaError_t launch_widen_f32(int dtype, const uint16_t *src, float *dst, size_t n, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    if (dtype != 1 && dtype != 2) return cudaErrorInvalidValue;
+    k_widen_f32<<<stream_grid(n), kThreads, 0, s>>>(dtype, src, dst, n);
+    return launched();
+}
+
+cudaError_t launch_narrow_bf16(const float *src, uint16_t *dst, size_t n, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    k_narrow_bf16<<<stream_grid(n), kThreads, 0, s>>>(src, dst, n);
+    return launched();
+}
+
+cudaError_t launch_f16_scales_to_f32(const uint16_t *src, float *dst, size_t n, cudaStream_t s) {
+    if (n == 0) return cudaSuccess;
+    k_f16_scales_to_f32<<<stream_grid(n), kThreads, 0, s>>>(src, dst, n);
     return launched();
 }
 

@@ -90,6 +90,13 @@ cudaError_t launch_lfm2_conv_block(const float *bcx, const float *w, float *ring
                                    int rows, int dim, int k, cudaStream_t s);
 cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes, float *scales,
                                uint16_t *scales16, cudaStream_t s);
+// Conversions for tables loaded from files (safetensors.rs / hf.rs): widen
+// n bf16 (dtype 1) or f16 (dtype 2) patterns to f32; narrow f32 to bf16 by
+// dropping the low half (hf.rs:182-188); widen f16 block scales the way
+// Q8_0x4 reads them (quant.rs:764-769).
+cudaError_t launch_widen_f32(int dtype, const uint16_t *src, float *dst, size_t n, cudaStream_t s);
+cudaError_t launch_narrow_bf16(const float *src, uint16_t *dst, size_t n, cudaStream_t s);
+cudaError_t launch_f16_scales_to_f32(const uint16_t *src, float *dst, size_t n, cudaStream_t s);
 cudaError_t launch_q8x4_to_row_major(const uint8_t *blocks, int out_dim, int in_dim,
                                      int8_t *quants, float *scales, cudaStream_t s);
 

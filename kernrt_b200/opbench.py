@@ -217,6 +217,10 @@ def run(reps: int, only: str | None = None):
     if B.want("project", "logits", "attention", "kv_write"):
         contractions(B)
 
+    # --- loading the token embedding from a safetensors file (hf.rs:141-191)
+    if B.want("prepare_embedding_file"):
+        load_table(B)
+
     # --- the chain on every workload
     for wk in (W.SMOLLM2_135M, W.SMOLLM2_17B_PREFILL, W.QWEN3_06B_Q8, W.LFM2_700M, W.SMOLLM2_17B_65K):
         if B.want(f"chain: {wk.name}"):
@@ -298,6 +302,39 @@ def model_decode(B, n_layers: int = 24, pos: int = 511, samples: int = 50):
                    "ms": None, "us_p10": times[len(times) // 10] * 1e3, "us_median": times[len(times) // 2] * 1e3,
                    "gbs": None, "frac": None, "launches": None,
                    "note": f"host wall clock, {samples} samples; {1e3 / times[len(times) // 2]:.0f} tokens/s"})
+
+
+def load_table(B, vocab: int = 49152, dim: int = 2048, samples: int = 5):
+    """SmolLM2-1.7B's token embedding (bf16) read from a safetensors file into
+    bf16 storage (bits handed over) and into Q8_0 (widened and quantised on the
+    device).  Host wall clock per call with the file in the page cache."""
+    import tempfile
+
+    rng = np.random.default_rng(5)
+    bits = (rng.standard_normal((vocab, dim), dtype=np.float32) * np.float32(0.02)).view(np.uint32)
+    table = (bits >> np.uint32(16)).astype(np.uint16)
+    header = json.dumps({"model.embed_tokens.weight": {"dtype": "BF16", "shape": [vocab, dim],
+                                                       "data_offsets": [0, table.nbytes]}}).encode()
+    nbytes = table.nbytes
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "model.safetensors")
+        with open(path, "wb") as f:
+            f.write(len(header).to_bytes(8, "little") + header)
+            f.write(table.tobytes())
+        del table, bits
+        for storage, label in ((BF16, "bf16 (bits handed over)"),
+                               (Q8_0, "q8_0 (widened and quantised on the device)")):
+            B.b.prepare_embedding_file(path, "model.embed_tokens.weight", storage)
+            times = []
+            for _ in range(samples):
+                t0 = time.perf_counter()
+                B.b.prepare_embedding_file(path, "model.embed_tokens.weight", storage)
+                times.append(time.perf_counter() - t0)
+            times.sort()
+            ms = times[len(times) // 2] * 1e3
+            B.rows.append({"name": f"prepare_embedding_file {vocab}x{dim} bf16 file -> {label}", "ms": ms,
+                           "gbs": nbytes / (ms * 1e-3) / 1e9, "frac": None, "launches": 0,
+                           "note": f"host wall clock, {samples} calls, file in the page cache; GB/s of file bytes"})
 
 
 # FP32 multiply + add pairs per second a B200 issues on its CUDA cores

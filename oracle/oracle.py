@@ -179,6 +179,75 @@ def q8_0x4_to_row_major(blocks: np.ndarray, out_dim: int, in_dim: int):
     return q, s
 
 
+# --- safetensors payloads and the HF loaders' storage rules ------------------------
+
+def st_f16_to_f32(bits) -> np.ndarray:
+    """src/formats/safetensors.rs:365-385 f16_to_f32_local, element by element:
+    zero keeps its sign; a subnormal mantissa is shifted left until the
+    implicit bit appears, the exponent counting down from 127 - 15 + 1; Inf and
+    NaN keep their mantissa bits; normals rebias the exponent."""
+    b = np.asarray(bits, dtype=np.uint16).ravel()
+    out = np.zeros(b.size, np.uint32)
+    for i, v in enumerate(b.tolist()):
+        sign = (v >> 15) << 31
+        exponent = (v >> 10) & 0x1F
+        mantissa = v & 0x3FF
+        if exponent == 0 and mantissa == 0:
+            w = sign
+        elif exponent == 0:
+            e = 127 - 15 + 1
+            while mantissa & 0x400 == 0:
+                mantissa <<= 1
+                e -= 1
+            w = sign | (e << 23) | ((mantissa & 0x3FF) << 13)
+        elif exponent == 0x1F:
+            w = sign | 0x7F800000 | (mantissa << 13)
+        else:
+            w = sign | ((exponent + (127 - 15)) << 23) | (mantissa << 13)
+        out[i] = w
+    return out.view(np.float32).reshape(np.shape(bits))
+
+
+def st_widen(dtype: str, raw: np.ndarray) -> np.ndarray:
+    """hf.rs:97-107 widen over safetensors.rs:280-300 decode: F32 as is, BF16
+    as the top half of an f32, F16 through f16_to_f32_local."""
+    if dtype == "F32":
+        return f32(raw)
+    if dtype == "BF16":
+        return bf16_to_f32(raw)
+    return st_f16_to_f32(raw)
+
+
+def table_from_raw(dtype: str, raw: np.ndarray, storage: int):
+    """hf.rs:151-191 matrix_from_raw for a [vocab, dim] payload, returned as what
+    embed_rows reads: (kind, data, scales).  A bf16 payload is handed over as
+    it is for bf16 storage; bf16 is quantised for block-aligned Q8_0 / Q8_0x4;
+    otherwise the payload is widened and kept f32, quantised for aligned
+    Q8_0x4, or narrowed to bf16 by dropping the low half.  Q8_0x4 reads back
+    de-interleaved with its f16 scales widened (quant.rs:198-220)."""
+    vocab, dim = raw.shape
+    aligned_q8 = dim % Q8_BLOCK == 0
+    aligned_q8x4 = aligned_q8 and vocab % 4 == 0
+
+    def q8x4(w):
+        q, s = q8_0x4_to_row_major(q8_0x4_pack(w), vocab, dim)
+        return Q8_0, q, s
+
+    if dtype == "BF16" and storage == BF16:
+        return BF16, np.ascontiguousarray(raw, dtype=np.uint16), None
+    if dtype == "BF16" and storage == Q8_0 and aligned_q8:
+        q, s = q8_0_from_f32(st_widen(dtype, raw))
+        return Q8_0, q, s
+    if dtype == "BF16" and storage == Q8_0X4 and aligned_q8x4:
+        return q8x4(st_widen(dtype, raw))
+    w = st_widen(dtype, raw)
+    if storage == F32:
+        return F32, w, None
+    if storage == Q8_0X4 and aligned_q8x4:
+        return q8x4(w)
+    return BF16, (np.ascontiguousarray(w).view(np.uint32) >> np.uint32(16)).astype(np.uint16), None
+
+
 # --- row ops ---------------------------------------------------------------------
 
 def embed_rows(kind: int, data: np.ndarray, scales, vocab: int, dim: int, tokens) -> np.ndarray:

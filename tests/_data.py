@@ -85,3 +85,24 @@ def q8_table_fast(vocab: int, dim: int, seed: int):
     codes = rng.integers(-127, 128, size=(vocab, dim), dtype=np.int8)
     scales = rng.uniform(1e-4, 1e-2, size=(vocab, dim // 32)).astype(np.float32)
     return codes, scales
+
+
+def safetensors_bytes(tensors, metadata=None) -> bytes:
+    """A safetensors image (src/formats/safetensors.rs:1-16): u64 LE header
+    length, the JSON header, then the payloads in the given order.  `tensors`
+    is a list of (name, dtype, shape, payload_bytes)."""
+    import json
+
+    header, data = {}, b""
+    for name, dtype, shape, payload in tensors:
+        header[name] = {"dtype": dtype, "shape": list(shape), "data_offsets": [len(data), len(data) + len(payload)]}
+        data += payload
+    if metadata is not None:
+        header["__metadata__"] = metadata
+    hb = json.dumps(header).encode()
+    return len(hb).to_bytes(8, "little") + hb + data
+
+
+def safetensors_raw(header_text: bytes, data: bytes = b"") -> bytes:
+    """A safetensors image around an exact header text (for malformed headers)."""
+    return len(header_text).to_bytes(8, "little") + header_text + data
