@@ -42,7 +42,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="kernrt", choices=["kernrt", "reference"])
     p.add_argument("--e2e-steps", type=int, default=3)
