@@ -139,6 +139,17 @@ def test_chain_ragged_shapes(gpu, oracle, rows, dim, q, kv, head, hidden):
     check(gpu_chain(gpu, wl, d), oracle_chain(oracle, wl, d), True)
 
 
+@pytest.mark.parametrize("rows,dim", [(300, 1024), (5, 96), (1000, 2048), (170, 544)])
+def test_chain_x_input_with_final_q8(gpu, oracle, rows, dim):
+    """An x input (no embed) with the final RMSNorm + Q8_0 and a residual: the
+    f32 norm stage sums x and x + resid and writes xb, x + resid and the codes
+    (the column-tiled pipeline, or a CTA per row for a few rows)."""
+    wl = W.Workload("x_fq", 64, dim, 4, 2, 16, 64, 1e4, 1e-6, "none", rows=rows, seq_len=64, qk_norm=False,
+                    final_q8=True)
+    d = make_inputs(wl, 1010 + rows)
+    check(gpu_chain(gpu, wl, d), oracle_chain(oracle, wl, d), True)
+
+
 def test_chain_bad_token_reports_and_recovers(gpu, oracle):
     wl = W.Workload("tiny", 16, 64, 2, 2, 32, 64, 1e4, 1e-5, "bf16", rows=8, seq_len=8)
     d = make_inputs(wl, 1004)
