@@ -81,6 +81,16 @@ int kernrt_cuda_stream(kernrt_cuda_ctx *ctx, void **stream);
 int kernrt_cuda_prepare_embedding(kernrt_cuda_ctx *ctx, int kind, const void *data,
                                   const float *scales, size_t vocab, size_t dim);
 
+/* Self-test of the bounded waits (no counterpart in the reference: its CPU
+ * backend has no device pipelines).  Every spin-wait in these kernels gives
+ * up after a cycle limit, sets the device error word and returns, so a stuck
+ * pipeline surfaces as KERNRT_E_DEVICE ("... timed out") at the next barrier
+ * instead of hanging the GPU.  This runs that wait alone on an mbarrier phase
+ * that nothing completes (complete = 0) for at most `cycles` SM cycles
+ * (<= 2^31), or on one it completes first (complete = 1); the first returns
+ * KERNRT_E_DEVICE and leaves the context usable, the second returns 0. */
+int kernrt_cuda_selftest_wait(kernrt_cuda_ctx *ctx, uint64_t cycles, int complete);
+
 /* --- Weights from a safetensors file (src/formats/safetensors.rs) ----------
  * A tensor's entry in a safetensors file, read and checked on the host only
  * (no device): the header is validated as read_with does

@@ -138,6 +138,7 @@ SIGNATURES = {
     "kernrt_cuda_embed_rows_noalloc": (C.c_int, [C.c_int, C.c_int, P, P, SZ, SZ, P, SZ, P, P]),
     "kernrt_cuda_safetensors_tensor": (C.c_int, [C.c_char_p, C.c_char_p, C.POINTER(StTensor)]),
     "kernrt_cuda_prepare_embedding_file": (C.c_int, [P, C.c_char_p, C.c_char_p, C.c_int]),
+    "kernrt_cuda_selftest_wait": (C.c_int, [P, C.c_uint64, C.c_int]),
 }
 
 # safetensors dtypes (kernrt_st_tensor.dtype)
@@ -255,6 +256,11 @@ class CudaBackend:
         storage matrix_from_raw picks for ``storage`` (default bf16)."""
         _ok(self._lib.kernrt_cuda_prepare_embedding_file(self._ctx, os.fsencode(path), name.encode(),
                                                          int(storage)))
+
+    def selftest_wait(self, cycles: int, complete: bool) -> None:
+        """The kernels' bounded wait run alone: raises KernrtCudaError
+        (E_DEVICE, "... timed out") when the phase is left incomplete."""
+        _ok(self._lib.kernrt_cuda_selftest_wait(self._ctx, int(cycles), int(bool(complete))))
 
     # -- buffers ---------------------------------------------------------------------
     def alloc(self, length: int) -> int:

@@ -410,6 +410,16 @@ public:
         }
     }
 
+    // The pipelines' bounded wait exercised on its own: after `cycles` SM
+    // cycles without the phase completing, the error word reports a timeout,
+    // which barrier() turns into KERNRT_E_DEVICE; the context stays usable.
+    void selftest_wait(uint64_t cycles, int complete) {
+        if (cycles > (1ull << 31)) fail(KERNRT_E_INVALID, "wait limit above 2^31 cycles");
+        flush();
+        launch_or_fail(launch_wait_selftest(d_err_, (long long)cycles, complete ? 1 : 0, stream_), "wait self-test");
+        barrier();
+    }
+
     // ---- Backend::embed (deferred, coalesced) --------------------------------
     void embed(size_t token, kernrt_buf out, size_t offset) {
         if (emb_kind_ < 0) fail(KERNRT_E_STATE, "prepare() runs before compute");
@@ -1579,6 +1589,10 @@ int kernrt_cuda_safetensors_tensor(const char *path, const char *name, kernrt_st
     out->file_offset = h.data_offset + t.start;
     out->bytes = t.end - t.start;
     return KERNRT_OK;
+}
+
+int kernrt_cuda_selftest_wait(kernrt_cuda_ctx *ctx, uint64_t cycles, int complete) {
+    return guard(ctx, [&](krt::Backend &b) { b.selftest_wait(cycles, complete); });
 }
 
 int kernrt_cuda_prepare_embedding_file(kernrt_cuda_ctx *ctx, const char *path, const char *name, int storage) {

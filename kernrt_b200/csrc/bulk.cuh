@@ -71,13 +71,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the phase with this parity to complete, for at most ~1 s of SM
-// clock; false if it did not.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+// Waits for the phase with this parity to complete, for at most `limit` SM
+// cycles (~1 s by default); false if it did not.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, long long limit = 1ll << 31) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity))
-        if (clock64() - t0 > (1ll << 31)) return false;
+        if (clock64() - t0 > limit) return false;
     return true;
 }
 

@@ -2341,6 +2341,20 @@ __device__ __forceinline__ float f16_scale_to_f32(uint16_t bits) {
     return __uint_as_float(sign | ((exp + 112u) << 23) | (mant << 13));
 }
 
+// Self-test of the bounded waits the pipelines use: one thread waits on an
+// mbarrier phase that nothing completes for at most `limit` SM cycles and
+// reports ERR_TIMEOUT through the error word, as a pipeline's wait would;
+// with `complete` set it first completes the phase itself and the wait ends
+// at once.  No copy is in flight, so giving up leaves nothing behind.
+__global__ void k_wait_selftest(int *err, long long limit, int complete) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+    if (complete) mbar_arrive(&bar);
+    if (!mbar_wait_bounded(&bar, 0u, limit)) set_err(err, ERR_TIMEOUT);
+}
+
 // src/formats/safetensors.rs:365-385 f16_to_f32_local: IEEE binary16 to
 // binary32.  A subnormal m * 2^-24 (m < 1024) is exact in f32, which is what
 // the reference's normalising loop produces; NaN keeps its payload bits.
@@ -2922,6 +2936,11 @@ cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes,
     }
     k_quantize_q8<<<grid_for((size_t)rows * 32, kThreads), kThreads, 0, s>>>(x, rows, dim, codes, scales,
                                                                               scales16);
+    return launched();
+}
+
+cudaError_t launch_wait_selftest(int *err, long long limit, int complete, cudaStream_t s) {
+    k_wait_selftest<<<1, 32, 0, s>>>(err, limit, complete);
     return launched();
 }
 

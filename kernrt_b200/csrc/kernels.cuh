@@ -95,6 +95,9 @@ cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes,
 // dropping the low half (hf.rs:182-188); widen f16 block scales the way
 // Q8_0x4 reads them (quant.rs:764-769).
 cudaError_t launch_widen_f32(int dtype, const uint16_t *src, float *dst, size_t n, cudaStream_t s);
+// The bounded mbarrier wait run out on purpose (complete = 0) or satisfied
+// (complete = 1), reporting through `err` like the pipelines' waits.
+cudaError_t launch_wait_selftest(int *err, long long limit, int complete, cudaStream_t s);
 cudaError_t launch_narrow_bf16(const float *src, uint16_t *dst, size_t n, cudaStream_t s);
 cudaError_t launch_f16_scales_to_f32(const uint16_t *src, float *dst, size_t n, cudaStream_t s);
 cudaError_t launch_q8x4_to_row_major(const uint8_t *blocks, int out_dim, int in_dim,
