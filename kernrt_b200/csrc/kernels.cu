@@ -1209,7 +1209,7 @@ struct RowsShape {
     static constexpr int writers = threads / 32 * 3 / 4;  // the warps off sub-partition 0
 };
 
-// f32 x rows with the three roles decoupled: one 16-warp CTA per SM, its
+// f32 x rows with the three roles decoupled: one CTA per SM (ColsShape), its
 // rows in groups of G, a group's rows cut into T column tiles of TC columns
 // (a unit = one tile of one group).
 //   warp 4    issues unit u's bulk copies (lane r: row r's x tile, and its
@@ -1222,7 +1222,7 @@ struct RowsShape {
 //   writers   (the warps off warp 0's sub-partition) take group after group
 //             once its scales are stored and write xb, x (+ resid) or the
 //             Q8_0 codes from x (and resid) loaded from L2, where the ring's
-//             copies left them a group earlier: eight 16-byte loads in flight
+//             copies left them a group earlier: U 16-byte loads in flight
 //             per lane, no barrier between tiles.
 // mbarriers connect the roles (full/empty per slot, ready/freed per scale
 // buffer), so each runs at its own rate: the summing lanes' chains, the copy
