@@ -34,16 +34,20 @@ constexpr int kPad = 4;   // floats of padding per staged k-row
 // A CTA computes a BM x 64 tile of y with 16 x 16 threads, TM rows x 4 outputs
 // each.  Per chunk of 32 k it stages x[rows, k] and the decoded W[outputs, k]
 // transposed in shared memory; every accumulator then takes the chunk's k in
-// order, so each output is the reference's sequential dot.  k past in_dim is
-// staged as zeros: 0*0 added to a partial sum that starts at +0 and never
-// becomes -0 leaves it unchanged.  Requires in_dim % 8 == 0 (% 32 for Q8_0).
+// order, so each output is the reference's sequential dot.  Two staging
+// buffers: chunk k + 1 is loaded from global memory into registers before
+// chunk k's products and stored after them, so the loads' latency overlaps
+// the arithmetic.  k past in_dim is staged as zeros: 0*0 added to a partial
+// sum that starts at +0 and never becomes -0 leaves it unchanged.  Requires
+// in_dim % 8 == 0 (% 32 for Q8_0).
 template <int SRC, int TM>
 __global__ void __launch_bounds__(256) k_project(const void *__restrict__ w, const float *__restrict__ wsc,
                                                  int out_dim, int in_dim, const float *__restrict__ x, int rows,
                                                  float *__restrict__ y) {
     constexpr int BM = 16 * TM;
-    __shared__ __align__(16) float xs[kBK][BM + kPad];
-    __shared__ __align__(16) float ws[kBK][kBN + kPad];
+    constexpr int XV = (BM * (kBK / 4) + 255) / 256;  // x float4 per thread per chunk
+    __shared__ __align__(16) float xs[2][kBK][BM + kPad];
+    __shared__ __align__(16) float ws[2][kBK][kBN + kPad];
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int o0 = blockIdx.x * kBN, r0 = blockIdx.y * BM;
     float acc[TM][4];
@@ -52,80 +56,116 @@ __global__ void __launch_bounds__(256) k_project(const void *__restrict__ w, con
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
 
-    for (int k0 = 0; k0 < in_dim; k0 += kBK) {
-        // x chunk: BM rows x 32 k as float4, stored k-major
-        for (int idx = tid; idx < BM * (kBK / 4); idx += 256) {
-            const int r = idx >> 3, c = (idx & 7) << 2;
-            float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (r0 + r < rows && k0 + c < in_dim)
-                v = __ldg(reinterpret_cast<const float4 *>(x + (size_t)(r0 + r) * in_dim + k0 + c));
-            xs[c][r] = v.x;
-            xs[c + 1][r] = v.y;
-            xs[c + 2][r] = v.z;
-            xs[c + 3][r] = v.w;
+    // one chunk's global loads, held in registers until they are staged
+    float4 xr[XV];
+    uint4 wt = make_uint4(0u, 0u, 0u, 0u);
+    float wsc_r = 0.0f;
+    float4 wf[2];
+    auto load = [&](int k0) {
+#pragma unroll
+        for (int v = 0; v < XV; ++v) {
+            const int idx = tid + 256 * v, r = idx >> 3, c = (idx & 7) << 2;
+            xr[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (idx < BM * (kBK / 4) && r0 + r < rows && k0 + c < in_dim)
+                xr[v] = __ldg(reinterpret_cast<const float4 *>(x + (size_t)(r0 + r) * in_dim + k0 + c));
         }
-        // W chunk: 64 outputs x 32 k, decoded as Matrix::decode_row does
         if constexpr (SRC == SRC_BF16) {
             const int o = tid >> 2, c = (tid & 3) << 3;
-            uint4 t = make_uint4(0u, 0u, 0u, 0u);
+            wt = make_uint4(0u, 0u, 0u, 0u);
             if (o0 + o < out_dim && k0 + c < in_dim)
-                t = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(w) +
-                                                          (size_t)(o0 + o) * in_dim + k0 + c));
-            const uint32_t p[4] = {t.x, t.y, t.z, t.w};
+                wt = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(w) + (size_t)(o0 + o) * in_dim +
+                                                           k0 + c));
+        } else if constexpr (SRC == SRC_Q8) {
+            const int o = tid >> 1, c = (tid & 1) << 4;
+            wt = make_uint4(0u, 0u, 0u, 0u);
+            wsc_r = 0.0f;
+            if (tid < 128 && o0 + o < out_dim && k0 + c < in_dim) {
+                wt = __ldg(reinterpret_cast<const uint4 *>(static_cast<const int8_t *>(w) + (size_t)(o0 + o) * in_dim +
+                                                           k0 + c));
+                wsc_r = __ldg(wsc + (size_t)(o0 + o) * (in_dim >> 5) + (k0 >> 5));
+            }
+        } else {
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                const int idx = tid + 256 * v, o = idx >> 3, c = (idx & 7) << 2;
+                wf[v] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (o0 + o < out_dim && k0 + c < in_dim)
+                    wf[v] = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(w) +
+                                                                   (size_t)(o0 + o) * in_dim + k0 + c));
+            }
+        }
+    };
+    // the held chunk into staging buffer b: x k-major, W decoded as
+    // Matrix::decode_row does, k-major
+    auto stage = [&](int b) {
+#pragma unroll
+        for (int v = 0; v < XV; ++v) {
+            const int idx = tid + 256 * v, r = idx >> 3, c = (idx & 7) << 2;
+            if (idx < BM * (kBK / 4)) {
+                xs[b][c][r] = xr[v].x;
+                xs[b][c + 1][r] = xr[v].y;
+                xs[b][c + 2][r] = xr[v].z;
+                xs[b][c + 3][r] = xr[v].w;
+            }
+        }
+        if constexpr (SRC == SRC_BF16) {
+            const int o = tid >> 2, c = (tid & 3) << 3;
+            const uint32_t p[4] = {wt.x, wt.y, wt.z, wt.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                ws[c + 2 * e][o] = bf16f(p[e] & 0xffffu);
-                ws[c + 2 * e + 1][o] = bf16f(p[e] >> 16);
+                ws[b][c + 2 * e][o] = bf16f(p[e] & 0xffffu);
+                ws[b][c + 2 * e + 1][o] = bf16f(p[e] >> 16);
             }
         } else if constexpr (SRC == SRC_Q8) {
             if (tid < 128) {
                 const int o = tid >> 1, c = (tid & 1) << 4;
-                uint4 t = make_uint4(0u, 0u, 0u, 0u);
-                float sc = 0.0f;
-                if (o0 + o < out_dim && k0 + c < in_dim) {
-                    t = __ldg(reinterpret_cast<const uint4 *>(static_cast<const int8_t *>(w) +
-                                                              (size_t)(o0 + o) * in_dim + k0 + c));
-                    sc = __ldg(wsc + (size_t)(o0 + o) * (in_dim >> 5) + (k0 >> 5));
-                }
-                const uint32_t p[4] = {t.x, t.y, t.z, t.w};
+                const uint32_t p[4] = {wt.x, wt.y, wt.z, wt.w};
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
-                    ws[c + e][o] = mul_rn((float)(int8_t)((p[e >> 2] >> (8 * (e & 3))) & 0xffu), sc);
+                    ws[b][c + e][o] = mul_rn((float)(int8_t)((p[e >> 2] >> (8 * (e & 3))) & 0xffu), wsc_r);
             }
         } else {
-            for (int idx = tid; idx < kBN * (kBK / 4); idx += 256) {
-                const int o = idx >> 3, c = (idx & 7) << 2;
-                float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (o0 + o < out_dim && k0 + c < in_dim)
-                    v = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(w) +
-                                                               (size_t)(o0 + o) * in_dim + k0 + c));
-                ws[c][o] = v.x;
-                ws[c + 1][o] = v.y;
-                ws[c + 2][o] = v.z;
-                ws[c + 3][o] = v.w;
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                const int idx = tid + 256 * v, o = idx >> 3, c = (idx & 7) << 2;
+                ws[b][c][o] = wf[v].x;
+                ws[b][c + 1][o] = wf[v].y;
+                ws[b][c + 2][o] = wf[v].z;
+                ws[b][c + 3][o] = wf[v].w;
             }
         }
-        __syncthreads();
+    };
+
+    load(0);
+    stage(0);
+    __syncthreads();
+    int b = 0;
+    for (int k0 = 0; k0 < in_dim; k0 += kBK) {
+        const bool more = k0 + kBK < in_dim;
+        if (more) load(k0 + kBK);
 #pragma unroll 8
         for (int kk = 0; kk < kBK; ++kk) {
             float a[TM];
             if constexpr (TM == 4) {
-                const float4 t = *reinterpret_cast<const float4 *>(&xs[kk][ty * 4]);
+                const float4 t = *reinterpret_cast<const float4 *>(&xs[b][kk][ty * 4]);
                 a[0] = t.x; a[1] = t.y; a[2] = t.z; a[3] = t.w;
             } else {
 #pragma unroll
-                for (int i = 0; i < TM; ++i) a[i] = xs[kk][ty * TM + i];
+                for (int i = 0; i < TM; ++i) a[i] = xs[b][kk][ty * TM + i];
             }
-            const float4 b = *reinterpret_cast<const float4 *>(&ws[kk][tx * 4]);
+            const float4 bv = *reinterpret_cast<const float4 *>(&ws[b][kk][tx * 4]);
 #pragma unroll
             for (int i = 0; i < TM; ++i) {
-                acc[i][0] = add_rn(acc[i][0], mul_rn(b.x, a[i]));
-                acc[i][1] = add_rn(acc[i][1], mul_rn(b.y, a[i]));
-                acc[i][2] = add_rn(acc[i][2], mul_rn(b.z, a[i]));
-                acc[i][3] = add_rn(acc[i][3], mul_rn(b.w, a[i]));
+                acc[i][0] = add_rn(acc[i][0], mul_rn(bv.x, a[i]));
+                acc[i][1] = add_rn(acc[i][1], mul_rn(bv.y, a[i]));
+                acc[i][2] = add_rn(acc[i][2], mul_rn(bv.z, a[i]));
+                acc[i][3] = add_rn(acc[i][3], mul_rn(bv.w, a[i]));
             }
         }
+        // the other buffer was last read before the previous barrier
+        if (more) stage(b ^ 1);
         __syncthreads();
+        b ^= 1;
     }
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
