@@ -644,10 +644,14 @@ public:
             check(cudaMalloc(&att_scratch_, need), "cudaMalloc(attention scratch)");
             att_scratch_bytes_ = need;
         }
+        // windows that differ only in their last slot map positions alike
+        bool shared_map = true;
+        for (size_t i = 1; i < n_windows && shared_map; ++i)
+            shared_map = win[4 * i] == win[0] && win[4 * i + 2] == win[2] && win[4 * i + 3] == win[3];
         const int32_t *d = static_cast<const int32_t *>(stage(win.data(), win.size() * sizeof(int32_t)));
         launch_or_fail(launch_attention(f(qb), f(ob), f(ab), kc_, vc_, d, (int)n_windows, (int)n_heads, (int)kv_mul,
                                         (int)head_size, (int)kv_dim, (int)seq_len, layer * seq_len * kv_dim,
-                                        (int)max_count, att_scratch_, stream_),
+                                        (int)max_count, att_scratch_, shared_map, stream_),
                        "attention");
     }
 

@@ -627,6 +627,80 @@ __global__ void __launch_bounds__(128) k_att_scores(const float *__restrict__ q,
     raw[((size_t)row * n_heads + h) * stride + i] = mul_rn(d, scale);
 }
 
+// Scores for windows that map window positions to the same cache slots (the
+// rows of one sequence: the same shared range and start, their own last
+// slot): a CTA takes 16 rows x 64 positions of one head.  The 64 key rows are
+// staged once in shared memory and serve all 16 rows, and each thread runs
+// eight dots (eight rows, one position), each over head_size in order
+// (reference.rs:439-446), so the eight chains overlap.  Grid (row blocks,
+// position blocks, heads); blocks past every row's window exit at once.
+constexpr int kScRows = 16, kScPos = 64;
+
+__global__ void __launch_bounds__(128) k_att_scores_rows(const float *__restrict__ q, float *__restrict__ raw,
+                                                         const float *__restrict__ kc,
+                                                         const int32_t *__restrict__ win, int n_rows, int n_heads,
+                                                         int kv_mul, int head_size, int kv_dim, int stride,
+                                                         size_t loff) {
+    extern __shared__ __align__(16) float scs[];
+    const int hs = head_size + 4;                 // row stride: 16-byte reads of one column in distinct banks
+    float *ks = scs;                              // [kScPos][hs]
+    float *qs = scs + kScPos * hs;                // [kScRows][hs]
+    __shared__ int cnt[kScRows];
+    const int r0 = blockIdx.x * kScRows, p0 = blockIdx.y * kScPos, h = blockIdx.z;
+    const int tid = threadIdx.x;
+    const int nr = min(kScRows, n_rows - r0);
+    if (tid < kScRows) {
+        int c = 0;
+        if (tid < nr) {
+            const int32_t *w = win + 4 * (r0 + tid);
+            c = (w[3] - w[2]) + w[1] - w[0] + 1;
+        }
+        cnt[tid] = c;
+    }
+    __syncthreads();
+    int maxc = 0;
+    for (int r = 0; r < nr; ++r) maxc = max(maxc, cnt[r]);
+    if (p0 >= maxc) return;
+    const int np = min(kScPos, maxc - p0);
+    const int32_t *w0 = win + 4 * r0;  // every row of the launch maps positions alike
+    const int h4 = head_size >> 2;
+    for (int idx = tid; idx < np * h4; idx += 128) {
+        const int p = idx / h4, e = (idx - p * h4) << 2;
+        *reinterpret_cast<float4 *>(ks + p * hs + e) = __ldg(reinterpret_cast<const float4 *>(
+            kc + loff + (size_t)win_pos(w0, p0 + p) * kv_dim + (size_t)(h / kv_mul) * head_size + e));
+    }
+    for (int idx = tid; idx < nr * h4; idx += 128) {
+        const int r = idx / h4, e = (idx - r * h4) << 2;
+        *reinterpret_cast<float4 *>(qs + r * hs + e) =
+            __ldg(reinterpret_cast<const float4 *>(q + ((size_t)(r0 + r) * n_heads + h) * head_size + e));
+    }
+    __syncthreads();
+    const int p = tid & (kScPos - 1), rg = tid >> 6;  // rows rg, rg + 2, ..., rg + 14
+    if (p >= np) return;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)head_size));
+    float d[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d[j] = 0.0f;
+    const float *kp = ks + p * hs;
+#pragma unroll 2
+    for (int e = 0; e < head_size; e += 4) {
+        const float4 k4 = *reinterpret_cast<const float4 *>(kp + e);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 q4 = *reinterpret_cast<const float4 *>(qs + (rg + 2 * j) * hs + e);  // broadcast
+            d[j] = add_rn(d[j], mul_rn(q4.x, k4.x));
+            d[j] = add_rn(d[j], mul_rn(q4.y, k4.y));
+            d[j] = add_rn(d[j], mul_rn(q4.z, k4.z));
+            d[j] = add_rn(d[j], mul_rn(q4.w, k4.w));
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int r = rg + 2 * j;
+        if (r < nr && p0 + p < cnt[r]) raw[((size_t)(r0 + r) * n_heads + h) * stride + p0 + p] = mul_rn(d[j], scale);
+    }
+}
+
 // Softmax and output (reference.rs:448-480) for one (row, head) and a slice
 // of `sw` output elements: the raw scores, their maximum (order-free),
 // exp(s - max), the sum by one thread in position order, s / sum (slice 0
@@ -794,7 +868,7 @@ size_t attention_scratch_floats(int n_rows, int n_heads, int max_count) {
 
 cudaError_t launch_attention(const float *q, float *out, float *att, const float *kc, const float *vc,
                              const int32_t *win, int n_rows, int n_heads, int kv_mul, int head_size, int kv_dim,
-                             int seq_len, size_t loff, int max_count, float *raw, cudaStream_t s) {
+                             int seq_len, size_t loff, int max_count, float *raw, bool shared_map, cudaStream_t s) {
     if (n_rows <= 0 || n_heads <= 0) return cudaSuccess;
     // Two kernels where the value slices move in 16-byte pieces and a scratch
     // for the raw scores is given: parallel scores, then per (row, head,
@@ -809,9 +883,18 @@ cudaError_t launch_attention(const float *q, float *out, float *att, const float
     const size_t out_smem = (size_t)(stride + stages * kAttTileFloats) * sizeof(float);
     const bool split = raw && (head_size & 3) == 0 && (kv_dim & 3) == 0 && out_smem <= 200 * 1024;
     if (split) {
-        k_att_scores<<<dim3((unsigned)(n_rows * n_heads), (unsigned)((max_count + 127) / 128)), 128,
-                       (size_t)head_size * sizeof(float), s>>>(q, raw, kc, win, n_heads, kv_mul, head_size, kv_dim,
-                                                               stride, loff);
+        // rows that map positions alike share their key tiles (16 rows x 64 positions per CTA)
+        const size_t rows_smem = (size_t)(kScPos + kScRows) * (head_size + 4) * sizeof(float);
+        if (shared_map && n_rows >= 2 && rows_smem <= 48 * 1024 && (((uintptr_t)q | (uintptr_t)kc) & 15) == 0) {
+            k_att_scores_rows<<<dim3((unsigned)((n_rows + kScRows - 1) / kScRows),
+                                     (unsigned)((max_count + kScPos - 1) / kScPos), (unsigned)n_heads),
+                                128, rows_smem, s>>>(q, raw, kc, win, n_rows, n_heads, kv_mul, head_size, kv_dim,
+                                                     stride, loff);
+        } else {
+            k_att_scores<<<dim3((unsigned)(n_rows * n_heads), (unsigned)((max_count + 127) / 128)), 128,
+                           (size_t)head_size * sizeof(float), s>>>(q, raw, kc, win, n_heads, kv_mul, head_size,
+                                                                   kv_dim, stride, loff);
+        }
         cudaError_t e = launched();
         if (e != cudaSuccess) return e;
         const int sw = few ? 32 : (head_size > 128 ? 128 : head_size);

@@ -122,8 +122,11 @@ cudaError_t launch_kv_write(float *kc, float *vc, int kv_dim, const int32_t *dst
 // single-kernel form).
 size_t attention_smem_bytes(int head_size, int max_count);
 size_t attention_scratch_floats(int n_rows, int n_heads, int max_count);
+// shared_map: every window maps window positions to the same cache slots (the
+// same start and shared range; the rows of one sequence), so rows can share
+// their key tiles.
 cudaError_t launch_attention(const float *q, float *out, float *att, const float *kc, const float *vc,
                              const int32_t *win, int n_rows, int n_heads, int kv_mul, int head_size, int kv_dim,
-                             int seq_len, size_t loff, int max_count, float *raw, cudaStream_t s);
+                             int seq_len, size_t loff, int max_count, float *raw, bool shared_map, cudaStream_t s);
 
 }  // namespace krt

@@ -101,6 +101,21 @@ def test_attention_prefill_causal_rows(gpu, oracle):
     attention_case(gpu, oracle, 1, 4, 4, 32, 64, 0, [(0, list(range(rows)))], wins, 310)
 
 
+def test_attention_prefill_row_tiles_with_gqa(gpu, oracle):
+    """70 causal rows (row blocks of 16 with a ragged last one), 8 query heads
+    on 2 key/value heads: the row-tiled scores share each key tile."""
+    rows = 70
+    wins = [(0, r, 0, 0) for r in range(rows)]
+    attention_case(gpu, oracle, 2, 8, 2, 64, 128, 1, [(1, list(range(rows)))], wins, 315)
+
+
+def test_attention_rows_sharing_a_prefix_and_start(gpu, oracle):
+    """Rows with one shared range and one start, their own last slots: the same
+    position map, so the row-tiled scores apply across the shared range."""
+    wins = [(40, 40 + r, 0, 24) for r in range(20)]
+    attention_case(gpu, oracle, 1, 4, 4, 32, 96, 0, [(0, list(range(96)))], wins, 318)
+
+
 def test_attention_shared_range_and_window_start(gpu, oracle):
     # rows attending a shared prefix [0, 6) plus their own sliding range
     wins = [(10, 12, 0, 6), (11, 14, 0, 6), (20, 20, 2, 5)]
