@@ -109,6 +109,15 @@ def test_attention_prefill_row_tiles_with_gqa(gpu, oracle):
     attention_case(gpu, oracle, 2, 8, 2, 64, 128, 1, [(1, list(range(rows)))], wins, 315)
 
 
+def test_attention_prefill_row_tiles_long_windows(gpu, oracle):
+    """260 causal rows of head size 64 (value tiles of 64 positions, a 48 KB
+    tile set past the default shared-memory limit) and 40 rows of 128."""
+    wins = [(0, r, 0, 0) for r in range(260)]
+    attention_case(gpu, oracle, 1, 2, 2, 64, 512, 0, [(0, list(range(260)))], wins, 316)
+    wins = [(0, 100 + r, 0, 0) for r in range(40)]
+    attention_case(gpu, oracle, 1, 2, 1, 128, 256, 0, [(0, list(range(140)))], wins, 317)
+
+
 def test_attention_rows_sharing_a_prefix_and_start(gpu, oracle):
     """Rows with one shared range and one start, their own last slots: the same
     position map, so the row-tiled scores apply across the shared range."""
