@@ -407,7 +407,7 @@ def contractions(B):
     wins = [(0, r, 0, 0) for r in range(rows)]
     B.time("attention prefill, 512 causal rows (32x64)",
            lambda: b.attention(qp, op, ap, 0, wins, n_heads, 1, head, kv_dim, seq), None,
-           note="per-(row, head) CTAs; scores and sums in order")
+           note="row-tiled scores (16 rows x 64 positions per CTA), then per-(row, head) softmax and sums in order")
 
 
 def chain_time(B, wk):
