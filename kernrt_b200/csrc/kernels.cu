@@ -1219,30 +1219,34 @@ struct RowsShape {
 //             reference's order, reference.rs:167-170) carried across tiles
 //             in a register, hands each slot back, and after a group's last
 //             tile stores its scales into one of two buffers;
-//   writers   (the warps off warp 0's sub-partition) take group after group
-//             once its scales are stored and write xb, x (+ resid) or the
-//             Q8_0 codes from x (and resid) loaded from L2, where the ring's
-//             copies left them a group earlier: U 16-byte loads in flight
-//             per lane, no barrier between tiles.
+//   writers   (the warps off warp 0's sub-partition; when quantising, all
+//             warps but 0 and 4) take group after group once its scales are
+//             stored and write xb, x (+ resid) or the Q8_0 codes from x (and
+//             resid) loaded from L2, where the ring's copies left them a
+//             group earlier: U 16-byte loads in flight per lane, no barrier
+//             between tiles.
 // mbarriers connect the roles (full/empty per slot, ready/freed per scale
 // buffer), so each runs at its own rate: the summing lanes' chains, the copy
 // engine and the writers' L2 traffic overlap instead of meeting at a CTA
-// barrier per tile.  The other warps of warp 0's sub-partition only wait at
-// the end.
+// barrier per tile.  In the plain forms the other warps of warp 0's
+// sub-partition only wait at the end.
 // PRE_ADD: the sums are of x + resid (the driver's add_in_place -> rms_norm,
 // llama.rs:762-765) and the writers store x = x + resid and xb.  FQ: a second
 // sum of x (+ resid) for the final norm, and the writers quantise it to Q8_0
 // (quant.rs:856-874).
 constexpr int kColsSlots = 4;
-// The quantising form runs 24 warps (18 writers, at most 85 registers
-// each, four items per batch): its writers' dependent block arithmetic needs
-// more warps to hide than the plain forms' loads and stores, which run 16
-// warps (12 writers, eight items per batch).
+// The quantising form runs 24 warps, all but the summing and the copying warp
+// writers (22, at most 85 registers each, four items per batch): its writers
+// are bound by their instruction issue (the block arithmetic), so they take
+// sub-partition 0's spare issue slots too, which the summing warp's chains
+// leave mostly free.  The plain forms' writers are bound by their loads and
+// stores and stay off sub-partition 0: 16 warps, 12 writers, eight items per
+// batch.
 template <bool FQ>
 struct ColsShape {
     static constexpr int threads = FQ ? 768 : 512;
-    static constexpr int writers = threads / 32 * 3 / 4;  // the warps off sub-partition 0
-    static constexpr int U = FQ ? 4 : 8;                  // items per writer lane and batch
+    static constexpr int writers = FQ ? threads / 32 - 2 : threads / 32 * 3 / 4;
+    static constexpr int U = FQ ? 4 : 8;  // items per writer lane and batch
 };
 constexpr unsigned kColsSleepNs = 128;  // poll interval of the issuer's and the writers' waits
 
@@ -1255,6 +1259,79 @@ struct ColsLayout {
     int slot;    // G * stride
     size_t smem;
 };
+
+// k_norm_cols' writers for the plain rms_norm_q8_0 (no residual, no xb, no x
+// copy), a group's rows r0.. at its scales s2[r].  The group is one contiguous
+// range, so its float4 item j sits at x + r0 * dim + 4 j, its four codes at the
+// same element offset and its block scale at r0 * nb + j / 8: no per-row
+// address arithmetic.  Writer thread wt takes items wt, wt + nwt, ...; (r, c4)
+// follow item j's row and float4 column (dr, dc = nwt / q, nwt % q).  The clamp
+// of the codes runs only for blocks whose 1/d overflows (q8_needs_clamp).
+template <int U>
+__device__ __forceinline__ void fq_write_group(const ChainArgs &a, const float *s2, int r0, int total, int q, int wt,
+                                               int nwt, int dr, int dc) {
+    const int dim = a.dim, nb = dim >> 5, lane = wt & 31;
+    const float4 *xg = reinterpret_cast<const float4 *>(a.x_in + (size_t)r0 * dim);
+    const float4 *wf = reinterpret_cast<const float4 *>(a.w_final);
+    uint32_t *cg = reinterpret_cast<uint32_t *>(a.codes + (size_t)r0 * dim);
+    float *sg = a.scales + (size_t)r0 * nb;
+    uint16_t *hg = a.scales16 ? a.scales16 + (size_t)r0 * nb : nullptr;
+    int r = wt / q, c4 = wt - r * q;
+    for (int j = wt; j - lane < total; j += U * nwt) {
+        float4 y[U];
+        float am[U];
+        int cs[U];
+        float ss[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const bool ok = j + k * nwt < total;
+            y[k] = ok ? __ldcs(xg + j + k * nwt) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            ss[k] = ok ? s2[r] : 0.0f;
+            cs[k] = c4;
+            c4 += dc;
+            r += dr;
+            if (c4 >= q) {
+                c4 -= q;
+                ++r;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const float4 w = __ldg(wf + cs[k]);
+            const float s = ss[k];
+            y[k] = make_float4(mul_rn(w.x, mul_rn(s, y[k].x)), mul_rn(w.y, mul_rn(s, y[k].y)),
+                               mul_rn(w.z, mul_rn(s, y[k].z)), mul_rn(w.w, mul_rn(s, y[k].w)));
+            // the fold of fmaxf from +0 (quant.rs:862): NaNs drop out
+            am[k] = fmaxf(0.0f, fmaxf(fmaxf(fabsf(y[k].x), fabsf(y[k].y)), fmaxf(fabsf(y[k].z), fabsf(y[k].w))));
+        }
+        // eight lanes per 32-element block, all in one warp and one row
+#pragma unroll
+        for (int m = 1; m < 8; m <<= 1)
+#pragma unroll
+            for (int k = 0; k < U; ++k) am[k] = fmaxf(am[k], __shfl_xor_sync(kFull, am[k], m));
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int jk = j + k * nwt;
+            if (jk >= total) continue;
+            const float d = q8_scale(am[k]);
+            const float inv = d > 0.0f ? q8_inv(d) : 0.0f;
+            int c0 = q8_round(mul_rn(y[k].x, inv)), c1 = q8_round(mul_rn(y[k].y, inv));
+            int c2 = q8_round(mul_rn(y[k].z, inv)), c3 = q8_round(mul_rn(y[k].w, inv));
+            if (q8_needs_clamp(d)) {
+                c0 = max(-127, min(127, c0));
+                c1 = max(-127, min(127, c1));
+                c2 = max(-127, min(127, c2));
+                c3 = max(-127, min(127, c3));
+            }
+            __stcs(cg + jk, (uint32_t)(c0 & 0xff) | ((uint32_t)(c1 & 0xff) << 8) | ((uint32_t)(c2 & 0xff) << 16) |
+                     ((uint32_t)c3 << 24));
+            if ((lane & 7) == 0) {
+                sg[jk >> 3] = d;
+                if (hg) hg[jk >> 3] = f16_bits(d);
+            }
+        }
+    }
+}
 
 template <bool PRE_ADD, bool FQ>
 __global__ void __launch_bounds__(ColsShape<FQ>::threads, 1) k_norm_cols(ChainArgs a, ColsLayout L) {
@@ -1407,16 +1484,23 @@ __global__ void __launch_bounds__(ColsShape<FQ>::threads, 1) k_norm_cols(ChainAr
         }
         // units whose copies were waited for
         if (lane == 0) s_consumed = u;
-    } else if (warp & 3) {
-        const int wi = warp - 1 - (warp >> 2);  // 0..11
+    } else if (FQ ? warp != 4 : (warp & 3) != 0) {
+        const int wi = FQ ? warp - 1 - (warp > 4) : warp - 1 - (warp >> 2);
         const int nwt = ColsShape<FQ>::writers * 32, wt = wi * 32 + lane;
         const int q = dim >> 2;                 // float4 items per row
         const int dr = nwt / q, dc = nwt - dr * q;
+        const bool lean = FQ && !a.xb && !a.x_out && !has_resid;
         for (int g = 0; g < nmine; ++g) {
             if (!wait(&ready[g & 1], (uint32_t)(g >> 1) & 1u, kColsSleepNs)) break;
             const float *sc = scales + (g & 1) * 64;
             const int r0 = first_row(g), gr = min(G, a.rows - r0);
             const int total = gr * q;  // the group's float4 items, row-major
+            if (FQ && lean) {
+                fq_write_group<ColsShape<FQ>::U>(a, sc + 32, r0, total, q, wt, nwt, dr, dc);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&freed[g & 1]);
+                continue;
+            }
             int r = wt / q, c4 = wt - r * q;
             constexpr int U = ColsShape<FQ>::U;
             for (int i = wt; i - lane < total; i += U * nwt) {

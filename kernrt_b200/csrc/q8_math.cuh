@@ -43,10 +43,20 @@ __device__ __forceinline__ float q8_inv(float d) {
 // above 2^23 the sum is |v| itself), and the conversion's truncation takes
 // that floor.  The conversion saturates and maps NaN to 0, so the clamp can
 // run on the integer.  Checked against roundf for every f32.
-__device__ __forceinline__ int8_t q8_code(float v) {
+__device__ __forceinline__ int q8_round(float v) {
     const float half = __int_as_float((__float_as_int(v) & (int)0x80000000u) | 0x3f000000);  // copysign(1/2, v)
-    const int i = __float2int_rz(__fadd_rz(v, half));
-    return (int8_t)max(-127, min(127, i));
+    return __float2int_rz(__fadd_rz(v, half));
 }
+
+__device__ __forceinline__ int8_t q8_code(float v) { return (int8_t)max(-127, min(127, q8_round(v))); }
+
+// When the clamp can be left out.  For a block with amax > 0, d = q8_scale(amax)
+// and inv = q8_inv(d), every |v| <= amax gives |v * inv| < 127.5, so
+// q8_round(v * inv) is already in [-127, 127], unless d <= 2^-128: then 1/d
+// overflows to +inf and the products are +-inf (or NaN).  Proof: d is amax/127
+// with relative error below 2^-22 (2^-24 when normal; d > 2^-128 bounds the
+// subnormal case), inv is 1/d within 2^-24, so amax * inv <= 127 (1 + 2^-21)
+// and the rounded product stays below 127.5.  amax = +inf gives inv = 0.
+__device__ __forceinline__ bool q8_needs_clamp(float d) { return d > 0.0f && d <= 0x1p-128f; }
 
 }  // namespace krt

@@ -362,6 +362,35 @@ def test_rms_norm_q8_0_fused(gpu, oracle, rows, dim, eps):
     assert_bits_equal(gpu.read_bytes(hh, rows * nb * 2, np.uint16).reshape(rows, -1), wh, "f16")
 
 
+@pytest.mark.parametrize("rows,dim", [(300, 1024), (40, 256)])
+def test_rms_norm_q8_0_edge_blocks(gpu, oracle, rows, dim):
+    """Blocks at the edges of the Q8_0 arithmetic through the fused kernel:
+    amax so small that 1/d overflows (codes +-127 by the clamp), d subnormal
+    just above that bound, all-zero blocks, blocks with an infinite product
+    (d = inf, inv = 0, codes 0) and a row whose sum overflows (scale 0, NaNs)."""
+    eps = 1e-6
+    x = _data.lcg_normal(rows * dim, 74 + dim).reshape(rows, dim)
+    w = _data.lcg_normal(dim, 75, 1.0, 0.1)
+    w[32:64] = 1e-41     # subnormal products: d <= 2^-128, 1/d = inf
+    w[64:96] = 1e-37     # amax about 3e-37: d on either side of 2^-128
+    w[96:128] = 0.0
+    w[128:160] = 3e-37   # d subnormal above 2^-128
+    if dim > 160:
+        w[160:192] = 3e38  # products past FLT_MAX
+    x[1, 7] = np.inf
+    x[2, 40] = np.nan
+    nb = dim // 32
+    hx, hw = up(gpu, x), up(gpu, w)
+    hc, hs, hh = gpu.alloc_bytes(rows * dim), gpu.alloc_bytes(rows * nb * 4), gpu.alloc_bytes(rows * nb * 2)
+    gpu.rms_norm_q8_0(hx, hw, rows, dim, eps, hc, hs, hh)
+    with np.errstate(all="ignore"):
+        wc, ws, wh = oracle.q8_quantize_rows(oracle.rms_norm(x, w, eps))
+    assert (np.abs(wc[3:, 32:64]) == 127).any()  # the clamp path ran
+    assert_bits_equal(gpu.read_bytes(hc, rows * dim, np.int8).reshape(rows, -1), wc, "codes")
+    assert_bits_equal(gpu.read_bytes(hs, rows * nb * 4, np.float32).reshape(rows, -1), ws, "scales")
+    assert_bits_equal(gpu.read_bytes(hh, rows * nb * 2, np.uint16).reshape(rows, -1), wh, "f16")
+
+
 def test_embed_many_calls_grow_the_staging_ring(gpu, oracle):
     """300 000 deferred embeds flush as one gather whose ids and offsets
     (3.6 MB) outgrow the initial staging ring: the grown ring must hold them
