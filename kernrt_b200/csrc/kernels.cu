@@ -1333,6 +1333,97 @@ __device__ __forceinline__ void fq_write_group(const ChainArgs &a, const float *
     }
 }
 
+// 256-bit loads (sm_100): eight floats per lane in one instruction, a warp's
+// 32 lanes one contiguous kilobyte.  p is 32-byte aligned.
+__device__ __forceinline__ void ld8_stream(const float *p, float (&v)[8]) {
+    asm("ld.global.cs.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+        : "l"(p));
+}
+__device__ __forceinline__ void ld8_ro(const float *p, float (&v)[8]) {
+    asm("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+        : "l"(p));
+}
+
+// fq_write_group with eight elements per lane and item (x, w_final 32-byte
+// aligned, codes 8-byte aligned): a 32-element block is four lanes, so the
+// block arithmetic, the amax shuffles (two rounds) and the index bookkeeping
+// are spent once per eight elements instead of once per four.  Items count
+// octets here (q = dim / 8 per row); the inverse is q8_inv_block's branchless
+// form.
+template <int U>
+__device__ __forceinline__ void fq_write_group8(const ChainArgs &a, const float *s2, int r0, int total, int q,
+                                                int wt, int nwt, int dr, int dc) {
+    const int dim = a.dim, nb = dim >> 5, lane = wt & 31;
+    const float *xg = a.x_in + (size_t)r0 * dim;
+    uint2 *cg = reinterpret_cast<uint2 *>(a.codes + (size_t)r0 * dim);
+    float *sg = a.scales + (size_t)r0 * nb;
+    uint16_t *hg = a.scales16 ? a.scales16 + (size_t)r0 * nb : nullptr;
+    int r = wt / q, c8 = wt - r * q;
+    for (int j = wt; j - lane < total; j += U * nwt) {
+        float y[U][8];
+        float am[U], ss[U];
+        int cs[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const bool ok = j + k * nwt < total;
+            if (ok) {
+                ld8_stream(xg + (size_t)8 * (j + k * nwt), y[k]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[k][e] = 0.0f;
+            }
+            ss[k] = ok ? s2[r] : 0.0f;
+            cs[k] = c8;
+            c8 += dc;
+            r += dr;
+            if (c8 >= q) {
+                c8 -= q;
+                ++r;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            float w[8];
+            ld8_ro(a.w_final + 8 * cs[k], w);
+            const float s = ss[k];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) y[k][e] = mul_rn(w[e], mul_rn(s, y[k][e]));
+            // the fold of fmaxf from +0 (quant.rs:862): NaNs drop out
+            const float m01 = fmaxf(fabsf(y[k][0]), fabsf(y[k][1])), m23 = fmaxf(fabsf(y[k][2]), fabsf(y[k][3]));
+            const float m45 = fmaxf(fabsf(y[k][4]), fabsf(y[k][5])), m67 = fmaxf(fabsf(y[k][6]), fabsf(y[k][7]));
+            am[k] = fmaxf(0.0f, fmaxf(fmaxf(m01, m23), fmaxf(m45, m67)));
+        }
+        // four lanes per 32-element block, all in one warp and one row
+#pragma unroll
+        for (int m = 1; m < 4; m <<= 1)
+#pragma unroll
+            for (int k = 0; k < U; ++k) am[k] = fmaxf(am[k], __shfl_xor_sync(kFull, am[k], m));
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int jk = j + k * nwt;
+            if (jk >= total) continue;
+            const float d = q8_scale(am[k]);
+            const float inv = q8_inv_block(d);
+            int c[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) c[e] = q8_round(mul_rn(y[k][e], inv));
+            if (q8_needs_clamp(d)) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) c[e] = max(-127, min(127, c[e]));
+            }
+            const uint32_t lo = __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
+            const uint32_t hi = __byte_perm(__byte_perm(c[4], c[5], 0x0040), __byte_perm(c[6], c[7], 0x0040), 0x5410);
+            __stcs(cg + jk, make_uint2(lo, hi));
+            if ((lane & 3) == 0) {
+                sg[jk >> 2] = d;
+                if (hg) hg[jk >> 2] = f16_bits(d);
+            }
+        }
+    }
+}
+
 template <bool PRE_ADD, bool FQ>
 __global__ void __launch_bounds__(ColsShape<FQ>::threads, 1) k_norm_cols(ChainArgs a, ColsLayout L) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -1490,13 +1581,18 @@ __global__ void __launch_bounds__(ColsShape<FQ>::threads, 1) k_norm_cols(ChainAr
         const int q = dim >> 2;                 // float4 items per row
         const int dr = nwt / q, dc = nwt - dr * q;
         const bool lean = FQ && !a.xb && !a.x_out && !has_resid;
+        const bool lean8 = lean && !((uintptr_t)a.x_in & 31) && !((uintptr_t)a.w_final & 31) && !((uintptr_t)a.codes & 7);
+        const int q8 = dim >> 3, dr8 = nwt / q8, dc8 = nwt - dr8 * q8;  // octets per row; their strides
         for (int g = 0; g < nmine; ++g) {
             if (!wait(&ready[g & 1], (uint32_t)(g >> 1) & 1u, kColsSleepNs)) break;
             const float *sc = scales + (g & 1) * 64;
             const int r0 = first_row(g), gr = min(G, a.rows - r0);
             const int total = gr * q;  // the group's float4 items, row-major
             if (FQ && lean) {
-                fq_write_group<ColsShape<FQ>::U>(a, sc + 32, r0, total, q, wt, nwt, dr, dc);
+                if (lean8)
+                    fq_write_group8<ColsShape<FQ>::U / 2>(a, sc + 32, r0, gr * q8, q8, wt, nwt, dr8, dc8);
+                else
+                    fq_write_group<ColsShape<FQ>::U>(a, sc + 32, r0, total, q, wt, nwt, dr, dc);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&freed[g & 1]);
                 continue;

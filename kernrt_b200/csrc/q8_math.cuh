@@ -59,4 +59,17 @@ __device__ __forceinline__ int8_t q8_code(float v) { return (int8_t)max(-127, mi
 // and the rounded product stays below 127.5.  amax = +inf gives inv = 0.
 __device__ __forceinline__ bool q8_needs_clamp(float d) { return d > 0.0f && d <= 0x1p-128f; }
 
+// The reference's `if d > 0 { 1 / d } else { 0 }` (quant.rs:866) for a block
+// scale d = q8_scale(amax), without branches: q8_inv's Newton step where it
+// applies; 1/d overflows to +inf for 0 < d <= 2^-128; d = +inf gives 0.  A
+// finite amax gives d < 2^121, so q8_inv's other division case (d > 2^126)
+// is only d = +inf here.
+__device__ __forceinline__ float q8_inv_block(float d) {
+    float y0;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(y0) : "f"(d));
+    const float e = __fmaf_rn(-d, y0, 1.0f);
+    const float y1 = __fmaf_rn(e, y0, y0);
+    return d > 0x1p-128f ? (d <= 0x1p126f ? y1 : 0.0f) : (d > 0.0f ? __int_as_float(0x7f800000) : 0.0f);
+}
+
 }  // namespace krt
