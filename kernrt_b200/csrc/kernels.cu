@@ -2513,6 +2513,58 @@ __global__ void __launch_bounds__(kThreads) k_quantize_q8v(const float *__restri
     }
 }
 
+// k_quantize_q8v with eight elements per lane (x 32-byte aligned, codes
+// 8-byte aligned): one 256-bit load per lane, four lanes per block, two
+// shuffle rounds, the block arithmetic once per eight elements, the branchless
+// reciprocal and the clamp only for blocks whose 1/d overflows.  `items`
+// counts octets.
+template <int U>
+__global__ void __launch_bounds__(kThreads) k_quantize_q8v8(const float *__restrict__ x, size_t items,
+                                                            int8_t *codes, float *scales, uint16_t *scales16) {
+    const unsigned lane = threadIdx.x & 31;
+    const size_t warp0 = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5;
+    const size_t nwarps = ((size_t)gridDim.x * blockDim.x) >> 5;
+    for (size_t base = warp0 * 32 * U; base < items; base += nwarps * 32 * U) {
+        float y[U][8];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const size_t idx = base + 32 * k + lane;
+            if (idx < items) {
+                ld8_stream(x + 8 * idx, y[k]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[k][e] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const size_t idx = base + 32 * k + lane;
+            const float m01 = fmaxf(fabsf(y[k][0]), fabsf(y[k][1])), m23 = fmaxf(fabsf(y[k][2]), fabsf(y[k][3]));
+            const float m45 = fmaxf(fabsf(y[k][4]), fabsf(y[k][5])), m67 = fmaxf(fabsf(y[k][6]), fabsf(y[k][7]));
+            float am = fmaxf(0.0f, fmaxf(fmaxf(m01, m23), fmaxf(m45, m67)));
+            am = fmaxf(am, __shfl_xor_sync(kFull, am, 1));
+            am = fmaxf(am, __shfl_xor_sync(kFull, am, 2));
+            if (idx >= items) continue;
+            const float d = q8_scale(am);
+            const float inv = q8_inv_block(d);
+            int c[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) c[e] = q8_round(mul_rn(y[k][e], inv));
+            if (q8_needs_clamp(d)) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) c[e] = max(-127, min(127, c[e]));
+            }
+            const uint32_t lo = __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
+            const uint32_t hi = __byte_perm(__byte_perm(c[4], c[5], 0x0040), __byte_perm(c[6], c[7], 0x0040), 0x5410);
+            __stcs(reinterpret_cast<uint2 *>(codes) + idx, make_uint2(lo, hi));
+            if ((idx & 3) == 0) {
+                scales[idx >> 2] = d;
+                if (scales16) scales16[idx >> 2] = f16_bits(d);
+            }
+        }
+    }
+}
+
 // quant.rs:198-220 Q8_0x4::to_row_major with quant.rs:764-769's widening.
 __device__ __forceinline__ float f16_scale_to_f32(uint16_t bits) {
     const uint32_t sign = (uint32_t)(bits >> 15) << 31;
@@ -3108,6 +3160,12 @@ cudaError_t launch_lfm2_conv_block(const float *bcx, const float *w, float *ring
 cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes, float *scales,
                                uint16_t *scales16, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
+    if (dim % 32 == 0 && ((uintptr_t)x & 31) == 0 && ((uintptr_t)codes & 7) == 0) {
+        const size_t items = (size_t)rows * dim / 8;
+        k_quantize_q8v8<2><<<stream_grid((size_t)rows * dim / 4), kThreads, 0, s>>>(x, items, codes, scales,
+                                                                                   scales16);
+        return launched();
+    }
     if (dim % 32 == 0 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)codes & 3) == 0) {
         const size_t items = (size_t)rows * dim / 4;
         k_quantize_q8v<4><<<stream_grid((size_t)rows * dim / 4), kThreads, 0, s>>>(x, items, codes, scales,

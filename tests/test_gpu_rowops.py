@@ -363,6 +363,31 @@ def test_rms_norm_q8_0_fused(gpu, oracle, rows, dim, eps):
 
 
 @pytest.mark.parametrize("rows,dim", [(300, 1024), (40, 256)])
+def test_quantize_q8_0_edge_blocks(gpu, oracle, rows, dim):
+    """The standalone quantiser on the same edge blocks: 1/d overflowing,
+    subnormal d, zero blocks, infinities and NaNs."""
+    x = _data.lcg_normal(rows * dim, 76 + dim).reshape(rows, dim)
+    x[:, 32:64] *= np.float32(1e-41)
+    x[:, 64:96] *= np.float32(1e-37)
+    x[:, 96:128] = 0.0
+    x[:, 128:160] *= np.float32(3e-37)
+    x[0, 200] = np.inf
+    x[1, 201] = -np.inf
+    x[2, 202] = np.nan
+    x[3, 224:256] = np.nan
+    nb = dim // 32
+    hx = up(gpu, x)
+    hc, hs, hh = gpu.alloc_bytes(rows * dim), gpu.alloc_bytes(rows * nb * 4), gpu.alloc_bytes(rows * nb * 2)
+    gpu.quantize_q8_0(hx, rows, dim, hc, hs, hh)
+    with np.errstate(all="ignore"):
+        wc, ws, wh = oracle.q8_quantize_rows(x)
+    assert (np.abs(wc[:, 32:64]) == 127).any()  # the clamp path ran
+    assert_bits_equal(gpu.read_bytes(hc, rows * dim, np.int8).reshape(rows, -1), wc, "codes")
+    assert_bits_equal(gpu.read_bytes(hs, rows * nb * 4, np.float32).reshape(rows, -1), ws, "scales")
+    assert_bits_equal(gpu.read_bytes(hh, rows * nb * 2, np.uint16).reshape(rows, -1), wh, "f16 scales")
+
+
+@pytest.mark.parametrize("rows,dim", [(300, 1024), (40, 256)])
 def test_rms_norm_q8_0_edge_blocks(gpu, oracle, rows, dim):
     """Blocks at the edges of the Q8_0 arithmetic through the fused kernel:
     amax so small that 1/d overflows (codes +-127 by the clamp), d subnormal
