@@ -88,6 +88,25 @@ __device__ __forceinline__ void set_err(int *err, int code) {
 __device__ __forceinline__ float4 ld4(const float *p) { return __ldcs(reinterpret_cast<const float4 *>(p)); }
 __device__ __forceinline__ void st4(float *p, float4 v) { __stcs(reinterpret_cast<float4 *>(p), v); }
 
+// 256-bit loads and stores (sm_100): eight floats per lane in one
+// instruction, a warp's 32 lanes one contiguous kilobyte.  p is 32-byte
+// aligned.
+__device__ __forceinline__ void ld8_stream(const float *p, float (&v)[8]) {
+    asm("ld.global.cs.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+        : "l"(p));
+}
+__device__ __forceinline__ void ld8_ro(const float *p, float (&v)[8]) {
+    asm("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
+        : "l"(p));
+}
+__device__ __forceinline__ void st8_stream(float *p, const float (&v)[8]) {
+    asm volatile("st.global.cs.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]),
+                 "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+                 : "memory");
+}
+
 // 16-byte global -> shared copies that need no registers: a warp issues all
 // of a row's copies back to back and waits once.
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
@@ -392,6 +411,38 @@ __device__ __forceinline__ int k_pairs_interleaved(int q_width, int kv_width) {
 template <int U>
 __device__ void silu_range(float *__restrict__ g, const float *__restrict__ u, size_t lo, size_t hi,
                            int t, int nt) {
+    if (((lo | hi) & 7) == 0 && !(((uintptr_t)g | (uintptr_t)u) & 31)) {
+        // 256-bit accesses, the same bytes in flight as U float4 pairs:
+        // measured on B200, silu_mul 1.053 -> 1.003 ms at 65 536 x 8192 and
+        // the 65 536-row chain 1.739 -> 1.657 ms (twice the bytes in flight
+        // was slower: 1.146 / 1.691 ms)
+        constexpr int V = U >= 2 ? U / 2 : 1;
+        const size_t step = 8 * (size_t)nt;
+        size_t i = lo + 8 * (size_t)t;
+        for (; i + (V - 1) * step < hi; i += V * step) {
+            float gv[V][8], uv[V][8];
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                ld8_stream(g + i + k * step, gv[k]);
+                ld8_stream(u + i + k * step, uv[k]);
+            }
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) gv[k][e] = silu_mul1(gv[k][e], uv[k][e]);
+                st8_stream(g + i + k * step, gv[k]);
+            }
+        }
+        for (; i < hi; i += step) {
+            float gv[8], uv[8];
+            ld8_stream(g + i, gv);
+            ld8_stream(u + i, uv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) gv[e] = silu_mul1(gv[e], uv[e]);
+            st8_stream(g + i, gv);
+        }
+        return;
+    }
     if (((lo | hi) & 3) == 0) {
         const size_t step = 4 * (size_t)nt;
         size_t i = lo + 4 * (size_t)t;
@@ -1336,19 +1387,6 @@ __device__ __forceinline__ void fq_write_group(const ChainArgs &a, const float *
             }
         }
     }
-}
-
-// 256-bit loads (sm_100): eight floats per lane in one instruction, a warp's
-// 32 lanes one contiguous kilobyte.  p is 32-byte aligned.
-__device__ __forceinline__ void ld8_stream(const float *p, float (&v)[8]) {
-    asm("ld.global.cs.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-        : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
-        : "l"(p));
-}
-__device__ __forceinline__ void ld8_ro(const float *p, float (&v)[8]) {
-    asm("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-        : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7])
-        : "l"(p));
 }
 
 // fq_write_group with eight elements per lane and item (x, w_final 32-byte

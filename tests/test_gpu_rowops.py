@@ -229,7 +229,7 @@ def test_rope_takes_min_of_rows_and_positions(gpu, oracle):
 
 # --- silu_mul / add / mul / copy -----------------------------------------------------------
 
-@pytest.mark.parametrize("n", [1, 3, 1000, 4608, 8192 * 5 + 3])
+@pytest.mark.parametrize("n", [1, 3, 1000, 1004, 4608, 8192 * 5 + 3])  # 1000, 4608: 256-bit path; 1004: float4
 def test_silu_mul(gpu, oracle, n):
     g = _data.lcg_normal(n, 40, 0.0, 3.0)
     u = _data.lcg_normal(n, 41)
