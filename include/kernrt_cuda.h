@@ -354,16 +354,19 @@ int kernrt_cuda_attention(kernrt_cuda_ctx *ctx, kernrt_buf q, kernrt_buf out, ke
  * The table is f32, bf16 or row-major Q8_0 (codes + f32 block scales), laid
  * out as for kernrt_cuda_prepare_embedding; results equal kernrt_cuda_embed's.
  *
- * The per-row ids and offsets go to a fixed scratch array compiled into the
- * library: KERNRT_NOALLOC_MAX_ROWS rows (768 KiB), held on every GPU that
- * loads the library until the process exits.  Larger n is rejected with
+ * The token ids go to a fixed scratch array compiled into the library:
+ * KERNRT_NOALLOC_MAX_ROWS int32 ids (256 KiB), held on every GPU that loads
+ * the library until the process exits.  Larger n is rejected with
  * KERNRT_E_INVALID; split the call.  All calls on a device share the array,
  * so calls that may overlap on the GPU (other streams, other threads) race
- * and must be ordered by the caller.  The first call on each device looks up
- * the array's device address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture begins.  The ids
- * are read from host memory during the call when pageable; page-locked ids
- * must stay unchanged until the stream has passed this call. */
+ * on the ids and must be ordered by the caller; a lost race gathers wrong
+ * table rows but writes only inside each call's own `out`.  The first call
+ * on each device does a one-time set-up: it looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture begins.  The ids are copied from host
+ * memory with cudaMemcpyAsync on `stream`: pageable ids are read during the
+ * call, page-locked ids must stay unchanged until the stream has passed this
+ * call.  The caller's current device is unchanged on return. */
 #define KERNRT_NOALLOC_MAX_ROWS 65536
 int kernrt_cuda_embed_rows_noalloc(int device, int kind, const void *table, const float *scales,
                                    size_t vocab, size_t dim, const int32_t *tokens, size_t n,

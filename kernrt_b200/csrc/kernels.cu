@@ -541,8 +541,8 @@ __global__ void __launch_bounds__(kThreads) k_embed_gather(GatherArgs a) {
     const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (row >= a.n) return;
     const int tok = a.tokens[row];
-    float *dst = a.dst + a.dst_off[row];
     const int dim = a.dim;
+    float *dst = a.dst + (a.dst_off ? a.dst_off[row] : (int64_t)row * dim);
     if ((unsigned)tok >= (unsigned)a.vocab) {
         if (lane == 0) set_err(a.err, ERR_TOKEN);
         for (int i = lane; i < dim; i += 32) dst[i] = 0.0f;

@@ -25,7 +25,7 @@ struct GatherArgs {
     const float *tscales;   // q8_0 block scales
     int vocab, dim;
     const int32_t *tokens;  // [n]
-    const int64_t *dst_off; // [n] element offsets into dst
+    const int64_t *dst_off; // [n] element offsets into dst, or null: row r at r * dim
     float *dst;
     int n;
     int *err;

@@ -25,21 +25,17 @@ namespace {
 
 constexpr size_t kMaxRows = KERNRT_NOALLOC_MAX_ROWS;
 constexpr int kMaxDevices = 64;
-constexpr size_t kOffsetBytes = kMaxRows * sizeof(int64_t);
 
-// The scratch: kMaxRows int64 destination offsets followed by kMaxRows int32
-// token ids (12 bytes per row, 768 KiB).  Every device that loads the library
-// holds one copy until the process exits.  All calls on a device share it; a
-// call overwrites every entry it later reads, so nothing needs clearing.
-static __device__ __align__(256) unsigned char g_gather_scratch[kMaxRows * (sizeof(int64_t) + sizeof(int32_t))];
+// The scratch: kMaxRows int32 token ids (256 KiB).  Every device that loads
+// the library holds one copy until the process exits.  All calls on a device
+// share it; a call writes every entry it later reads, so nothing needs
+// clearing.  Output rows are addressed as row * dim inside the gather, so a
+// call that overwrites the ids while another call's gather runs gives that
+// call wrong rows of the table, never a write outside its own `out`.
+static __device__ __align__(256) int32_t g_gather_ids[kMaxRows];
 
 std::mutex g_setup_mu;
-void *g_scratch_addr[kMaxDevices];  // device address of g_gather_scratch, per device
-
-__global__ void k_row_offsets(int64_t *off, int n, int64_t dim) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) off[i] = (int64_t)i * dim;
-}
+void *g_ids_addr[kMaxDevices];  // device address of g_gather_ids, per device
 
 int fail(int code, const std::string &msg) {
     krt::set_last_error("kernrt_cuda_embed_rows_noalloc: " + msg);
@@ -74,7 +70,10 @@ extern "C" int kernrt_cuda_embed_rows_noalloc(int device, int kind, const void *
     }
     int prev = -1;
     cudaGetDevice(&prev);
-    if (prev != device && cudaSetDevice(device) != cudaSuccess) return fail(KERNRT_E_CUDA, "cudaSetDevice failed");
+    if (prev != device && cudaSetDevice(device) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(KERNRT_E_CUDA, "cudaSetDevice failed");
+    }
 
     // Set-up, once per device and with that device current: the host-side
     // name of the array is only a stand-in, so fetch its device address.
@@ -82,23 +81,17 @@ extern "C" int kernrt_cuda_embed_rows_noalloc(int device, int kind, const void *
     cudaError_t e = cudaSuccess;
     {
         std::lock_guard<std::mutex> lock(g_setup_mu);
-        if (!g_scratch_addr[device]) {
+        if (!g_ids_addr[device]) {
             void *p = nullptr;
-            e = cudaGetSymbolAddress(&p, g_gather_scratch);
-            if (e == cudaSuccess) g_scratch_addr[device] = p;
+            e = cudaGetSymbolAddress(&p, g_gather_ids);
+            if (e == cudaSuccess) g_ids_addr[device] = p;
         }
-        base = g_scratch_addr[device];
+        base = g_ids_addr[device];
     }
     if (e == cudaSuccess && base) {
-        int64_t *off = static_cast<int64_t *>(base);
-        int32_t *tok = reinterpret_cast<int32_t *>(static_cast<unsigned char *>(base) + kOffsetBytes);
+        int32_t *tok = static_cast<int32_t *>(base);
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         e = cudaMemcpyAsync(tok, tokens, n * sizeof(int32_t), cudaMemcpyHostToDevice, s);
-        if (e == cudaSuccess) {
-            k_row_offsets<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(off, (int)n, (int64_t)dim);
-            krt::count_launch();
-            e = cudaGetLastError();
-        }
         if (e == cudaSuccess) {
             krt::GatherArgs a{};
             a.table = table;
@@ -106,7 +99,7 @@ extern "C" int kernrt_cuda_embed_rows_noalloc(int device, int kind, const void *
             a.vocab = (int)vocab;
             a.dim = (int)dim;
             a.tokens = tok;
-            a.dst_off = off;
+            a.dst_off = nullptr;  // row r at out + r * dim
             a.dst = out;
             a.n = (int)n;
             a.err = nullptr;  // ids were checked above
@@ -117,6 +110,8 @@ extern "C" int kernrt_cuda_embed_rows_noalloc(int device, int kind, const void *
     } else if (e == cudaSuccess) {
         e = cudaErrorInvalidSymbol;
     }
+    // Leave no stale error behind for the caller's next launch check.
+    if (e != cudaSuccess) cudaGetLastError();
     if (prev >= 0 && prev != device) cudaSetDevice(prev);
     if (e != cudaSuccess) return fail(KERNRT_E_CUDA, cudaGetErrorString(e));
     return KERNRT_OK;

@@ -54,6 +54,30 @@ def test_noalloc_gather_matches_embed_on_two_calls(kind, vocab, dim):
             assert_bits_equal(got, want, f"no-alloc gather, call {call + 1}")
 
 
+def test_noalloc_gather_scalar_path_default_stream_and_device():
+    """An output one float past a 16-byte boundary and a bf16 width of 40 take
+    the gather's element-wise form; the call goes on the legacy default stream
+    (stream 0) and leaves the caller's current device as it found it."""
+    import torch
+
+    vocab, dim, n = 700, 40, 333
+    with kernrt_b200.CudaBackend(0) as b:
+        table = _data.bf16_table_fast(vocab, dim, 15)
+        b.prepare_embedding(kernrt_b200.BF16, table, None, vocab, dim)
+        dev_table = b.upload_bytes(table)
+        out = b.alloc(n * dim + 4)
+        for call in range(2):
+            tokens = _data.tokens(n, vocab, 300 + call)
+            want = _embed_reference_path(b, tokens, dim)
+            before = torch.cuda.current_device()
+            kernrt_b200.embed_rows_noalloc(0, kernrt_b200.BF16, b.device_ptr(dev_table), 0, vocab, dim, tokens,
+                                           b.device_ptr(out) + 4, 0)
+            assert torch.cuda.current_device() == before
+            torch.cuda.synchronize()
+            got = b.read_bytes(out, (n * dim + 1) * 4, np.float32)[1:]
+            assert_bits_equal(got, want, f"no-alloc gather, unaligned rows, call {call + 1}")
+
+
 def test_noalloc_gather_rejects_what_it_cannot_hold():
     with kernrt_b200.CudaBackend(0) as b:
         vocab, dim = 64, 128
