@@ -166,14 +166,34 @@ class ClockSampler:
 # reference arm: KernRT's CPU path (the oracle port of its scalar loops)
 # ---------------------------------------------------------------------------------
 
-def cpu_sample_inputs(rows: int, seed: int = 5):
-    rng = np.random.default_rng(seed)
-    table_rows = 4096  # gathered rows drawn from a 4096-row slice of the table
-    table = (rng.standard_normal((table_rows, WL.dim), dtype=np.float32) * np.float32(0.02))
-    from oracle.oracle import f32_to_bf16_bits
+_CPU_TABLE = None
 
-    d = dict(table=f32_to_bf16_bits(table), vocab=table_rows,
-             tokens=rng.integers(0, table_rows, rows).astype(np.int32),
+
+def cpu_table():
+    """The full bf16 embedding table of the workload (vocab 49152 x 2048,
+    ~N(0, 0.02), RNE to bf16), made once per process on the host."""
+    global _CPU_TABLE
+    if _CPU_TABLE is None:
+        from oracle.oracle import f32_to_bf16_bits
+
+        rng = np.random.default_rng(1)
+        out = np.empty((WL.vocab, WL.dim), np.uint16)
+        step = 4096
+        for lo in range(0, WL.vocab, step):
+            hi = min(WL.vocab, lo + step)
+            out[lo:hi] = f32_to_bf16_bits(rng.standard_normal((hi - lo, WL.dim), dtype=np.float32)
+                                          * np.float32(0.02))
+        _CPU_TABLE = out
+    return _CPU_TABLE
+
+
+def cpu_sample_inputs(rows: int, seed: int = 5):
+    """`rows` rows of the workload's inputs; token ids span the whole table.
+    q/k/gate are updated in place by each pass, so pristine copies are kept
+    (`*0`) and restored before every pass, outside the timing."""
+    rng = np.random.default_rng(seed)
+    d = dict(table=cpu_table(), vocab=WL.vocab,
+             tokens=rng.integers(0, WL.vocab, rows).astype(np.int32),
              positions=WL.positions(0, rows).astype(np.uint64),
              w_att=(1 + 0.1 * rng.standard_normal(WL.dim)).astype(np.float32),
              q=rng.standard_normal((rows, WL.q_dim), dtype=np.float32),
@@ -181,29 +201,67 @@ def cpu_sample_inputs(rows: int, seed: int = 5):
              gate=rng.standard_normal((rows, WL.hidden), dtype=np.float32),
              up=rng.standard_normal((rows, WL.hidden), dtype=np.float32),
              resid=rng.standard_normal((rows, WL.dim), dtype=np.float32))
+    for n in ("q", "k", "gate"):
+        d[n + "0"] = d[n].copy()
     return d
 
 
-def cpu_chain_once(d, threads: int) -> None:
+def cpu_restore(d) -> None:
+    for n in ("q", "k", "gate"):
+        np.copyto(d[n], d[n + "0"])
+
+
+def cpu_chain_once(d, threads: int) -> float:
+    """One timed pass of the oracle chain over the sample (in place); the
+    restore of q/k/gate before it is not timed.  Returns seconds."""
     from oracle import oracle
 
+    cpu_restore(d)
+    t0 = time.perf_counter()
     oracle.chain(dim=WL.dim, q_dim=WL.q_dim, kv_dim=WL.kv_dim, hidden=WL.hidden, head=WL.head,
                  eps=WL.eps, theta=WL.theta, positions=d["positions"], w_att=d["w_att"], q=d["q"],
                  k=d["k"], gate=d["gate"], up=d["up"], resid=d["resid"], tokens=d["tokens"],
                  table=(oracle.BF16, d["table"], None, d["vocab"]), threads=threads, in_place=True)
+    return time.perf_counter() - t0
+
+
+def host_cpu():
+    """The host CPU as lscpu names it, with its online and usable cores."""
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        usable = len(os.sched_getaffinity(0))
+    except AttributeError:
+        usable = os.cpu_count()
+    return {"model": model, "nproc_online": os.cpu_count(), "usable_cores": usable}
 
 
 def cpu_chain_rate(threads: int, seconds: float, rows: int):
     """Rows/s of the oracle chain on `threads` host threads over a bounded
-    sample: the same rows are re-run until `seconds` of work accumulate."""
+    sample: passes over the same input rows (restored before each pass) until
+    `seconds` of timed work accumulate."""
     d = cpu_sample_inputs(rows)
-    done, t0 = 0, time.perf_counter()
-    while True:
-        cpu_chain_once(d, threads)
+    done, el = 0, 0.0
+    while el < seconds:
+        el += cpu_chain_once(d, threads)
         done += rows
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            return done / el, done, el
+    return done / el, done, el
+
+
+def base_config(world: int) -> dict:
+    """The workload both arms run (the same dict in both JSON lines)."""
+    return {"workload": WL.name, "rows": WL.rows, "hidden": WL.dim, "q_heads": WL.n_heads,
+            "kv_heads": WL.n_kv_heads, "head_dim": WL.head, "intermediate": WL.hidden, "vocab": WL.vocab,
+            "rope_theta": WL.theta, "positions": "row % 4096",
+            "parallelism": f"row-shard x{world}, no collective",
+            "l2": "inputs 10.5 GB per step > 126 MB L2; no flush needed"}
 
 
 def run_reference(args, rank, world):
@@ -212,27 +270,27 @@ def run_reference(args, rank, world):
     from oracle import oracle
 
     threads = oracle.max_threads()
-    per_step_rows = threads * 64
+    per_step_rows = threads * 256
     d = cpu_sample_inputs(per_step_rows)
     times = []
     for i in range(args.warmup + args.steps):
-        t0 = time.perf_counter()
-        cpu_chain_once(d, threads)
+        t = cpu_chain_once(d, threads)
         if i >= args.warmup:
-            times.append(time.perf_counter() - t0)
+            times.append(t)
     value = per_step_rows * len(times) / sum(times)
+    cpu = host_cpu()
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sum(times) / len(times),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded; bf16 embedding ~N(0,0.02), activations ~N(0,1))",
-        "config": {"workload": WL.name, "rows": WL.rows, "hidden": WL.dim, "q_heads": WL.n_heads,
-                   "kv_heads": WL.n_kv_heads, "head_dim": WL.head, "intermediate": WL.hidden,
-                   "rope_theta": WL.theta, "sample_rows_per_step": per_step_rows},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{per_step_rows} rows of the {WL.rows}-row workload per step, "
-                                   f"row-parallel over {threads} host threads (KernRT is Rust and "
-                                   f"cannot be built here; the C restatement of its scalar loops runs)"},
+        "data": "synthetic (seeded; bf16 embedding ~N(0,0.02), activations ~N(0,1), random init)",
+        "config": base_config(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "threads": threads, "kind": "port",
+                         "cpu": cpu,
+                         "sample": f"{per_step_rows} rows of the {WL.rows}-row workload per step (ids over the "
+                                   f"full {WL.vocab}-row table; q/k/gate restored before each step, untimed), "
+                                   f"row-parallel over {threads} host threads (KernRT is Rust and cannot be "
+                                   f"built here; the C restatement of its scalar loops runs)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -402,12 +460,16 @@ def run_kernrt(args, rank, world, local):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, n, el = cpu_chain_rate(1, args.cpu_seconds, 256)
-        cpu = {"value": rate, "unit": UNIT, "cores": 1, "kind": "port",
-               "sample": f"{n} rows ({el:.1f} s) of the {WL.rows}-row workload, single thread: the C "
-                         f"restatement of KernRT's scalar row-op loops (its cpu backend runs these "
-                         f"single-threaded)"}
+        cpu = {"value": rate, "unit": UNIT, "cores": 1, "threads": 1, "kind": "port", "cpu": host_cpu(),
+               "sample": f"{n} rows ({el:.1f} s timed) of the {WL.rows}-row workload in passes of 256 rows "
+                         f"(ids over the full {WL.vocab}-row table; q/k/gate restored before each pass, "
+                         f"untimed), single thread: the C restatement of KernRT's scalar row-op loops "
+                         f"(its cpu backend runs these single-threaded)"}
 
     clocks = clk.summary()
+    config = base_config(world)
+    if total_rows != WL.rows:
+        config["rows"] = total_rows
     barrier()
     if rank == 0:
         line = {
@@ -415,13 +477,10 @@ def run_kernrt(args, rank, world, local):
             "warmup": max(3, args.warmup), "ms_per_step": total_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded; bf16 embedding ~N(0,0.02), activations ~N(0,1), random init)",
-            "config": {"workload": WL.name, "rows": total_rows, "rows_per_gpu": R, "hidden": H,
-                       "q_heads": WL.n_heads, "kv_heads": WL.n_kv_heads, "head_dim": WL.head,
-                       "intermediate": I, "vocab": WL.vocab, "rope_theta": WL.theta,
-                       "positions": "row % 4096", "parallelism": f"row-shard x{world}, no collective",
-                       "l2": "inputs 10.5 GB per step > 126 MB L2; no flush needed",
-                       "timing": "CUDA events around each step's launch(es); gate restored from a "
-                                 "pristine device copy before each step, outside the events",
+            "config": config,
+            "timing": {"rows_per_gpu": R,
+                       "how": "CUDA events around each step's launch(es) on the backend's stream; gate "
+                              "restored from a pristine device copy before each step, outside the events",
                        "region_wall_s_incl_restores": region_s},
             "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
