@@ -396,9 +396,10 @@ def run_kernrt(args, rank, world, local):
     torch.cuda.synchronize()
     region_s = time.perf_counter() - t_region
     launches = int(sum_over_ranks(float(kernrt_b200.kernel_launches() - launches0)))
-    # The headline's rows (bf16 embedding rows, hidden 2048) take the whole-row
-    # norm pipeline, so the norm stage's events time k_norm_rows.
-    stage_kernel = {"norm": "k_norm_rows", "stream": "k_stream", "fused": "k_chain"}
+    # The headline's rows (gathered bf16 embedding rows, hidden 2048) take the
+    # two-pass norm stage: its events time k_row_scales (the row scales) and
+    # k_stream_dyn (the norm rows' writes, RoPE and SwiGLU).
+    stage_kernel = {"norm": "k_row_scales", "stream": "k_stream_dyn", "fused": "k_chain"}
     stages = {stage_kernel[k]: v for k, v in b.stage_times().items()}
     b.stage_timing(False)
     per_launch = [s.elapsed_time(e) for s, e in ev]  # ms
@@ -408,7 +409,7 @@ def run_kernrt(args, rank, world, local):
     peak, peak_kind = peaks()
     # The roofline is the dominant kernel's: its algorithmic bytes per launch
     # over its own mean launch time, from the backend's stage events.
-    stage_bytes = {stage_kernel[k]: v for k, v in WL.stage_bytes_per_row().items()}
+    stage_bytes = {stage_kernel[k]: v for k, v in WL.stage_bytes_per_row(two_pass=True).items()}
     dominant = max((k for k in stages if stages[k][1] > 0), key=lambda k: stages[k][0])
     dom_ms, dom_n = stages[dominant]
     dom_bytes = stage_bytes.get(dominant, bpr) * R

@@ -62,6 +62,8 @@ public:
         check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
         check(cudaMalloc(&d_err_, sizeof(int)), "cudaMalloc(error word)");
         check(cudaMemsetAsync(d_err_, 0, sizeof(int), stream_), "cudaMemset");
+        check(cudaMalloc(&d_ticket_, sizeof(unsigned)), "cudaMalloc(stream ticket)");
+        check(cudaMemsetAsync(d_ticket_, 0, sizeof(unsigned), stream_), "cudaMemset");
         check(cudaMallocHost(&h_err_, sizeof(int)), "cudaMallocHost");
         grow_staging(1 << 20);
         check(cudaStreamCreateWithFlags(&h2d_, cudaStreamNonBlocking), "cudaStreamCreate");
@@ -89,6 +91,8 @@ public:
         cudaFree(vc_);
         cudaFree(att_scratch_);
         cudaFree(d_err_);
+        cudaFree(d_ticket_);
+        cudaFree(row_scales_);
         cudaFreeHost(h_err_);
         cudaFreeHost(stage_host_);
         cudaFree(stage_dev_);
@@ -932,6 +936,7 @@ public:
             a.vocab = (int)vocab_;
             a.tokens = reinterpret_cast<const int32_t *>(tb.ptr);
             a.x_out = f(xb);
+            a.row_scale = row_scales(rows);
         } else {
             a.x_in = f(xb);
             if (c.resid) a.x_out = f(xb);
@@ -1131,6 +1136,7 @@ public:
                     a.vocab = (int)vocab_;
                     a.tokens = reinterpret_cast<const int32_t *>(dev(p_tok));
                     a.x_out = reinterpret_cast<float *>(dev(p_x));
+                    a.row_scale = row_scales(n);
                 } else {
                     a.x_in = reinterpret_cast<const float *>(dev(p_x));
                     if (h.resid) a.x_out = reinterpret_cast<float *>(dev(p_x));
@@ -1358,11 +1364,25 @@ private:
     }
     static void launch_or_fail(cudaError_t e, const char *what) { check(e, what); }
 
+    // Scratch for `rows` row scales of a chain on stream_, grown as needed
+    // (cudaFree waits for queued kernels that may still read the old one).
+    float *row_scales(size_t rows) {
+        if (rows > row_scales_cap_) {
+            cudaFree(row_scales_);
+            row_scales_ = nullptr;
+            row_scales_cap_ = 0;
+            check(cudaMalloc(&row_scales_, rows * sizeof(float)), "cudaMalloc(row scales)");
+            row_scales_cap_ = rows;
+        }
+        return row_scales_;
+    }
+
     ChainArgs blank(size_t rows, size_t dim) const {
         ChainArgs a{};
         a.rows = (int)rows;
         a.dim = (int)dim;
         a.err = d_err_;
+        a.ticket = d_ticket_;  // every chain launches on stream_
         return a;
     }
 
@@ -1523,6 +1543,9 @@ private:
     cudaEvent_t file_ev_[2] = {nullptr, nullptr};
     const char *storage_ = "f32";
     int *d_err_ = nullptr;
+    unsigned *d_ticket_ = nullptr;  // the chain streams' work counter on stream_ (zero between launches)
+    float *row_scales_ = nullptr;   // the two-pass norm stage's row scales (chains on stream_)
+    size_t row_scales_cap_ = 0;
     int *h_err_ = nullptr;
     char *stage_host_ = nullptr;
     char *stage_dev_ = nullptr;

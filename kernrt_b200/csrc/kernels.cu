@@ -2089,6 +2089,215 @@ __global__ void __launch_bounds__(kThreads) k_stream(ChainArgs a) {
     if (a.gate) silu_range<U>(a.gate, a.up, 0, (size_t)a.rows * a.hidden, t, nt);
 }
 
+// The norm stage in two passes, for gathered bf16 / f32 embedding rows
+// (the Llama chain's embed -> rms_norm, llama.rs:734-740).
+//
+// Pass 1, k_row_scales: each row's RMSNorm scale (reference.rs:161-173), lane
+// r of a one-warp CTA summing row r's squares left to right (the reference's
+// order) out of a ring of column tiles that the same warp fills with 16-byte
+// cp.async copies, 16 lanes per 256-byte row tile.  Many CTAs per SM keep
+// many rows' chains in flight at once.
+// Pass 2 is a ticket type of k_stream_dyn that writes xb = w * (scale * v)
+// and x = v + resid from the gathered row v (norm_rows_write): balanced with
+// the chain's other streams, no pipeline to fill.
+constexpr int kScaleSlots = 4;
+constexpr int kScaleTile = 256;                // bytes of a row per tile
+constexpr int kScaleStride = kScaleTile + 16;  // odd multiple of 16: lane r's reads hit distinct banks
+constexpr size_t kScaleSmem = (size_t)kScaleSlots * 32 * kScaleStride;
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+template <int SRC>
+__global__ void __launch_bounds__(32) k_row_scales(ChainArgs a, float *row_scale) {
+    static_assert(SRC == SRC_BF16 || SRC == SRC_F32, "bf16 or f32 rows");
+    constexpr int ESZ = SRC == SRC_BF16 ? 2 : 4;
+    extern __shared__ __align__(16) unsigned char ring_smem[];  // [kScaleSlots][32 * kScaleStride]
+    __shared__ const unsigned char *src_row[32];
+    auto ring = [&](int slot) { return ring_smem + (size_t)slot * 32 * kScaleStride; };
+    const int lane = threadIdx.x, r0 = blockIdx.x * 32, gr = min(32, a.rows - r0);
+    const int rb = a.dim * ESZ;  // a multiple of 16
+    const int ntiles = (rb + kScaleTile - 1) / kScaleTile;
+    bool valid = false;
+    if (lane < gr) {
+        const int tok = a.tokens[r0 + lane];
+        valid = (unsigned)tok < (unsigned)a.vocab;
+        if (!valid) set_err(a.err, ERR_TOKEN);
+        src_row[lane] = valid ? static_cast<const unsigned char *>(a.table) + (size_t)tok * rb : nullptr;
+    } else {
+        src_row[lane] = nullptr;
+    }
+    __syncwarp();
+    // tile t: lane l copies chunk (l & 15) of rows 2j + (l >> 4), j < 16
+    auto issue = [&](int t) {
+        const int off = t * kScaleTile + 16 * (lane & 15);
+        if (off >= rb) return;
+        unsigned char *dst = ring(t % kScaleSlots) + (lane >> 4) * kScaleStride + 16 * (lane & 15);
+#pragma unroll 4
+        for (int j = 0; j < 16; ++j) {
+            const unsigned char *sp = src_row[2 * j + (lane >> 4)];
+            if (sp) cp_async16(dst + 2 * j * kScaleStride, sp + off);
+        }
+    };
+#pragma unroll
+    for (int t = 0; t < kScaleSlots - 1; ++t) {
+        if (t < ntiles) issue(t);
+        cp_async_commit();
+    }
+    float ss = 0.0f;
+    for (int t = 0; t < ntiles; ++t) {
+        cp_async_wait_group<kScaleSlots - 2>();  // this lane's copies of tile t
+        __syncwarp();                            // and every lane's
+        if (t + kScaleSlots - 1 < ntiles) issue(t + kScaleSlots - 1);  // the slot tile t - 1 used
+        cp_async_commit();
+        if (valid) {
+            const unsigned char *row = ring(t % kScaleSlots) + lane * kScaleStride;
+            const int n16 = min(kScaleTile, rb - t * kScaleTile) >> 4;
+#pragma unroll 4
+            for (int c = 0; c < n16; ++c) {
+                const uint4 u = *reinterpret_cast<const uint4 *>(row + 16 * c);
+                if constexpr (SRC == SRC_BF16) {
+                    const float v[8] = {bf16f(u.x & 0xffffu), bf16f(u.x >> 16), bf16f(u.y & 0xffffu), bf16f(u.y >> 16),
+                                        bf16f(u.z & 0xffffu), bf16f(u.z >> 16), bf16f(u.w & 0xffffu), bf16f(u.w >> 16)};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
+                } else {
+                    const float v[4] = {__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
+                                        __uint_as_float(u.w)};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
+                }
+            }
+        }
+    }
+    cp_async_wait_group<0>();
+    if (lane < gr) row_scale[r0 + lane] = rms_scale(ss, (float)a.dim, a.eps);
+}
+
+// Pass 2's norm rows [r0, r0 + g): v = the gathered row (0 for a token out of
+// range, as the norm pipelines use), xb = w * (scale * v), x = v + resid (or
+// v), threads t of nt over the rows' float4 items, U items in flight.
+template <int SRC, int U>
+__device__ void norm_rows_write(const ChainArgs &a, const float *__restrict__ row_scale, int r0, int g, int t,
+                                int nt) {
+    const int dim = a.dim, q = dim >> 2, n = g * q;
+    for (int i = t; i < n; i += U * nt) {
+        float4 v[U], rv[U];
+        int row[U], c[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const int it = i + k * nt;
+            row[k] = -1;
+            if (it >= n) continue;
+            const int r = it / q;
+            row[k] = r0 + r;
+            c[k] = 4 * (it - r * q);
+            const int tok = a.tokens[row[k]];
+            v[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if ((unsigned)tok < (unsigned)a.vocab) {
+                if constexpr (SRC == SRC_BF16) {
+                    const uint2 b = __ldg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(a.table) +
+                                                                           (size_t)tok * dim + c[k]));
+                    v[k] = make_float4(bf16f(b.x & 0xffffu), bf16f(b.x >> 16), bf16f(b.y & 0xffffu), bf16f(b.y >> 16));
+                } else {
+                    v[k] = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(a.table) +
+                                                                  (size_t)tok * dim + c[k]));
+                }
+            }
+            if (a.resid && a.x_out) rv[k] = ld4(a.resid + (size_t)row[k] * dim + c[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            if (row[k] < 0) continue;
+            const size_t o = (size_t)row[k] * dim + c[k];
+            if (a.xb) {
+                const float s = row_scale[row[k]];
+                const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + c[k]));
+                st4(a.xb + o, make_float4(mul_rn(w.x, mul_rn(s, v[k].x)), mul_rn(w.y, mul_rn(s, v[k].y)),
+                                          mul_rn(w.z, mul_rn(s, v[k].z)), mul_rn(w.w, mul_rn(s, v[k].w))));
+            }
+            if (a.x_out) {
+                float4 xo = v[k];
+                if (a.resid)
+                    xo = make_float4(add_rn(xo.x, rv[k].x), add_rn(xo.y, rv[k].y), add_rn(xo.z, rv[k].z),
+                                     add_rn(xo.w, rv[k].w));
+                st4(a.x_out + o, xo);
+            }
+        }
+    }
+}
+
+// The chain's streams with dynamic work.  The work is cut into tickets that
+// the CTAs draw in order from a counter, so no CTA is left with a share of the
+// work after the others finish (measured on B200 against the grid-stride
+// k_stream over the 65 536-row chain: 1.337 -> 1.243 ms).  In ticket order:
+//   the norm rows of the two-pass norm stage (NSRC = SRC_BF16 / SRC_F32),
+//   kNormRows rows each, last rows first: pass 1 read them last, so they are
+//   the likeliest still to be in L2;
+//   SwiGLU spans of kSpanElems elements; RoPE spans of kSpanRows rows of q,
+//   then of k.
+// Every CTA draws exactly one ticket past the end, so the launch draws
+// total + gridDim.x tickets; the CTA holding the last one returns the counter
+// to zero for the next launch on this stream.
+constexpr unsigned kSpanElems = 16384;  // 192 KB of SwiGLU traffic
+constexpr int kSpanRows = 4;            // 64 KB of RoPE traffic at width 2048
+constexpr int kNormRows = 4;            // 112 KB of norm traffic at hidden 2048
+
+template <int NSRC, int U>
+__global__ void __launch_bounds__(kThreads, 5) k_stream_dyn(ChainArgs a, const float *__restrict__ row_scale,
+                                                            unsigned n_norm, unsigned n_silu, unsigned n_q,
+                                                            unsigned n_k) {
+    __shared__ unsigned s_t[2];
+    const unsigned total = n_norm + n_silu + n_q + n_k;
+    // Ticket `it` of this CTA is in s_t[it & 1]; thread 0 draws ticket it + 1
+    // while the CTA works on ticket it.  Tickets rise, so each work type has a
+    // loop of its own.
+    int it = 0;
+    if (threadIdx.x == 0) s_t[0] = atomicAdd(a.ticket, 1u);
+    __syncthreads();
+    unsigned t = s_t[0];
+    auto next = [&]() {
+        __syncthreads();
+        t = s_t[++it & 1];
+    };
+    if constexpr (NSRC >= 0) {
+        while (t < n_norm) {
+            if (threadIdx.x == 0) s_t[(it + 1) & 1] = atomicAdd(a.ticket, 1u);
+            const int r0 = (int)(n_norm - 1 - t) * kNormRows;
+            norm_rows_write<NSRC, 2>(a, row_scale, r0, min(kNormRows, a.rows - r0), threadIdx.x, blockDim.x);
+            next();
+        }
+    }
+    const size_t n = (size_t)a.rows * a.hidden;
+    unsigned base = n_norm;
+    while (t < base + n_silu) {
+        if (threadIdx.x == 0) s_t[(it + 1) & 1] = atomicAdd(a.ticket, 1u);
+        const size_t lo = (size_t)(t - base) * kSpanElems;
+        silu_range<U>(a.gate, a.up, lo, lo + kSpanElems < n ? lo + kSpanElems : n, threadIdx.x, blockDim.x);
+        next();
+    }
+    base += n_silu;
+    while (t < base + n_q) {
+        if (threadIdx.x == 0) s_t[(it + 1) & 1] = atomicAdd(a.ticket, 1u);
+        const int r0 = (int)(t - base) * kSpanRows;
+        rope_half_rows<U>(a.q, a.q_dim, a.head, a.half, r0, min(kSpanRows, a.rows - r0), a.pos, a.cos_t, a.sin_t,
+                          a.max_pos, a.err, threadIdx.x, blockDim.x);
+        next();
+    }
+    base += n_q;
+    while (t < total) {
+        if (threadIdx.x == 0) s_t[(it + 1) & 1] = atomicAdd(a.ticket, 1u);
+        const int r0 = (int)(t - base) * kSpanRows;
+        rope_half_rows<U>(a.k, a.kv_dim, a.head, a.half, r0, min(kSpanRows, a.rows - r0), a.pos, a.cos_t, a.sin_t,
+                          a.max_pos, a.err, threadIdx.x, blockDim.x);
+        next();
+    }
+    if (threadIdx.x == 0 && t == total + gridDim.x - 1) atomicExch(a.ticket, 0u);
+}
+
 // --------------------------------------------------------------------------
 // Standalone row ops
 // --------------------------------------------------------------------------
@@ -2960,7 +3169,29 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
         return e;
     }
     cudaError_t e = cudaSuccess;
-    if (fq_pipe) {
+    // Gathered bf16 / f32 rows ahead of the streams: the two-pass norm stage,
+    // its writes a ticket type of the streams' kernel.
+    const bool two_pass = (SRC == SRC_BF16 || SRC == SRC_F32) && a.tokens && a.ticket && a.row_scale && !a.w_final &&
+                          (a.xb || a.x_out) && any_stream && !qk_stream && streams_vec && vec && al16(a.table) &&
+                          (!a.xb || al16(a.xb)) && (!a.x_out || al16(a.x_out)) && (!a.resid || al16(a.resid)) &&
+                          al16(a.w_att);
+    if (two_pass) {
+        mark(hook, STAGE_NORM);
+        if constexpr (SRC == SRC_BF16 || SRC == SRC_F32) {
+            static bool attr_set[64] = {false};
+            int dev = 0;
+            cudaGetDevice(&dev);
+            if (dev < 0 || dev >= 64) dev = 0;
+            if (!attr_set[dev]) {
+                e = cudaFuncSetAttribute(k_row_scales<SRC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScaleSmem);
+                attr_set[dev] = e == cudaSuccess;
+            }
+            if (e == cudaSuccess) {
+                k_row_scales<SRC><<<(unsigned)((a.rows + 31) / 32), 32, kScaleSmem, s>>>(a, a.row_scale);
+                e = launched();
+            }
+        }
+    } else if (fq_pipe) {
         mark(hook, STAGE_NORM);
         // f32 x rows: the column-tiled pipeline (32 rows' sums in flight);
         // whole staged rows of f32 leave room for fewer
@@ -2987,7 +3218,7 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
         k_stream_qk<<<grid, c.warps * 32, c.smem, s>>>(a, c.smf);
         e = launched();
     } else if (any_stream) {
-        static unsigned grid[64] = {0};
+        static unsigned grid[64] = {0}, grid_dyn[64] = {0};
         int dev = 0;
         cudaGetDevice(&dev);
         if (dev < 0 || dev >= 64) dev = 0;
@@ -2995,9 +3226,26 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
             int per_sm = 0;
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_stream<2>, kThreads, 0);
             grid[dev] = (unsigned)(device_sms() * (per_sm > 0 ? per_sm : 1));
+            per_sm = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_stream_dyn<-1, 2>, kThreads, 0);
+            grid_dyn[dev] = (unsigned)(device_sms() * (per_sm > 0 ? per_sm : 1));
         }
         mark(hook, STAGE_STREAM);
-        k_stream<2><<<grid[dev], kThreads, 0, s>>>(a);
+        if (a.ticket) {
+            const bool rope = a.rope_mode == 1;
+            const unsigned n_silu = a.gate ? (unsigned)(((size_t)a.rows * a.hidden + kSpanElems - 1) / kSpanElems) : 0;
+            const unsigned n_rows = (unsigned)((a.rows + kSpanRows - 1) / kSpanRows);
+            const unsigned n_q = rope && a.q ? n_rows : 0, n_k = rope && a.k ? n_rows : 0;
+            if (two_pass) {
+                const unsigned n_norm = (unsigned)((a.rows + kNormRows - 1) / kNormRows);
+                if constexpr (SRC == SRC_BF16 || SRC == SRC_F32)
+                    k_stream_dyn<SRC, 2><<<grid_dyn[dev], kThreads, 0, s>>>(a, a.row_scale, n_norm, n_silu, n_q, n_k);
+            } else {
+                k_stream_dyn<-1, 2><<<grid_dyn[dev], kThreads, 0, s>>>(a, nullptr, 0, n_silu, n_q, n_k);
+            }
+        } else {
+            k_stream<2><<<grid[dev], kThreads, 0, s>>>(a);
+        }
         e = launched();
     }
     mark(hook, STAGE_END);

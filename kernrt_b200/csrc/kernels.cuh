@@ -47,6 +47,12 @@ struct ChainArgs {
     const float *resid;
     const float *w_final; int8_t *codes; float *scales; uint16_t *scales16;
     int *err;
+    // The streams' work counter (one per stream that launches chains; zero
+    // between launches), or null: the streams then split their work statically.
+    unsigned *ticket;
+    // Scratch of `rows` floats for the two-pass norm stage's row scales, or
+    // null (the norm stage then runs as one pipeline).
+    float *row_scale;
 };
 // Optional callback around the kernels a chain launch issues: called with the
 // stage about to launch, and with STAGE_END after the last one (the backend

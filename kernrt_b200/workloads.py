@@ -67,11 +67,18 @@ class Workload:
             b += 32 * nb + 4 * nb                 # codes + f32 scales
         return b
 
-    def stage_bytes_per_row(self) -> dict:
+    def stage_bytes_per_row(self, two_pass: bool = False) -> dict:
         """The same compulsory bytes split by the stage that moves them when
-        the chain runs as the norm stage plus the RoPE/SwiGLU stream."""
+        the chain runs as the norm stage plus the RoPE/SwiGLU stream.  With
+        the two-pass norm stage (gathered bf16 / f32 rows) the norm stage
+        only reads the gathered row for the row scales and the stream kernel
+        moves everything else (its second read of the gathered row is traffic
+        beyond the compulsory bytes, so it is not counted)."""
         f = 4
         stream = 2 * f * self.q_dim + 2 * f * self.kv_dim + 3 * f * self.hidden
+        if two_pass:
+            gathered = (2 if self.storage == "bf16" else f) * self.dim
+            return {"norm": gathered, "stream": self.bytes_per_row() - gathered}
         return {"norm": self.bytes_per_row() - stream, "stream": stream}
 
 
