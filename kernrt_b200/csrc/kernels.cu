@@ -2111,36 +2111,53 @@ __device__ __forceinline__ void cp_async_wait_group() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+// n16 16-byte chunks of a staged row added into ss, left to right.
+template <int SRC>
+__device__ __forceinline__ void chain_chunk(float &ss, const uint4 u) {
+    if constexpr (SRC == SRC_BF16) {
+        const float v[8] = {bf16f(u.x & 0xffffu), bf16f(u.x >> 16), bf16f(u.y & 0xffffu), bf16f(u.y >> 16),
+                            bf16f(u.z & 0xffffu), bf16f(u.z >> 16), bf16f(u.w & 0xffffu), bf16f(u.w >> 16)};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
+    } else {
+        const float v[4] = {__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w)};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
+    }
+}
+
 template <int SRC>
 __global__ void __launch_bounds__(32) k_row_scales(ChainArgs a, float *row_scale) {
     static_assert(SRC == SRC_BF16 || SRC == SRC_F32, "bf16 or f32 rows");
     constexpr int ESZ = SRC == SRC_BF16 ? 2 : 4;
+    constexpr int N16 = kScaleTile / 16;  // chunks of a full tile
     extern __shared__ __align__(16) unsigned char ring_smem[];  // [kScaleSlots][32 * kScaleStride]
-    __shared__ const unsigned char *src_row[32];
     auto ring = [&](int slot) { return ring_smem + (size_t)slot * 32 * kScaleStride; };
     const int lane = threadIdx.x, r0 = blockIdx.x * 32, gr = min(32, a.rows - r0);
     const int rb = a.dim * ESZ;  // a multiple of 16
     const int ntiles = (rb + kScaleTile - 1) / kScaleTile;
     bool valid = false;
+    const unsigned char *mine = nullptr;
     if (lane < gr) {
         const int tok = a.tokens[r0 + lane];
         valid = (unsigned)tok < (unsigned)a.vocab;
         if (!valid) set_err(a.err, ERR_TOKEN);
-        src_row[lane] = valid ? static_cast<const unsigned char *>(a.table) + (size_t)tok * rb : nullptr;
-    } else {
-        src_row[lane] = nullptr;
+        else mine = static_cast<const unsigned char *>(a.table) + (size_t)tok * rb;
     }
-    __syncwarp();
-    // tile t: lane l copies chunk (l & 15) of rows 2j + (l >> 4), j < 16
+    // Lane l copies chunk (l & 15) of rows 2j + (l >> 4), j < 16: their row
+    // addresses stay in registers.
+    const unsigned char *src[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+        src[j] = reinterpret_cast<const unsigned char *>(
+            __shfl_sync(kFull, reinterpret_cast<unsigned long long>(mine), 2 * j + (lane >> 4)));
     auto issue = [&](int t) {
         const int off = t * kScaleTile + 16 * (lane & 15);
         if (off >= rb) return;
         unsigned char *dst = ring(t % kScaleSlots) + (lane >> 4) * kScaleStride + 16 * (lane & 15);
-#pragma unroll 4
-        for (int j = 0; j < 16; ++j) {
-            const unsigned char *sp = src_row[2 * j + (lane >> 4)];
-            if (sp) cp_async16(dst + 2 * j * kScaleStride, sp + off);
-        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            if (src[j]) cp_async16(dst + 2 * j * kScaleStride, src[j] + off);
     };
 #pragma unroll
     for (int t = 0; t < kScaleSlots - 1; ++t) {
@@ -2154,22 +2171,18 @@ __global__ void __launch_bounds__(32) k_row_scales(ChainArgs a, float *row_scale
         if (t + kScaleSlots - 1 < ntiles) issue(t + kScaleSlots - 1);  // the slot tile t - 1 used
         cp_async_commit();
         if (valid) {
-            const unsigned char *row = ring(t % kScaleSlots) + lane * kScaleStride;
+            const uint4 *row = reinterpret_cast<const uint4 *>(ring(t % kScaleSlots) + lane * kScaleStride);
             const int n16 = min(kScaleTile, rb - t * kScaleTile) >> 4;
-#pragma unroll 4
-            for (int c = 0; c < n16; ++c) {
-                const uint4 u = *reinterpret_cast<const uint4 *>(row + 16 * c);
-                if constexpr (SRC == SRC_BF16) {
-                    const float v[8] = {bf16f(u.x & 0xffffu), bf16f(u.x >> 16), bf16f(u.y & 0xffffu), bf16f(u.y >> 16),
-                                        bf16f(u.z & 0xffffu), bf16f(u.z >> 16), bf16f(u.w & 0xffffu), bf16f(u.w >> 16)};
+            if (n16 == N16) {
+                // a full tile as one straight block: its loads can run ahead
+                // of the dependent adds
+                uint4 u[N16];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
-                } else {
-                    const float v[4] = {__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
-                                        __uint_as_float(u.w)};
+                for (int c = 0; c < N16; ++c) u[c] = row[c];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) ss = add_rn(ss, mul_rn(v[e], v[e]));
-                }
+                for (int c = 0; c < N16; ++c) chain_chunk<SRC>(ss, u[c]);
+            } else {
+                for (int c = 0; c < n16; ++c) chain_chunk<SRC>(ss, row[c]);
             }
         }
     }
