@@ -326,6 +326,14 @@ def run_kernrt(args, rank, world, local):
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return float(t.item())
 
+    def gather_over_ranks(v: float) -> list:
+        if dist is None:
+            return [v]
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+        out = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(out, t)
+        return [float(x.item()) for x in out]
+
     def max_over_ranks(v: float) -> float:
         if dist is None:
             return v
@@ -409,7 +417,8 @@ def run_kernrt(args, rank, world, local):
     stages = {stage_kernel[k]: v for k, v in b.stage_times().items()}
     b.stage_timing(False)
     per_launch = [s.elapsed_time(e) for s, e in ev]  # ms
-    total_ms = max_over_ranks(sum(per_launch))
+    rank_ms = gather_over_ranks(sum(per_launch))  # each rank's timed steps, device ms
+    total_ms = max(rank_ms)
     value = total_rows * args.steps / (total_ms / 1000.0)
     bpr = WL.bytes_per_row()
     peak, peak_kind = peaks()
@@ -489,7 +498,8 @@ def run_kernrt(args, rank, world, local):
                        "how": "CUDA events around each step's launch(es) on the backend's stream; gate "
                               "restored from a pristine device copy before each step, outside the events; "
                               "per-kernel times (roofline) from further steps with the backend's stage events",
-                       "region_wall_s_incl_restores": region_s},
+                       "region_wall_s_incl_restores": region_s,
+                       "per_rank_ms_per_step": [m / args.steps for m in rank_ms]},
             "roofline": {"bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peak,
                          "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": None if tpr is None else tpr * R,
