@@ -300,6 +300,19 @@ typedef uint64_t kernrt_mat;
 int kernrt_cuda_prepare_matrix(kernrt_cuda_ctx *ctx, int kind, const void *data, const float *scales,
                                size_t out_dim, size_t in_dim, kernrt_mat *out);
 
+/* Exact or tolerance mode of the projections (no counterpart in the
+ * reference: its backends each have one arithmetic).  exact = 1 (the default)
+ * keeps every projection in the reference's order, bit-identical to it.
+ * exact = 0 runs bf16 projections of at least 16 rows (prefill) on the tensor
+ * cores: x is split into bf16 hi + lo halves and both are multiplied by W
+ * (tcgen05.mma, f32 accumulation), which keeps ~16 bits of each activation's
+ * mantissa; results differ from the reference's sequential dot by the
+ * reordered f32 sum (the bar tests/backends.rs:129-148 sets for a non-oracle
+ * backend is 1e-3 on a model's logits).  Other storages and decode-sized calls
+ * stay exact.  KERNRT_CUDA_EXACT=0 in the environment sets exact = 0 at
+ * kernrt_cuda_create. */
+int kernrt_cuda_set_exact(kernrt_cuda_ctx *ctx, int exact);
+
 /* Backend::project (mod.rs:318; reference.rs:259-274): y[r, o] =
  * dot(decode_row(W, o), x[r]) for rows r; x [rows, in_dim], y [rows, out_dim].
  * The trait's project_qkv / project_gate_up defaults (mod.rs:326-337) are

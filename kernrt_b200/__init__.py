@@ -139,6 +139,7 @@ SIGNATURES = {
     "kernrt_cuda_safetensors_tensor": (C.c_int, [C.c_char_p, C.c_char_p, C.POINTER(StTensor)]),
     "kernrt_cuda_prepare_embedding_file": (C.c_int, [P, C.c_char_p, C.c_char_p, C.c_int]),
     "kernrt_cuda_selftest_wait": (C.c_int, [P, C.c_uint64, C.c_int]),
+    "kernrt_cuda_set_exact": (C.c_int, [P, C.c_int]),
 }
 
 # safetensors dtypes (kernrt_st_tensor.dtype)
@@ -420,6 +421,12 @@ class CudaBackend:
         _ok(self._lib.kernrt_cuda_prepare_matrix(self._ctx, kind, _ptr(data), None if sc is None else _ptr(sc),
                                                  out_dim, in_dim, C.byref(h)))
         return h.value
+
+    def set_exact(self, exact: bool) -> None:
+        """kernrt_cuda_set_exact: False sends bf16 projections of >= 16 rows to
+        the tensor cores (tolerance mode); True (the default) keeps them in
+        the reference's order."""
+        _ok(self._lib.kernrt_cuda_set_exact(self._ctx, int(bool(exact))))
 
     def project(self, w: int, x: int, y: int, rows: int) -> None:
         _ok(self._lib.kernrt_cuda_project(self._ctx, w, x, y, rows))

@@ -92,6 +92,7 @@ public:
         cudaFree(att_scratch_);
         cudaFree(d_err_);
         cudaFree(d_ticket_);
+        cudaFree(split_);
         cudaFree(row_scales_);
         cudaFreeHost(h_err_);
         cudaFreeHost(stage_host_);
@@ -501,6 +502,32 @@ public:
         return mats_[h - 1];
     }
 
+    // Tolerance mode: bf16 projections of at least kTcMinRows rows go to the
+    // tensor cores (tc_project.cu) instead of the exact-order kernels.
+    static constexpr size_t kTcMinRows = 16;
+    bool tc_path(const DevMatrix &m, const float *x, const float *y, size_t rows) const {
+        return !exact_ && m.src == SRC_BF16 && rows >= kTcMinRows &&
+               project_tc_supported((int)m.out_dim, (int)m.in_dim, m.data, x, y);
+    }
+    // x split into bf16 hi and lo halves ([rows, in_dim] each), in scratch
+    // grown as needed (cudaFree waits for queued kernels still reading it).
+    uint16_t *split_x(const float *x, size_t rows, size_t in_dim) {
+        const size_t n = rows * in_dim;
+        if (2 * n > split_cap_) {
+            cudaFree(split_);
+            split_ = nullptr;
+            split_cap_ = 0;
+            check(cudaMalloc(&split_, 2 * n * sizeof(uint16_t)), "cudaMalloc(split activations)");
+            split_cap_ = 2 * n;
+        }
+        launch_or_fail(launch_split_bf16(x, split_, split_ + n, n, stream_), "project (split)");
+        return split_;
+    }
+    void set_exact(bool exact) {
+        flush();
+        exact_ = exact;
+    }
+
     // reference.rs:259-274: y[r, o] = dot(decode_row(W, o), x[r]).
     void project(uint64_t w, kernrt_buf x, kernrt_buf y, size_t rows) {
         const DevMatrix &m = mat(w);
@@ -511,6 +538,13 @@ public:
         fits_int(rows * std::max(m.in_dim, m.out_dim), "project");
         flush();
         if (rows == 0) return;
+        if (tc_path(m, f(xb), f(yb), rows)) {
+            const uint16_t *hi = split_x(f(xb), rows, m.in_dim);
+            launch_or_fail(launch_project_tc(static_cast<const uint16_t *>(m.data), (int)m.out_dim, (int)m.in_dim, hi,
+                                             hi + rows * m.in_dim, (int)rows, f(yb), d_err_, stream_),
+                           "project (tensor cores)");
+            return;
+        }
         launch_or_fail(launch_project(m.src, m.data, m.scales, (int)m.out_dim, (int)m.in_dim, f(xb), (int)rows, f(yb),
                                       d_err_, stream_),
                        "project");
@@ -550,6 +584,16 @@ public:
         }
         flush();
         if (rows == 0) return;
+        bool tc = true;
+        for (int i = 0; i < n; ++i) tc = tc && tc_path(mat(ws[i]), f(xb), yp[i], rows);
+        if (tc) {  // one split of x for the n projections
+            const uint16_t *hi = split_x(f(xb), rows, m0.in_dim);
+            for (int i = 0; i < n; ++i)
+                launch_or_fail(launch_project_tc(static_cast<const uint16_t *>(wp[i]), outs[i], (int)m0.in_dim, hi,
+                                                 hi + rows * m0.in_dim, (int)rows, yp[i], d_err_, stream_),
+                               "project (tensor cores)");
+            return;
+        }
         launch_or_fail(launch_project_set(m0.src, n, wp, sp, outs, (int)m0.in_dim, f(xb), (int)rows, yp, d_err_,
                                           stream_),
                        "project");
@@ -1544,6 +1588,9 @@ private:
     const char *storage_ = "f32";
     int *d_err_ = nullptr;
     unsigned *d_ticket_ = nullptr;  // the chain streams' work counter on stream_ (zero between launches)
+    bool exact_ = true;             // false: tolerance-mode tensor-core projections (KERNRT_CUDA_EXACT=0)
+    uint16_t *split_ = nullptr;     // bf16 hi / lo halves of a projection's x
+    size_t split_cap_ = 0;          // elements
     float *row_scales_ = nullptr;   // the two-pass norm stage's row scales (chains on stream_)
     size_t row_scales_cap_ = 0;
     int *h_err_ = nullptr;
@@ -1618,6 +1665,10 @@ int kernrt_cuda_safetensors_tensor(const char *path, const char *name, kernrt_st
     return KERNRT_OK;
 }
 
+int kernrt_cuda_set_exact(kernrt_cuda_ctx *ctx, int exact) {
+    return guard(ctx, [&](krt::Backend &b) { b.set_exact(exact != 0); });
+}
+
 int kernrt_cuda_selftest_wait(kernrt_cuda_ctx *ctx, uint64_t cycles, int complete) {
     return guard(ctx, [&](krt::Backend &b) { b.selftest_wait(cycles, complete); });
 }
@@ -1667,6 +1718,9 @@ int kernrt_cuda_create(int device, kernrt_cuda_ctx **out) {
     }
     try {
         auto *c = new kernrt_cuda_ctx{new krt::Backend(device)};
+        // KERNRT_CUDA_EXACT=0: tolerance-mode tensor-core projections
+        const char *exact = std::getenv("KERNRT_CUDA_EXACT");
+        if (exact && exact[0] == '0' && exact[1] == '\0') c->b->set_exact(false);
         *out = c;
         return KERNRT_OK;
     } catch (const krt::Error &e) {

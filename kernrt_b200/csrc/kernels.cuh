@@ -119,6 +119,13 @@ cudaError_t launch_project(int src, const void *w, const float *wsc, int out_dim
 // kernel takes them all (the trait's project_qkv / project_gate_up).
 cudaError_t launch_project_set(int src, int n, const void *const *w, const float *const *wsc, const int *out_dim,
                                int in_dim, const float *x, int rows, float *const *y, int *err, cudaStream_t s);
+// Tolerance-mode projections on the tensor cores (tc_project.cu): W bf16
+// [out_dim, in_dim], in_dim % 8 == 0; x is first split into bf16 hi and lo
+// halves ([rows, in_dim] each) by launch_split_bf16.
+bool project_tc_supported(int out_dim, int in_dim, const void *w, const float *x, const float *y);
+cudaError_t launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t n, cudaStream_t s);
+cudaError_t launch_project_tc(const uint16_t *w, int out_dim, int in_dim, const uint16_t *hi, const uint16_t *lo,
+                              int rows, float *y, int *err, cudaStream_t s);
 // Row i of k and v into cache row dst_rows[i] of caches [rows_total, kv_dim].
 cudaError_t launch_kv_write(float *kc, float *vc, int kv_dim, const int32_t *dst_rows, const float *k, const float *v,
                             int rows, cudaStream_t s);
