@@ -319,6 +319,19 @@ def run_kernrt(args, rank, world, local):
         if dist is not None:
             dist.barrier()
 
+    # Host-side check between phases (never inside the timed steps): every
+    # rank must reach the phase within a bounded time, or the run stops with
+    # the missing ranks named before any of the phase's launches.
+    watch = None
+    if dist is not None:
+        from kernrt_b200.ranks import StepWatch
+
+        watch = StepWatch(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=120.0)
+
+    def phase(name):
+        if watch is not None:
+            watch.enter(name)
+
     def sum_over_ranks(v: float) -> float:
         if dist is None:
             return v
@@ -383,10 +396,12 @@ def run_kernrt(args, rank, world, local):
     def restore_gate():
         b.copy(h["gate0"], 0, h["gate"], 0, R * I)
 
+    phase("warmup")
     for _ in range(max(3, args.warmup)):
         restore_gate()
         b.layer_chain(**chain)
     b.synchronize()
+    phase("timed")
     barrier()
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -461,6 +476,7 @@ def run_kernrt(args, rank, world, local):
                                k_out=host_out["k"].data_ptr(), gate_out=host_out["gate"].data_ptr(),
                                w_att=h["w_att"])
 
+        phase("e2e")
         e2e_step()
         barrier()
         t0 = time.perf_counter()

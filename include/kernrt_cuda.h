@@ -286,6 +286,19 @@ int kernrt_cuda_stage_times(kernrt_cuda_ctx *ctx, double ms[3], uint64_t launche
 int kernrt_cuda_lfm2_conv_block(kernrt_cuda_ctx *ctx, kernrt_buf bcx, kernrt_buf kernel,
                                 kernrt_buf ring, kernrt_buf cy, size_t rows, size_t dim, size_t k);
 
+/* The same block for one shard of a sequence split across devices (no
+ * counterpart in the reference: KernRT runs one device).  bcx holds `halo`
+ * (< k) rows before the shard, staged by the caller from the preceding shard's
+ * rows, then the shard's `rows` rows; the halo rows feed the conv of the
+ * shard's first rows exactly as in the unsharded sequence and give no output,
+ * so cy (`rows` rows) equals the unsharded block's rows of the shard bit for
+ * bit.  halo = 0 is the sequence's first shard (zero padding, as
+ * kernrt_cuda_lfm2_conv_block).  ring = 0 skips the ring update (a shard that
+ * does not end the sequence); the last shard passes the ring, and then needs at
+ * least k - 1 rows when halo > 0. */
+int kernrt_cuda_lfm2_conv_block_halo(kernrt_cuda_ctx *ctx, kernrt_buf bcx, kernrt_buf kernel, kernrt_buf ring,
+                                     kernrt_buf cy, size_t rows, size_t dim, size_t k, size_t halo);
+
 /* --- Contractions: Backend::project / logits / kv_write / attention ----------
  * The reference backend's arithmetic order (reference.rs:73-79 dot, one f32
  * accumulator left to right, multiply then add): projections, logits and the

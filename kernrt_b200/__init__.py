@@ -124,6 +124,7 @@ SIGNATURES = {
     "kernrt_cuda_rope_prepare": (C.c_int, [P, C.c_float, SZ, SZ]),
     "kernrt_cuda_layer_chain": (C.c_int, [P, C.POINTER(ChainArgs)]),
     "kernrt_cuda_lfm2_conv_block": (C.c_int, [P, Buf, Buf, Buf, Buf, SZ, SZ, SZ]),
+    "kernrt_cuda_lfm2_conv_block_halo": (C.c_int, [P, Buf, Buf, Buf, Buf, SZ, SZ, SZ, SZ]),
     "kernrt_cuda_layer_chain_host": (C.c_int, [P, C.POINTER(ChainHostArgs)]),
     "kernrt_cuda_stage_timing": (C.c_int, [P, C.c_int]),
     "kernrt_cuda_stage_times": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
@@ -457,6 +458,12 @@ class CudaBackend:
     def lfm2_conv_block(self, bcx: int, kernel: int, ring: int, cy: int, rows: int, dim: int,
                         k: int) -> None:
         _ok(self._lib.kernrt_cuda_lfm2_conv_block(self._ctx, bcx, kernel, ring, cy, rows, dim, k))
+
+    def lfm2_conv_block_halo(self, bcx: int, kernel: int, ring: int, cy: int, rows: int, dim: int, k: int,
+                             halo: int) -> None:
+        """kernrt_cuda_lfm2_conv_block_halo: one shard of a sequence, bcx with
+        `halo` preceding rows first; ring 0 skips the ring update."""
+        _ok(self._lib.kernrt_cuda_lfm2_conv_block_halo(self._ctx, bcx, kernel, ring, cy, rows, dim, k, halo))
 
 
 def embed_rows_noalloc(device: int, kind: int, table_ptr: int, scales_ptr: int, vocab: int, dim: int,

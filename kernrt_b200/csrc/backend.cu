@@ -351,6 +351,9 @@ public:
     kernrt_buf alloc_bytes(size_t bytes) {
         Buffer b;
         b.bytes = bytes;
+        // Fault injection for tests: KERNRT_CUDA_FAIL_ALLOC=n makes this
+        // context's n-th buffer allocation fail as an exhausted device would.
+        if (++allocs_ == fail_alloc_at_) check(cudaErrorMemoryAllocation, "cudaMalloc");
         check(cudaMalloc(&b.ptr, std::max<size_t>(bytes, 16)), "cudaMalloc");
         check(cudaMemsetAsync(b.ptr, 0, std::max<size_t>(bytes, 16), stream_), "cudaMemset");
         bufs_.push_back(b);
@@ -523,6 +526,7 @@ public:
         launch_or_fail(launch_split_bf16(x, split_, split_ + n, n, stream_), "project (split)");
         return split_;
     }
+    void set_fail_alloc(uint64_t n) { fail_alloc_at_ = n; }
     void set_exact(bool exact) {
         flush();
         exact_ = exact;
@@ -1040,18 +1044,24 @@ public:
         launch_or_fail(chain_launch(src, a), "layer_chain");
     }
 
+    // `halo` (< k) leading rows of bcx belong to the rows before this shard of
+    // the sequence: they feed h and give no output; cy gets `rows` rows.  A 0
+    // ring handle skips the ring (a shard that does not end the sequence).
     void lfm2_conv_block(kernrt_buf bcx, kernrt_buf kernel, kernrt_buf ring, kernrt_buf cy, size_t rows,
-                         size_t dim, size_t k) {
+                         size_t dim, size_t k, size_t halo = 0) {
         if (k == 0) fail(KERNRT_E_INVALID, "conv kernel size must be positive");
-        if (cy == bcx || ring == bcx || ring == cy) fail(KERNRT_E_INVALID, "buffers must be distinct");
-        span(buf(bcx), 0, rows * 3 * dim, "conv block bcx");
+        if (halo >= k) fail(KERNRT_E_INVALID, "conv block halo must be shorter than the kernel");
+        if (cy == bcx || (ring && (ring == bcx || ring == cy))) fail(KERNRT_E_INVALID, "buffers must be distinct");
+        if (ring && halo && rows < k - 1) fail(KERNRT_E_INVALID, "a shard that seeds the ring needs k - 1 rows");
+        span(buf(bcx), 0, (halo + rows) * 3 * dim, "conv block bcx");
         span(buf(kernel), 0, dim * k, "conv block kernel");
         span(buf(cy), 0, rows * dim, "conv block cy");
-        if (k > 1) span(buf(ring), 0, (k - 1) * dim, "conv block ring");
-        fits_int(rows * 3 * dim, "lfm2_conv_block");
+        if (ring && k > 1) span(buf(ring), 0, (k - 1) * dim, "conv block ring");
+        fits_int((halo + rows) * 3 * dim, "lfm2_conv_block");
         flush();
-        launch_or_fail(launch_lfm2_conv_block(f(buf(bcx)), f(buf(kernel)), f(buf(ring)), f(buf(cy)), (int)rows,
-                                              (int)dim, (int)k, stream_),
+        if (rows == 0) return;
+        launch_or_fail(launch_lfm2_conv_block(f(buf(bcx)), f(buf(kernel)), ring ? f(buf(ring)) : nullptr, f(buf(cy)),
+                                              (int)(halo + rows), (int)dim, (int)k, stream_, (int)halo),
                        "lfm2_conv_block");
     }
 
@@ -1589,6 +1599,8 @@ private:
     int *d_err_ = nullptr;
     unsigned *d_ticket_ = nullptr;  // the chain streams' work counter on stream_ (zero between launches)
     bool exact_ = true;             // false: tolerance-mode tensor-core projections (KERNRT_CUDA_EXACT=0)
+    uint64_t allocs_ = 0;           // buffer allocations so far
+    uint64_t fail_alloc_at_ = 0;    // the allocation to fail (KERNRT_CUDA_FAIL_ALLOC; 0 = none)
     uint16_t *split_ = nullptr;     // bf16 hi / lo halves of a projection's x
     size_t split_cap_ = 0;          // elements
     float *row_scales_ = nullptr;   // the two-pass norm stage's row scales (chains on stream_)
@@ -1721,6 +1733,9 @@ int kernrt_cuda_create(int device, kernrt_cuda_ctx **out) {
         // KERNRT_CUDA_EXACT=0: tolerance-mode tensor-core projections
         const char *exact = std::getenv("KERNRT_CUDA_EXACT");
         if (exact && exact[0] == '0' && exact[1] == '\0') c->b->set_exact(false);
+        // test hook, off unless set: fail this context's n-th buffer allocation
+        const char *fail_at = std::getenv("KERNRT_CUDA_FAIL_ALLOC");
+        if (fail_at && *fail_at) c->b->set_fail_alloc(std::strtoull(fail_at, nullptr, 10));
         *out = c;
         return KERNRT_OK;
     } catch (const krt::Error &e) {
@@ -1891,7 +1906,15 @@ int kernrt_cuda_stage_times(kernrt_cuda_ctx *ctx, double *ms, uint64_t *launches
 
 int kernrt_cuda_lfm2_conv_block(kernrt_cuda_ctx *ctx, kernrt_buf bcx, kernrt_buf kernel, kernrt_buf ring,
                                 kernrt_buf cy, size_t rows, size_t dim, size_t k) {
-    return guard(ctx, [&](krt::Backend &b) { b.lfm2_conv_block(bcx, kernel, ring, cy, rows, dim, k); });
+    return guard(ctx, [&](krt::Backend &b) {
+        if (!ring && k > 1) krt::fail(KERNRT_E_INVALID, "conv block needs its ring");
+        b.lfm2_conv_block(bcx, kernel, ring, cy, rows, dim, k);
+    });
+}
+
+int kernrt_cuda_lfm2_conv_block_halo(kernrt_cuda_ctx *ctx, kernrt_buf bcx, kernrt_buf kernel, kernrt_buf ring,
+                                     kernrt_buf cy, size_t rows, size_t dim, size_t k, size_t halo) {
+    return guard(ctx, [&](krt::Backend &b) { b.lfm2_conv_block(bcx, kernel, ring, cy, rows, dim, k, halo); });
 }
 
 int kernrt_cuda_prepare_matrix(kernrt_cuda_ctx *ctx, int kind, const void *data, const float *scales, size_t out_dim,

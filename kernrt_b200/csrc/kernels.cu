@@ -2573,11 +2573,13 @@ __global__ void __launch_bounds__(kThreads) k_conv_decode(float *out, const floa
 __global__ void __launch_bounds__(kThreads) k_lfm2_conv_block(const float *__restrict__ bcx,
                                                               const float *__restrict__ w,
                                                               float *__restrict__ ring,
-                                                              float *__restrict__ cy, int rows,
+                                                              float *__restrict__ cy, int lead, int rows,
                                                               int dim, int k) {
+    // output element idx: bcx row lead + idx / dim (the first `lead` rows are
+    // a shard's halo, as in k_lfm2_conv_block_tiled)
     const size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-    if (idx >= (size_t)rows * dim) return;
-    const int r = (int)(idx / dim), i = (int)(idx - (size_t)r * dim);
+    if (idx >= (size_t)(rows - lead) * dim) return;
+    const int r = lead + (int)(idx / dim), i = (int)(idx - (size_t)(r - lead) * dim);
     const size_t w3 = (size_t)3 * dim;
     float acc = 0.0f, hr = 0.0f;
     for (int j = 0; j < k; ++j) {
@@ -2589,7 +2591,7 @@ __global__ void __launch_bounds__(kThreads) k_lfm2_conv_block(const float *__res
         }
     }
     cy[idx] = mul_rn(__ldg(bcx + r * w3 + dim + i), acc);
-    if (k > 1) {
+    if (ring && k > 1) {
         const int take = min(rows, k - 1);
         if (r >= rows - take) ring[(size_t)(k - 1 - take + (r - (rows - take))) * dim + i] = hr;
     }
@@ -2658,16 +2660,20 @@ __global__ void __launch_bounds__(kThreads) k_conv_prefill_tiled(float *__restri
 }
 
 // lfm2.rs:584-624, row-tiled: h = B*x for the tile's rows and its halo, the
-// taps in order, cy = C*co, and the last k-1 rows of h into the ring.
+// taps in order, cy = C*co, and the last k-1 rows of h into the ring.  The
+// first `lead` (< K) rows of bcx are a shard's halo: they feed h of the rows
+// after them and give no output (cy row r - lead for bcx row r); zero padding
+// applies before bcx row 0.
 template <int K, int V, int RT>
 __global__ void __launch_bounds__(kThreads) k_lfm2_conv_block_tiled(const float *__restrict__ bcx,
                                                                     const float *__restrict__ w,
                                                                     float *__restrict__ ring,
-                                                                    float *__restrict__ cy, int rows, int dim) {
+                                                                    float *__restrict__ cy, int lead, int rows,
+                                                                    int dim) {
     const int ncg = dim / V;
     const unsigned t = blockIdx.x * blockDim.x + threadIdx.x;
     const int tile = (int)(t / (unsigned)ncg), c = (int)(t - (unsigned)tile * ncg) * V;
-    const int r0 = tile * RT;
+    const int r0 = lead + tile * RT;
     if (r0 >= rows) return;
     const size_t w3 = (size_t)3 * dim;
     float wk[V][K];
@@ -2704,8 +2710,8 @@ __global__ void __launch_bounds__(kThreads) k_lfm2_conv_block_tiled(const float 
                 if (r - (K - 1) + j >= 0) acc = add_rn(acc, mul_rn(wk[v][j], hs[q + j][v]));
             o[v] = mul_rn(cs[q][v], acc);
         }
-        stv<V>(cy + (size_t)r * dim + c, o);
-        if (r >= rows - take) stv<V>(ring + (size_t)(K - 1 - take + (r - (rows - take))) * dim + c, hs[q + K - 1]);
+        stv<V>(cy + (size_t)(r - lead) * dim + c, o);
+        if (ring && r >= rows - take) stv<V>(ring + (size_t)(K - 1 - take + (r - (rows - take))) * dim + c, hs[q + K - 1]);
     }
 }
 
@@ -3408,10 +3414,11 @@ cudaError_t launch_mul(float *o, const float *a, const float *b, size_t n, bool 
 
 // The row-tiled kernels for K = 2..4 (float4 channels when dim and the
 // pointers allow), the per-element kernel for other sizes.
+// `rows` output rows of `dim` channels; `args` are the kernel's arguments.
 template <int K, int V, int RT, typename Kern, typename... Args>
 cudaError_t launch_conv_tiled(Kern kern, int rows, int dim, cudaStream_t s, Args... args) {
     const size_t threads = (size_t)(dim / V) * (size_t)((rows + RT - 1) / RT);
-    kern<<<grid_for(threads, kThreads), kThreads, 0, s>>>(args..., rows, dim);
+    kern<<<grid_for(threads, kThreads), kThreads, 0, s>>>(args...);
     return launched();
 }
 
@@ -3424,8 +3431,8 @@ cudaError_t launch_conv_prefill(float *out, const float *x, const float *w, int 
     constexpr int RT = 8;
 #define KRT_CONV(KK)                                                                                        \
     if (k == KK)                                                                                            \
-        return v4 ? launch_conv_tiled<KK, 4, RT>(k_conv_prefill_tiled<KK, 4, RT>, rows, dim, s, out, x, w)  \
-                  : launch_conv_tiled<KK, 1, RT>(k_conv_prefill_tiled<KK, 1, RT>, rows, dim, s, out, x, w);
+        return v4 ? launch_conv_tiled<KK, 4, RT>(k_conv_prefill_tiled<KK, 4, RT>, rows, dim, s, out, x, w, rows, dim) \
+                  : launch_conv_tiled<KK, 1, RT>(k_conv_prefill_tiled<KK, 1, RT>, rows, dim, s, out, x, w, rows, dim);
     KRT_CONV(2)
     KRT_CONV(3)
     KRT_CONV(4)
@@ -3442,22 +3449,23 @@ cudaError_t launch_conv_decode(float *out, const float *x, const float *w, float
 }
 
 cudaError_t launch_lfm2_conv_block(const float *bcx, const float *w, float *ring, float *cy, int rows,
-                                   int dim, int k, cudaStream_t s) {
+                                   int dim, int k, cudaStream_t s, int lead) {
     if (rows <= 0 || dim <= 0) return cudaSuccess;
-    const bool v4 = dim % 4 == 0 && aligned16(bcx) && aligned16(cy) && aligned16(ring);
+    const bool v4 = dim % 4 == 0 && aligned16(bcx) && aligned16(cy) && (!ring || aligned16(ring));
     constexpr int RT = 4;
-#define KRT_CONV(KK)                                                                                     \
-    if (k == KK)                                                                                         \
-        return v4 ? launch_conv_tiled<KK, 4, RT>(k_lfm2_conv_block_tiled<KK, 4, RT>, rows, dim, s, bcx, w, \
-                                                 ring, cy)                                               \
-                  : launch_conv_tiled<KK, 1, RT>(k_lfm2_conv_block_tiled<KK, 1, RT>, rows, dim, s, bcx, w, \
-                                                 ring, cy);
+    // threads cover the output rows only
+#define KRT_CONV(KK)                                                                                           \
+    if (k == KK)                                                                                               \
+        return v4 ? launch_conv_tiled<KK, 4, RT>(k_lfm2_conv_block_tiled<KK, 4, RT>, rows - lead, dim, s, bcx, w, \
+                                                 ring, cy, lead, rows, dim)                                    \
+                  : launch_conv_tiled<KK, 1, RT>(k_lfm2_conv_block_tiled<KK, 1, RT>, rows - lead, dim, s, bcx, w, \
+                                                 ring, cy, lead, rows, dim);
     KRT_CONV(2)
     KRT_CONV(3)
     KRT_CONV(4)
 #undef KRT_CONV
-    k_lfm2_conv_block<<<grid_for((size_t)rows * dim, kThreads), kThreads, 0, s>>>(bcx, w, ring, cy,
-                                                                                  rows, dim, k);
+    k_lfm2_conv_block<<<grid_for((size_t)(rows - lead) * dim, kThreads), kThreads, 0, s>>>(bcx, w, ring, cy, lead,
+                                                                                           rows, dim, k);
     return launched();
 }
 

@@ -92,8 +92,11 @@ cudaError_t launch_conv_prefill(float *out, const float *x, const float *w, int 
                                 int k, cudaStream_t s);
 cudaError_t launch_conv_decode(float *out, const float *x, const float *w, float *state, int dim,
                                int k, cudaStream_t s);
+// The first `lead` (< k) of the `rows` rows of bcx are a shard's halo: they
+// only feed the conv of the rows after them; cy gets rows - lead rows.  A null
+// ring skips the ring update.
 cudaError_t launch_lfm2_conv_block(const float *bcx, const float *w, float *ring, float *cy,
-                                   int rows, int dim, int k, cudaStream_t s);
+                                   int rows, int dim, int k, cudaStream_t s, int lead = 0);
 cudaError_t launch_quantize_q8(const float *x, int rows, int dim, int8_t *codes, float *scales,
                                uint16_t *scales16, cudaStream_t s);
 // Conversions for tables loaded from files (safetensors.rs / hf.rs): widen

@@ -231,7 +231,82 @@ def run(reps: int, only: str | None = None):
         decode_latency(B)
     if B.want("decode token"):
         model_decode(B)
+    # --- LFM2-700M's whole layer stack of row ops
+    if B.want("lfm2 layer stack"):
+        lfm2_stack(B)
     return B
+
+
+# LFM2-700M's attention layers (the other 10 of its 16 are short-conv layers).
+LFM2_ATTENTION_LAYERS = (2, 5, 8, 10, 12, 14)
+
+
+def lfm2_stack(B, n_layers: int = 16):
+    """the row ops of LFM2-700M's 16 layers (10 short-conv, 6
+    attention, in the model's order) over one 1024-token prefill, as the
+    driver issues them (lfm2.rs:560-632) with the contractions elided: each
+    projection's output is a fixed random buffer (bcx for the conv
+    in-projection, o for the out / o / down projections).  Per layer: rms_norm;
+    the conv block (h = B*x, conv, ring, C*co) or qk_norm(q), qk_norm(k), rope;
+    add; rms_norm; silu_mul; add.  The backend fuses each add with the
+    rms_norm after it and the q/k norms with RoPE; the bytes counted are those
+    fused ops' compulsory reads and writes."""
+    wk = W.LFM2_700M
+    b = B.b
+    R, H, Q, KV, I, hd, k = wk.rows, wk.dim, wk.q_dim, wk.kv_dim, wk.hidden, wk.head, wk.conv_k
+    x, xb, o = B.buf(R * H), B.b.alloc(R * H), B.buf(R * H, 0.01)
+    bcx, cy = B.buf(R * 3 * H), b.alloc(R * H)
+    q, kk, gate, up = B.buf(R * Q), B.buf(R * KV), B.buf(R * I), B.buf(R * I)
+    w_op, w_ffn = b.upload(np.ones(H, np.float32)), b.upload(np.ones(H, np.float32))
+    wq, wkk = b.upload(np.ones(hd, np.float32)), b.upload(np.ones(hd, np.float32))
+    conv = {l: (B.buf(H * k, 0.3), b.alloc((k - 1) * H)) for l in range(n_layers) if l not in LFM2_ATTENTION_LAYERS}
+    pos = np.arange(R, dtype=np.uint64)
+    b.rope_prepare(wk.theta, hd, R)
+    x0, gate0 = b.alloc(R * H), b.alloc(R * I)
+    b.copy(x, 0, x0, 0, R * H)
+    b.copy(gate, 0, gate0, 0, R * I)
+
+    def setup():  # the stack's in-place inputs back to their start
+        b.copy(x0, 0, x, 0, R * H)
+        b.copy(gate0, 0, gate, 0, R * I)
+
+    def stack():
+        for l in range(n_layers):
+            b.rms_norm(xb, x, w_op, R, H, wk.eps)
+            if l in LFM2_ATTENTION_LAYERS:
+                b.qk_norm(q, R, Q, hd, wq, wk.eps)
+                b.qk_norm(kk, R, KV, hd, wkk, wk.eps)
+                b.rope(q, kk, Q, KV, R, pos, hd, wk.theta, False)
+            else:
+                kern, ring = conv[l]
+                b.lfm2_conv_block(bcx, kern, ring, cy, R, H, k)
+            b.add_in_place(x, o, R * H)
+            b.rms_norm(xb, x, w_ffn, R, H, wk.eps)
+            b.silu_mul(gate, up, R * I)
+            b.add_in_place(x, o, R * H)
+
+    f = 4
+    n_attn = sum(1 for l in range(n_layers) if l in LFM2_ATTENTION_LAYERS)
+    nbytes = R * (2 * f * H                      # the first rms_norm: x read, xb written
+                  + (2 * n_layers - 1) * 4 * f * H  # each add + rms_norm pair: x, o read; x, xb written
+                  + 3 * f * H                    # the last add: x, o read; x written
+                  + (n_layers - n_attn) * 4 * f * H  # conv block: bcx read, cy written
+                  + n_attn * 2 * f * (Q + KV)    # q/k norms + RoPE: q, k read and written
+                  + n_layers * 3 * f * I)        # SwiGLU: gate, up read; gate written
+    B.time(f"lfm2 layer stack: {wk.name} ({n_layers} layers: {n_layers - n_attn} conv + {n_attn} attention, "
+           f"{R} rows, row ops)", stack, nbytes, setup=setup,
+           note="contractions elided (fixed projection outputs)")
+    # One of four ranks' share of a conv block when the sequence is split on
+    # rows (W.conv_shards): 256 rows and the 2 rows of h before them.
+    seg = [sg for sg in W.conv_shards([R], 4, 1, k)][0]
+    _, lo, hi, halo, _ = seg
+    kern, _ = conv[0]
+    shard_cy = b.alloc((hi - lo) * H)
+    bcx_shard = b.alloc((hi - lo + halo) * 3 * H)
+    b.copy(bcx, (lo - halo) * 3 * H, bcx_shard, 0, (hi - lo + halo) * 3 * H)
+    B.time(f"lfm2 layer stack: conv block shard ({hi - lo} rows + {halo}-row halo, rank 1 of 4)",
+           lambda: b.lfm2_conv_block_halo(bcx_shard, kern, 0, shard_cy, hi - lo, H, k, halo),
+           (hi - lo + halo) * 3 * H * f + (hi - lo) * H * f)
 
 
 def model_decode(B, n_layers: int = 24, pos: int = 511, samples: int = 50):

@@ -107,3 +107,24 @@ def shard_rows(total: int, world: int, rank: int) -> tuple[int, int]:
     base, extra = divmod(total, world)
     lo = rank * base + min(rank, extra)
     return lo, lo + base + (1 if rank < extra else 0)
+
+
+def conv_shards(seq_lens, world: int, rank: int, k: int) -> list[tuple[int, int, int, int, bool]]:
+    """The LFM2 short-conv rows of `rank` when the concatenated sequences
+    (lengths `seq_lens`) are split into contiguous row blocks (shard_rows): a
+    list of (sequence, lo, hi, halo, ends) segments, rows [lo, hi) of that
+    sequence.  The causal conv of row r reads h of rows r - k + 1 .. r of its
+    own sequence (lfm2.rs:584-624), so a segment that starts inside a sequence
+    takes halo = min(k - 1, lo) preceding rows of it, staged locally with the
+    segment before the run; `ends` marks the segment holding the sequence's
+    last row, the one that seeds the decode ring (lfm2.rs:601-610)."""
+    total = sum(seq_lens)
+    lo_r, hi_r = shard_rows(total, world, rank)
+    out, start = [], 0
+    for i, n in enumerate(seq_lens):
+        lo, hi = max(lo_r, start) - start, min(hi_r, start + n) - start
+        if lo < hi:
+            out.append((i, lo, hi, min(k - 1, lo), hi == n))
+        start += n
+    return out
+

@@ -335,6 +335,19 @@ def lfm2_conv_block(bcx, kernel, ring, k):
     return cy, ring
 
 
+def lfm2_conv_block_shard(bcx, kernel, k, lo, hi, halo):
+    """Rows [lo, hi) of one sequence's conv block computed from its rows
+    lo - halo .. hi alone (the shard's own rows and its staged halo): the
+    oracle's block over those rows, outputs of the halo rows dropped.  With
+    halo = min(k - 1, lo) this equals the unsharded block's rows [lo, hi)
+    (a row's conv reads only the k - 1 rows before it).  Returns (cy, ring) with
+    ring the last k - 1 rows of h over those rows (the sequence's ring when
+    hi is its end)."""
+    cy, ring = lfm2_conv_block(f32(bcx)[lo - halo:hi], kernel, np.zeros((max(k - 1, 0), f32(bcx).shape[1] // 3),
+                                                                        np.float32), k)
+    return cy[halo:], ring
+
+
 def chain(*, dim, q_dim, kv_dim, hidden, head, eps, theta, positions, w_att, q, k, gate, up,
           resid, tokens=None, table=None, x=None, interleaved=False, w_q=None, w_k=None,
           w_final=None, final_eps=None, threads=1, in_place=False):

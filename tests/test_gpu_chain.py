@@ -207,6 +207,49 @@ def test_lfm2_conv_block_short_prompt_ring(gpu, oracle, rows):
     assert_bits_equal(gpu.read(hr, (k - 1) * dim), ring, "ring")
 
 
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
+@pytest.mark.parametrize("seq_lens,dim,k", [([1024], 1536, 3), ([100, 50, 200], 48, 3), ([9, 40], 64, 4),
+                                            ([30], 12, 2), ([64], 7, 5)])
+def test_lfm2_conv_block_sharded_with_halo(gpu, oracle, world, seq_lens, dim, k):
+    """kernrt_cuda_lfm2_conv_block_halo: the sequences cut into the row blocks
+    of `world` ranks (W.conv_shards), each segment run from its own rows and
+    its staged halo (the k - 1 rows of the sequence before it), emulated one
+    rank after another on one device: the segments reassemble the unsharded
+    block bit for bit, and the segment that ends each sequence seeds its ring."""
+    rng = np.random.default_rng(sum(seq_lens) + dim + k)
+    bcx = [rng.standard_normal((n, 3 * dim), dtype=f32) for n in seq_lens]
+    kernel = (0.3 * rng.standard_normal(dim * k)).astype(f32)
+    hk = gpu.upload(kernel)
+    full = [oracle.lfm2_conv_block(b, kernel, np.zeros((k - 1) * dim, f32), k) for b in bcx]
+    covered = [np.zeros(n, bool) for n in seq_lens]
+    for rank in range(world):
+        for seq, lo, hi, halo, ends in W.conv_shards(seq_lens, world, rank, k):
+            n = hi - lo
+            hb, hc = gpu.upload(bcx[seq][lo - halo:hi]), gpu.alloc(n * dim)
+            hr = gpu.alloc((k - 1) * dim) if ends and (halo == 0 or n >= k - 1) else 0
+            gpu.lfm2_conv_block_halo(hb, hk, hr, hc, n, dim, k, halo)
+            assert_bits_equal(gpu.read(hc, n * dim).reshape(n, dim), full[seq][0][lo:hi],
+                              f"world {world} rank {rank}: sequence {seq} rows {lo}:{hi}")
+            if hr:
+                assert_bits_equal(gpu.read(hr, (k - 1) * dim), full[seq][1], f"ring of sequence {seq}")
+            covered[seq][lo:hi] = True
+    assert all(c.all() for c in covered)
+
+
+def test_lfm2_conv_block_halo_rejects_what_it_cannot_do(gpu):
+    dim, k = 16, 3
+    hb, hk, hr, hc = gpu.upload(np.zeros((4, 3 * dim), f32)), gpu.upload(np.zeros(dim * k, f32)), \
+        gpu.alloc((k - 1) * dim), gpu.alloc(4 * dim)
+    for args, words in [((hb, hk, hr, hc, 2, dim, k, 3), "halo"), ((hb, hk, hr, hc, 1, dim, k, 2), "k - 1 rows"),
+                        ((hb, hk, hr, hc, 4, dim, k, 1), "conv block bcx")]:
+        with pytest.raises(kernrt_b200.KernrtCudaError) as e:
+            gpu.lfm2_conv_block_halo(*args)
+        assert e.value.code == kernrt_b200.E_INVALID and words in str(e.value), str(e.value)
+    with pytest.raises(kernrt_b200.KernrtCudaError) as e:
+        gpu.lfm2_conv_block(hb, hk, 0, hc, 4, dim, k)
+    assert "ring" in str(e.value)
+
+
 def test_lfm2_conv_block_matches_the_unfused_ops(gpu):
     """The fused block equals the driver's own op sequence (lfm2.rs:584-624)
     run through the backend's trait ops."""
