@@ -102,6 +102,8 @@ public:
             cudaFree(r.second);
         }
         for (auto e : events_) cudaEventDestroy(e);
+        for (auto e : stage_ev_)
+            if (e) cudaEventDestroy(e);
         for (int k = 0; k < 2; ++k) {
             if (file_ev_[k]) cudaEventDestroy(file_ev_[k]);
             cudaFreeHost(file_pin_[k]);
@@ -1473,36 +1475,53 @@ private:
         const size_t half = head / 2, n = cap * half;
         std::vector<float> hc(n), hs(n);
         build_rope_table(theta, (int)head, cap, hc.data(), hs.data());
-        check(cudaStreamSynchronize(stream_), "synchronize");  // old table may still be read
         if (!t) {
             ropes_.push_back(RopeTable{theta, head, 0, nullptr, nullptr});
             t = &ropes_.back();
         }
-        cudaFree(t->cos);
-        cudaFree(t->sin);
+        // Stream-ordered: the old table is freed after the work that may
+        // still read it, the new one is allocated and filled in order, and
+        // nothing waits on the host (the copies from pageable vectors return
+        // once their source is staged).
+        if (t->cos) check(cudaFreeAsync(t->cos, stream_), "cudaFreeAsync(rope)");
+        if (t->sin) check(cudaFreeAsync(t->sin, stream_), "cudaFreeAsync(rope)");
         t->cos = t->sin = nullptr;
-        check(cudaMalloc(&t->cos, n * 4), "cudaMalloc(rope)");
-        check(cudaMalloc(&t->sin, n * 4), "cudaMalloc(rope)");
-        check(cudaMemcpy(t->cos, hc.data(), n * 4, cudaMemcpyHostToDevice), "upload rope table");
-        check(cudaMemcpy(t->sin, hs.data(), n * 4, cudaMemcpyHostToDevice), "upload rope table");
+        t->max_pos = 0;
+        check(cudaMallocAsync(reinterpret_cast<void **>(&t->cos), n * 4, stream_), "cudaMallocAsync(rope)");
+        check(cudaMallocAsync(reinterpret_cast<void **>(&t->sin), n * 4, stream_), "cudaMallocAsync(rope)");
+        check(cudaMemcpyAsync(t->cos, hc.data(), n * 4, cudaMemcpyHostToDevice, stream_), "upload rope table");
+        check(cudaMemcpyAsync(t->sin, hs.data(), n * 4, cudaMemcpyHostToDevice, stream_), "upload rope table");
         t->max_pos = cap;
         return *t;
     }
 
     // Copy a host slice into the pinned ring and enqueue its upload; returns
-    // the device address.  The ring wraps after a stream synchronize, so a
-    // region is never rewritten while a copy from it, or a kernel reading it,
-    // may be pending.  Each launch takes its staged data from one call, made
-    // right before the launch; a ring that grows is retired, not freed, until
-    // the next barrier.
+    // the device address.  Each launch takes its staged data from one call,
+    // made right before the launch, so when a call starts, the consumers of
+    // everything staged before it are enqueued.  The ring is cut into
+    // kStageSegs segments: leaving a segment records an event after those
+    // consumers, and entering a segment waits for the event recorded when the
+    // ring last left it (a whole ring earlier, normally long complete), so a
+    // region is never rewritten while a copy from it or a kernel reading it
+    // may be pending, and the stream is never drained.  A slice larger than a
+    // segment grows the ring; the old one is retired, not freed, until the
+    // next barrier.
+    static constexpr int kStageSegs = 8;
     void *stage(const void *src, size_t bytes) {
         const size_t need = (bytes + 255) & ~(size_t)255;
-        if (need > stage_cap_) {
-            check(cudaStreamSynchronize(stream_), "synchronize");
-            grow_staging(2 * need);
-        } else if (stage_head_ + need > stage_cap_) {
-            check(cudaStreamSynchronize(stream_), "synchronize");
-            stage_head_ = 0;
+        size_t seg = stage_cap_ / kStageSegs;
+        if (need > seg) {
+            grow_staging(kStageSegs * std::max<size_t>(2 * need, 1 << 17));
+            seg = stage_cap_ / kStageSegs;
+        }
+        const size_t cur = stage_head_ / seg;
+        if (stage_head_ % seg + need > seg) {  // into the next segment
+            const size_t next = (cur + 1) % kStageSegs;
+            check(cudaEventRecord(stage_ev_[cur], stream_), "cudaEventRecord(staging)");
+            stage_ev_set_[cur] = true;
+            if (stage_ev_set_[next]) check(cudaEventSynchronize(stage_ev_[next]), "staging ring");
+            stage_ev_set_[next] = false;
+            stage_head_ = next * seg;
         }
         char *h = stage_host_ + stage_head_;
         char *d = stage_dev_ + stage_head_;
@@ -1520,6 +1539,10 @@ private:
         check(cudaMalloc(&stage_dev_, cap), "cudaMalloc(staging)");
         stage_cap_ = cap;
         stage_head_ = 0;
+        for (int i = 0; i < kStageSegs; ++i) {  // a new ring: every segment free
+            if (!stage_ev_[i]) check(cudaEventCreateWithFlags(&stage_ev_[i], cudaEventDisableTiming), "cudaEventCreate");
+            stage_ev_set_[i] = false;
+        }
     }
 
     struct Mark {
@@ -1609,6 +1632,8 @@ private:
     char *stage_host_ = nullptr;
     char *stage_dev_ = nullptr;
     std::vector<std::pair<char *, char *>> retired_;  // grown-out staging rings, freed at the next barrier
+    cudaEvent_t stage_ev_[kStageSegs] = {};  // per staging segment: recorded when the ring last left it
+    bool stage_ev_set_[kStageSegs] = {};
     size_t stage_cap_ = 0, stage_head_ = 0;
 };
 
