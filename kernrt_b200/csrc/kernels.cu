@@ -58,6 +58,57 @@ __device__ __forceinline__ float rms_scale(float ss, float n, float eps) {
     return div_rn(1.0f, __fsqrt_rn(ss));
 }
 
+// The exact-order sum of squares (reference.rs:167-170): ss + q(0) + q(1) + ...
+// in that order, where sq16(b, q) computes the 16 squares of block b (elements
+// 16b .. 16b + 15).  The squares of block b + 1 are computed before the adds
+// of block b, so the dependent adds run back to back instead of each waiting
+// on its own load and multiply.  Measured on B200, one lane per row out of
+// shared memory: 7.26 cycles per element for a plain unrolled loop, 4.95 this
+// way, 4.59 for the bare dependent add.
+template <class Sq16>
+__device__ __forceinline__ float chain_add16(float ss, int n16, Sq16 sq16) {
+    if (n16 <= 0) return ss;
+    float cur[16], nxt[16];
+    sq16(0, cur);
+    for (int b = 1; b < n16; ++b) {
+        sq16(b, nxt);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) ss = add_rn(ss, cur[e]);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) cur[e] = nxt[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) ss = add_rn(ss, cur[e]);
+    return ss;
+}
+
+// The 16 squares of f32 values at p[0..16) (16-byte aligned).
+__device__ __forceinline__ void squares16_f32(const float *p, float (&q)[16]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 v = reinterpret_cast<const float4 *>(p)[i];
+        q[4 * i] = mul_rn(v.x, v.x);
+        q[4 * i + 1] = mul_rn(v.y, v.y);
+        q[4 * i + 2] = mul_rn(v.z, v.z);
+        q[4 * i + 3] = mul_rn(v.w, v.w);
+    }
+}
+
+// The 16 squares of bf16 patterns at p[0..16) (16-byte aligned).
+__device__ __forceinline__ void squares16_bf16(const uint16_t *p, float (&q)[16]) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint4 u = reinterpret_cast<const uint4 *>(p)[i];
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float lo = bf16f(w4[j] & 0xffffu), hi = bf16f(w4[j] >> 16);
+            q[8 * i + 2 * j] = mul_rn(lo, lo);
+            q[8 * i + 2 * j + 1] = mul_rn(hi, hi);
+        }
+    }
+}
+
 // quant.rs:722-758 is IEEE binary16 round-to-nearest-even; the block scale it
 // converts is never NaN (the amax fold drops NaNs), and for every other input
 // CUDA's RN conversion gives the same bits.
@@ -1565,6 +1616,12 @@ __global__ void __launch_bounds__(ColsShape<FQ>::threads, 1) k_norm_cols(ChainAr
                     v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
                 };
                 float v[8], rv[8] = {}, nv[8], nrv[8] = {};
+                if (!sum_resid && tc % 16 == 0) {
+                    // one chain of x alone: the squares of the next 16
+                    // columns ahead of the current adds (with x + resid the
+                    // loop below measured faster)
+                    ss = chain_add16(ss, tc / 16, [&](int b, float(&q)[16]) { squares16_f32(xr + 16 * b, q); });
+                } else {
                 ld8(xr, 0, v);
                 if (sum_resid) ld8(rr, 0, rv);
 #pragma unroll 2
@@ -1594,6 +1651,7 @@ __global__ void __launch_bounds__(ColsShape<FQ>::threads, 1) k_norm_cols(ChainAr
                         v[e] = nv[e];
                         rv[e] = nrv[e];
                     }
+                }
                 }
             }
             // every lane's reads of the slot are done before it goes back
@@ -1865,7 +1923,14 @@ __global__ void __launch_bounds__(RowsShape<FQ>::threads, 1) k_norm_rows(ChainAr
             sc[32 + lane] = rms_scale(ss2, (float)dim, a.final_eps);
             return;
         }
-        if (valid) {
+        if (valid && dim % 16 == 0) {
+            ss = chain_add16(ss, dim / 16, [&](int b, float(&q)[16]) {
+                decode_staged<SRC, 8>(xr, dim, 16 * b, q);
+                decode_staged<SRC, 8>(xr, dim, 16 * b + 8, q + 8);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) q[e] = mul_rn(q[e], q[e]);
+            });
+        } else if (valid) {
 #pragma unroll 4
             for (int c = 0; c < dim; c += 8) {
                 float v[8];
@@ -2046,20 +2111,8 @@ __global__ void __launch_bounds__(256) k_norm_small(ChainArgs a) {
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        float ss = 0.0f;
-        int i = 0;
-        for (; i + 16 <= dim; i += 16) {
-            float4 t[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) t[j] = *reinterpret_cast<const float4 *>(row_s + i + 4 * j);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                ss = add_rn(ss, mul_rn(t[j].x, t[j].x));
-                ss = add_rn(ss, mul_rn(t[j].y, t[j].y));
-                ss = add_rn(ss, mul_rn(t[j].z, t[j].z));
-                ss = add_rn(ss, mul_rn(t[j].w, t[j].w));
-            }
-        }
+        float ss = chain_add16(0.0f, dim / 16, [&](int b, float(&q)[16]) { squares16_f32(row_s + 16 * b, q); });
+        int i = dim & ~15;
         for (; i < dim; ++i) ss = add_rn(ss, mul_rn(row_s[i], row_s[i]));
         scale_s = rms_scale(ss, (float)dim, a.eps);
     }
@@ -2173,14 +2226,16 @@ __global__ void __launch_bounds__(32) k_row_scales(ChainArgs a, float *row_scale
         if (valid) {
             const uint4 *row = reinterpret_cast<const uint4 *>(ring(t % kScaleSlots) + lane * kScaleStride);
             const int n16 = min(kScaleTile, rb - t * kScaleTile) >> 4;
-            if (n16 == N16) {
-                // a full tile as one straight block: its loads can run ahead
-                // of the dependent adds
-                uint4 u[N16];
-#pragma unroll
-                for (int c = 0; c < N16; ++c) u[c] = row[c];
-#pragma unroll
-                for (int c = 0; c < N16; ++c) chain_chunk<SRC>(ss, u[c]);
+            constexpr int EPC = 16 / ESZ;  // elements per 16-byte chunk
+            const int elems = n16 * EPC;
+            if (elems % 16 == 0) {
+                // the squares of the next 16 elements ahead of the current adds
+                ss = chain_add16(ss, elems / 16, [&](int b, float(&q)[16]) {
+                    if constexpr (SRC == SRC_BF16)
+                        squares16_bf16(reinterpret_cast<const uint16_t *>(row) + 16 * b, q);
+                    else
+                        squares16_f32(reinterpret_cast<const float *>(row) + 16 * b, q);
+                });
             } else {
                 for (int c = 0; c < n16; ++c) chain_chunk<SRC>(ss, row[c]);
             }
@@ -3362,7 +3417,8 @@ cudaError_t launch_add_rms_norm(const ChainArgs &a, cudaStream_t s) {
     if (a.rows <= 0) return cudaSuccess;
     if (a.dim % 8 != 0) return cudaErrorInvalidValue;
     cudaError_t e = cudaSuccess;
-    if (try_norm_small<true>(a, s, &e) || try_norm_cols<true, false>(a, s, &e)) return e;
+    if (try_norm_small<true>(a, s, &e) || try_norm_cols<true, false>(a, s, &e))
+        return e;
     return launch_norm_pipe<SRC_X, true, true, false>(a, s);
 }
 

@@ -97,13 +97,14 @@ def test_embed_rejects_bad_token_and_offset(gpu, oracle):
 # --- rms_norm (reference.rs:161-178) ---------------------------------------------------
 
 # Enough rows for several row groups per CTA and several column tiles per row
-# in the tiled pipeline (5000x2048, 3001x576, 2000x8192), few rows, and widths
-# that take the unaligned fallback.
+# in the tiled pipeline (2000x8192), rows that wrap each CTA's whole-row ring
+# several times (20000x1024, 9001x2048), few rows, and widths that take the
+# unaligned fallback.
 @pytest.mark.parametrize("rows,dim,eps", [(1, 2048, 1e-5), (7, 576, 1e-5), (33, 1536, 1e-6),
                                           (5, 37, 1e-5), (64, 1024, 1e-6), (3, 8192, 1e-5),
                                           (2, 12, 0.0), (100, 2048, 1e-5), (5000, 2048, 1e-5),
                                           (3001, 576, 1e-6), (2000, 8192, 1e-5), (700, 1000, 1e-5),
-                                          (1200, 96, 1e-6)])
+                                          (1200, 96, 1e-6), (20000, 1024, 1e-5), (9001, 2048, 1e-6)])
 def test_rms_norm(gpu, oracle, rows, dim, eps):
     x = _data.lcg_normal(rows * dim, 10 + dim).reshape(rows, dim)
     w = _data.lcg_normal(dim, 11, 1.0, 0.1)
@@ -112,7 +113,8 @@ def test_rms_norm(gpu, oracle, rows, dim, eps):
     assert_bits_equal(rd(gpu, ho, (rows, dim)), oracle.rms_norm(x, w, eps), f"rms {rows}x{dim}")
 
 
-@pytest.mark.parametrize("rows,dim", [(4000, 2048), (300, 1536), (7, 64), (9, 20), (640, 1000), (2000, 64)])
+@pytest.mark.parametrize("rows,dim", [(4000, 2048), (300, 1536), (7, 64), (9, 20), (640, 1000), (2000, 64),
+                                      (9001, 2048), (5000, 3072)])
 def test_add_in_place_then_rms_norm_fuses(gpu, oracle, rows, dim):
     """The driver's add_in_place(x, o) -> rms_norm(xb, x) pair (llama.rs:762-765)
     runs as one launch (for rows of whole float4 pairs) and matches the two ops
@@ -348,7 +350,8 @@ def test_quantize_q8_0(gpu, oracle, rows, dim):
 
 @pytest.mark.parametrize("rows,dim,eps", [(256, 1024, 1e-6), (5, 2048, 1e-5), (3, 40, 1e-5),
                                           (5000, 1024, 1e-6), (1000, 4096, 1e-5), (333, 96, 1e-5),
-                                          (800, 96, 1e-5), (700, 1536, 1e-6)])
+                                          (800, 96, 1e-5), (700, 1536, 1e-6), (20000, 1024, 1e-6),
+                                          (1500, 160, 1e-5)])
 def test_rms_norm_q8_0_fused(gpu, oracle, rows, dim, eps):
     x = _data.lcg_normal(rows * dim, 70 + dim).reshape(rows, dim)
     w = _data.lcg_normal(dim, 71, 1.0, 0.1)
