@@ -646,7 +646,7 @@ public:
             if (slots[i] >= kv_seq_) fail(KERNRT_E_INVALID, "slot " + std::to_string(slots[i]) + " out of range");
             dst[i] = (int32_t)(layer * kv_seq_ + slots[i]);
         }
-        const int32_t *d = static_cast<const int32_t *>(stage(dst.data(), rows * sizeof(int32_t)));
+        const int32_t *d = static_cast<const int32_t *>(stage(dst.data(), rows * sizeof(int32_t), true));
         launch_or_fail(launch_kv_write(kc_, vc_, (int)kv_dim_, d, f(kb), f(vb), (int)rows, stream_), "kv_write");
     }
 
@@ -808,7 +808,7 @@ public:
         float eps = pqk_.eps;
         if (fuse) pqk_.n = 0;
         flush();
-        const int32_t *dpos = static_cast<const int32_t *>(stage(pos.data(), rows * sizeof(int32_t)));
+        const int32_t *dpos = static_cast<const int32_t *>(stage(pos.data(), rows * sizeof(int32_t), true));
         if (fuse) {
             launch_or_fail(launch_qk_rope(f(qb), f(kb), (int)qw, (int)kvw, (int)rows, (int)head, wq, wk, eps, dpos,
                                           t.cos, t.sin, (int)t.max_pos, interleaved, d_err_, stream_),
@@ -1324,7 +1324,7 @@ public:
         a.table = emb_data_;
         a.tscales = emb_scales_;
         a.vocab = (int)vocab_;
-        a.tokens = static_cast<const int32_t *>(stage(tok.data(), rows * sizeof(int32_t)));
+        a.tokens = static_cast<const int32_t *>(stage(tok.data(), rows * sizeof(int32_t), true));
         a.x_out = f(buf(x));
         a.xb = f(buf(out));
         a.w_att = f(buf(weight));
@@ -1368,7 +1368,7 @@ public:
         std::vector<unsigned char> packed(n * (sizeof(int64_t) + sizeof(int32_t)));
         std::memcpy(packed.data(), off.data(), n * sizeof(int64_t));
         std::memcpy(packed.data() + n * sizeof(int64_t), tok.data(), n * sizeof(int32_t));
-        unsigned char *dev = static_cast<unsigned char *>(stage(packed.data(), packed.size()));
+        unsigned char *dev = static_cast<unsigned char *>(stage(packed.data(), packed.size(), true));
         GatherArgs g{};
         g.table = emb_data_;
         g.tscales = emb_scales_;
@@ -1496,7 +1496,13 @@ private:
     }
 
     // Copy a host slice into the pinned ring and enqueue its upload; returns
-    // the device address.  Each launch takes its staged data from one call,
+    // the device address.  With `in_place`, a slice of a few values (a decode
+    // step's token id, position or cache slot, which its kernel reads about
+    // once per row) is not uploaded: the kernel reads it from the pinned ring
+    // through the ring's device mapping, which saves the copy call on the host
+    // and the copy in the stream ahead of the kernel.  Slices that kernels read
+    // many times over (attention windows) are always uploaded: each of those
+    // reads would cross PCIe.  Each launch takes its staged data from one call,
     // made right before the launch, so when a call starts, the consumers of
     // everything staged before it are enqueued.  The ring is cut into
     // kStageSegs segments: leaving a segment records an event after those
@@ -1507,7 +1513,8 @@ private:
     // segment grows the ring; the old one is retired, not freed, until the
     // next barrier.
     static constexpr int kStageSegs = 8;
-    void *stage(const void *src, size_t bytes) {
+    static constexpr size_t kStageMapped = 64;  // slices read in place through the mapping
+    void *stage(const void *src, size_t bytes, bool in_place = false) {
         const size_t need = (bytes + 255) & ~(size_t)255;
         size_t seg = stage_cap_ / kStageSegs;
         if (need > seg) {
@@ -1526,6 +1533,10 @@ private:
         char *h = stage_host_ + stage_head_;
         char *d = stage_dev_ + stage_head_;
         std::memcpy(h, src, bytes);
+        if (in_place && bytes <= kStageMapped && stage_map_) {
+            stage_head_ += need;
+            return stage_map_ + (h - stage_host_);
+        }
         check(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, stream_), "stage");
         stage_head_ += need;
         return d;
@@ -1535,8 +1546,12 @@ private:
         if (stage_host_ || stage_dev_) retired_.push_back({stage_host_, stage_dev_});
         stage_host_ = nullptr;
         stage_dev_ = nullptr;
-        check(cudaMallocHost(&stage_host_, cap), "cudaMallocHost(staging)");
+        check(cudaHostAlloc(&stage_host_, cap, cudaHostAllocMapped), "cudaHostAlloc(staging)");
         check(cudaMalloc(&stage_dev_, cap), "cudaMalloc(staging)");
+        void *map = nullptr;
+        stage_map_ = nullptr;
+        if (cudaHostGetDevicePointer(&map, stage_host_, 0) == cudaSuccess) stage_map_ = static_cast<char *>(map);
+        else cudaGetLastError();  // no mapping: every slice is uploaded
         stage_cap_ = cap;
         stage_head_ = 0;
         for (int i = 0; i < kStageSegs; ++i) {  // a new ring: every segment free
@@ -1631,6 +1646,7 @@ private:
     int *h_err_ = nullptr;
     char *stage_host_ = nullptr;
     char *stage_dev_ = nullptr;
+    char *stage_map_ = nullptr;  // stage_host_ as the device addresses it
     std::vector<std::pair<char *, char *>> retired_;  // grown-out staging rings, freed at the next barrier
     cudaEvent_t stage_ev_[kStageSegs] = {};  // per staging segment: recorded when the ring last left it
     bool stage_ev_set_[kStageSegs] = {};
