@@ -117,6 +117,27 @@ def test_chain_matches_oracle(gpu, oracle, wl):
     check(gpu_chain(gpu, wl, d), oracle_chain(oracle, wl, d), wl.final_q8)
 
 
+@pytest.mark.parametrize("rows", [8192, 5000, 149, 37])
+def test_chain_few_rows_per_sm(gpu, oracle, rows):
+    """A shard's row count on 8 GPUs (8 192) and ragged counts: the row-scale
+    pass with its last CTA partly filled, and fewer rows than SMs."""
+    wl = W.SMOLLM2_17B_PREFILL
+    d = make_inputs(wl, 1010 + rows, rows=rows, vocab=4096)
+    check(gpu_chain(gpu, wl, d), oracle_chain(oracle, wl, d), False)
+
+
+def test_chain_few_rows_bad_token_reports_and_recovers(gpu, oracle):
+    wl = W.Workload("small", 512, 64, 2, 2, 32, 64, 1e4, 1e-5, "bf16", rows=300, seq_len=300)
+    d = make_inputs(wl, 1011)
+    d["tokens"][171] = 512  # one past the vocabulary
+    with pytest.raises(kernrt_b200.KernrtCudaError) as e:
+        gpu_chain(gpu, wl, d)
+    assert e.value.code == kernrt_b200.E_DEVICE
+    assert "token id out of range" in str(e.value)
+    d["tokens"][171] = 511
+    check(gpu_chain(gpu, wl, d), oracle_chain(oracle, wl, d), False)
+
+
 def test_chain_interleaved_rope(gpu, oracle):
     wl = W.SMOLLM2_135M
     d = make_inputs(wl, 1001, vocab=512)
