@@ -14,25 +14,31 @@
 //
 // x is split once per call by k_split_bf16 (x f32 -> hi, lo bf16 [rows,
 // in_dim], also shared by the matrices of a project_qkv / project_gate_up).
-// One CTA computes a tile of 128 outputs x 64 rows over the whole K in stages
-// of 64 (one 128-byte swizzled row of bf16 per matrix row), six stages in
-// flight.  The stage's hi and lo tiles sit back to back with the same 1 KB
-// group stride, so they are one 128-row B operand: one MMA per K-step (M = 128,
-// N = 128) gives W.hi in accumulator columns 0-63 and W.lo in 64-127, reading
-// the W slice once (two N = 64 MMAs per K-step, each reading it, measured
-// 24.8 us for 512 x 2048 x 2048, bound by the operand reads):
+// One CTA computes a tile of 128 outputs x 128 rows over the whole K in
+// stages of 64 (one 128-byte swizzled row of bf16 per matrix row), four 48 KB
+// stages in flight.  The stage's hi and lo tiles sit back to back with the
+// same 1 KB group stride, so they are one 256-row B operand: one MMA per K-step
+// (M = 128, N = 256) gives W.hi in accumulator columns 0-127 and W.lo in
+// 128-255, reading the W slice once.  The kernel is bound by the operand bytes
+// it pulls through L2: 128 rows a tile carry 48 KB of operands per 64-wide
+// K-step for twice the MMA work of 64 rows (32 KB), and measured 1.5-1.7x
+// faster where the grid still fills the SMs (4096 x 8192 x 2048: 419 -> 249
+// us; 512 x 8192 x 2048: 65 -> 41 us), the same where it does not (512 x 2048
+// x 2048: 64 tiles, 22.4 -> 22.7 us):
 //   warp 0   one thread issues the TMA copies of stage kb: the W tile (128 x 64)
-//            and the hi and lo tiles (64 x 64), all 128-byte swizzled, counted
-//            on full[s];
-//   warp 1   allocates the 128 TMEM columns, and one thread issues the MMAs:
+//            and the hi and lo tiles (128 x 64), all 128-byte swizzled,
+//            counted on full[s];
+//   warp 1   allocates the 256 TMEM columns, and one thread issues the MMAs:
 //            per stage 4 K-steps of 16, then tcgen05.commit frees the stage
 //            (empty[s]); a last commit signals `done`;
 //   warps 2-5 read the accumulator (tcgen05.ld, warp w owns TMEM lanes
 //            32 (w % 4) ..), add the hi and lo columns of each row, and store
 //            y: for each row a warp writes 32 consecutive outputs.
-// Also measured on B200 (same shape, split included): four stages 25.5 us; the
-// split done in the kernel, by four or eight converting warps writing the
-// swizzled hi / lo tiles in place of a TMA-loaded f32 tile, 32.9 / 30.9 us.
+// Also measured on B200 (64-row tiles, 512 x 2048 x 2048, split included): two
+// N = 64 MMAs per K-step, each reading the W slice, 24.8 us; four stages
+// instead of six 25.5 us; the split done in the kernel, by four or eight
+// converting warps writing the swizzled hi / lo tiles in place of a TMA-loaded
+// f32 tile, 32.9 / 30.9 us; the stage's copies issued by three lanes, 24.9 us.
 // The TMA tensor maps cover this GPU's memory only, with no cluster multicast.
 // Every mbarrier wait is bounded: a wait that runs out sets ERR_TIMEOUT in the
 // error word, the roles stop, the producer waits (bounded) for the copies it
@@ -53,13 +59,13 @@ namespace krt {
 namespace {
 
 constexpr int kTcM = 128;  // outputs per tile (MMA M)
-constexpr int kTcN = 64;   // rows per tile (MMA N)
+constexpr int kTcN = 128;  // rows per tile (MMA N = 2 kTcN: their hi and lo halves)
 constexpr int kTcK = 64;   // K per stage: 64 bf16 = one 128-byte swizzled row
-constexpr int kTcStages = 6;
+constexpr int kTcStages = 4;
 constexpr int kTcThreads = 192;
 constexpr uint32_t kTileA = kTcM * kTcK * 2;      // 16 KB of W
-constexpr uint32_t kTileB = kTcN * kTcK * 2;      // 8 KB: one of hi, lo
-constexpr uint32_t kStage = kTileA + 2 * kTileB;  // 32 KB
+constexpr uint32_t kTileB = kTcN * kTcK * 2;      // 16 KB: one of hi, lo
+constexpr uint32_t kStage = kTileA + 2 * kTileB;  // 48 KB
 constexpr size_t kTcSmem = (size_t)kTcStages * kStage + 1024;  // + slack to align the tiles to 1 KB
 constexpr uint32_t kTmemCols = 2 * kTcN;  // f32 accumulator columns: W.hi, then W.lo (a power of 2, >= 32)
 
