@@ -433,12 +433,29 @@ def contractions(B):
                    note="bound by each output's 2048-long add chain" if rows == 1 else "")
         if r is not None and rows > 1:
             r["note"] = f"{macs / (r['ms'] / 1e3) / 1e12:.2f} T MAC/s = {macs / (r['ms'] / 1e3) / EXACT_MAC_PEAK:.2f} of the exact-order FP32 ceiling"
-    # the decode projections of one SmolLM2-1.7B layer (fused q/k/v and gate/up)
-    wk = W.SMOLLM2_17B_DECODE
 
     def bf16_mat(o, i):
         m = (rng.standard_normal((o, i), dtype=np.float32) * np.float32(0.02)).view(np.uint32) >> 16
         return b.prepare_matrix(BF16, m.astype(np.uint16), None, o, i)
+
+    # tolerance mode (kernrt_cuda_set_exact(ctx, 0)): prefill projections on the
+    # tensor cores, x split into bf16 hi + lo inside the call
+    for o, i, rows in [(H, H, 512), (8192, H, 512), (8192, H, 4096)]:
+        if not B.want(f"project bf16 {o}x{i}, {rows} rows, tensor cores"):
+            continue
+        wm = mq if (o, i) == (H, H) else bf16_mat(o, i)
+        x, y = B.buf(rows * i), b.alloc(rows * o)
+        b.set_exact(False)
+        try:
+            r = B.time(f"project bf16 {o}x{i}, {rows} rows, tensor cores (tolerance mode)",
+                       lambda: b.project(wm, x, y, rows), o * i * 2 + rows * i * 4 + rows * o * 4)
+        finally:
+            b.set_exact(True)
+        if r is not None:
+            r["note"] = (f"{4 * o * i * rows / (r['ms'] / 1e3) / 1e12:.0f} TFLOP/s of tensor work (W.hi and W.lo), "
+                         "the split of x included")
+    # the decode projections of one SmolLM2-1.7B layer (fused q/k/v and gate/up)
+    wk = W.SMOLLM2_17B_DECODE
 
     mqkv = [bf16_mat(wk.q_dim, H), bf16_mat(wk.kv_dim, H), bf16_mat(wk.kv_dim, H)]
     mgu = [bf16_mat(wk.hidden, H), bf16_mat(wk.hidden, H)]
