@@ -514,6 +514,11 @@ public:
         return !exact_ && m.src == SRC_BF16 && rows >= kTcMinRows &&
                project_tc_supported((int)m.out_dim, (int)m.in_dim, m.data, x, y);
     }
+    // Tolerance mode: bf16 projections of 1-4 rows (decode) sum each output
+    // across a warp instead of in the reference's order (tc_project.cu).
+    bool tol_gemv_path(const DevMatrix &m, const float *x, size_t rows) const {
+        return !exact_ && m.src == SRC_BF16 && gemv_tol_supported(m.data, x, (int)m.in_dim, (int)rows);
+    }
     // x split into bf16 hi and lo halves ([rows, in_dim] each), in scratch
     // grown as needed (cudaFree waits for queued kernels still reading it).
     uint16_t *split_x(const float *x, size_t rows, size_t in_dim) {
@@ -549,6 +554,14 @@ public:
             launch_or_fail(launch_project_tc(static_cast<const uint16_t *>(m.data), (int)m.out_dim, (int)m.in_dim, hi,
                                              hi + rows * m.in_dim, (int)rows, f(yb), d_err_, stream_),
                            "project (tensor cores)");
+            return;
+        }
+        if (tol_gemv_path(m, f(xb), rows)) {
+            const uint16_t *w16 = static_cast<const uint16_t *>(m.data);
+            const int out = (int)m.out_dim;
+            float *y = f(yb);
+            launch_or_fail(launch_gemv_tol(1, &w16, &out, (int)m.in_dim, f(xb), (int)rows, &y, stream_),
+                           "project (tolerance)");
             return;
         }
         launch_or_fail(launch_project(m.src, m.data, m.scales, (int)m.out_dim, (int)m.in_dim, f(xb), (int)rows, f(yb),
@@ -598,6 +611,15 @@ public:
                 launch_or_fail(launch_project_tc(static_cast<const uint16_t *>(wp[i]), outs[i], (int)m0.in_dim, hi,
                                                  hi + rows * m0.in_dim, (int)rows, yp[i], d_err_, stream_),
                                "project (tensor cores)");
+            return;
+        }
+        bool tol = true;
+        for (int i = 0; i < n; ++i) tol = tol && tol_gemv_path(mat(ws[i]), f(xb), rows);
+        if (tol) {  // one launch over the n matrices' outputs
+            const uint16_t *w16[3];
+            for (int i = 0; i < n; ++i) w16[i] = static_cast<const uint16_t *>(wp[i]);
+            launch_or_fail(launch_gemv_tol(n, w16, outs, (int)m0.in_dim, f(xb), (int)rows, yp, stream_),
+                           "project (tolerance)");
             return;
         }
         launch_or_fail(launch_project_set(m0.src, n, wp, sp, outs, (int)m0.in_dim, f(xb), (int)rows, yp, d_err_,
@@ -1521,24 +1543,27 @@ private:
             grow_staging(kStageSegs * std::max<size_t>(2 * need, 1 << 17));
             seg = stage_cap_ / kStageSegs;
         }
-        const size_t cur = stage_head_ / seg;
-        if (stage_head_ % seg + need > seg) {  // into the next segment
-            const size_t next = (cur + 1) % kStageSegs;
-            check(cudaEventRecord(stage_ev_[cur], stream_), "cudaEventRecord(staging)");
-            stage_ev_set_[cur] = true;
+        // The segment in use is kept apart from the offset in it: a slice
+        // that ends exactly at a segment's end leaves the offset at the end,
+        // and the next slice then moves on through the event hand-over (an
+        // offset taken from one running head would slip into the next
+        // segment, or past the ring's end, without it).
+        if (stage_off_ + need > seg) {  // into the next segment
+            const size_t next = (stage_seg_ + 1) % kStageSegs;
+            check(cudaEventRecord(stage_ev_[stage_seg_], stream_), "cudaEventRecord(staging)");
+            stage_ev_set_[stage_seg_] = true;
             if (stage_ev_set_[next]) check(cudaEventSynchronize(stage_ev_[next]), "staging ring");
             stage_ev_set_[next] = false;
-            stage_head_ = next * seg;
+            stage_seg_ = next;
+            stage_off_ = 0;
         }
-        char *h = stage_host_ + stage_head_;
-        char *d = stage_dev_ + stage_head_;
+        const size_t at = stage_seg_ * seg + stage_off_;
+        stage_off_ += need;
+        char *h = stage_host_ + at;
+        char *d = stage_dev_ + at;
         std::memcpy(h, src, bytes);
-        if (in_place && bytes <= kStageMapped && stage_map_) {
-            stage_head_ += need;
-            return stage_map_ + (h - stage_host_);
-        }
+        if (in_place && bytes <= kStageMapped && stage_map_) return stage_map_ + at;
         check(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, stream_), "stage");
-        stage_head_ += need;
         return d;
     }
 
@@ -1553,7 +1578,8 @@ private:
         if (cudaHostGetDevicePointer(&map, stage_host_, 0) == cudaSuccess) stage_map_ = static_cast<char *>(map);
         else cudaGetLastError();  // no mapping: every slice is uploaded
         stage_cap_ = cap;
-        stage_head_ = 0;
+        stage_seg_ = 0;
+        stage_off_ = 0;
         for (int i = 0; i < kStageSegs; ++i) {  // a new ring: every segment free
             if (!stage_ev_[i]) check(cudaEventCreateWithFlags(&stage_ev_[i], cudaEventDisableTiming), "cudaEventCreate");
             stage_ev_set_[i] = false;
@@ -1650,7 +1676,7 @@ private:
     std::vector<std::pair<char *, char *>> retired_;  // grown-out staging rings, freed at the next barrier
     cudaEvent_t stage_ev_[kStageSegs] = {};  // per staging segment: recorded when the ring last left it
     bool stage_ev_set_[kStageSegs] = {};
-    size_t stage_cap_ = 0, stage_head_ = 0;
+    size_t stage_cap_ = 0, stage_seg_ = 0, stage_off_ = 0;  // the ring, its segment in use, the offset in it
 };
 
 }  // namespace krt

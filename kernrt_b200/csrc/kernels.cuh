@@ -129,6 +129,21 @@ bool project_tc_supported(int out_dim, int in_dim, const void *w, const float *x
 cudaError_t launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t n, cudaStream_t s);
 cudaError_t launch_project_tc(const uint16_t *w, int out_dim, int in_dim, const uint16_t *hi, const uint16_t *lo,
                               int rows, float *y, int *err, cudaStream_t s);
+
+// Tolerance mode, decode-sized calls: up to three bf16 matrices [out_dim[i],
+// in_dim] over one x of 1..4 rows, y[i] = W[i] x, each output a warp-wide sum
+// (not the reference's left-to-right order).  in_dim % 8 == 0, x and the
+// matrices 16-byte aligned.
+struct TolGemvSet {
+    const uint16_t *w[3];
+    float *y[3];
+    int out_dim[3];
+    int end[3];  // running totals of out_dim
+    int n;
+};
+bool gemv_tol_supported(const void *w, const float *x, int in_dim, int rows);
+cudaError_t launch_gemv_tol(int n, const uint16_t *const *w, const int *out_dim, int in_dim, const float *x, int rows,
+                            float *const *y, cudaStream_t s);
 // Row i of k and v into cache row dst_rows[i] of caches [rows_total, kv_dim].
 cudaError_t launch_kv_write(float *kc, float *vc, int kv_dim, const int32_t *dst_rows, const float *k, const float *v,
                             int rows, cudaStream_t s);

@@ -305,6 +305,66 @@ bool bf16_map(CUtensorMap *m, const void *ptr, int inner, int outer, int box_out
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tolerance mode, decode-sized calls (at most 4 rows, bf16 weights): the
+// reference's dot (reference.rs:73-79) is one left-to-right chain per output,
+// 2048 to 8192 dependent adds, which caps the exact kernels far below HBM.
+// Here each output is one warp's: lane l takes 16-byte chunks l, l + 32, ...
+// of the weight row (four in flight; eight measured slower), keeps a partial sum per row with fused
+// multiply-adds, and the warp adds the 32 partials by shuffles, so the weights
+// stream at HBM speed.  A set of up to three matrices over one x (q/k/v,
+// gate/up) is one launch over their outputs end to end.
+constexpr int kTolWarps = 8;
+template <int R>
+__global__ void __launch_bounds__(32 * kTolWarps) k_gemv_tol(TolGemvSet set, int in_dim, const float *__restrict__ x) {
+    const int lane = threadIdx.x & 31;
+    const int g = blockIdx.x * kTolWarps + (threadIdx.x >> 5);
+    const int e0 = set.end[0], e1 = set.end[1], e2 = set.end[2];
+    if (g >= (set.n == 1 ? e0 : set.n == 2 ? e1 : e2)) return;
+    const int m = g < e0 ? 0 : (g < e1 ? 1 : 2);
+    const int o = g - (m == 0 ? 0 : (m == 1 ? e0 : e1));
+    const uint16_t *w = m == 0 ? set.w[0] : (m == 1 ? set.w[1] : set.w[2]);
+    float *y = m == 0 ? set.y[0] : (m == 1 ? set.y[1] : set.y[2]);
+    const int out_dim = m == 0 ? set.out_dim[0] : (m == 1 ? set.out_dim[1] : set.out_dim[2]);
+    const uint4 *wr = reinterpret_cast<const uint4 *>(w + (size_t)o * in_dim);
+    const int n8 = in_dim >> 3;
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+    auto step = [&](int c, uint4 u) {
+        const float wv[8] = {__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u),
+                             __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xffff0000u),
+                             __uint_as_float(u.z << 16), __uint_as_float(u.z & 0xffff0000u),
+                             __uint_as_float(u.w << 16), __uint_as_float(u.w & 0xffff0000u)};
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const float4 a = __ldg(reinterpret_cast<const float4 *>(x + (size_t)r * in_dim) + 2 * c);
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(x + (size_t)r * in_dim) + 2 * c + 1);
+            float t = acc[r];
+            t = __fmaf_rn(wv[0], a.x, t); t = __fmaf_rn(wv[1], a.y, t);
+            t = __fmaf_rn(wv[2], a.z, t); t = __fmaf_rn(wv[3], a.w, t);
+            t = __fmaf_rn(wv[4], b.x, t); t = __fmaf_rn(wv[5], b.y, t);
+            t = __fmaf_rn(wv[6], b.z, t); t = __fmaf_rn(wv[7], b.w, t);
+            acc[r] = t;
+        }
+    };
+    int c = lane;
+    for (; c + 96 < n8; c += 128) {  // four chunks in flight
+        const uint4 u0 = __ldcs(wr + c), u1 = __ldcs(wr + c + 32), u2 = __ldcs(wr + c + 64), u3 = __ldcs(wr + c + 96);
+        step(c, u0);
+        step(c + 32, u1);
+        step(c + 64, u2);
+        step(c + 96, u3);
+    }
+    for (; c < n8; c += 32) step(c, __ldcs(wr + c));
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], d);
+    if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < R; ++r) y[(size_t)r * out_dim + o] = acc[r];
+}
+
 }  // namespace
 
 bool project_tc_supported(int out_dim, int in_dim, const void *w, const float *x, const float *y) {
@@ -341,6 +401,38 @@ cudaError_t launch_project_tc(const uint16_t *w, int out_dim, int in_dim, const 
     }
     const dim3 grid((unsigned)((out_dim + kTcM - 1) / kTcM), (unsigned)((rows + kTcN - 1) / kTcN));
     k_project_tc<<<grid, kTcThreads, kTcSmem, s>>>(tw, thi, tlo, out_dim, in_dim, rows, y, err);
+    count_launch();
+    return cudaGetLastError();
+}
+
+bool gemv_tol_supported(const void *w, const float *x, int in_dim, int rows) {
+    return rows >= 1 && rows <= 4 && in_dim > 0 && in_dim % 8 == 0 && ((uintptr_t)w & 15) == 0 &&
+           ((uintptr_t)x & 15) == 0;
+}
+
+cudaError_t launch_gemv_tol(int n, const uint16_t *const *w, const int *out_dim, int in_dim, const float *x, int rows,
+                            float *const *y, cudaStream_t s) {
+    if (n < 1 || n > 3 || rows < 1 || rows > 4) return cudaErrorInvalidValue;
+    TolGemvSet set{};
+    int total = 0;
+    for (int i = 0; i < 3; ++i) {
+        if (i < n) {
+            set.w[i] = w[i];
+            set.y[i] = y[i];
+            set.out_dim[i] = out_dim[i];
+            total += out_dim[i];
+        }
+        set.end[i] = total;
+    }
+    set.n = n;
+    if (total == 0) return cudaSuccess;
+    const unsigned grid = (unsigned)((total + kTolWarps - 1) / kTolWarps);
+    switch (rows) {
+    case 1: k_gemv_tol<1><<<grid, 32 * kTolWarps, 0, s>>>(set, in_dim, x); break;
+    case 2: k_gemv_tol<2><<<grid, 32 * kTolWarps, 0, s>>>(set, in_dim, x); break;
+    case 3: k_gemv_tol<3><<<grid, 32 * kTolWarps, 0, s>>>(set, in_dim, x); break;
+    default: k_gemv_tol<4><<<grid, 32 * kTolWarps, 0, s>>>(set, in_dim, x); break;
+    }
     count_launch();
     return cudaGetLastError();
 }

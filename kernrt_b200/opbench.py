@@ -365,18 +365,25 @@ def model_decode(B, n_layers: int = 24, pos: int = 511, samples: int = 50):
         b.logits(cls, xb, logits)
         b.read_into(logits, out)
 
-    for _ in range(3):
-        step(pos)
-    times = []
-    for _ in range(samples):
-        t0 = time.perf_counter()
-        step(pos)
-        times.append((time.perf_counter() - t0) * 1e3)
-    times.sort()
-    B.rows.append({"name": f"decode token, SmolLM2-1.7B ({n_layers} layers, bf16, pos {pos}): trait ops + read()",
-                   "ms": None, "us_p10": times[len(times) // 10] * 1e3, "us_median": times[len(times) // 2] * 1e3,
-                   "gbs": None, "frac": None, "launches": None,
-                   "note": f"host wall clock, {samples} samples; {1e3 / times[len(times) // 2]:.0f} tokens/s"})
+    for exact in (True, False):
+        # tolerance mode: every projection and the classifier as warp sums
+        b.set_exact(exact)
+        try:
+            for _ in range(3):
+                step(pos)
+            times = []
+            for _ in range(samples):
+                t0 = time.perf_counter()
+                step(pos)
+                times.append((time.perf_counter() - t0) * 1e3)
+        finally:
+            b.set_exact(True)
+        times.sort()
+        mode = "" if exact else ", tolerance mode"
+        B.rows.append({"name": f"decode token, SmolLM2-1.7B ({n_layers} layers, bf16, pos {pos}{mode}): trait ops + read()",
+                       "ms": None, "us_p10": times[len(times) // 10] * 1e3, "us_median": times[len(times) // 2] * 1e3,
+                       "gbs": None, "frac": None, "launches": None,
+                       "note": f"host wall clock, {samples} samples; {1e3 / times[len(times) // 2]:.0f} tokens/s"})
 
 
 def load_table(B, vocab: int = 49152, dim: int = 2048, samples: int = 5):
@@ -468,6 +475,18 @@ def contractions(B):
            2 * wk.hidden * H * 2, note="one launch; chains of 2048")
     B.time("project down decode (2048x8192 bf16)", lambda: b.project(mdown, xd, yd, 1), H * wk.hidden * 2,
            note="chains of 8192")
+    # the same in tolerance mode: each output a warp-wide sum
+    if B.want("decode, tolerance mode"):
+        b.set_exact(False)
+        try:
+            B.time("project_qkv decode, tolerance mode", lambda: b.project_qkv(*mqkv, xd, yq, yk, yv, 1),
+                   3 * H * H * 2, note="one launch; warp sums")
+            B.time("project_gate_up decode, tolerance mode", lambda: b.project_gate_up(*mgu, xd, yg, yu, 1),
+                   2 * wk.hidden * H * 2, note="one launch; warp sums")
+            B.time("project down decode, tolerance mode", lambda: b.project(mdown, xd, yd, 1), H * wk.hidden * 2,
+                   note="warp sums")
+        finally:
+            b.set_exact(True)
     codes = rng.integers(-127, 128, size=(3072, 1024), dtype=np.int8)
     sc = rng.uniform(1e-4, 1e-2, size=(3072, 32)).astype(np.float32)
     mg = b.prepare_matrix(Q8_0, codes, sc, 3072, 1024)
@@ -478,6 +497,13 @@ def contractions(B):
     ml = b.prepare_matrix(BF16, emb.astype(np.uint16), None, vocab, H)
     xl, yl = B.buf(H), b.alloc(vocab)
     B.time(f"logits bf16 {vocab}x{H}", lambda: b.logits(ml, xl, yl), vocab * H * 2 + vocab * 4)
+    if B.want(f"logits bf16 {vocab}x{H}, tolerance mode"):
+        b.set_exact(False)
+        try:
+            B.time(f"logits bf16 {vocab}x{H}, tolerance mode", lambda: b.logits(ml, xl, yl), vocab * H * 2 + vocab * 4,
+                   note="warp sums")
+        finally:
+            b.set_exact(True)
     # attention: 32 heads x 64, the cache of one layer, seq 4096
     n_heads, head, seq = 32, 64, 4096
     kv_dim = n_heads * head

@@ -217,6 +217,28 @@ def test_rope(gpu, oracle, rows, qw, kvw, head, theta, interleaved):
     assert_bits_equal(rd(gpu, hk, (rows, kvw)), wk, "rope k")
 
 
+def test_many_small_staged_slices_wrap_the_staging_ring(oracle):
+    """12 000 one-row rope calls with no barrier between them: each stages its
+    position (256 bytes of the 1 MB staging ring, read in place by the
+    kernel), so the ring wraps three times, every slice ending exactly on a
+    segment boundary at some point.  The rotations must come out as the same
+    sequence applied by the oracle."""
+    head, w = 8, 16
+    q = _data.lcg_normal(w, 35).reshape(1, w)
+    k = _data.lcg_normal(w, 36).reshape(1, w)
+    positions = [int(p) for p in np.random.default_rng(37).integers(0, 64, 12000)]
+    with kernrt_b200.CudaBackend(0) as b:  # a fresh ring of the default size
+        hq, hk = up(b, q), up(b, k)
+        for p in positions:
+            b.rope(hq, hk, w, w, 1, [p], head, 1e4, False)
+        got_q, got_k = rd(b, hq, (1, w)), rd(b, hk, (1, w))
+    wq, wk = q, k
+    for p in positions:
+        wq, wk = oracle.rope(wq, wk, [p], head, 1e4)
+    assert_bits_equal(got_q, wq, "q after 12 000 rotations")
+    assert_bits_equal(got_k, wk, "k after 12 000 rotations")
+
+
 def test_rope_takes_min_of_rows_and_positions(gpu, oracle):
     rows, w, head = 4, 64, 16
     q = _data.lcg_normal(rows * w, 33).reshape(rows, w)
