@@ -321,9 +321,10 @@ int kernrt_cuda_prepare_matrix(kernrt_cuda_ctx *ctx, int kind, const void *data,
  * (tcgen05.mma, f32 accumulation), which keeps ~16 bits of each activation's
  * mantissa; results differ from the reference's sequential dot by the
  * reordered f32 sum (the bar tests/backends.rs:129-148 sets for a non-oracle
- * backend is 1e-3 on a model's logits).  Other storages and decode-sized calls
- * stay exact.  KERNRT_CUDA_EXACT=0 in the environment sets exact = 0 at
- * kernrt_cuda_create. */
+ * backend is 1e-3 on a model's logits).  bf16 projections of 1 to 4 rows
+ * (decode, the classifier) sum each output across a warp instead of in one
+ * chain.  5 to 15 rows and other storages stay exact.  KERNRT_CUDA_EXACT=0 in
+ * the environment sets exact = 0 at kernrt_cuda_create. */
 int kernrt_cuda_set_exact(kernrt_cuda_ctx *ctx, int exact);
 
 /* Backend::project (mod.rs:318; reference.rs:259-274): y[r, o] =

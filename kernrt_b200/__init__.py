@@ -425,8 +425,8 @@ class CudaBackend:
 
     def set_exact(self, exact: bool) -> None:
         """kernrt_cuda_set_exact: False sends bf16 projections of >= 16 rows to
-        the tensor cores (tolerance mode); True (the default) keeps them in
-        the reference's order."""
+        the tensor cores and those of 1-4 rows to warp-wide sums (tolerance
+        mode); True (the default) keeps them in the reference's order."""
         _ok(self._lib.kernrt_cuda_set_exact(self._ctx, int(bool(exact))))
 
     def project(self, w: int, x: int, y: int, rows: int) -> None:
