@@ -710,8 +710,16 @@ public:
         }
         if (attention_smem_bytes((int)head_size, (int)max_count) > 200 * 1024)
             fail(KERNRT_E_INVALID, "attention window too long for one SM's shared memory");
-        // raw scores go to a scratch the backend keeps (grown, never shrunk)
-        const size_t need = attention_scratch_floats((int)n_windows, (int)n_heads, (int)max_count) * sizeof(float);
+        // Tolerance mode, decode-sized calls (at most 4 windows): the window
+        // in chunks summed in parallel (prefill keeps the exact kernels, whose
+        // row-tiled scores share key tiles and measured faster there).
+        const bool tol_att = !exact_ && n_windows <= 4;
+        // raw scores (or the chunks' partial sums) go to a scratch the backend
+        // keeps (grown, never shrunk)
+        const size_t need =
+            (tol_att ? attention_tol_scratch_floats((int)n_windows, (int)n_heads, (int)head_size, (int)max_count)
+                     : attention_scratch_floats((int)n_windows, (int)n_heads, (int)max_count)) *
+            sizeof(float);
         if (need > att_scratch_bytes_) {
             check(cudaStreamSynchronize(stream_), "synchronize");
             cudaFree(att_scratch_);
@@ -725,6 +733,13 @@ public:
         for (size_t i = 1; i < n_windows && shared_map; ++i)
             shared_map = win[4 * i] == win[0] && win[4 * i + 2] == win[2] && win[4 * i + 3] == win[3];
         const int32_t *d = static_cast<const int32_t *>(stage(win.data(), win.size() * sizeof(int32_t)));
+        if (tol_att) {
+            launch_or_fail(launch_attention_tol(f(qb), f(ob), f(ab), kc_, vc_, d, (int)n_windows, (int)n_heads,
+                                                (int)kv_mul, (int)head_size, (int)kv_dim, (int)seq_len,
+                                                layer * seq_len * kv_dim, (int)max_count, att_scratch_, stream_),
+                           "attention (tolerance)");
+            return;
+        }
         launch_or_fail(launch_attention(f(qb), f(ob), f(ab), kc_, vc_, d, (int)n_windows, (int)n_heads, (int)kv_mul,
                                         (int)head_size, (int)kv_dim, (int)seq_len, layer * seq_len * kv_dim,
                                         (int)max_count, att_scratch_, shared_map, stream_),

@@ -793,6 +793,154 @@ __global__ void __launch_bounds__(128) k_att_out(float *__restrict__ out, float 
     if (tid < ne) out[(size_t)rh * head_size + e0 + tid] = o;
 }
 
+// ---- attention in tolerance mode ------------------------------------------------
+// The reference's softmax sum and output elements are chains over the window
+// (reference.rs:448-480); in tolerance mode (kernrt_cuda_set_exact(ctx, 0))
+// the window is cut into chunks of kTolChunk positions summed in parallel
+// (64: a decode row at position 511 spreads over 8 chunks per head).
+// Pass 1, per (row, head, chunk): the scores (fused multiply-adds), the
+// chunk's maximum m, its sum l of exp(s - m) by a block reduction, and its
+// partial output o[e] = sum of exp(s_i - m) v_i[e]; the raw scores go to att.
+// Pass 2, per (row, head): M = max m, L = sum of l exp(m - M), out = sum of o
+// exp(m - M) / L, att[i] = exp(s_i - M) / L.
+constexpr int kTolChunk = 64;
+
+__device__ __forceinline__ float block_reduce128(float v, bool is_max, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float t = __shfl_xor_sync(kFullMask, v, o);
+        v = is_max ? fmaxf(v, t) : v + t;
+    }
+    __syncthreads();  // red is free
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    return is_max ? fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])) : (red[0] + red[1]) + (red[2] + red[3]);
+}
+
+__global__ void __launch_bounds__(128) k_att_tol_part(const float *__restrict__ q, float *__restrict__ att,
+                                                      float *__restrict__ part, const float *__restrict__ kc,
+                                                      const float *__restrict__ vc, const int32_t *__restrict__ win,
+                                                      int n_heads, int kv_mul, int head_size, int kv_dim,
+                                                      int seq_len, size_t loff, int nch) {
+    extern __shared__ __align__(16) float tsm[];
+    const int rh = blockIdx.x, row = rh / n_heads, h = rh - row * n_heads, c = blockIdx.y, tid = threadIdx.x;
+    const int32_t *w = win + 4 * row;
+    const int count = (w[3] - w[2]) + w[1] - w[0] + 1, i0 = c * kTolChunk;
+    if (i0 >= count) return;
+    const int np = min(kTolChunk, count - i0), hs4 = (head_size + 3) & ~3;
+    float *qh = tsm, *p = tsm + hs4, *acc = p + kTolChunk;  // acc: [128]
+    __shared__ float red[4];
+    const float *qg = q + (size_t)rh * head_size;
+    for (int e = tid; e < head_size; e += 128) qh[e] = qg[e];
+    __syncthreads();
+    const size_t kv = loff + (size_t)(h / kv_mul) * head_size;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)head_size));
+    float m = -INFINITY;
+    for (int i = tid; i < np; i += 128) {
+        const float *kr = kc + kv + (size_t)win_pos(w, i0 + i) * kv_dim;
+        float d = 0.0f;
+        if ((head_size & 3) == 0 && ((uintptr_t)kr & 15) == 0) {
+            // eight float4 of the key in flight, then their products
+            for (int e0 = 0; e0 < head_size; e0 += 32) {
+                float4 k4[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (e0 + 4 * j < head_size) k4[j] = __ldg(reinterpret_cast<const float4 *>(kr + e0) + j);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (e0 + 4 * j >= head_size) break;
+                    const float4 q4 = *reinterpret_cast<const float4 *>(qh + e0 + 4 * j);
+                    d = __fmaf_rn(q4.x, k4[j].x, d);
+                    d = __fmaf_rn(q4.y, k4[j].y, d);
+                    d = __fmaf_rn(q4.z, k4[j].z, d);
+                    d = __fmaf_rn(q4.w, k4[j].w, d);
+                }
+            }
+        } else {
+            for (int e = 0; e < head_size; ++e) d = __fmaf_rn(qh[e], __ldg(kr + e), d);
+        }
+        const float sc = d * scale;
+        p[i] = sc;
+        att[(size_t)rh * seq_len + i0 + i] = sc;
+        m = fmaxf(m, sc);  // NaN scores skipped, as the reference's `>` does
+    }
+    m = block_reduce128(m, true, red);
+    float l = 0.0f;
+    for (int i = tid; i < np; i += 128) {
+        const float e = expf(p[i] - m);
+        p[i] = e;
+        l += e;
+    }
+    l = block_reduce128(l, false, red);  // its barriers also publish p
+    // partial output: thread t takes element t % hs of positions t / hs, t / hs
+    // + G, ... (G = 128 / hs groups when hs <= 128), the groups then added
+    float *pg = part + ((size_t)rh * nch + c) * (2 + head_size);
+    if (head_size <= 128) {
+        const int G = 128 / head_size, e = tid % head_size, gi = tid / head_size;
+        float o = 0.0f;
+        if (gi < G) {
+            int i = gi;
+            for (; i + 7 * G < np; i += 8 * G) {  // eight value rows in flight
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = __ldg(vc + kv + (size_t)win_pos(w, i0 + i + j * G) * kv_dim + e);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o = __fmaf_rn(p[i + j * G], v[j], o);
+            }
+            for (; i < np; i += G) o = __fmaf_rn(p[i], __ldg(vc + kv + (size_t)win_pos(w, i0 + i) * kv_dim + e), o);
+        }
+        acc[tid] = o;
+        __syncthreads();
+        if (tid < head_size) {
+            float t = 0.0f;
+            for (int g2 = 0; g2 < G; ++g2) t += acc[g2 * head_size + tid];
+            pg[2 + tid] = t;
+        }
+    } else {
+        for (int e = tid; e < head_size; e += 128) {
+            float o = 0.0f;
+            int i = 0;
+            for (; i + 8 <= np; i += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = __ldg(vc + kv + (size_t)win_pos(w, i0 + i + j) * kv_dim + e);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o = __fmaf_rn(p[i + j], v[j], o);
+            }
+            for (; i < np; ++i) o = __fmaf_rn(p[i], __ldg(vc + kv + (size_t)win_pos(w, i0 + i) * kv_dim + e), o);
+            pg[2 + e] = o;
+        }
+    }
+    if (tid == 0) {
+        pg[0] = m;
+        pg[1] = l;
+    }
+}
+
+__global__ void __launch_bounds__(128) k_att_tol_combine(float *__restrict__ out, float *__restrict__ att,
+                                                         const float *__restrict__ part,
+                                                         const int32_t *__restrict__ win, int n_heads, int head_size,
+                                                         int seq_len, int nch) {
+    const int rh = blockIdx.x, row = rh / n_heads, tid = threadIdx.x;
+    const int32_t *w = win + 4 * row;
+    const int count = (w[3] - w[2]) + w[1] - w[0] + 1;
+    const int nc = (count + kTolChunk - 1) / kTolChunk;
+    const float *pr = part + (size_t)rh * nch * (2 + head_size);
+    float M = -INFINITY;
+    for (int c = 0; c < nc; ++c) M = fmaxf(M, pr[(size_t)c * (2 + head_size)]);
+    float L = 0.0f;
+    for (int c = 0; c < nc; ++c) L += pr[(size_t)c * (2 + head_size) + 1] * expf(pr[(size_t)c * (2 + head_size)] - M);
+    const float inv = 1.0f / L;
+    for (int e = tid; e < head_size; e += 128) {
+        float o = 0.0f;
+        for (int c = 0; c < nc; ++c)
+            o += pr[(size_t)c * (2 + head_size) + 2 + e] * expf(pr[(size_t)c * (2 + head_size)] - M);
+        out[(size_t)rh * head_size + e] = o * inv;
+    }
+    float *ar = att + (size_t)rh * seq_len;
+    for (int i = tid; i < count; i += 128) ar[i] = expf(ar[i] - M) * inv;
+}
+
 }  // namespace
 
 cudaError_t launch_project(int src, const void *w, const float *wsc, int out_dim, int in_dim, const float *x,
@@ -915,6 +1063,30 @@ cudaError_t launch_attention(const float *q, float *out, float *att, const float
     }
     k_attention<<<(unsigned)(n_rows * n_heads), 128, smem, s>>>(q, out, att, kc, vc, win, n_heads, kv_mul, head_size,
                                                                 kv_dim, seq_len, loff);
+    return launched();
+}
+
+size_t attention_tol_scratch_floats(int n_rows, int n_heads, int head_size, int max_count) {
+    const int nch = (max_count + kTolChunk - 1) / kTolChunk;
+    return (size_t)n_rows * n_heads * nch * (2 + head_size);
+}
+
+cudaError_t launch_attention_tol(const float *q, float *out, float *att, const float *kc, const float *vc,
+                                 const int32_t *win, int n_rows, int n_heads, int kv_mul, int head_size, int kv_dim,
+                                 int seq_len, size_t loff, int max_count, float *part, cudaStream_t s) {
+    if (n_rows <= 0 || n_heads <= 0) return cudaSuccess;
+    const int nch = (max_count + kTolChunk - 1) / kTolChunk;
+    const size_t smem = (size_t)(((head_size + 3) & ~3) + kTolChunk + 128) * sizeof(float);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(k_att_tol_part, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    k_att_tol_part<<<dim3((unsigned)(n_rows * n_heads), (unsigned)nch), 128, smem, s>>>(
+        q, att, part, kc, vc, win, n_heads, kv_mul, head_size, kv_dim, seq_len, loff, nch);
+    cudaError_t e = launched();
+    if (e != cudaSuccess) return e;
+    k_att_tol_combine<<<(unsigned)(n_rows * n_heads), 128, 0, s>>>(out, att, part, win, n_heads, head_size, seq_len,
+                                                                    nch);
     return launched();
 }
 

@@ -526,6 +526,15 @@ def contractions(B):
     B.time("attention prefill, 512 causal rows (32x64)",
            lambda: b.attention(qp, op, ap, 0, wins, n_heads, 1, head, kv_dim, seq), None,
            note="row-tiled scores (16 rows x 64 positions per CTA), then per-(row, head) softmax and sums in order")
+    if B.want("attention, tolerance mode"):
+        b.set_exact(False)
+        try:
+            for p in (511, 4095):
+                B.time(f"attention decode, 1 row at pos {p} (32x64), tolerance mode",
+                       lambda: b.attention(q1, o1, a1, 0, [(0, p, 0, 0)], n_heads, 1, head, kv_dim, seq),
+                       (p + 1) * kv_dim * 8 + 32 * (p + 1) * 4, note="chunks of 64 positions, then combined")
+        finally:
+            b.set_exact(True)
 
 
 def chain_time(B, wk):

@@ -63,7 +63,7 @@ def test_logits_is_the_classifier_over_row_zero(gpu, oracle):
     assert_bits_equal(gpu.read(hy, vocab), want[0], "logits")
 
 
-def attention_case(gpu, oracle, n_layers, n_heads, n_kv, head, seq_len, layer, writes, windows, seed):
+def attention_case(gpu, oracle, n_layers, n_heads, n_kv, head, seq_len, layer, writes, windows, seed, exact=True):
     kv_dim = n_kv * head
     kv_mul = n_heads // n_kv
     gpu.kv_prepare(n_layers, kv_dim, seq_len)
@@ -80,7 +80,11 @@ def attention_case(gpu, oracle, n_layers, n_heads, n_kv, head, seq_len, layer, w
     q = _data.lcg_normal(len(windows) * width, seed + 50).reshape(len(windows), width)
     hq, ho = gpu.upload(q), gpu.alloc(len(windows) * width)
     ha = gpu.alloc(len(windows) * n_heads * seq_len)
-    gpu.attention(hq, ho, ha, layer, windows, n_heads, kv_mul, head, kv_dim, seq_len)
+    gpu.set_exact(exact)
+    try:
+        gpu.attention(hq, ho, ha, layer, windows, n_heads, kv_mul, head, kv_dim, seq_len)
+    finally:
+        gpu.set_exact(True)
     want_o, want_a = oracle.attention(q, kc, vc, layer, windows, n_heads, kv_mul, head, kv_dim, seq_len)
     got_o = gpu.read(ho, len(windows) * width).reshape(want_o.shape)
     got_a = gpu.read(ha, want_a.size).reshape(want_a.shape)
@@ -129,6 +133,26 @@ def test_attention_shared_range_and_window_start(gpu, oracle):
     # rows attending a shared prefix [0, 6) plus their own sliding range
     wins = [(10, 12, 0, 6), (11, 14, 0, 6), (20, 20, 2, 5)]
     attention_case(gpu, oracle, 3, 6, 3, 16, 32, 2, [(2, list(range(32)))], wins, 320)
+
+
+TOL_CASES = {
+    "decode_gqa": (2, 8, 2, 64, 128, 1, [(1, list(range(41))), (0, [3, 4])], [(0, 40, 0, 0)], 340),
+    "prefill_causal": (1, 4, 4, 32, 64, 0, [(0, list(range(37)))], [(0, r, 0, 0) for r in range(37)], 341),
+    "shared_range": (3, 6, 3, 16, 32, 2, [(2, list(range(32)))], [(10, 12, 0, 6), (11, 14, 0, 6), (20, 20, 2, 5)], 342),
+    "long_window": (1, 2, 1, 128, 4096, 0, [(0, list(range(4096)))], [(0, 4095, 0, 0)], 343),
+    "chunk_edges": (1, 4, 2, 128, 1024, 0, [(0, list(range(600)))], [(0, 63, 0, 0), (0, 64, 0, 0), (0, 599, 0, 0)],
+                    344),
+    "odd_head": (1, 3, 3, 6, 16, 0, [(0, list(range(10)))], [(0, 9, 0, 0), (2, 5, 0, 2)], 345),
+    "wide_head": (1, 2, 1, 256, 64, 0, [(0, list(range(50)))], [(0, 49, 0, 0)], 346),
+}
+
+
+@pytest.mark.parametrize("case", list(TOL_CASES))
+def test_attention_tolerance_mode(gpu, oracle, case):
+    """kernrt_cuda_set_exact(ctx, 0): calls of at most 4 windows take the
+    window in chunks of 64 positions summed in parallel and combined; longer
+    calls (prefill) stay exact; both within the same bounds."""
+    attention_case(gpu, oracle, *TOL_CASES[case], exact=False)
 
 
 def test_attention_long_window(gpu, oracle):
