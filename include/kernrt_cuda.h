@@ -323,9 +323,9 @@ int kernrt_cuda_prepare_matrix(kernrt_cuda_ctx *ctx, int kind, const void *data,
  * reordered f32 sum (the bar tests/backends.rs:129-148 sets for a non-oracle
  * backend is 1e-3 on a model's logits).  bf16 projections of 1 to 4 rows
  * (decode, the classifier) sum each output across a warp instead of in one
- * chain, and attention over at most 4 windows sums each window in chunks of
- * 64 positions combined by their maxima.  5 to 15 rows, longer attention calls
- * and other storages stay exact.  KERNRT_CUDA_EXACT=0 in
+ * chain, attention over at most 4 windows sums each window in chunks of 64
+ * positions combined by their maxima, and rms_norm of at most 4 rows sums its
+ * squares by a block reduction.  Larger calls and other storages stay exact.  KERNRT_CUDA_EXACT=0 in
  * the environment sets exact = 0 at kernrt_cuda_create. */
 int kernrt_cuda_set_exact(kernrt_cuda_ctx *ctx, int exact);
 

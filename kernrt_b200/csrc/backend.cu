@@ -782,6 +782,7 @@ public:
         a.x_in = f(xi);
         a.xb = f(o);
         a.w_att = f(w);
+        a.tol = !exact_ && rows <= 4;  // decode-sized: a block reduction
         launch_or_fail(chain_launch(SRC_X, a), "rms_norm");
     }
 
@@ -1383,6 +1384,7 @@ public:
         a.resid = f(buf(p.src));
         a.xb = f(buf(out));
         a.w_att = f(buf(weight));
+        a.tol = !exact_ && rows <= 4;  // decode-sized: a block reduction
         launch_or_fail(launch_add_rms_norm(a, stream_), "add_in_place+rms_norm");
         return true;
     }

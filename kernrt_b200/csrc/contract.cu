@@ -921,20 +921,39 @@ __global__ void __launch_bounds__(128) k_att_tol_combine(float *__restrict__ out
                                                          const float *__restrict__ part,
                                                          const int32_t *__restrict__ win, int n_heads, int head_size,
                                                          int seq_len, int nch) {
+    extern __shared__ __align__(16) float csm[];  // [nch] maxima, then [nch] scales
     const int rh = blockIdx.x, row = rh / n_heads, tid = threadIdx.x;
     const int32_t *w = win + 4 * row;
     const int count = (w[3] - w[2]) + w[1] - w[0] + 1;
-    const int nc = (count + kTolChunk - 1) / kTolChunk;
-    const float *pr = part + (size_t)rh * nch * (2 + head_size);
-    float M = -INFINITY;
-    for (int c = 0; c < nc; ++c) M = fmaxf(M, pr[(size_t)c * (2 + head_size)]);
-    float L = 0.0f;
-    for (int c = 0; c < nc; ++c) L += pr[(size_t)c * (2 + head_size) + 1] * expf(pr[(size_t)c * (2 + head_size)] - M);
-    const float inv = 1.0f / L;
+    const int nc = (count + kTolChunk - 1) / kTolChunk, stride = 2 + head_size;
+    const float *pr = part + (size_t)rh * nch * stride;
+    float *cm = csm, *cf = csm + nch;
+    __shared__ float red[4];
+    // the chunks' maxima and sums, loaded side by side
+    float m = -INFINITY;
+    for (int c = tid; c < nc; c += 128) {
+        cm[c] = pr[(size_t)c * stride];
+        m = fmaxf(m, cm[c]);
+    }
+    const float M = block_reduce128(m, true, red);
+    float l = 0.0f;
+    for (int c = tid; c < nc; c += 128) {
+        const float f = expf(cm[c] - M);
+        cf[c] = f;
+        l += pr[(size_t)c * stride + 1] * f;
+    }
+    const float inv = 1.0f / block_reduce128(l, false, red);  // its barriers also publish cf
     for (int e = tid; e < head_size; e += 128) {
         float o = 0.0f;
-        for (int c = 0; c < nc; ++c)
-            o += pr[(size_t)c * (2 + head_size) + 2 + e] * expf(pr[(size_t)c * (2 + head_size)] - M);
+        int c = 0;
+        for (; c + 8 <= nc; c += 8) {  // eight chunks' partials in flight
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = pr[(size_t)(c + j) * stride + 2 + e];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o = __fmaf_rn(v[j], cf[c + j], o);
+        }
+        for (; c < nc; ++c) o = __fmaf_rn(pr[(size_t)c * stride + 2 + e], cf[c], o);
         out[(size_t)rh * head_size + e] = o * inv;
     }
     float *ar = att + (size_t)rh * seq_len;
@@ -1085,8 +1104,8 @@ cudaError_t launch_attention_tol(const float *q, float *out, float *att, const f
         q, att, part, kc, vc, win, n_heads, kv_mul, head_size, kv_dim, seq_len, loff, nch);
     cudaError_t e = launched();
     if (e != cudaSuccess) return e;
-    k_att_tol_combine<<<(unsigned)(n_rows * n_heads), 128, 0, s>>>(out, att, part, win, n_heads, head_size, seq_len,
-                                                                    nch);
+    k_att_tol_combine<<<(unsigned)(n_rows * n_heads), 128, (size_t)2 * nch * sizeof(float), s>>>(
+        out, att, part, win, n_heads, head_size, seq_len, nch);
     return launched();
 }
 

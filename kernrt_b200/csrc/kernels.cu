@@ -2100,6 +2100,7 @@ __global__ void __launch_bounds__(256) k_norm_small(ChainArgs a) {
     __shared__ float scale_s;
     const int r = blockIdx.x, dim = a.dim, n4 = dim >> 2;
     const float *xr = a.x_in + (size_t)r * dim;
+    float part = 0.0f;  // tolerance mode: this thread's squares
     for (int i = threadIdx.x; i < n4; i += blockDim.x) {
         float4 v = *reinterpret_cast<const float4 *>(xr + 4 * i);
         if constexpr (PRE_ADD) {
@@ -2108,9 +2109,23 @@ __global__ void __launch_bounds__(256) k_norm_small(ChainArgs a) {
             *reinterpret_cast<float4 *>(a.x_out + (size_t)r * dim + 4 * i) = v;
         }
         *reinterpret_cast<float4 *>(row_s + 4 * i) = v;
+        part = __fmaf_rn(v.x, v.x, __fmaf_rn(v.y, v.y, __fmaf_rn(v.z, v.z, __fmaf_rn(v.w, v.w, part))));
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (a.tol) {
+        // tolerance mode: the squares summed by warps, then the 8 warp sums
+        // by thread 0 (dim % 4 == 0: the float4 items cover the row)
+        __shared__ float wsum[8];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(kFull, part, o);
+        if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = part;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float ss = 0.0f;
+            for (int w8 = 0; w8 < (int)(blockDim.x >> 5); ++w8) ss += wsum[w8];
+            scale_s = rms_scale(ss, (float)dim, a.eps);
+        }
+    } else if (threadIdx.x == 0) {
         float ss = chain_add16(0.0f, dim / 16, [&](int b, float(&q)[16]) { squares16_f32(row_s + 16 * b, q); });
         int i = dim & ~15;
         for (; i < dim; ++i) ss = add_rn(ss, mul_rn(row_s[i], row_s[i]));

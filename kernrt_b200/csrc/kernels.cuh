@@ -53,6 +53,9 @@ struct ChainArgs {
     // Scratch of `rows` floats for the two-pass norm stage's row scales, or
     // null (the norm stage then runs as one pipeline).
     float *row_scale;
+    // Tolerance mode, decode-sized norms (k_norm_small): the sum of squares
+    // by a block reduction instead of one left-to-right chain.
+    int tol;
 };
 // Optional callback around the kernels a chain launch issues: called with the
 // stage about to launch, and with STAGE_END after the last one (the backend

@@ -134,6 +134,33 @@ def test_add_in_place_then_rms_norm_fuses(gpu, oracle, rows, dim):
     assert_bits_equal(rd(gpu, hxb, (rows, dim)), oracle.rms_norm(xs, w, 1e-5), "xb")
 
 
+@pytest.mark.parametrize("rows,dim", [(1, 2048), (4, 576), (2, 8192), (1, 36), (5, 2048)])
+def test_rms_norm_tolerance_mode(gpu, oracle, rows, dim):
+    """kernrt_cuda_set_exact(ctx, 0): decode-sized norms (1-4 rows) sum their
+    squares by a block reduction (within 1e-5 relative); 5 rows stay exact.
+    The add_in_place -> rms_norm pair likewise."""
+    x = _data.lcg_normal(rows * dim, 16 + dim).reshape(rows, dim)
+    o = _data.lcg_normal(rows * dim, 17 + dim).reshape(rows, dim)
+    w = _data.lcg_normal(dim, 18, 1.0, 0.1)
+    hx, ho, hw, hxb, hyb = up(gpu, x), up(gpu, o), up(gpu, w), gpu.alloc(rows * dim), gpu.alloc(rows * dim)
+    gpu.set_exact(False)
+    try:
+        gpu.rms_norm(hxb, hx, hw, rows, dim, 1e-5)
+        gpu.add_in_place(hx, ho, rows * dim)
+        gpu.rms_norm(hyb, hx, hw, rows, dim, 1e-5)
+        got, got_add = rd(gpu, hxb, (rows, dim)), rd(gpu, hyb, (rows, dim))
+    finally:
+        gpu.set_exact(True)
+    want = oracle.rms_norm(x, w, 1e-5)
+    want_add = oracle.rms_norm(oracle.add_in_place(x, o), w, 1e-5)
+    if rows <= 4:
+        assert_close_rel(got, want, rtol=1e-5, what="rms_norm (block reduction)")
+        assert_close_rel(got_add, want_add, rtol=1e-5, what="add + rms_norm (block reduction)")
+    else:
+        assert_bits_equal(got, want, "rms_norm, 5 rows")
+        assert_bits_equal(got_add, want_add, "add + rms_norm, 5 rows")
+
+
 def test_rms_norm_partial_rows_leave_the_rest(gpu, oracle):
     rows, dim = 9, 64
     x = _data.lcg_normal(rows * dim, 12).reshape(rows, dim)
