@@ -17,7 +17,9 @@
  * and once in tolerance mode (kernrt_cuda_set_exact(ctx, 0)); one JSON line
  * each.
  *
- * Prints one JSON line: per step the host wall time (issue + read barrier),
+ * Prints one JSON line per mode (exact, then tolerance: kernrt_cuda_set_exact
+ * (ctx, 0), the step's RMSNorms by block reduction): per step the host wall
+ * time (issue + read barrier),
  * p10 and median; the host time to issue the ops before the barrier; the
  * device span from the step's first launch to its last (CUDA events on the
  * backend's stream); and the kernels launched per step.
@@ -226,40 +228,43 @@ int main(int argc, char **argv) {
     float out[DIM];
     double *wall = malloc(steps * sizeof(double)), *issue = malloc(steps * sizeof(double)),
            *span = malloc(steps * sizeof(double));
-    uint64_t l0 = 0, l1 = 0;
-    for (int i = -WARM; i < steps; ++i) {
-        if (i == 0) ok(kernrt_cuda_kernel_launches(&l0), "launches");
-        const double t0 = now_us();
-        cuda_ok(cudaEventRecord(ev0, stream), "record");
-        ok(kernrt_cuda_embed(ctx, 7, x, 0), "embed");
-        ok(kernrt_cuda_rms_norm(ctx, xb, x, w, 1, DIM, eps), "rms_norm");
-        ok(kernrt_cuda_rope(ctx, q, k, QD, KVD, 1, &pos, 1, HEAD, theta, 0), "rope");
-        ok(kernrt_cuda_add_in_place(ctx, x, o, DIM), "add");
-        ok(kernrt_cuda_rms_norm(ctx, xb, x, w, 1, DIM, eps), "rms_norm");
-        ok(kernrt_cuda_silu_mul(ctx, g, u, HIDDEN), "silu_mul");
-        ok(kernrt_cuda_add_in_place(ctx, x, o, DIM), "add");
-        ok(kernrt_cuda_flush(ctx), "flush");
-        const double t_issued = now_us();
-        cuda_ok(cudaEventRecord(ev1, stream), "record");
-        ok(kernrt_cuda_read(ctx, x, out, DIM), "read");
-        const double t1 = now_us();
-        if (i >= 0) {
-            float ms = 0.0f;
-            cuda_ok(cudaEventElapsedTime(&ms, ev0, ev1), "elapsed");
-            wall[i] = t1 - t0;
-            issue[i] = t_issued - t0;
-            span[i] = ms * 1e3;
+    for (int exact = 1; exact >= 0; --exact) {
+        ok(kernrt_cuda_set_exact(ctx, exact), "set_exact");
+        uint64_t l0 = 0, l1 = 0;
+        for (int i = -WARM; i < steps; ++i) {
+            if (i == 0) ok(kernrt_cuda_kernel_launches(&l0), "launches");
+            const double t0 = now_us();
+            cuda_ok(cudaEventRecord(ev0, stream), "record");
+            ok(kernrt_cuda_embed(ctx, 7, x, 0), "embed");
+            ok(kernrt_cuda_rms_norm(ctx, xb, x, w, 1, DIM, eps), "rms_norm");
+            ok(kernrt_cuda_rope(ctx, q, k, QD, KVD, 1, &pos, 1, HEAD, theta, 0), "rope");
+            ok(kernrt_cuda_add_in_place(ctx, x, o, DIM), "add");
+            ok(kernrt_cuda_rms_norm(ctx, xb, x, w, 1, DIM, eps), "rms_norm");
+            ok(kernrt_cuda_silu_mul(ctx, g, u, HIDDEN), "silu_mul");
+            ok(kernrt_cuda_add_in_place(ctx, x, o, DIM), "add");
+            ok(kernrt_cuda_flush(ctx), "flush");
+            const double t_issued = now_us();
+            cuda_ok(cudaEventRecord(ev1, stream), "record");
+            ok(kernrt_cuda_read(ctx, x, out, DIM), "read");
+            const double t1 = now_us();
+            if (i >= 0) {
+                float ms = 0.0f;
+                cuda_ok(cudaEventElapsedTime(&ms, ev0, ev1), "elapsed");
+                wall[i] = t1 - t0;
+                issue[i] = t_issued - t0;
+                span[i] = ms * 1e3;
+            }
         }
+        ok(kernrt_cuda_kernel_launches(&l1), "launches");
+        qsort(wall, steps, sizeof(double), cmp);
+        qsort(issue, steps, sizeof(double), cmp);
+        qsort(span, steps, sizeof(double), cmp);
+        printf("{\"name\": \"decode step, configs[1] row ops, C ABI%s\", \"steps\": %d, \"wall_us_p10\": %.2f, "
+               "\"wall_us_median\": %.2f, \"issue_us_median\": %.2f, \"ops\": 7, \"issue_us_per_op\": %.2f, "
+               "\"device_span_us_median\": %.2f, \"launches_per_step\": %.2f}\n",
+               exact ? "" : ", tolerance mode", steps, wall[steps / 10], wall[steps / 2], issue[steps / 2],
+               issue[steps / 2] / 7.0, span[steps / 2], (double)(l1 - l0) / steps);
     }
-    ok(kernrt_cuda_kernel_launches(&l1), "launches");
-    qsort(wall, steps, sizeof(double), cmp);
-    qsort(issue, steps, sizeof(double), cmp);
-    qsort(span, steps, sizeof(double), cmp);
-    printf("{\"name\": \"decode step, configs[1] row ops, C ABI\", \"steps\": %d, \"wall_us_p10\": %.2f, "
-           "\"wall_us_median\": %.2f, \"issue_us_median\": %.2f, \"ops\": 7, \"issue_us_per_op\": %.2f, "
-           "\"device_span_us_median\": %.2f, \"launches_per_step\": %.2f}\n",
-           steps, wall[steps / 10], wall[steps / 2], issue[steps / 2], issue[steps / 2] / 7.0, span[steps / 2],
-           (double)(l1 - l0) / steps);
     free(wall);
     free(issue);
     free(span);
