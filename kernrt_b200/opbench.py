@@ -476,7 +476,8 @@ def contractions(B):
     B.time("project down decode (2048x8192 bf16)", lambda: b.project(mdown, xd, yd, 1), H * wk.hidden * 2,
            note="chains of 8192")
     # the same in tolerance mode: each output a warp-wide sum
-    if B.want("decode, tolerance mode"):
+    if B.want("project_qkv decode, tolerance mode", "project_gate_up decode, tolerance mode",
+              "project down decode, tolerance mode"):
         b.set_exact(False)
         try:
             B.time("project_qkv decode, tolerance mode", lambda: b.project_qkv(*mqkv, xd, yq, yk, yv, 1),
