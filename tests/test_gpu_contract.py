@@ -33,7 +33,8 @@ def weights(kind, out_dim, in_dim, seed, oracle):
 # decode (1 row) and prefill (>= 64 rows) tiles, the scalar kernel otherwise
 SHAPES = [(96, 64, 1), (2048, 2048, 1), (256, 512, 100), (130, 72, 5), (64, 32, 64), (33, 36, 3), (7, 8, 70),
           (100, 1152, 2), (40, 640, 3), (3000, 1024, 4), (77, 8, 1), (64, 96, 2),
-          (5000, 1280, 1), (64, 2560, 2)]  # 512- and 1024-column GEMV chunks, partial last chunks
+          (5000, 1280, 1), (64, 2560, 2),  # 512- and 1024-column GEMV chunks, partial last chunks
+          (64, 1032, 1), (40, 2056, 1)]  # single rows: 16-column steps, then a last chunk of 8 columns
 
 
 @pytest.mark.parametrize("kind", ["f32", "bf16", "q8_0", "q8_0x4"])
