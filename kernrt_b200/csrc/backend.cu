@@ -742,7 +742,7 @@ public:
         }
         launch_or_fail(launch_attention(f(qb), f(ob), f(ab), kc_, vc_, d, (int)n_windows, (int)n_heads, (int)kv_mul,
                                         (int)head_size, (int)kv_dim, (int)seq_len, layer * seq_len * kv_dim,
-                                        (int)max_count, att_scratch_, shared_map, stream_),
+                                        (int)max_count, att_scratch_, shared_map, d_err_, stream_),
                        "attention");
     }
 

@@ -867,6 +867,159 @@ __global__ void __launch_bounds__(128) k_att_out(float *__restrict__ out, float 
     if (tid < ne) out[(size_t)rh * head_size + e0 + tid] = o;
 }
 
+// Decode form of k_att_out (few (row, head) pairs, 32-element slices): the
+// same operations in the same order, with the roles split so the value rows
+// stream while the chains run.  All 128 threads load the raw scores, take the
+// maximum and exp(s - max); then
+//   warps 1-3 stream the slice's value rows through a ring of kDecStages tiles
+//            of kDecTile positions (16-byte cp.async pieces; each thread's
+//            pieces arrive on full[s] when they land, mbarrier.arrive.noinc),
+//            starting while warp 0 still sums;
+//   warp 0   lane 0 runs the sum in position order; then per tile the warp
+//            divides the tile's exps by the sum (writing att for slice 0),
+//            runs out[e] = sum_i a_i v_pos(i)[e] over the tile in position
+//            order, 16 positions a step with the next step's words loaded
+//            ahead, and hands the tile back (empty[s]).
+// One warp issuing the copies of every tile between its chain steps, with a
+// block barrier per tile, ran the chain at ~25 cycles a position; alone it
+// runs at ~6.
+constexpr int kDecTile = 128, kDecStages = 6, kDecSw = 32;
+constexpr int kDecLoaders = 96;
+
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__global__ void __launch_bounds__(128) k_att_out_dec(float *__restrict__ out, float *__restrict__ att,
+                                                     const float *__restrict__ raw, const float *__restrict__ vc,
+                                                     const int32_t *__restrict__ win, int n_heads, int kv_mul,
+                                                     int head_size, int kv_dim, int seq_len, size_t loff, int stride,
+                                                     int *err) {
+    extern __shared__ __align__(16) float osm[];
+    __shared__ __align__(8) uint64_t full[kDecStages], empty[kDecStages];
+    __shared__ float red[4];
+    const int nsl = (head_size + kDecSw - 1) / kDecSw;
+    const int rh = blockIdx.x / nsl, sl = blockIdx.x - rh * nsl;
+    const int row = rh / n_heads, h = rh - row * n_heads;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int32_t *w = win + 4 * row;
+    const int count = (w[3] - w[2]) + w[1] - w[0] + 1;
+    const int e0 = sl * kDecSw, ne = min(kDecSw, head_size - e0), chunks = ne >> 2;
+    float *sc = osm;                           // [stride]
+    float *ring = osm + ((stride + 3) & ~3);   // [kDecStages][kDecTile][kDecSw]
+    if (tid == 0) {
+        for (int i = 0; i < kDecStages; ++i) {
+            mbar_init(&full[i], kDecLoaders);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_fence_init();
+    }
+    const float *rg = raw + (size_t)rh * stride;
+    for (int i = tid; i < count; i += 128) sc[i] = rg[i];
+    __syncthreads();
+    float m = -INFINITY;  // NaN scores skipped, as the reference's `>` does
+    for (int i = tid; i < count; i += 128) m = fmaxf(m, sc[i]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(kFullMask, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    for (int i = tid; i < count; i += 128) sc[i] = expf(__fsub_rn(sc[i], m));
+    __syncthreads();
+    const int ntiles = (count + kDecTile - 1) / kDecTile;
+    if (warp > 0) {
+        const int lt = tid - 32;
+        const size_t vo = loff + (size_t)(h / kv_mul) * head_size + e0;
+        for (int t = 0; t < ntiles; ++t) {
+            const int st = t % kDecStages;
+            if (t >= kDecStages && !mbar_wait_bounded(&empty[st], (uint32_t)(t / kDecStages - 1) & 1u)) {
+                atomicOr(err, ERR_TIMEOUT);
+                break;  // the summing warp stopped
+            }
+            float *dst = ring + (size_t)st * kDecTile * kDecSw;
+            const int p0 = t * kDecTile, np = min(kDecTile, count - p0);
+            for (int c = lt; c < np * chunks; c += kDecLoaders) {
+                const int p = c / chunks, j = c - p * chunks;
+                cp_async16(dst + p * kDecSw + 4 * j, vc + vo + (size_t)win_pos(w, p0 + p) * kv_dim + 4 * j);
+            }
+            cp_async_arrive_noinc(&full[st]);
+        }
+        cp_async_wait<0>();  // nothing in flight when the CTA ends
+        return;
+    }
+    // warp 0
+    float sum = 0.0f;
+    if (lane == 0) sum = seq_sum_smem(sc, count);
+    sum = __shfl_sync(kFullMask, sum, 0);
+    float *ag = att + (size_t)rh * seq_len;
+    float o = 0.0f;
+    for (int t = 0; t < ntiles; ++t) {
+        const int st = t % kDecStages;
+        if (!__all_sync(kFullMask, mbar_wait_bounded(&full[st], (uint32_t)(t / kDecStages) & 1u))) {
+            if (lane == 0) atomicOr(err, ERR_TIMEOUT);
+            return;
+        }
+        const int p0 = t * kDecTile, np = min(kDecTile, count - p0);
+        if (np == kDecTile) {
+            // the tile's kDecTile / 32 quotients of a lane are independent:
+            // loaded, divided and stored side by side
+            float a[kDecTile / 32];
+#pragma unroll
+            for (int j = 0; j < kDecTile / 32; ++j) a[j] = sc[p0 + lane + 32 * j];
+#pragma unroll
+            for (int j = 0; j < kDecTile / 32; ++j) a[j] = __fdiv_rn(a[j], sum);
+#pragma unroll
+            for (int j = 0; j < kDecTile / 32; ++j) {
+                sc[p0 + lane + 32 * j] = a[j];
+                if (sl == 0) ag[p0 + lane + 32 * j] = a[j];
+            }
+        } else {
+            for (int i = lane; i < np; i += 32) {
+                const float a = __fdiv_rn(sc[p0 + i], sum);
+                sc[p0 + i] = a;
+                if (sl == 0) ag[p0 + i] = a;
+            }
+        }
+        __syncwarp();
+        const float *tl = ring + (size_t)st * kDecTile * kDecSw;
+        const float *as = sc + p0;
+        if (lane < ne) {
+            int p = 0;
+            if (np >= 16 && ((uintptr_t)as & 15) == 0) {
+                float4 a4[4];
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) a4[j] = *reinterpret_cast<const float4 *>(as + 4 * j);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = tl[j * kDecSw + lane];
+                for (; p + 16 <= np; p += 16) {
+                    const int pn = p + 32 <= np ? p + 16 : p;  // the next full step, or this one again
+                    float4 na[4];
+                    float nv[16];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) na[j] = *reinterpret_cast<const float4 *>(as + pn + 4 * j);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) nv[j] = tl[(pn + j) * kDecSw + lane];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        o = add_rn(o, mul_rn(a4[j].x, v[4 * j]));
+                        o = add_rn(o, mul_rn(a4[j].y, v[4 * j + 1]));
+                        o = add_rn(o, mul_rn(a4[j].z, v[4 * j + 2]));
+                        o = add_rn(o, mul_rn(a4[j].w, v[4 * j + 3]));
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) a4[j] = na[j];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = nv[j];
+                }
+            }
+            for (; p < np; ++p) o = add_rn(o, mul_rn(as[p], tl[p * kDecSw + lane]));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    if (lane < ne) out[(size_t)rh * head_size + e0 + lane] = o;
+}
+
 // ---- attention in tolerance mode ------------------------------------------------
 // The reference's softmax sum and output elements are chains over the window
 // (reference.rs:448-480); in tolerance mode (kernrt_cuda_set_exact(ctx, 0))
@@ -1109,7 +1262,8 @@ size_t attention_scratch_floats(int n_rows, int n_heads, int max_count) {
 
 cudaError_t launch_attention(const float *q, float *out, float *att, const float *kc, const float *vc,
                              const int32_t *win, int n_rows, int n_heads, int kv_mul, int head_size, int kv_dim,
-                             int seq_len, size_t loff, int max_count, float *raw, bool shared_map, cudaStream_t s) {
+                             int seq_len, size_t loff, int max_count, float *raw, bool shared_map, int *err,
+                             cudaStream_t s) {
     if (n_rows <= 0 || n_heads <= 0) return cudaSuccess;
     // Two kernels where the value slices move in 16-byte pieces and a scratch
     // for the raw scores is given: parallel scores, then per (row, head,
@@ -1138,6 +1292,15 @@ cudaError_t launch_attention(const float *q, float *out, float *att, const float
         }
         cudaError_t e = launched();
         if (e != cudaSuccess) return e;
+        const size_t dec_smem = (size_t)(stride + kDecStages * kDecTile * kDecSw) * sizeof(float);
+        if (few && err && dec_smem <= 200 * 1024) {
+            e = cudaFuncSetAttribute(k_att_out_dec, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dec_smem);
+            if (e != cudaSuccess) return e;
+            const int nsl = (head_size + kDecSw - 1) / kDecSw;
+            k_att_out_dec<<<(unsigned)(n_rows * n_heads * nsl), 128, dec_smem, s>>>(
+                out, att, raw, vc, win, n_heads, kv_mul, head_size, kv_dim, seq_len, loff, stride, err);
+            return launched();
+        }
         const int sw = few ? 32 : (head_size > 128 ? 128 : head_size);
         const int nsl = (head_size + sw - 1) / sw;
         auto kern = few ? k_att_out<12> : k_att_out<3>;

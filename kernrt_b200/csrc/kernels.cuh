@@ -161,7 +161,8 @@ size_t attention_scratch_floats(int n_rows, int n_heads, int max_count);
 // their key tiles.
 cudaError_t launch_attention(const float *q, float *out, float *att, const float *kc, const float *vc,
                              const int32_t *win, int n_rows, int n_heads, int kv_mul, int head_size, int kv_dim,
-                             int seq_len, size_t loff, int max_count, float *raw, bool shared_map, cudaStream_t s);
+                             int seq_len, size_t loff, int max_count, float *raw, bool shared_map, int *err,
+                             cudaStream_t s);
 // Tolerance mode: the window in chunks of 256 positions summed in parallel,
 // then combined (not the reference's order).  part: scratch of
 // attention_tol_scratch_floats() floats.
