@@ -156,6 +156,15 @@ def test_attention_tolerance_mode(gpu, oracle, case):
     attention_case(gpu, oracle, *TOL_CASES[case], exact=False)
 
 
+def test_attention_decode_rows_partial_slices_and_ring_wrap(gpu, oracle):
+    """Decode-sized calls (few (row, head) pairs): head size 80 (value slices
+    of 32, 32 and 16), two query heads per key/value head, windows of 1000 and
+    777 positions (the streamed value tiles wrap their ring and end in a
+    partial tile), one with a shared range, and a 3-position window."""
+    wins = [(0, 999, 0, 0), (300, 1000, 0, 76), (0, 2, 0, 0)]
+    attention_case(gpu, oracle, 1, 4, 2, 80, 1024, 0, [(0, list(range(1024)))], wins, 335)
+
+
 def test_attention_long_window(gpu, oracle):
     attention_case(gpu, oracle, 1, 2, 1, 128, 4096, 0, [(0, list(range(4096)))], [(0, 4095, 0, 0)], 330)
 
