@@ -660,14 +660,34 @@ public:
         Buffer &kb = buf(k), &vb = buf(v);
         span(kb, 0, rows * kv_dim_, "kv_write k");
         span(vb, 0, rows * kv_dim_, "kv_write v");
+        std::vector<int32_t> dst(rows);
+        if (rows > 0) {
+            if (!slots) {
+                flush();
+                fail(KERNRT_E_INVALID, "null slots");
+            }
+            for (size_t i = 0; i < rows; ++i) {
+                if (slots[i] >= kv_seq_) {
+                    flush();
+                    fail(KERNRT_E_INVALID, "slot " + std::to_string(slots[i]) + " out of range");
+                }
+                dst[i] = (int32_t)(layer * kv_seq_ + slots[i]);
+            }
+        }
+        // the driver's rope(q, k) right before: one launch for both
+        if (prope_.on && rows > 0 && prope_.k == k && prope_.rows == rows && v != prope_.q) {
+            PendRope p = std::move(prope_);
+            prope_ = PendRope{};
+            flush();
+            const int32_t *dpos = static_cast<const int32_t *>(stage(p.pos.data(), rows * sizeof(int32_t), true));
+            const int32_t *d = static_cast<const int32_t *>(stage(dst.data(), rows * sizeof(int32_t), true));
+            launch_or_fail(launch_rope_kv(f(buf(p.q)), f(kb), (int)p.qw, (int)p.kvw, (int)rows, (int)p.head, dpos,
+                                          p.cos, p.sin, p.max_pos, d_err_, f(vb), kc_, vc_, d, stream_),
+                           "rope+kv_write");
+            return;
+        }
         flush();
         if (rows == 0) return;
-        if (!slots) fail(KERNRT_E_INVALID, "null slots");
-        std::vector<int32_t> dst(rows);
-        for (size_t i = 0; i < rows; ++i) {
-            if (slots[i] >= kv_seq_) fail(KERNRT_E_INVALID, "slot " + std::to_string(slots[i]) + " out of range");
-            dst[i] = (int32_t)(layer * kv_seq_ + slots[i]);
-        }
         const int32_t *d = static_cast<const int32_t *>(stage(dst.data(), rows * sizeof(int32_t), true));
         launch_or_fail(launch_kv_write(kc_, vc_, (int)kv_dim_, d, f(kb), f(vb), (int)rows, stream_), "kv_write");
     }
@@ -813,6 +833,10 @@ public:
 
     void rope(kernrt_buf q, kernrt_buf k, size_t qw, size_t kvw, size_t rows, const uint64_t *positions,
               size_t n_positions, size_t head, float theta, int interleaved) {
+        // a rope still held back launches first: the table lookup below may
+        // replace (and free, stream-ordered) the table it reads.  Nothing else
+        // is pending beside it.
+        if (prope_.on) flush();
         distinct(q, k);
         if (head == 0 || head % 2) fail(KERNRT_E_INVALID, "head_size must be a positive even number");
         if (interleaved && kvw % 2) fail(KERNRT_E_INVALID, "interleaved RoPE needs an even kv width");
@@ -846,6 +870,20 @@ public:
         float eps = pqk_.eps;
         if (fuse) pqk_.n = 0;
         flush();
+        if (!fuse && !interleaved && kc_ && kvw == kv_dim_ && kvw % head == 0) {
+            prope_.on = true;
+            prope_.q = q;
+            prope_.k = k;
+            prope_.qw = qw;
+            prope_.kvw = kvw;
+            prope_.rows = rows;
+            prope_.head = head;
+            prope_.pos = std::move(pos);
+            prope_.cos = t.cos;
+            prope_.sin = t.sin;
+            prope_.max_pos = (int)t.max_pos;
+            return;
+        }
         const int32_t *dpos = static_cast<const int32_t *>(stage(pos.data(), rows * sizeof(int32_t), true));
         if (fuse) {
             launch_or_fail(launch_qk_rope(f(qb), f(kb), (int)qw, (int)kvw, (int)rows, (int)head, wq, wk, eps, dpos,
@@ -1325,6 +1363,15 @@ public:
     }
 
     void flush_deferred() {
+        if (prope_.on) {
+            prope_.on = false;
+            const int32_t *dpos =
+                static_cast<const int32_t *>(stage(prope_.pos.data(), prope_.rows * sizeof(int32_t), true));
+            launch_or_fail(launch_rope(f(buf(prope_.q)), f(buf(prope_.k)), (int)prope_.qw, (int)prope_.kvw,
+                                       (int)prope_.rows, (int)prope_.head, dpos, prope_.cos, prope_.sin,
+                                       prope_.max_pos, 0, d_err_, stream_),
+                           "rope");
+        }
         if (padd_.len) {
             const PendAdd p = padd_;
             padd_ = PendAdd{};
@@ -1642,9 +1689,21 @@ private:
         long long so = 0, sa = 0, sb = 0;
         long long count = 0;
     };
+    // A half-split rope held back for one call: a kv_write of its k rows that
+    // follows runs with it in one launch (k_rope_kv).  The positions stay on
+    // the host until the launch stages them.
+    struct PendRope {
+        bool on = false;
+        kernrt_buf q = 0, k = 0;
+        size_t qw = 0, kvw = 0, rows = 0, head = 0;
+        std::vector<int32_t> pos;
+        const float *cos = nullptr, *sin = nullptr;
+        int max_pos = 0;
+    };
     PendAdd padd_;
     PendQK pqk_;
     PendMul pmul_;
+    PendRope prope_;
 
     struct PipeSet {
         void *arena = nullptr;

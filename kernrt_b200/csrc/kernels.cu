@@ -233,7 +233,7 @@ __device__ void qk_norm_row_warp(float *v, int width, int head, const float *__r
 // ct/st: the table row of this row's position, `half` entries each.
 // `lane` of `nl` cooperating threads (a warp, or several warps on one row).
 __device__ void rope_half_row(float *v, int nh, int head, int half, const float *__restrict__ ct,
-                              const float *__restrict__ st, bool vec, int lane, int nl = 32) {
+                              const float *__restrict__ st, bool vec, int lane, int nl = 32, float *dup = nullptr) {
     if (vec) {
         const int per = half >> 2, n = nh * per;
         for (int t = lane; t < n; t += nl) {
@@ -255,6 +255,10 @@ __device__ void rope_half_row(float *v, int nh, int head, int half, const float 
             nhv.w = add_rn(mul_rn(lo.w, s.w), mul_rn(hi.w, c.w));
             *reinterpret_cast<float4 *>(b + j) = nl;
             *reinterpret_cast<float4 *>(b + half + j) = nhv;
+            if (dup) {  // the rotated values to a second row as well (a cache row)
+                *reinterpret_cast<float4 *>(dup + h * head + j) = nl;
+                *reinterpret_cast<float4 *>(dup + h * head + half + j) = nhv;
+            }
         }
     } else {
         const int n = nh * half;
@@ -262,8 +266,13 @@ __device__ void rope_half_row(float *v, int nh, int head, int half, const float 
             const int h = t / half, j = t - h * half;
             float *b = v + h * head;
             const float lo = b[j], hi = b[j + half], c = ct[j], s = st[j];
-            b[j] = sub_rn(mul_rn(lo, c), mul_rn(hi, s));
-            b[j + half] = add_rn(mul_rn(lo, s), mul_rn(hi, c));
+            const float a0 = sub_rn(mul_rn(lo, c), mul_rn(hi, s)), a1 = add_rn(mul_rn(lo, s), mul_rn(hi, c));
+            b[j] = a0;
+            b[j + half] = a1;
+            if (dup) {
+                dup[h * head + j] = a0;
+                dup[h * head + j + half] = a1;
+            }
         }
     }
 }
@@ -2421,6 +2430,42 @@ __global__ void __launch_bounds__(kThreads) k_rope(float *q, float *k, int q_wid
     }
 }
 
+// The driver's rope(q, k) then kv_write(layer, slots, k, v) (llama.rs:744-757)
+// in one pass: k_rope's half-split rotation, each lane also storing the k
+// values it rotated to the row's cache slot, and the v row copied to its slot
+// (reference.rs:151-159, 209-257).  kv_width == the cache's kv_dim, a whole
+// number of heads.  A row whose position is out of the table reports it and
+// still writes its k and v rows unrotated, as the two separate calls would.
+__global__ void __launch_bounds__(kThreads) k_rope_kv(float *q, float *k, int q_width, int kv_width, int rows,
+                                                      int head, const int32_t *pos, const float *cos_t,
+                                                      const float *sin_t, int max_pos, int *err, int wpr,
+                                                      const float *v, float *kc, float *vc,
+                                                      const int32_t *dst_rows) {
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int row = gw / wpr;
+    const int lane = (gw - row * wpr) * 32 + (threadIdx.x & 31), nl = 32 * wpr;
+    if (row >= rows) return;
+    float *qr = q + (size_t)row * q_width, *kr = k + (size_t)row * kv_width;
+    float *kd = kc + (size_t)dst_rows[row] * kv_width, *vd = vc + (size_t)dst_rows[row] * kv_width;
+    const float *vr = v + (size_t)row * kv_width;
+    const int p = pos[row];
+    if ((unsigned)p >= (unsigned)max_pos) {
+        if (lane == 0) set_err(err, ERR_POSITION);
+        for (int e = lane; e < kv_width; e += nl) kd[e] = kr[e];
+    } else {
+        const int half = head >> 1;
+        const float *ct = cos_t + (size_t)p * half, *st = sin_t + (size_t)p * half;
+        const bool vec = ((half | q_width | kv_width) & 3) == 0;
+        rope_half_row(qr, q_width / head, head, half, ct, st, vec, lane, nl);
+        rope_half_row(kr, kv_width / head, head, half, ct, st, vec, lane, nl, kd);
+    }
+    if ((kv_width & 3) == 0 && (((uintptr_t)vr | (uintptr_t)vd) & 15) == 0)
+        for (int e = lane; e < kv_width / 4; e += nl)
+            reinterpret_cast<float4 *>(vd)[e] = reinterpret_cast<const float4 *>(vr)[e];
+    else
+        for (int e = lane; e < kv_width; e += nl) vd[e] = vr[e];
+}
+
 // The driver's qk_norm(q), qk_norm(k), rope(q, k) sequence (llama.rs:744-754)
 // in one pass per row: one warp per row normalises each head (reference.rs
 // :180-207) and rotates it (reference.rs:209-257).  Either norm weight may
@@ -3425,6 +3470,18 @@ cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows,
     while (wpr < 8 && (long)rows * 32 * wpr * 2 <= (long)device_sms() * kThreads) wpr *= 2;
     k_rope<<<grid_for((size_t)rows * 32 * wpr, kThreads), kThreads, 0, s>>>(
         q, k, q_width, kv_width, rows, head, pos, cos_t, sin_t, max_pos, interleaved, err, wpr);
+    return launched();
+}
+
+cudaError_t launch_rope_kv(float *q, float *k, int q_width, int kv_width, int rows, int head, const int32_t *pos,
+                           const float *cos_t, const float *sin_t, int max_pos, int *err, const float *v, float *kc,
+                           float *vc, const int32_t *dst_rows, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    if (head <= 0 || kv_width % head != 0) return cudaErrorInvalidValue;
+    int wpr = 1;
+    while (wpr < 8 && (long)rows * 32 * wpr * 2 <= (long)device_sms() * kThreads) wpr *= 2;
+    k_rope_kv<<<grid_for((size_t)rows * 32 * wpr, kThreads), kThreads, 0, s>>>(
+        q, k, q_width, kv_width, rows, head, pos, cos_t, sin_t, max_pos, err, wpr, v, kc, vc, dst_rows);
     return launched();
 }
 

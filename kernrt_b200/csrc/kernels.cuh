@@ -87,6 +87,12 @@ cudaError_t launch_mul_strided(float *out, const float *a, const float *b, long 
 cudaError_t launch_rope(float *q, float *k, int q_width, int kv_width, int rows, int head,
                         const int32_t *pos, const float *cos_t, const float *sin_t, int max_pos,
                         int interleaved, int *err, cudaStream_t s);
+// rope(q, k) and kv_write of k (rotated) and v into cache rows dst_rows (the
+// layer's slots) in one launch; half-split RoPE, kv_width a whole number of
+// heads and the cache's row width.
+cudaError_t launch_rope_kv(float *q, float *k, int q_width, int kv_width, int rows, int head, const int32_t *pos,
+                           const float *cos_t, const float *sin_t, int max_pos, int *err, const float *v, float *kc,
+                           float *vc, const int32_t *dst_rows, cudaStream_t s);
 cudaError_t launch_silu_mul(float *g, const float *u, size_t n, cudaStream_t s);
 cudaError_t launch_add(float *d, const float *src, size_t n, cudaStream_t s);
 cudaError_t launch_mul(float *o, const float *a, const float *b, size_t n, bool sequential,

@@ -165,6 +165,48 @@ def test_attention_decode_rows_partial_slices_and_ring_wrap(gpu, oracle):
     attention_case(gpu, oracle, 1, 4, 2, 80, 1024, 0, [(0, list(range(1024)))], wins, 335)
 
 
+@pytest.mark.parametrize("rows,qw,kvw,head", [(1, 2048, 2048, 64), (5, 1536, 512, 64), (37, 256, 128, 32),
+                                            (3, 96, 48, 12)])
+def test_rope_then_kv_write_is_one_launch(oracle, rows, qw, kvw, head):
+    """The driver's rope(q, k) then kv_write(k, v) (llama.rs:744-757) runs as
+    one launch: q and k come out as the oracle's rotation, and the cache holds
+    what the separate calls write (a barrier between them keeps them apart):
+    attention over either cache gives the same bits."""
+    theta, seq, layer = 1.3e5, 64, 1
+    q = _data.lcg_normal(rows * qw, 360 + rows).reshape(rows, qw)
+    k = _data.lcg_normal(rows * kvw, 361 + rows).reshape(rows, kvw)
+    v = _data.lcg_normal(rows * kvw, 362 + rows).reshape(rows, kvw)
+    slots = np.array([(7 * r + 3) % seq for r in range(rows)], np.uint64)
+    if len(set(slots.tolist())) < rows:
+        slots = np.arange(rows, dtype=np.uint64)
+    n_heads, kv_mul = qw // head, qw // kvw
+    results = {}
+    for fused in (True, False):
+        with kernrt_b200.CudaBackend(0) as b:
+            b.kv_prepare(2, kvw, seq)
+            hq, hk, hv = b.upload(q), b.upload(k), b.upload(v)
+            b.synchronize()
+            n0 = kernrt_b200.kernel_launches()
+            b.rope(hq, hk, qw, kvw, rows, slots, head, theta, False)
+            if not fused:
+                b.synchronize()
+            b.kv_write(layer, slots, hk, hv, rows)
+            b.synchronize()
+            launches = kernrt_b200.kernel_launches() - n0
+            got_q, got_k = b.read(hq, rows * qw).reshape(rows, qw), b.read(hk, rows * kvw).reshape(rows, kvw)
+            hqa = b.upload(_data.lcg_normal(qw, 363))
+            ho, ha = b.alloc(qw), b.alloc(n_heads * seq)
+            b.attention(hqa, ho, ha, layer, [(0, seq - 1, 0, 0)], n_heads, kv_mul, head, kvw, seq)
+            results[fused] = (launches, got_q, got_k, b.read(ho, qw), b.read(ha, n_heads * seq))
+    assert results[True][0] == 1 and results[False][0] == 2
+    want_q, want_k = oracle.rope(q, k, slots, head, theta)
+    for fused in (True, False):
+        assert_bits_equal(results[fused][1], want_q, "rope q")
+        assert_bits_equal(results[fused][2], want_k, "rope k")
+    assert_bits_equal(results[True][3], results[False][3], "attention over the fused cache")
+    assert_bits_equal(results[True][4], results[False][4], "attention weights over the fused cache")
+
+
 def test_attention_long_window(gpu, oracle):
     attention_case(gpu, oracle, 1, 2, 1, 128, 4096, 0, [(0, list(range(4096)))], [(0, 4095, 0, 0)], 330)
 
