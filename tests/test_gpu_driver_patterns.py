@@ -4,9 +4,9 @@ KernRT's drivers call the row ops one trait method at a time, interleaved with
 contractions (src/arch/llm/llama.rs:734-770, lfm2.rs:584-624).  The backend
 defers one op and fuses it with the next when they form one of the driver's
 pairs: embed x R -> rms_norm, add_in_place -> rms_norm, qk_norm(q), qk_norm(k)
--> rope, and per-row mul runs.  These tests replay those sequences (with the
-contractions' outputs uploaded in their place) and require the oracle's bits
-and the fused launch counts.
+-> rope, rope -> kv_write (tests/test_gpu_contract.py), and per-row mul runs.
+These tests replay those sequences (with the contractions' outputs uploaded in
+their place) and require the oracle's bits and the fused launch counts.
 """
 import numpy as np
 import pytest
