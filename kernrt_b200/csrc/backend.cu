@@ -1406,6 +1406,7 @@ public:
         pending_.clear();
         ChainArgs a = blank(rows, dim);
         a.eps = eps;
+        a.tol = !exact_ && rows <= 4;  // decode-sized: a block reduction
         a.table = emb_data_;
         a.tscales = emb_scales_;
         a.vocab = (int)vocab_;

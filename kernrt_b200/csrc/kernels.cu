@@ -2151,6 +2151,71 @@ __global__ void __launch_bounds__(256) k_norm_small(ChainArgs a) {
     }
 }
 
+// The embed -> rms_norm pair for a few rows (decode, llama.rs:734-740): a CTA
+// per row gathers table row tokens[r], decoded to f32 as Matrix::decode_row
+// does (bf16 bits; a Q8_0 code times its block scale, one multiply; f32),
+// into shared memory and x, then runs k_norm_small's exact sum and writes xb.
+// An out-of-range token reports ERR_TOKEN and reads as zeros, as the
+// pipelines do.  dim % 4 == 0 (% 32 for Q8_0).
+template <int SRC>
+__global__ void __launch_bounds__(256) k_norm_small_emb(ChainArgs a) {
+    extern __shared__ __align__(16) float row_s[];
+    __shared__ float scale_s;
+    const int r = blockIdx.x, dim = a.dim, n4 = dim >> 2;
+    const int tok = a.tokens[r];
+    const bool valid = (unsigned)tok < (unsigned)a.vocab;
+    if (!valid && threadIdx.x == 0) set_err(a.err, ERR_TOKEN);
+    float part = 0.0f;  // tolerance mode: this thread's squares
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (valid) {
+            if constexpr (SRC == SRC_BF16) {
+                const uint2 t = reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(a.table) +
+                                                                (size_t)tok * dim)[i];
+                v = make_float4(bf16f(t.x & 0xffffu), bf16f(t.x >> 16), bf16f(t.y & 0xffffu), bf16f(t.y >> 16));
+            } else if constexpr (SRC == SRC_Q8) {
+                const uint32_t t = reinterpret_cast<const uint32_t *>(static_cast<const int8_t *>(a.table) +
+                                                                      (size_t)tok * dim)[i];
+                const float sc = a.tscales[(size_t)tok * (dim >> 5) + (i >> 3)];
+                v = make_float4(mul_rn((float)(int8_t)(t & 0xffu), sc), mul_rn((float)(int8_t)((t >> 8) & 0xffu), sc),
+                                mul_rn((float)(int8_t)((t >> 16) & 0xffu), sc), mul_rn((float)(int8_t)(t >> 24), sc));
+            } else {
+                v = reinterpret_cast<const float4 *>(static_cast<const float *>(a.table) + (size_t)tok * dim)[i];
+            }
+        }
+        if (a.x_out) *reinterpret_cast<float4 *>(a.x_out + (size_t)r * dim + 4 * i) = v;
+        *reinterpret_cast<float4 *>(row_s + 4 * i) = v;
+        part = __fmaf_rn(v.x, v.x, __fmaf_rn(v.y, v.y, __fmaf_rn(v.z, v.z, __fmaf_rn(v.w, v.w, part))));
+    }
+    __syncthreads();
+    if (a.tol) {
+        __shared__ float wsum[8];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(kFull, part, o);
+        if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = part;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float ss = 0.0f;
+            for (int w8 = 0; w8 < (int)(blockDim.x >> 5); ++w8) ss += wsum[w8];
+            scale_s = rms_scale(ss, (float)dim, a.eps);
+        }
+    } else if (threadIdx.x == 0) {
+        float ss = chain_add16(0.0f, dim / 16, [&](int b, float(&q)[16]) { squares16_f32(row_s + 16 * b, q); });
+        int i = dim & ~15;
+        for (; i < dim; ++i) ss = add_rn(ss, mul_rn(row_s[i], row_s[i]));
+        scale_s = rms_scale(ss, (float)dim, a.eps);
+    }
+    __syncthreads();
+    const float sc = scale_s;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+        const float4 v = *reinterpret_cast<const float4 *>(row_s + 4 * i);
+        const float4 w = __ldg(reinterpret_cast<const float4 *>(a.w_att + 4 * i));
+        *reinterpret_cast<float4 *>(a.xb + (size_t)r * dim + 4 * i) =
+            make_float4(mul_rn(w.x, mul_rn(sc, v.x)), mul_rn(w.y, mul_rn(sc, v.y)), mul_rn(w.z, mul_rn(sc, v.z)),
+                        mul_rn(w.w, mul_rn(sc, v.w)));
+    }
+}
+
 // The chain's pure streams (RoPE on Q and K, SwiGLU) over all rows: no
 // shared memory and few registers, so an SM holds many more warps than the
 // norm stage's CTAs allow.  Grid-stride over one flat index space.
@@ -3174,6 +3239,20 @@ bool try_norm_small(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
     return true;
 }
 
+// A CTA per row for a few embed -> rms_norm rows (fewer than half the SMs).
+template <int SRC>
+bool try_norm_small_emb(const ChainArgs &a, cudaStream_t s, cudaError_t *err) {
+    if (a.rows <= 0 || a.rows * 2 > device_sms() || a.dim <= 0 || a.dim % (SRC == SRC_Q8 ? 32 : 4) ||
+        a.dim > 12288)
+        return false;
+    if (!a.xb || !a.tokens || a.resid || a.w_final || !al16(a.table) || !al16(a.xb) || !al16(a.w_att) ||
+        (a.x_out && !al16(a.x_out)) || (SRC == SRC_Q8 && !a.tscales))
+        return false;
+    k_norm_small_emb<SRC><<<(unsigned)a.rows, 256, (size_t)a.dim * sizeof(float), s>>>(a);
+    *err = launched();
+    return true;
+}
+
 // The decoupled column-tiled pipeline for f32 x rows (dim % 8, % 32 when
 // quantising; 16-byte aligned rows).  Returns false (nothing launched) when it
 // does not apply.
@@ -3337,7 +3416,7 @@ cudaError_t launch_chain_src(const ChainArgs &a, cudaStream_t s, const LaunchHoo
         // keeps more rows' sums in flight
         const bool done =
             vec && (SRC == SRC_X ? (try_norm_small<false>(a, s, &e) || try_norm_cols<false, false>(a, s, &e))
-                                 : try_norm_rows<SRC, false>(a, s, &e));
+                                 : (try_norm_small_emb<SRC>(a, s, &e) || try_norm_rows<SRC, false>(a, s, &e)));
         if (!done) e = vec ? launch_norm_pipe<SRC, true>(a, s) : launch_norm_pipe<SRC, false>(a, s);
     }
     if (e != cudaSuccess) return e;

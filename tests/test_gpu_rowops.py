@@ -94,6 +94,47 @@ def test_embed_rejects_bad_token_and_offset(gpu, oracle):
     assert_bits_equal(gpu.read(out, 32)[16:], oracle.bf16_to_f32(table[1]), "embed after error")
 
 
+@pytest.mark.parametrize("kind", ["bf16", "q8_0", "f32"])
+@pytest.mark.parametrize("rows", [1, 3, 40])
+def test_embed_then_rms_norm_few_rows(gpu, oracle, kind, rows):
+    """The driver's embed x rows -> rms_norm pair (llama.rs:734-740) for a few
+    rows (decode): one launch, a CTA per row gathering and normalising in the
+    reference's order, x keeping the gathered rows; in tolerance mode the
+    one-to-four-row form sums the squares by a block reduction."""
+    vocab, dim, eps = 300, 1024, 1e-5
+    if kind == "bf16":
+        table, sc, k = _data.bf16_table(vocab, dim, 60), None, oracle.BF16
+    elif kind == "q8_0":
+        (table, sc), k = _data.q8_table(vocab, dim, 61), oracle.Q8_0
+    else:
+        table, sc, k = _data.lcg_normal(vocab * dim, 62).reshape(vocab, dim), None, oracle.F32
+    toks = _data.tokens(rows, vocab, 63)
+    w = _data.lcg_normal(dim, 64, 1.0, 0.1)
+    gpu.prepare_embedding(k, table, sc, vocab, dim)
+    hw = gpu.upload(w)
+    want_x = oracle.embed_rows(k, table, sc, vocab, dim, toks)
+    want = oracle.rms_norm(want_x, w, eps)
+    for exact in (True, False):
+        x, xb = gpu.alloc(rows * dim), gpu.alloc(rows * dim)
+        gpu.set_exact(exact)
+        try:
+            gpu.synchronize()
+            n0 = kernrt_b200.kernel_launches()
+            for r, t in enumerate(toks):
+                gpu.embed(int(t), x, r * dim)
+            gpu.rms_norm(xb, x, hw, rows, dim, eps)
+            gpu.synchronize()
+            launches = kernrt_b200.kernel_launches() - n0
+        finally:
+            gpu.set_exact(True)
+        assert launches == 1
+        assert_bits_equal(rd(gpu, x, (rows, dim)), want_x, f"x ({kind})")
+        if exact or rows > 4:
+            assert_bits_equal(rd(gpu, xb, (rows, dim)), want, f"xb ({kind})")
+        else:
+            assert_close_rel(rd(gpu, xb, (rows, dim)), want, rtol=1e-5, what=f"xb ({kind}, block reduction)")
+
+
 # --- rms_norm (reference.rs:161-178) ---------------------------------------------------
 
 # Enough rows for several row groups per CTA and several column tiles per row
